@@ -1,0 +1,184 @@
+/*
+ * cuda_bridge.h — C ABI of the B200 (sm_100a) forward + loss engine.
+ *
+ * This library replaces the reference engine's Apple Neural Engine bridge
+ * (crates/ane-bridge + the external `ane` crate: Graph/MIL compile,
+ * Executable::run_cached_direct, IOSurface TensorData staging) for the
+ * transformer forward pass and next-token cross-entropy loss. The engine-level
+ * API it serves is kept: ModelConfig (crates/engine/src/model.rs:5-17),
+ * ModelWeights / LayerWeights (full_model.rs:19-23, layer.rs:52-63),
+ * CompiledKernels::compile_forward_only (layer.rs:967), forward_only_ws /
+ * forward_ws / forward (full_model.rs:378,494,915) and forward_losses
+ * (full_model.rs:1603).
+ *
+ * Conventions
+ *  - Every call returns a cb_status; none aborts the process. The reference
+ *    panics on ANE eval failure (layer.rs:1678, `.expect("ANE eval failed")`);
+ *    here the caller receives CB_ERR_* and cb_last_error() describes it.
+ *  - One cb_ctx per host thread and device (the reference keeps one
+ *    CompiledKernels per worker thread, multistream.rs:70-79). A context is not
+ *    thread-safe.
+ *  - Layout: row-major, token-major [batch*seq, dim] (the reference is
+ *    channel-first [dim, seq] per sequence; its transposes disappear here).
+ *  - Host pointers are plain CPU memory (pinned memory makes copies faster).
+ *    Functions whose names end in _async take device pointers and a CUDA
+ *    stream (cudaStream_t passed as void*; NULL = the context's own stream)
+ *    and do not synchronise.
+ */
+#ifndef RUSTANE_CUDA_BRIDGE_H
+#define RUSTANE_CUDA_BRIDGE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t cb_status;
+#define CB_OK 0
+#define CB_ERR_INVALID_ARG 1   /* bad config, size, pointer or token id */
+#define CB_ERR_CUDA 2          /* CUDA runtime/driver error */
+#define CB_ERR_OUT_OF_MEMORY 3 /* device allocation failed */
+#define CB_ERR_NOT_READY 4     /* weights not loaded */
+#define CB_ERR_UNSUPPORTED 5   /* shape or device the kernels do not handle */
+#define CB_ERR_DEVICE_TIMEOUT 6 /* a bounded device-side wait expired */
+#define CB_ERR_NCCL 7          /* NCCL error (tensor-parallel contexts) */
+
+/* Mirrors ModelConfig (crates/engine/src/model.rs:5-17). q_dim = heads*hd,
+ * kv_dim = kv_heads*hd and gqa_ratio = heads/kv_heads are derived. hd must be
+ * 128 (the reference fixes head_dim = 128, model.rs presets). */
+typedef struct cb_model_config {
+  int32_t dim;
+  int32_t hidden;
+  int32_t heads;
+  int32_t kv_heads;
+  int32_t hd;
+  int32_t seq;
+  int32_t nlayers;
+  int32_t vocab;
+} cb_model_config;
+
+/* Weight init schemes for cb_init_weights. */
+#define CB_INIT_NORMAL 0    /* all matrices ~N(0, sigma), RMSNorm gains 1.0 */
+#define CB_INIT_REFERENCE 1 /* the reference LCG init: ModelWeights::random
+                               (full_model.rs:132-141) + LayerWeights::random
+                               (layer.rs:1509-1524); sigma ignored */
+
+/* Per-layer host weights in the reference orientation (layer.rs:52-63):
+ * wq [dim, q_dim], wk/wv [dim, kv_dim] (x @ W), wo [q_dim, dim],
+ * w1/w3 [dim, hidden], w2 [dim, hidden] (used transposed: gate @ W2^T,
+ * ffn_fused.rs:130), gamma1/gamma2 [dim]. */
+typedef struct cb_layer_weights_f32 {
+  const float* wq;
+  const float* wk;
+  const float* wv;
+  const float* wo;
+  const float* w1;
+  const float* w3;
+  const float* w2;
+  const float* gamma1;
+  const float* gamma2;
+} cb_layer_weights_f32;
+
+/* Per-kernel-class timing collected while profiling is enabled. */
+typedef struct cb_kernel_time {
+  char name[32];
+  int64_t launches;
+  double total_ms;      /* sum of CUDA-event durations */
+  double flops;         /* algorithmic FLOPs over all launches */
+  double bytes;         /* algorithmic HBM bytes over all launches */
+} cb_kernel_time;
+
+typedef struct cb_ctx cb_ctx;
+
+/* Library version string. */
+const char* cb_version(void);
+
+/* Number of visible CUDA devices (0 when there is none). */
+cb_status cb_device_count(int32_t* count);
+
+/* Replaces CompiledKernels::compile_forward_only(&cfg) (layer.rs:967) together
+ * with ModelForwardWorkspace::new_lean (full_model.rs:245): allocates device
+ * weights and a workspace for up to max_batch sequences of cfg->seq tokens on
+ * `device`. Weights are uninitialised until cb_init_weights/cb_load_weights_f32. */
+cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batch,
+                    cb_ctx** out);
+
+/* Frees every device resource of the context. NULL is accepted. */
+cb_status cb_destroy(cb_ctx* ctx);
+
+/* Generates weights on the device (no host copy of the model is needed).
+ * Bit-identical to the CPU oracle's generator for the same (seed, scheme). */
+cb_status cb_init_weights(cb_ctx* ctx, uint64_t seed, int32_t scheme, float sigma);
+
+/* Uploads host f32 weights in the reference orientation (ModelWeights,
+ * full_model.rs:19-23): embed [vocab, dim], gamma_final [dim], and
+ * cfg.nlayers cb_layer_weights_f32. Values are rounded to fp16 on the device;
+ * gains stay fp32. */
+cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamma_final,
+                              const cb_layer_weights_f32* layers);
+
+/* forward_only_ws / forward_ws (full_model.rs:378,494) for `batch` sequences
+ * back to back: tokens/targets are host u32 [batch*seq]. loss_out receives the
+ * mean next-token cross-entropy over all batch*seq positions (= the mean of the
+ * per-sequence losses). per_token_loss (nullable, host [batch*seq]) receives
+ * the per-position losses of forward_losses (full_model.rs:1603). softcap > 0
+ * applies logits = softcap*tanh(logits/softcap) (full_model.rs:456-461).
+ * Synchronous. */
+cb_status cb_forward_loss(cb_ctx* ctx, const uint32_t* tokens, const uint32_t* targets,
+                          int32_t batch, float softcap, float* loss_out,
+                          float* per_token_loss);
+
+/* Same computation on device buffers, enqueued on `stream` without a host
+ * synchronisation. d_loss (device float) and d_per_token_loss (nullable,
+ * device [batch*seq]) are written when the stream reaches them. Device-side
+ * errors (a bad token id, an expired wait) are reported by the next
+ * cb_check_device_error. */
+cb_status cb_forward_loss_async(cb_ctx* ctx, const uint32_t* d_tokens, const uint32_t* d_targets,
+                                int32_t batch, float softcap, float* d_loss,
+                                float* d_per_token_loss, void* stream);
+
+/* Synchronises the context's stream and reports (and clears) a device-side
+ * error flag raised by earlier asynchronous forwards. */
+cb_status cb_check_device_error(cb_ctx* ctx);
+
+/* Logits of selected positions of the LAST forward (row = b*seq + s), the
+ * sampled-row dump used for parity checks (the full [T, vocab] logits never
+ * reach device memory otherwise). logits_out: host [n_rows * vocab] f32, with
+ * the last forward's softcap applied. Synchronous. */
+cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, float* logits_out);
+
+/* Per-kernel-class CUDA-event timing of forwards run while enabled. */
+cb_status cb_set_profiling(cb_ctx* ctx, int32_t enable);
+cb_status cb_kernel_times(cb_ctx* ctx, cb_kernel_time* out, int32_t max_entries,
+                          int32_t* n_entries);
+cb_status cb_reset_kernel_times(cb_ctx* ctx);
+
+/* The context's CUDA stream (cudaStream_t) and device. */
+cb_status cb_get_stream(cb_ctx* ctx, void** stream);
+
+/* Human-readable description of the last error on this context (never NULL). */
+const char* cb_last_error(const cb_ctx* ctx);
+
+/* Last error of a failed cb_create (no context exists yet). */
+const char* cb_create_error(void);
+
+/* ---- Kernel-level entry points (device pointers; used by the tests and the
+ * micro-benchmarks; they sit below the model API). -------------------------- */
+
+/* C[M,N] = A[M,K] * B[N,K]^T with fp16 A/B (K contiguous) on the tcgen05 GEMM.
+ * out_f32 = 0: C is fp16; 1: C is f32. K % 64 == 0, N % 32 == 0, 16-byte
+ * aligned pointers. Enqueued on `stream` (NULL = default stream). */
+cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N, int32_t K,
+                      int32_t out_f32, int32_t block_n, void* stream);
+
+/* Causal attention: q/k/v [batch, heads, seq, 128] fp16 -> out [batch*seq,
+ * heads*128] fp16, scale 1/sqrt(128). seq % 64 == 0. */
+cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out,
+                           int32_t batch, int32_t heads, int32_t seq, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RUSTANE_CUDA_BRIDGE_H */

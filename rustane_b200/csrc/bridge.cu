@@ -1,0 +1,956 @@
+// C-ABI implementation of the B200 forward + loss engine (include/cuda_bridge.h).
+//
+// A cb_ctx owns, on one device: fp16 weights in GEMM-ready layouts (weights.cuh),
+// a workspace for max_batch sequences, TMA tensor maps for every GEMM operand,
+// and one CUDA graph per (batch, softcap) holding the whole forward:
+//
+//   embed_rmsnorm                                     full_model.rs:396-397 + rmsnorm
+//   for each layer (layer.rs:4409-4624 / forward_into_pipelined :5563):
+//     rmsnorm(gamma1)            [layer > 0]          cpu/rmsnorm.rs:149-183
+//     GEMM Xn*Wqkv^T  -> RoPE -> Q,K,V head-major     kernels/sdpa_fwd.rs:117-150,213-221
+//     causal flash attention                          kernels/sdpa_fwd.rs:223-258
+//     GEMM A*Wo       -> x += alpha*o                 dyn_matmul.rs:15-75; layer.rs:4471
+//     rmsnorm(gamma2)                                 layer.rs:4932-4940
+//     GEMM Xn*W13^T   -> g = silu(h1)*h3              kernels/ffn_fused.rs:79-107
+//     GEMM g*W2^T     -> x += alpha*ffn               kernels/ffn_fused.rs:130-154
+//   rmsnorm(gamma_final)                              full_model.rs:436-444
+//   GEMM Xf*E^T -> per-tile (max, sumexp), target     full_model.rs:446-461
+//   ce_finalize -> per-token loss; loss_mean           cpu/cross_entropy.rs:58-96; full_model.rs:471
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "cuda_bridge.h"
+#include "attention.cuh"
+#include "gemm_tc.cuh"
+#include "ptx.cuh"
+#include "rowwise.cuh"
+#include "weights.cuh"
+
+using namespace cb;
+
+#define CB_VERSION_STR "rustane_b200 cuda_bridge 0.1 (sm_100a)"
+
+namespace {
+
+// ------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor [depth][rows][k] (k contiguous) tiled as 64 x box_rows x 1 boxes, 128B swizzle.
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t k, uint64_t rows, uint64_t depth,
+               uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {k, rows, depth};
+  cuuint64_t strides[2] = {k * 2, k * rows * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------ GEMM launch
+template <int BN, class Epi>
+void set_gemm_attr() {
+  cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       GemmCfg<BN>::SMEM_BYTES);
+}
+
+template <class Epi>
+void set_gemm_attrs_for() {
+  set_gemm_attr<128, Epi>();
+  set_gemm_attr<256, Epi>();
+}
+
+void set_all_kernel_attrs() {
+  set_gemm_attrs_for<EpiStoreF16>();
+  set_gemm_attrs_for<EpiStoreF32>();
+  set_gemm_attrs_for<EpiQkvRope>();
+  set_gemm_attrs_for<EpiResidual>();
+  set_gemm_attrs_for<EpiSwiglu>();
+  set_gemm_attrs_for<EpiCrossEntropy>();
+  cudaFuncSetAttribute(attn_fwd_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       ATT_SMEM);
+}
+
+// Attributes are per device; remember which devices are done.
+void ensure_attrs(int device) {
+  static std::mutex mu;
+  static uint64_t done = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (device >= 0 && device < 64 && (done & (1ull << device))) return;
+  set_all_kernel_attrs();
+  if (device >= 0 && device < 64) done |= (1ull << device);
+}
+
+int num_sms_of(int device) {
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  return n;
+}
+
+template <int BN, class Epi>
+cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                           int bz, const Epi& epi, int* err, int num_sms, cudaStream_t st) {
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  gemm_tn_kernel<BN, Epi><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K,
+                                                                               bz, epi, err);
+  return cudaGetLastError();
+}
+
+// Tile width choice: the one whose last wave is fullest; ties go to 256 (less
+// operand traffic per FLOP).
+int pick_bn(int M, int N, int num_sms) {
+  auto eff = [&](int bn) {
+    long tiles = (long)((M + 127) / 128) * ((N + bn - 1) / bn);
+    long waves = (tiles + num_sms - 1) / num_sms;
+    return (double)tiles / (double)(waves * num_sms);
+  };
+  if (N % 256 != 0) return 128;
+  return eff(128) > eff(256) * 1.15 ? 128 : 256;
+}
+
+template <class Epi>
+cudaError_t launch_gemm(int bn, const CUtensorMap& ta, const CUtensorMap& tb128,
+                        const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
+                        int* err, int num_sms, cudaStream_t st) {
+  if (bn == 128) return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, num_sms, st);
+  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, num_sms, st);
+}
+
+// ------------------------------------------------------------ kernel classes
+enum KClass {
+  K_EMBED_NORM = 0,
+  K_RMSNORM,
+  K_GEMM_QKV,
+  K_ATTN,
+  K_GEMM_O,
+  K_GEMM_W13,
+  K_GEMM_W2,
+  K_GEMM_HEAD,
+  K_CE_FINAL,
+  K_LOSS_MEAN,
+  K_NUM
+};
+const char* kclass_name[K_NUM] = {"embed_rmsnorm",   "rmsnorm",          "gemm_qkv_rope",
+                                  "attention",       "gemm_o_residual",  "gemm_w13_swiglu",
+                                  "gemm_w2_residual", "gemm_lmhead_ce",  "ce_finalize",
+                                  "loss_mean"};
+
+struct KStat {
+  int64_t launches = 0;
+  double ms = 0, flops = 0, bytes = 0;
+};
+
+}  // namespace
+
+// ------------------------------------------------------------ context
+struct cb_ctx {
+  cb_model_config cfg{};
+  int device = 0;
+  int max_batch = 0;
+  int num_sms = 148;
+  int q_dim = 0, kv_dim = 0, n_qkv = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  bool weights_ready = false;
+
+  // weights
+  __half* embed = nullptr;
+  __half* wqkv = nullptr;
+  __half* wo = nullptr;
+  __half* w13 = nullptr;
+  __half* w2 = nullptr;
+  float* gamma = nullptr;        // [L][2][dim]
+  float* gamma_final = nullptr;  // [dim]
+
+  // workspace
+  float* x = nullptr;          // [T, dim] fp32 residual stream
+  __half* xn = nullptr;        // [T, dim] normalised activations (final: Xf)
+  __half* q = nullptr;         // [B, H, S, 128]
+  __half* k = nullptr;
+  __half* v = nullptr;
+  __half* attn = nullptr;      // [T, q_dim]
+  __half* g = nullptr;         // [T, hidden]
+  float2* ce_part = nullptr;   // [T, vocab/128]
+  float* tgt_logit = nullptr;  // [T]
+  float* tok_loss = nullptr;   // [T]
+  float* block_sums = nullptr; // [ceil(T/8)]
+  float* loss = nullptr;       // [1]
+  uint32_t* tokens = nullptr;  // [T]
+  uint32_t* targets = nullptr; // [T]
+  float2* rope = nullptr;      // [S, 64]
+  int* dev_err = nullptr;      // device error flag
+  float* h_loss = nullptr;     // pinned
+  int* h_err = nullptr;        // pinned
+
+  // tensor maps (A operands sized for max_batch; B per weight kind, both tile widths)
+  CUtensorMap tm_xn, tm_attn, tm_g;
+  CUtensorMap tm_wqkv[2], tm_wo[2], tm_w13[2], tm_w2[2], tm_embed[2];  // [0]=BN128 [1]=BN256
+
+  // graphs
+  std::map<std::pair<int, uint32_t>, cudaGraphExec_t> graphs;
+
+  // last forward (for sampled logits)
+  int last_batch = 0;
+  float last_softcap = 0.f;
+
+  // sampled-logit buffers
+  __half* samp_a = nullptr;
+  float* samp_out = nullptr;
+  int samp_cap = 0;
+
+  // profiling
+  bool profiling = false;
+  KStat stats[K_NUM];
+  std::vector<cudaEvent_t> events;
+  std::vector<int> ev_class;
+  std::vector<double> ev_flops, ev_bytes;
+  bool pending_harvest = false;
+
+  size_t T_max() const { return (size_t)max_batch * cfg.seq; }
+};
+
+namespace {
+
+thread_local std::string g_create_error;
+
+cb_status fail(cb_ctx* c, cb_status code, const std::string& msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+#define CB_CUDA(call)                                                                  \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? CB_ERR_OUT_OF_MEMORY : CB_ERR_CUDA, \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                 \
+  } while (0)
+
+template <class T>
+cudaError_t dmalloc(T** p, size_t n) {
+  return cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T) + 256);
+}
+
+size_t wqkv_layer_elems(const cb_ctx* c) { return (size_t)c->n_qkv * c->cfg.dim; }
+size_t wo_layer_elems(const cb_ctx* c) { return (size_t)c->cfg.dim * c->q_dim; }
+size_t w13_layer_elems(const cb_ctx* c) { return (size_t)2 * c->cfg.hidden * c->cfg.dim; }
+size_t w2_layer_elems(const cb_ctx* c) { return (size_t)c->cfg.dim * c->cfg.hidden; }
+
+ShapeInfo shape_of(const cb_ctx* c) {
+  ShapeInfo s;
+  s.dim = c->cfg.dim;
+  s.hidden = c->cfg.hidden;
+  s.q_dim = c->q_dim;
+  s.kv_dim = c->kv_dim;
+  s.vocab = c->cfg.vocab;
+  return s;
+}
+
+void free_ctx(cb_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  c->graphs.clear();
+  for (auto e : c->events) cudaEventDestroy(e);
+  void* ptrs[] = {c->embed, c->wqkv, c->wo,        c->w13,      c->w2,       c->gamma,
+                  c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
+                  c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
+                  c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
+                  c->samp_out};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  if (c->h_loss) cudaFreeHost(c->h_loss);
+  if (c->h_err) cudaFreeHost(c->h_err);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+// Enqueue one forward for `batch` sequences on `st`. When `prof` is set,
+// CUDA events bracket every launch (eager mode only).
+cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof) {
+  const cb_model_config& cfg = c->cfg;
+  const int S = cfg.seq, d = cfg.dim, hid = cfg.hidden, V = cfg.vocab, L = cfg.nlayers;
+  const int T = batch * S;
+  const float alpha = 1.0f / sqrtf(2.0f * (float)L);  // layer.rs:4420
+  const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
+  int ev = 0;
+  auto mark = [&](int cls, double flops, double bytes) {
+    if (!prof) return;
+    c->ev_class.push_back(cls);
+    c->ev_flops.push_back(flops);
+    c->ev_bytes.push_back(bytes);
+    cudaEventRecord(c->events[++ev], st);
+  };
+  if (prof) {
+    c->ev_class.clear();
+    c->ev_flops.clear();
+    c->ev_bytes.clear();
+    cudaEventRecord(c->events[0], st);
+  }
+  cudaError_t e;
+  const double Td = (double)T;
+
+  embed_rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->tokens, c->embed, c->gamma, c->x,
+                                                                c->xn, T, d, V, c->dev_err);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(K_EMBED_NORM, 0, Td * 4 + Td * d * (2 + 4 + 2));
+
+  const int bn_qkv = pick_bn(T, c->n_qkv, c->num_sms);
+  const int bn_o = pick_bn(T, d, c->num_sms);
+  const int bn_13 = pick_bn(T, 2 * hid, c->num_sms);
+  const int bn_2 = pick_bn(T, d, c->num_sms);
+  const double attn_flops = 2.0 * 2.0 * (double)batch * cfg.heads * 128.0 * S * (S + 1) / 2.0;
+
+  for (int l = 0; l < L; ++l) {
+    if (l > 0) {
+      rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma + (size_t)l * 2 * d,
+                                                            c->xn, T, d);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      mark(K_RMSNORM, 0, Td * d * 6);
+    }
+    {
+      EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, cfg.heads, cfg.kv_heads};
+      e = launch_gemm(bn_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
+                      c->dev_err, c->num_sms, st);
+      if (e != cudaSuccess) return e;
+      mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
+           Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
+    }
+    {
+      dim3 grid(S / ATT_BQ, cfg.heads, batch);
+      attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(
+          c->q, c->k, c->v, c->attn, S, cfg.heads, cfg.kv_heads,
+          1.4426950408889634f / sqrtf(128.0f));
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
+    }
+    {
+      EpiResidual ep{c->x, d, alpha};
+      e = launch_gemm(bn_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], T, d, c->q_dim, l, ep,
+                      c->dev_err, c->num_sms, st);
+      if (e != cudaSuccess) return e;
+      mark(K_GEMM_O, 2.0 * Td * d * c->q_dim,
+           Td * c->q_dim * 2 + (double)d * c->q_dim * 2 + Td * d * 8);
+    }
+    rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma + (size_t)l * 2 * d + d,
+                                                          c->xn, T, d);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    mark(K_RMSNORM, 0, Td * d * 6);
+    {
+      EpiSwiglu ep{c->g, hid};
+      e = launch_gemm(bn_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
+                      c->dev_err, c->num_sms, st);
+      if (e != cudaSuccess) return e;
+      mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
+    }
+    {
+      EpiResidual ep{c->x, d, alpha};
+      e = launch_gemm(bn_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err,
+                      c->num_sms, st);
+      if (e != cudaSuccess) return e;
+      mark(K_GEMM_W2, 2.0 * Td * d * hid, Td * hid * 2 + (double)d * hid * 2 + Td * d * 8);
+    }
+  }
+
+  rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma_final, c->xn, T, d);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(K_RMSNORM, 0, Td * d * 6);
+
+  const int bn_head = pick_bn(T, V, c->num_sms);
+  const int nparts = (V + bn_head - 1) / bn_head;
+  {
+    EpiCrossEntropy ep{};
+    ep.part = c->ce_part;
+    ep.nparts = nparts;
+    ep.targets = c->targets;
+    ep.tgt_logit = c->tgt_logit;
+    ep.softcap = softcap;
+    e = launch_gemm(bn_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
+                    c->dev_err, c->num_sms, st);
+    if (e != cudaSuccess) return e;
+    mark(K_GEMM_HEAD, 2.0 * Td * V * d, Td * d * 2 + (double)V * d * 2 + Td * nparts * 8 + Td * 8);
+  }
+  ce_finalize_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->ce_part, nparts, c->tgt_logit,
+                                                            c->tok_loss, c->block_sums, T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(K_CE_FINAL, 0, Td * nparts * 8 + Td * 8);
+  loss_mean_kernel<<<1, 256, 0, st>>>(c->block_sums, row_blocks, T, c->loss);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(K_LOSS_MEAN, 0, row_blocks * 4.0);
+  return cudaSuccess;
+}
+
+int launches_per_forward(const cb_ctx* c) { return 7 * c->cfg.nlayers + 4; }
+
+void harvest(cb_ctx* c) {
+  if (!c->pending_harvest) return;
+  c->pending_harvest = false;
+  const int n = (int)c->ev_class.size();
+  if (n == 0) return;
+  if (cudaEventSynchronize(c->events[n]) != cudaSuccess) return;
+  for (int i = 0; i < n; ++i) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, c->events[i], c->events[i + 1]) != cudaSuccess) continue;
+    KStat& s = c->stats[c->ev_class[i]];
+    s.launches += 1;
+    s.ms += ms;
+    s.flops += c->ev_flops[i];
+    s.bytes += c->ev_bytes[i];
+  }
+}
+
+cb_status validate_cfg(const cb_model_config* cfg, std::string* why) {
+  auto bad = [&](const char* m) {
+    *why = m;
+    return CB_ERR_INVALID_ARG;
+  };
+  if (!cfg) return bad("null config");
+  if (cfg->hd != 128) return bad("hd must be 128");
+  if (cfg->dim <= 0 || cfg->hidden <= 0 || cfg->heads <= 0 || cfg->kv_heads <= 0 ||
+      cfg->seq <= 0 || cfg->nlayers <= 0 || cfg->vocab <= 0)
+    return bad("non-positive dimension");
+  if (cfg->heads % cfg->kv_heads != 0) return bad("heads must be a multiple of kv_heads");
+  if (cfg->dim % 256 != 0) return bad("dim must be a multiple of 256");
+  if (cfg->hidden % 64 != 0) return bad("hidden must be a multiple of 64");
+  if (cfg->seq % 64 != 0) return bad("seq must be a multiple of 64");
+  if (cfg->vocab % 32 != 0) return bad("vocab must be a multiple of 32");
+  return CB_OK;
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+
+extern "C" {
+
+const char* cb_version(void) { return CB_VERSION_STR; }
+
+const char* cb_create_error(void) { return g_create_error.c_str(); }
+
+cb_status cb_device_count(int32_t* count) {
+  if (!count) return CB_ERR_INVALID_ARG;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) n = 0;
+  *count = n;
+  return CB_OK;
+}
+
+const char* cb_last_error(const cb_ctx* ctx) {
+  if (!ctx) return "null context";
+  return ctx->err.c_str();
+}
+
+cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batch, cb_ctx** out) {
+  g_create_error.clear();
+  if (!out) {
+    g_create_error = "null output pointer";
+    return CB_ERR_INVALID_ARG;
+  }
+  *out = nullptr;
+  std::string why;
+  if (validate_cfg(cfg, &why) != CB_OK) {
+    g_create_error = why;
+    return CB_ERR_INVALID_ARG;
+  }
+  if (max_batch <= 0) {
+    g_create_error = "max_batch must be positive";
+    return CB_ERR_INVALID_ARG;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    g_create_error = "no CUDA device";
+    return CB_ERR_UNSUPPORTED;
+  }
+  if (device < 0 || device >= ndev) {
+    g_create_error = "device index out of range";
+    return CB_ERR_INVALID_ARG;
+  }
+  cudaDeviceProp prop;
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major != 10) {
+    g_create_error = std::string("kernels are built for sm_100a; device is ") + prop.name;
+    return CB_ERR_UNSUPPORTED;
+  }
+  if (!encode_fn()) {
+    g_create_error = "cuTensorMapEncodeTiled unavailable";
+    return CB_ERR_UNSUPPORTED;
+  }
+
+  cb_ctx* ctx = new cb_ctx();
+  ctx->cfg = *cfg;
+  ctx->device = device;
+  ctx->max_batch = max_batch;
+  ctx->q_dim = cfg->heads * 128;
+  ctx->kv_dim = cfg->kv_heads * 128;
+  ctx->n_qkv = ctx->q_dim + 2 * ctx->kv_dim;
+
+  auto bail = [&](cb_status code, const std::string& m) {
+    g_create_error = m;
+    free_ctx(ctx);
+    return code;
+  };
+#define CREATE_CUDA(call)                                                                     \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return bail(e_ == cudaErrorMemoryAllocation ? CB_ERR_OUT_OF_MEMORY : CB_ERR_CUDA,       \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                        \
+  } while (0)
+
+  CREATE_CUDA(cudaSetDevice(device));
+  ctx->num_sms = num_sms_of(device);
+  CREATE_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+  ensure_attrs(device);
+
+  const int L = cfg->nlayers, d = cfg->dim, hid = cfg->hidden, V = cfg->vocab, S = cfg->seq;
+  const size_t T = ctx->T_max();
+  CREATE_CUDA(dmalloc(&ctx->embed, (size_t)V * d));
+  CREATE_CUDA(dmalloc(&ctx->wqkv, (size_t)L * wqkv_layer_elems(ctx)));
+  CREATE_CUDA(dmalloc(&ctx->wo, (size_t)L * wo_layer_elems(ctx)));
+  CREATE_CUDA(dmalloc(&ctx->w13, (size_t)L * w13_layer_elems(ctx)));
+  CREATE_CUDA(dmalloc(&ctx->w2, (size_t)L * w2_layer_elems(ctx)));
+  CREATE_CUDA(dmalloc(&ctx->gamma, (size_t)L * 2 * d));
+  CREATE_CUDA(dmalloc(&ctx->gamma_final, (size_t)d));
+  CREATE_CUDA(dmalloc(&ctx->x, T * d));
+  CREATE_CUDA(dmalloc(&ctx->xn, T * d));
+  CREATE_CUDA(dmalloc(&ctx->q, T * ctx->q_dim));
+  CREATE_CUDA(dmalloc(&ctx->k, T * ctx->kv_dim));
+  CREATE_CUDA(dmalloc(&ctx->v, T * ctx->kv_dim));
+  CREATE_CUDA(dmalloc(&ctx->attn, T * ctx->q_dim));
+  CREATE_CUDA(dmalloc(&ctx->g, T * hid));
+  CREATE_CUDA(dmalloc(&ctx->ce_part, T * ((V + 127) / 128)));
+  CREATE_CUDA(dmalloc(&ctx->tgt_logit, T));
+  CREATE_CUDA(dmalloc(&ctx->tok_loss, T));
+  CREATE_CUDA(dmalloc(&ctx->block_sums, (T + ROW_WARPS - 1) / ROW_WARPS));
+  CREATE_CUDA(dmalloc(&ctx->loss, 1));
+  CREATE_CUDA(dmalloc(&ctx->tokens, T));
+  CREATE_CUDA(dmalloc(&ctx->targets, T));
+  CREATE_CUDA(dmalloc(&ctx->rope, (size_t)S * 64));
+  CREATE_CUDA(dmalloc(&ctx->dev_err, 1));
+  CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_loss), sizeof(float)));
+  CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_err), sizeof(int)));
+  CREATE_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+  CREATE_CUDA(cudaMemset(ctx->x, 0, T * d * sizeof(float)));
+  CREATE_CUDA(cudaMemset(ctx->tgt_logit, 0, T * sizeof(float)));
+
+  // RoPE table: theta = p * 10000^(-2i/128)  (sdpa_fwd.rs:24-39, layer.rs:645-666),
+  // evaluated in double and rounded to f32 (the CPU oracle builds the same table).
+  {
+    std::vector<float2> tab((size_t)S * 64);
+    for (int p = 0; p < S; ++p)
+      for (int i = 0; i < 64; ++i) {
+        double th = (double)p * std::pow(10000.0, -2.0 * i / 128.0);
+        tab[(size_t)p * 64 + i] = make_float2((float)std::cos(th), (float)std::sin(th));
+      }
+    CREATE_CUDA(cudaMemcpy(ctx->rope, tab.data(), tab.size() * sizeof(float2),
+                           cudaMemcpyHostToDevice));
+  }
+
+  bool ok = true;
+  ok &= make_tmap(&ctx->tm_xn, ctx->xn, d, T, 1, 128);
+  ok &= make_tmap(&ctx->tm_attn, ctx->attn, ctx->q_dim, T, 1, 128);
+  ok &= make_tmap(&ctx->tm_g, ctx->g, hid, T, 1, 128);
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t bn = i ? 256 : 128;
+    ok &= make_tmap(&ctx->tm_wqkv[i], ctx->wqkv, d, ctx->n_qkv, L, bn);
+    ok &= make_tmap(&ctx->tm_wo[i], ctx->wo, ctx->q_dim, d, L, bn);
+    ok &= make_tmap(&ctx->tm_w13[i], ctx->w13, d, 2 * hid, L, bn);
+    ok &= make_tmap(&ctx->tm_w2[i], ctx->w2, hid, d, L, bn);
+    ok &= make_tmap(&ctx->tm_embed[i], ctx->embed, d, V, 1, bn);
+  }
+  if (!ok) return bail(CB_ERR_UNSUPPORTED, "tensor map encoding failed");
+
+  const int nev = launches_per_forward(ctx) + 1;
+  ctx->events.resize(nev);
+  for (int i = 0; i < nev; ++i) CREATE_CUDA(cudaEventCreate(&ctx->events[i]));
+#undef CREATE_CUDA
+  *out = ctx;
+  return CB_OK;
+}
+
+cb_status cb_destroy(cb_ctx* ctx) {
+  if (!ctx) return CB_OK;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  free_ctx(ctx);
+  return CB_OK;
+}
+
+cb_status cb_init_weights(cb_ctx* ctx, uint64_t seed, int32_t scheme, float sigma) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (scheme != CB_INIT_NORMAL && scheme != CB_INIT_REFERENCE)
+    return fail(ctx, CB_ERR_INVALID_ARG, "unknown init scheme");
+  if (scheme == CB_INIT_NORMAL && !(sigma > 0.f))
+    return fail(ctx, CB_ERR_INVALID_ARG, "sigma must be positive");
+  CB_CUDA(cudaSetDevice(ctx->device));
+  const cb_model_config& cfg = ctx->cfg;
+  InitParams p;
+  p.seed = seed;
+  p.scheme = scheme;
+  p.normal_mul = (float)((double)sigma / CB_IRWIN_HALL4_STD);
+  p.scale_embed = 0.005f;
+  p.scale_qkv = 1.0f / sqrtf((float)cfg.dim);
+  p.scale_ffn = 1.0f / sqrtf((float)cfg.hidden);
+  const ShapeInfo s = shape_of(ctx);
+  const int grid = ctx->num_sms * 8, block = 256;
+  cudaStream_t st = ctx->stream;
+  init_weight_kernel<<<grid, block, 0, st>>>(ctx->embed, ST_EMBED, -1, cfg.vocab, cfg.dim, s, p);
+  for (int l = 0; l < cfg.nlayers; ++l) {
+    init_weight_kernel<<<grid, block, 0, st>>>(ctx->wqkv + l * wqkv_layer_elems(ctx), ST_QKV, l,
+                                               ctx->n_qkv, cfg.dim, s, p);
+    init_weight_kernel<<<grid, block, 0, st>>>(ctx->wo + l * wo_layer_elems(ctx), ST_WO, l,
+                                               cfg.dim, ctx->q_dim, s, p);
+    init_weight_kernel<<<grid, block, 0, st>>>(ctx->w13 + l * w13_layer_elems(ctx), ST_W13, l,
+                                               2 * cfg.hidden, cfg.dim, s, p);
+    init_weight_kernel<<<grid, block, 0, st>>>(ctx->w2 + l * w2_layer_elems(ctx), ST_W2, l,
+                                               cfg.dim, cfg.hidden, s, p);
+  }
+  fill_f32_kernel<<<grid, block, 0, st>>>(ctx->gamma, (size_t)cfg.nlayers * 2 * cfg.dim, 1.0f);
+  fill_f32_kernel<<<grid, block, 0, st>>>(ctx->gamma_final, (size_t)cfg.dim, 1.0f);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaStreamSynchronize(st));
+  ctx->weights_ready = true;
+  return CB_OK;
+}
+
+cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamma_final,
+                              const cb_layer_weights_f32* layers) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (!embed || !gamma_final || !layers)
+    return fail(ctx, CB_ERR_INVALID_ARG, "null weight pointer");
+  const cb_model_config& cfg = ctx->cfg;
+  for (int l = 0; l < cfg.nlayers; ++l) {
+    const cb_layer_weights_f32& w = layers[l];
+    if (!w.wq || !w.wk || !w.wv || !w.wo || !w.w1 || !w.w3 || !w.w2 || !w.gamma1 || !w.gamma2)
+      return fail(ctx, CB_ERR_INVALID_ARG, "null pointer in layer " + std::to_string(l));
+  }
+  CB_CUDA(cudaSetDevice(ctx->device));
+  const ShapeInfo s = shape_of(ctx);
+  const size_t d = cfg.dim, hid = cfg.hidden, V = cfg.vocab;
+  size_t stage_n = std::max(std::max(V * d, d * hid), std::max(d * (size_t)ctx->q_dim,
+                                                               d * (size_t)ctx->kv_dim));
+  float* stage = nullptr;
+  CB_CUDA(cudaMalloc(&stage, stage_n * sizeof(float)));
+  cudaStream_t st = ctx->stream;
+  const int grid = ctx->num_sms * 8, block = 256;
+  cb_status rc = CB_OK;
+  auto up = [&](const float* src, size_t n, __half* dst, int kind, int rows, int cols,
+                int sub) -> bool {
+    if (cudaMemcpyAsync(stage, src, n * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess)
+      return false;
+    load_weight_kernel<<<grid, block, 0, st>>>(dst, kind, rows, cols, s, sub, stage);
+    return cudaStreamSynchronize(st) == cudaSuccess;
+  };
+  bool ok = up(embed, V * d, ctx->embed, ST_EMBED, (int)V, (int)d, -1);
+  for (int l = 0; ok && l < cfg.nlayers; ++l) {
+    const cb_layer_weights_f32& w = layers[l];
+    __half* qkv = ctx->wqkv + l * wqkv_layer_elems(ctx);
+    ok = ok && up(w.wq, d * ctx->q_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WQ);
+    ok = ok && up(w.wk, d * ctx->kv_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WK);
+    ok = ok && up(w.wv, d * ctx->kv_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WV);
+    ok = ok && up(w.wo, d * ctx->q_dim, ctx->wo + l * wo_layer_elems(ctx), ST_WO, (int)d,
+                  ctx->q_dim, CB_T_WO);
+    __half* w13 = ctx->w13 + l * w13_layer_elems(ctx);
+    ok = ok && up(w.w1, d * hid, w13, ST_W13, 2 * (int)hid, (int)d, CB_T_W1);
+    ok = ok && up(w.w3, d * hid, w13, ST_W13, 2 * (int)hid, (int)d, CB_T_W3);
+    ok = ok && up(w.w2, d * hid, ctx->w2 + l * w2_layer_elems(ctx), ST_W2, (int)d, (int)hid,
+                  CB_T_W2);
+    ok = ok && cudaMemcpy(ctx->gamma + (size_t)l * 2 * d, w.gamma1, d * sizeof(float),
+                          cudaMemcpyHostToDevice) == cudaSuccess;
+    ok = ok && cudaMemcpy(ctx->gamma + (size_t)l * 2 * d + d, w.gamma2, d * sizeof(float),
+                          cudaMemcpyHostToDevice) == cudaSuccess;
+  }
+  ok = ok && cudaMemcpy(ctx->gamma_final, gamma_final, d * sizeof(float),
+                        cudaMemcpyHostToDevice) == cudaSuccess;
+  cudaError_t e = cudaGetLastError();
+  cudaFree(stage);
+  if (!ok || e != cudaSuccess) {
+    rc = fail(ctx, CB_ERR_CUDA, std::string("weight upload failed: ") + cudaGetErrorString(e));
+    return rc;
+  }
+  ctx->weights_ready = true;
+  return CB_OK;
+}
+
+static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStream_t st) {
+  if (ctx->profiling) {
+    harvest(ctx);
+    cudaError_t e = enqueue_forward(ctx, batch, softcap, st, true);
+    if (e != cudaSuccess) return fail(ctx, CB_ERR_CUDA, std::string("forward: ") + cudaGetErrorString(e));
+    ctx->pending_harvest = true;
+  } else {
+    uint32_t sc_bits;
+    std::memcpy(&sc_bits, &softcap, 4);
+    auto key = std::make_pair((int)batch, sc_bits);
+    auto it = ctx->graphs.find(key);
+    if (it == ctx->graphs.end()) {
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      CB_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+      cudaError_t e = enqueue_forward(ctx, batch, softcap, ctx->stream, false);
+      cudaError_t e2 = cudaStreamEndCapture(ctx->stream, &graph);
+      if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return fail(ctx, CB_ERR_CUDA,
+                    std::string("graph capture: ") +
+                        cudaGetErrorString(e != cudaSuccess ? e : e2));
+      }
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess)
+        return fail(ctx, CB_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+      it = ctx->graphs.emplace(key, exec).first;
+    }
+    CB_CUDA(cudaGraphLaunch(it->second, st));
+  }
+  ctx->last_batch = batch;
+  ctx->last_softcap = softcap;
+  return CB_OK;
+}
+
+static cb_status check_forward_args(cb_ctx* ctx, const void* tokens, const void* targets,
+                                    int32_t batch) {
+  if (!ctx->weights_ready) return fail(ctx, CB_ERR_NOT_READY, "weights are not loaded");
+  if (!tokens || !targets) return fail(ctx, CB_ERR_INVALID_ARG, "null tokens/targets");
+  if (batch <= 0 || batch > ctx->max_batch)
+    return fail(ctx, CB_ERR_INVALID_ARG,
+                "batch " + std::to_string(batch) + " outside [1, " +
+                    std::to_string(ctx->max_batch) + "]");
+  return CB_OK;
+}
+
+cb_status cb_forward_loss(cb_ctx* ctx, const uint32_t* tokens, const uint32_t* targets,
+                          int32_t batch, float softcap, float* loss_out, float* per_token_loss) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  cb_status rc = check_forward_args(ctx, tokens, targets, batch);
+  if (rc != CB_OK) return rc;
+  if (!loss_out) return fail(ctx, CB_ERR_INVALID_ARG, "null loss_out");
+  const size_t T = (size_t)batch * ctx->cfg.seq;
+  const uint32_t V = (uint32_t)ctx->cfg.vocab;
+  for (size_t i = 0; i < T; ++i)
+    if (tokens[i] >= V || targets[i] >= V)
+      return fail(ctx, CB_ERR_INVALID_ARG, "token id out of range at position " + std::to_string(i));
+  CB_CUDA(cudaSetDevice(ctx->device));
+  cudaStream_t st = ctx->stream;
+  CB_CUDA(cudaMemcpyAsync(ctx->tokens, tokens, T * 4, cudaMemcpyHostToDevice, st));
+  CB_CUDA(cudaMemcpyAsync(ctx->targets, targets, T * 4, cudaMemcpyHostToDevice, st));
+  rc = run_forward(ctx, batch, softcap, st);
+  if (rc != CB_OK) return rc;
+  CB_CUDA(cudaMemcpyAsync(ctx->h_loss, ctx->loss, sizeof(float), cudaMemcpyDeviceToHost, st));
+  CB_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (per_token_loss)
+    CB_CUDA(cudaMemcpyAsync(per_token_loss, ctx->tok_loss, T * sizeof(float),
+                            cudaMemcpyDeviceToHost, st));
+  CB_CUDA(cudaStreamSynchronize(st));
+  if (*ctx->h_err != 0) {
+    int code = *ctx->h_err;
+    cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
+                "device error flag " + std::to_string(code));
+  }
+  *loss_out = *ctx->h_loss;
+  return CB_OK;
+}
+
+cb_status cb_forward_loss_async(cb_ctx* ctx, const uint32_t* d_tokens, const uint32_t* d_targets,
+                                int32_t batch, float softcap, float* d_loss,
+                                float* d_per_token_loss, void* stream) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  cb_status rc = check_forward_args(ctx, d_tokens, d_targets, batch);
+  if (rc != CB_OK) return rc;
+  CB_CUDA(cudaSetDevice(ctx->device));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  const size_t T = (size_t)batch * ctx->cfg.seq;
+  if (d_tokens != ctx->tokens)
+    CB_CUDA(cudaMemcpyAsync(ctx->tokens, d_tokens, T * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_targets != ctx->targets)
+    CB_CUDA(cudaMemcpyAsync(ctx->targets, d_targets, T * 4, cudaMemcpyDeviceToDevice, st));
+  rc = run_forward(ctx, batch, softcap, st);
+  if (rc != CB_OK) return rc;
+  if (d_loss)
+    CB_CUDA(cudaMemcpyAsync(d_loss, ctx->loss, sizeof(float), cudaMemcpyDeviceToDevice, st));
+  if (d_per_token_loss)
+    CB_CUDA(cudaMemcpyAsync(d_per_token_loss, ctx->tok_loss, T * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st));
+  return CB_OK;
+}
+
+cb_status cb_check_device_error(cb_ctx* ctx) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  CB_CUDA(cudaSetDevice(ctx->device));
+  CB_CUDA(cudaDeviceSynchronize());
+  CB_CUDA(cudaMemcpy(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (*ctx->h_err != 0) {
+    int code = *ctx->h_err;
+    cudaMemset(ctx->dev_err, 0, sizeof(int));
+    return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
+                "device error flag " + std::to_string(code));
+  }
+  return CB_OK;
+}
+
+cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, float* logits_out) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (ctx->last_batch <= 0) return fail(ctx, CB_ERR_NOT_READY, "no forward has run");
+  if (!rows || !logits_out || n_rows <= 0)
+    return fail(ctx, CB_ERR_INVALID_ARG, "bad sampled-logit arguments");
+  const int T = ctx->last_batch * ctx->cfg.seq;
+  for (int i = 0; i < n_rows; ++i)
+    if (rows[i] < 0 || rows[i] >= T)
+      return fail(ctx, CB_ERR_INVALID_ARG, "sampled row out of range");
+  CB_CUDA(cudaSetDevice(ctx->device));
+  const int d = ctx->cfg.dim, V = ctx->cfg.vocab;
+  const int n_pad = (n_rows + 127) / 128 * 128;
+  cudaStream_t st = ctx->stream;
+  CB_CUDA(cudaStreamSynchronize(st));
+  if (n_pad > ctx->samp_cap) {
+    if (ctx->samp_a) cudaFree(ctx->samp_a);
+    if (ctx->samp_out) cudaFree(ctx->samp_out);
+    ctx->samp_a = nullptr;
+    ctx->samp_out = nullptr;
+    ctx->samp_cap = 0;
+    CB_CUDA(dmalloc(&ctx->samp_a, (size_t)n_pad * d));
+    CB_CUDA(dmalloc(&ctx->samp_out, (size_t)n_pad * V));
+    ctx->samp_cap = n_pad;
+  }
+  int32_t* d_rows = nullptr;
+  CB_CUDA(cudaMalloc(&d_rows, n_rows * sizeof(int32_t)));
+  cudaError_t e = cudaMemcpyAsync(d_rows, rows, n_rows * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) {
+    gather_rows_kernel<<<n_pad, 128, 0, st>>>(ctx->xn, d_rows, n_rows, n_pad, d, ctx->samp_a);
+    e = cudaGetLastError();
+  }
+  CUtensorMap ta;
+  if (e == cudaSuccess && !make_tmap(&ta, ctx->samp_a, d, n_pad, 1, 128)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess) {
+    EpiStoreF32 ep{ctx->samp_out, V, ctx->last_softcap};
+    const int bn = (V % 256 == 0) ? 256 : 128;
+    e = launch_gemm(bn, ta, ctx->tm_embed[0], ctx->tm_embed[1], n_pad, V, d, 0, ep, ctx->dev_err,
+                    ctx->num_sms, st);
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(logits_out, ctx->samp_out, (size_t)n_rows * V * sizeof(float),
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  cudaFree(d_rows);
+  if (e != cudaSuccess)
+    return fail(ctx, CB_ERR_CUDA, std::string("sampled logits: ") + cudaGetErrorString(e));
+  return CB_OK;
+}
+
+cb_status cb_set_profiling(cb_ctx* ctx, int32_t enable) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (!enable) harvest(ctx);
+  ctx->profiling = enable != 0;
+  return CB_OK;
+}
+
+cb_status cb_kernel_times(cb_ctx* ctx, cb_kernel_time* out, int32_t max_entries,
+                          int32_t* n_entries) {
+  if (!ctx || !n_entries) return CB_ERR_INVALID_ARG;
+  CB_CUDA(cudaSetDevice(ctx->device));
+  harvest(ctx);
+  int n = 0;
+  for (int i = 0; i < K_NUM; ++i) {
+    if (ctx->stats[i].launches == 0) continue;
+    if (out && n < max_entries) {
+      cb_kernel_time& t = out[n];
+      std::memset(&t, 0, sizeof(t));
+      std::strncpy(t.name, kclass_name[i], sizeof(t.name) - 1);
+      t.launches = ctx->stats[i].launches;
+      t.total_ms = ctx->stats[i].ms;
+      t.flops = ctx->stats[i].flops;
+      t.bytes = ctx->stats[i].bytes;
+    }
+    ++n;
+  }
+  *n_entries = n;
+  return CB_OK;
+}
+
+cb_status cb_reset_kernel_times(cb_ctx* ctx) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  harvest(ctx);
+  for (auto& s : ctx->stats) s = KStat();
+  return CB_OK;
+}
+
+cb_status cb_get_stream(cb_ctx* ctx, void** stream) {
+  if (!ctx || !stream) return CB_ERR_INVALID_ARG;
+  *stream = ctx->stream;
+  return CB_OK;
+}
+
+cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N, int32_t K,
+                      int32_t out_f32, int32_t block_n, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return CB_ERR_INVALID_ARG;
+  if (K % 64 != 0 || N % 32 != 0) return CB_ERR_INVALID_ARG;
+  if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return CB_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  ensure_attrs(dev);
+  const int sms = num_sms_of(dev);
+  int bn = block_n;
+  if (bn != 128 && bn != 256) bn = pick_bn(M, N, sms);
+  if (bn == 256 && N % 256 != 0) bn = 128;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, A, K, M, 1, 128) || !make_tmap(&tb, B, K, N, 1, bn))
+    return CB_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (out_f32) {
+    EpiStoreF32 ep{static_cast<float*>(C), N, 0.f};
+    e = launch_gemm(bn, ta, tb, tb, M, N, K, 0, ep, nullptr, sms, st);
+  } else {
+    EpiStoreF16 ep{static_cast<__half*>(C), N};
+    e = launch_gemm(bn, ta, tb, tb, M, N, K, 0, ep, nullptr, sms, st);
+  }
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out, int32_t batch,
+                           int32_t heads, int32_t seq, void* stream) {
+  if (!q || !k || !v || !out || batch <= 0 || heads <= 0 || seq <= 0 || seq % 64 != 0)
+    return CB_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  ensure_attrs(dev);
+  dim3 grid(seq / ATT_BQ, heads, batch);
+  attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
+      static_cast<__half*>(out), seq, heads, heads, 1.4426950408889634f / sqrtf(128.0f));
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+}  // extern "C"

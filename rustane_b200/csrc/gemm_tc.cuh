@@ -1,0 +1,412 @@
+// Persistent tcgen05 GEMM for sm_100a:  C[M,N] = A[M,K] * B[N,K]^T  (both K-major fp16,
+// fp32 accumulation in TMEM), with the forward pass's fusions applied in the
+// epilogue while the accumulator is still in registers.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0, lane 0 : TMA producer. 128x64 A tile + BNx64 B tile per stage,
+//                    128-byte swizzle, mbarrier expect-tx completion.
+//   warp 1         : allocates TMEM (2 x BN columns: double-buffered
+//                    accumulator); lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
+//                    and tcgen05.commit to release smem stages / hand over
+//                    finished accumulators.
+//   warps 2..5     : epilogue. Warp w reads TMEM lanes 32*(w%4)..+31, i.e. each
+//                    thread owns one output row of the tile and walks its BN
+//                    columns in chunks of 32 (tcgen05.ld 32x32b.x32).
+// Tiles are visited n-fastest so CTAs running at the same time share A rows
+// and the weight matrix (B) stays resident in L2.
+//
+// Epilogues (the reference ops they replace):
+//   EpiStoreF16   plain fp16 store (tests / generic use)
+//   EpiStoreF32   fp32 store with optional softcap (sampled-logit dump)
+//   EpiQkvRope    Q/K/V split + RoPE on interleaved pairs, head-major store
+//                 (crates/engine/src/kernels/sdpa_fwd.rs:24-60,117-150,213-221)
+//   EpiResidual   x += alpha * acc (crates/engine/src/layer.rs:4471, ffn_fused.rs:144-154)
+//   EpiSwiglu     g = silu(h1) * h3 from interleaved W1/W3 columns
+//                 (crates/engine/src/kernels/ffn_fused.rs:79-80,105-107)
+//   EpiCrossEntropy  per-(row, N-tile) running max / sum-exp and target logit
+//                 of the tied LM head, so logits never reach HBM
+//                 (crates/engine/src/full_model.rs:436-471, cpu/cross_entropy.rs:58-96)
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+
+namespace cb {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+};
+
+// ------------------------------------------------------------------ epilogues
+
+struct EpiStoreF16 {
+  __half* out;
+  int ldo;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_half2(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_half2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_half2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_half2(v[8 * j + 6], v[8 * j + 7]);
+      dst[j] = w;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+struct EpiStoreF32 {
+  float* out;
+  int ldo;
+  float softcap;  // > 0: out = softcap * tanh(acc / softcap)
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+    float4* dst = reinterpret_cast<float4*>(out + (size_t)row * ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      if (softcap > 0.f) {
+        float inv = 1.0f / softcap;
+        w.x = softcap * tanhf(w.x * inv);
+        w.y = softcap * tanhf(w.y * inv);
+        w.z = softcap * tanhf(w.z * inv);
+        w.w = softcap * tanhf(w.w * inv);
+      }
+      dst[j] = w;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// Columns [0, q_dim) -> Q, [q_dim, q_dim+kv_dim) -> K, rest -> V. Head dim 128.
+// Output layout [batch, heads, seq, 128] (row = b*seq + s).
+struct EpiQkvRope {
+  __half* q;
+  __half* k;
+  __half* v;
+  const float2* rope;  // [seq, 64] (cos, sin) of theta = s * 10000^(-2i/128)
+  int seq;
+  int heads;
+  int kv_heads;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32]) {
+    const int q_dim = heads * 128;
+    const int kv_dim = kv_heads * 128;
+    int b = row / seq;
+    int s = row - b * seq;
+    __half* dst;
+    int c = col0;
+    bool rot = true;
+    int nh;
+    if (c < q_dim) {
+      dst = q;
+      nh = heads;
+    } else if (c < q_dim + kv_dim) {
+      dst = k;
+      c -= q_dim;
+      nh = kv_heads;
+    } else {
+      dst = v;
+      c -= q_dim + kv_dim;
+      nh = kv_heads;
+      rot = false;
+    }
+    int h = c >> 7;
+    int d0 = c & 127;
+    float o[32];
+    if (rot) {
+      const float2* rs = rope + (size_t)s * 64 + (d0 >> 1);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float2 cs = rs[i];
+        float a = acc[2 * i], bb = acc[2 * i + 1];
+        o[2 * i] = a * cs.x - bb * cs.y;
+        o[2 * i + 1] = bb * cs.x + a * cs.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = acc[i];
+    }
+    uint4* p = reinterpret_cast<uint4*>(dst + (((size_t)b * nh + h) * seq + s) * 128 + d0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_half2(o[8 * j + 0], o[8 * j + 1]);
+      w.y = pack_half2(o[8 * j + 2], o[8 * j + 3]);
+      w.z = pack_half2(o[8 * j + 4], o[8 * j + 5]);
+      w.w = pack_half2(o[8 * j + 6], o[8 * j + 7]);
+      p[j] = w;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// x[row, col] += alpha * acc   (fp32 residual stream, updated in place)
+struct EpiResidual {
+  float* x;
+  int ldx;
+  float alpha;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+    float4* p = reinterpret_cast<float4*>(x + (size_t)row * ldx + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 r = p[j];
+      r.x += alpha * v[4 * j + 0];
+      r.y += alpha * v[4 * j + 1];
+      r.z += alpha * v[4 * j + 2];
+      r.w += alpha * v[4 * j + 3];
+      p[j] = r;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// B rows interleave W1 and W3 columns: row 2j = W1[:, j], row 2j+1 = W3[:, j].
+// g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
+struct EpiSwiglu {
+  __half* g;
+  int ldg;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float h1 = v[2 * j], h3 = v[2 * j + 1];
+      o[j] = h1 / (1.0f + __expf(-h1)) * h3;
+    }
+    uint4* p = reinterpret_cast<uint4*>(g + (size_t)row * ldg + (col0 >> 1));
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint4 w;
+      w.x = pack_half2(o[8 * j + 0], o[8 * j + 1]);
+      w.y = pack_half2(o[8 * j + 2], o[8 * j + 3]);
+      w.z = pack_half2(o[8 * j + 4], o[8 * j + 5]);
+      w.w = pack_half2(o[8 * j + 6], o[8 * j + 7]);
+      p[j] = w;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// Fused LM head + cross-entropy partials. For each row and N-tile writes
+// (max_z, sum exp(z - max_z)) over the tile's logits z (softcapped if
+// softcap > 0) and, for the tile holding targets[row], that logit.
+struct EpiCrossEntropy {
+  float2* part;      // [M, nparts]
+  int nparts;
+  const uint32_t* targets;
+  float* tgt_logit;  // [M]
+  float softcap;
+  // per-thread running state
+  float m, s;
+  int tgt;
+  __device__ __forceinline__ void begin_row(int row, bool valid) {
+    m = -CUDART_INF_F;
+    s = 0.f;
+    tgt = valid ? (int)targets[row] : -1;
+  }
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+    float z[32];
+    float cm = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float t = v[i];
+      if (softcap > 0.f) t = softcap * tanhf(t / softcap);
+      z[i] = t;
+      cm = fmaxf(cm, t);
+    }
+    unsigned rel = (unsigned)(tgt - col0);
+    if (rel < 32u) {
+      float zt = z[0];
+#pragma unroll
+      for (int i = 1; i < 32; ++i) zt = (rel == (unsigned)i) ? z[i] : zt;
+      tgt_logit[row] = zt;
+    }
+    const float L2E = 1.4426950408889634f;
+    if (cm > m) {
+      s *= exp2f((m - cm) * L2E);
+      m = cm;
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc += exp2f((z[i] - m) * L2E);
+    s += acc;
+  }
+  __device__ __forceinline__ void end_row(int row, int n_blk) {
+    part[(size_t)row * nparts + n_blk] = make_float2(m, s);
+  }
+};
+
+// ------------------------------------------------------------------ kernel
+
+template <int BN, class Epi>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, int b_z, Epi epi, int* err) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const uint64_t pol_a = policy_evict_first();
+      const uint64_t pol_b = policy_evict_last();
+      uint32_t it = 0;  // loads issued
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * GEMM_BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          tma_load_3d(sA + s * Cfg::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m0, 0, pol_a);
+          tma_load_3d(sB + s * Cfg::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n0, b_z, pol_b);
+        }
+      }
+      // Drain: wait (bounded) for the copies this thread may still have in flight.
+      uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(GEMM_BM, BN);
+      uint32_t it = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            umma_f16_ss(d_tmem, sw128_kmajor_desc(a_addr + k * 32),
+                        sw128_kmajor_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+      // Drain: all MMAs issued by this thread complete before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, err);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_blk = tile / n_tiles;
+      const int n_blk = tile % n_tiles;
+      if (!mbar_wait(&tfull[acc], acc_ph, err)) break;
+      tc_fence_after();
+      const int row = m_blk * GEMM_BM + quad * 32 + lane;
+      const bool row_ok = row < M;
+      Epi e = epi;
+      e.begin_row(row, row_ok);
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = n_blk * BN + c * 32;
+        if (row_ok && col0 < N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          e.chunk(row, col0, v);
+        }
+      }
+      if (row_ok) e.end_row(row, n_blk);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace cb

@@ -1,0 +1,179 @@
+// Memory-bound row kernels of the forward pass: one warp per token row,
+// 128-bit vector loads/stores, warp-shuffle reductions.
+//
+//   embed_rmsnorm_kernel : X[t,:] = E[tok[t],:] (fp32 residual) and the layer-0
+//                          RMSNorm output Xn = X * rinv * gamma in fp16
+//                          (crates/engine/src/cpu/embedding.rs:8-17,
+//                           cpu/rmsnorm.rs:149-183, EPS = 1e-5 at :10)
+//   rmsnorm_kernel       : Xn = X * rinv * gamma (fp32 in, fp16 out)
+//   ce_finalize_kernel   : per-token loss from the LM-head epilogue partials,
+//                          loss_t = log(sum_v e^{z_v - m}) + m - z_tgt
+//                          (crates/engine/src/cpu/cross_entropy.rs:58-96)
+//   loss_mean_kernel     : fixed-order mean over tokens (deterministic)
+#pragma once
+#include <cuda_fp16.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+namespace cb {
+
+constexpr float RMS_EPS = 1e-5f;
+constexpr int ROW_WARPS = 8;  // warps per block for the row kernels
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void h8_to_f8(uint4 u, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f8_to_h8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_half2(f[0], f[1]);
+  u.y = pack_half2(f[2], f[3]);
+  u.z = pack_half2(f[4], f[5]);
+  u.w = pack_half2(f[6], f[7]);
+  return u;
+}
+
+// dim must be a multiple of 256 (8 elements per lane per step).
+__global__ void embed_rmsnorm_kernel(const uint32_t* __restrict__ tokens,
+                                     const __half* __restrict__ embed,
+                                     const float* __restrict__ gamma, float* __restrict__ x,
+                                     __half* __restrict__ xn, int T, int dim, int vocab,
+                                     int* err) {
+  const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  uint32_t tok = tokens[row];
+  if (tok >= (uint32_t)vocab) {  // out-of-range token id: report, use row 0
+    if (lane == 0) atomicExch(err, 2);
+    tok = 0;
+  }
+  const __half* e = embed + (size_t)tok * dim;
+  float* xr = x + (size_t)row * dim;
+  float ss = 0.f;
+  for (int c = lane * 8; c < dim; c += 256) {
+    float f[8];
+    h8_to_f8(*reinterpret_cast<const uint4*>(e + c), f);
+    *reinterpret_cast<float4*>(xr + c) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(xr + c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+  ss = warp_sum(ss);
+  const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  __half* o = xn + (size_t)row * dim;
+  for (int c = lane * 8; c < dim; c += 256) {
+    float f[8];
+    h8_to_f8(*reinterpret_cast<const uint4*>(e + c), f);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = f[i] * rinv * gg[i];
+    *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
+  }
+}
+
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                               __half* __restrict__ xn, int T, int dim) {
+  const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const float* xr = x + (size_t)row * dim;
+  float ss = 0.f;
+  for (int c = lane * 8; c < dim; c += 256) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z +
+          b.w * b.w;
+  }
+  ss = warp_sum(ss);
+  const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  __half* o = xn + (size_t)row * dim;
+  for (int c = lane * 8; c < dim; c += 256) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    float f[8] = {a.x * rinv * g0.x, a.y * rinv * g0.y, a.z * rinv * g0.z, a.w * rinv * g0.w,
+                  b.x * rinv * g1.x, b.y * rinv * g1.y, b.z * rinv * g1.z, b.w * rinv * g1.w};
+    *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
+  }
+}
+
+// One warp per token: combine `nparts` (max, sumexp) partials, subtract the target logit.
+// Writes tok_loss[t] and one partial sum per block into block_sums[blockIdx.x].
+__global__ void ce_finalize_kernel(const float2* __restrict__ part, int nparts,
+                                   const float* __restrict__ tgt_logit,
+                                   float* __restrict__ tok_loss, float* __restrict__ block_sums,
+                                   int T) {
+  __shared__ float wsum[ROW_WARPS];
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * ROW_WARPS + w;
+  const int lane = threadIdx.x & 31;
+  float loss = 0.f;
+  if (row < T) {
+    const float2* p = part + (size_t)row * nparts;
+    float m = -CUDART_INF_F;
+    for (int i = lane; i < nparts; i += 32) m = fmaxf(m, p[i].x);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int i = lane; i < nparts; i += 32) s += p[i].y * __expf(p[i].x - m);
+    s = warp_sum(s);
+    loss = logf(s) + m - tgt_logit[row];
+    if (lane == 0) tok_loss[row] = loss;
+  }
+  if (lane == 0) wsum[w] = (row < T) ? loss : 0.f;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int i = 0; i < ROW_WARPS; ++i) acc += wsum[i];
+    block_sums[blockIdx.x] = acc;
+  }
+}
+
+// Single block: mean over T tokens from the per-block sums (fixed order).
+__global__ void loss_mean_kernel(const float* __restrict__ block_sums, int nblocks, int T,
+                                 float* __restrict__ loss) {
+  __shared__ double sh[256];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < nblocks; i += blockDim.x) acc += (double)block_sums[i];
+  sh[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) loss[0] = (float)(sh[0] / (double)T);
+}
+
+// Copy selected rows of src [*, dim] fp16 into dst [n, dim] (zero rows past n up to n_pad).
+__global__ void gather_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ rows,
+                                   int n, int n_pad, int dim, __half* __restrict__ dst) {
+  const int r = blockIdx.x;
+  if (r >= n_pad) return;
+  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)r * dim);
+  if (r < n) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)rows[r] * dim);
+    for (int c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = s[c];
+  } else {
+    for (int c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+}  // namespace cb

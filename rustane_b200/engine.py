@@ -1,0 +1,319 @@
+"""Engine-level forward/loss API over the CUDA bridge.
+
+Names and argument meaning follow the reference engine so callers switch
+without changes:
+  CompiledKernels.compile_forward_only(cfg)      layer.rs:967
+  ModelWeights (random / from host arrays)        full_model.rs:19-23,132-141
+  ModelForwardWorkspace.new / new_lean            full_model.rs:221-263
+  forward_only_ws / forward_ws / forward          full_model.rs:378,494,915
+  forward_losses                                  full_model.rs:1603
+  ForwardScheduler (sequence-parallel workers)    multistream.rs:54-161
+Errors raise CudaBridgeError (the reference panics on ANE eval failure,
+layer.rs:1678).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import bridge as B
+from .model import ModelConfig
+
+
+def _cfg_struct(cfg: ModelConfig) -> B.cb_model_config:
+    return B.cb_model_config(cfg.dim, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.hd, cfg.seq,
+                             cfg.nlayers, cfg.vocab)
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+@dataclass
+class LayerWeights:
+    """Host f32 layer weights in the reference orientation (layer.rs:52-63)."""
+    wq: np.ndarray
+    wk: np.ndarray
+    wv: np.ndarray
+    wo: np.ndarray
+    w1: np.ndarray
+    w3: np.ndarray
+    w2: np.ndarray
+    gamma1: np.ndarray
+    gamma2: np.ndarray
+
+
+@dataclass
+class ModelWeights:
+    """Model weights. Either host f32 arrays (embed/layers/gamma_final) or a
+    device-side generator spec (scheme, seed, sigma) the bridge expands on the
+    GPU without a host copy of the model."""
+    embed: Optional[np.ndarray] = None
+    layers: Optional[list] = None
+    gamma_final: Optional[np.ndarray] = None
+    scheme: Optional[int] = None
+    seed: int = 0
+    sigma: float = 0.02
+    generation: int = field(default_factory=lambda: ModelWeights._next_gen())
+
+    _gen_lock = threading.Lock()
+    _gen_counter = [0]
+
+    @staticmethod
+    def _next_gen() -> int:
+        with ModelWeights._gen_lock:
+            ModelWeights._gen_counter[0] += 1
+            return ModelWeights._gen_counter[0]
+
+    @classmethod
+    def random(cls, cfg: ModelConfig) -> "ModelWeights":
+        """The reference's own init (ModelWeights::random, full_model.rs:132-141)."""
+        return cls(scheme=B.CB_INIT_REFERENCE)
+
+    @classmethod
+    def normal(cls, cfg: ModelConfig, seed: int = 0, sigma: float = 0.02) -> "ModelWeights":
+        """All matrices ~N(0, sigma), gains 1.0 (the benchmark init)."""
+        return cls(scheme=B.CB_INIT_NORMAL, seed=seed, sigma=sigma)
+
+    @classmethod
+    def from_arrays(cls, embed, layers: Sequence[LayerWeights], gamma_final) -> "ModelWeights":
+        return cls(embed=np.ascontiguousarray(embed, np.float32), layers=list(layers),
+                   gamma_final=np.ascontiguousarray(gamma_final, np.float32))
+
+
+class ModelForwardWorkspace:
+    """Accepted for API compatibility. The device workspace lives inside
+    CompiledKernels (sized by its max_batch); nothing is allocated here."""
+
+    def __init__(self, cfg: ModelConfig):
+        self.cfg = cfg
+
+    @classmethod
+    def new(cls, cfg: ModelConfig) -> "ModelForwardWorkspace":
+        return cls(cfg)
+
+    @classmethod
+    def new_lean(cls, cfg: ModelConfig) -> "ModelForwardWorkspace":
+        return cls(cfg)
+
+
+class CompiledKernels:
+    """Owns one cb_ctx: device weights, workspace and captured forward graphs
+    for `max_batch` sequences on one GPU. Not thread-safe (one per thread)."""
+
+    def __init__(self, cfg: ModelConfig, device: int = 0, max_batch: int = 1):
+        self.lib = B.load_library()
+        self.cfg = cfg
+        self.device = device
+        self.max_batch = max_batch
+        h = C.c_void_p()
+        B.check(self.lib.cb_create(C.byref(_cfg_struct(cfg)), device, max_batch, C.byref(h)))
+        self._h = h
+        self._loaded_generation: Optional[int] = None
+
+    @classmethod
+    def compile_forward_only(cls, cfg: ModelConfig, device: int = 0,
+                             max_batch: int = 1) -> "CompiledKernels":
+        return cls(cfg, device, max_batch)
+
+    compile = compile_forward_only
+
+    # ---- lifecycle
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.cb_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if not self._h:
+            raise RuntimeError("CompiledKernels is closed")
+        return self._h
+
+    def _check(self, status: int) -> None:
+        B.check(status, self._h)
+
+    # ---- weights
+    def init_weights(self, seed: int = 0, scheme: int = B.CB_INIT_NORMAL,
+                     sigma: float = 0.02) -> None:
+        self._check(self.lib.cb_init_weights(self.handle, seed, scheme, sigma))
+        self._loaded_generation = None
+
+    def load_weights(self, w: ModelWeights) -> None:
+        if self._loaded_generation == w.generation:
+            return
+        if w.scheme is not None:
+            self.init_weights(w.seed, w.scheme, w.sigma)
+        else:
+            cfg = self.cfg
+            if len(w.layers) != cfg.nlayers:
+                raise ValueError("layer count does not match the config")
+            keep = []
+            arr = (B.cb_layer_weights_f32 * cfg.nlayers)()
+            for i, lw in enumerate(w.layers):
+                fields = {}
+                for name in ("wq", "wk", "wv", "wo", "w1", "w3", "w2", "gamma1", "gamma2"):
+                    a = np.ascontiguousarray(getattr(lw, name), np.float32)
+                    keep.append(a)
+                    fields[name] = _fptr(a)
+                arr[i] = B.cb_layer_weights_f32(**fields)
+            self._check(self.lib.cb_load_weights_f32(self.handle, _fptr(w.embed),
+                                                     _fptr(w.gamma_final), arr))
+        self._loaded_generation = w.generation
+
+    # ---- forward
+    def _tokens(self, tokens, targets):
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        g = np.ascontiguousarray(np.asarray(targets, dtype=np.uint32).reshape(-1))
+        if t.size != g.size or t.size % self.cfg.seq != 0:
+            raise ValueError("tokens/targets must hold whole sequences of cfg.seq")
+        return t, g, t.size // self.cfg.seq
+
+    def forward_loss(self, tokens, targets, softcap: float = 0.0,
+                     per_token: bool = False):
+        t, g, batch = self._tokens(tokens, targets)
+        loss = C.c_float()
+        ptl = np.empty(t.size, np.float32) if per_token else None
+        self._check(self.lib.cb_forward_loss(
+            self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)),
+            g.ctypes.data_as(C.POINTER(C.c_uint32)), batch, softcap, C.byref(loss),
+            _fptr(ptl) if ptl is not None else None))
+        return (loss.value, ptl) if per_token else loss.value
+
+    def forward_loss_async(self, d_tokens: int, d_targets: int, batch: int, softcap: float,
+                           d_loss: int, d_per_token: int = 0, stream: int = 0) -> None:
+        """Device-pointer variant (ints are raw device addresses)."""
+        self._check(self.lib.cb_forward_loss_async(
+            self.handle, C.c_void_p(d_tokens), C.c_void_p(d_targets), batch, softcap,
+            C.c_void_p(d_loss), C.c_void_p(d_per_token or None), C.c_void_p(stream or None)))
+
+    def check_device_error(self) -> None:
+        self._check(self.lib.cb_check_device_error(self.handle))
+
+    def sampled_logits(self, rows) -> np.ndarray:
+        r = np.ascontiguousarray(np.asarray(rows, dtype=np.int32).reshape(-1))
+        out = np.empty((r.size, self.cfg.vocab), np.float32)
+        self._check(self.lib.cb_sampled_logits(
+            self.handle, r.ctypes.data_as(C.POINTER(C.c_int32)), r.size, _fptr(out)))
+        return out
+
+    # ---- profiling
+    def set_profiling(self, enable: bool) -> None:
+        self._check(self.lib.cb_set_profiling(self.handle, 1 if enable else 0))
+
+    def reset_kernel_times(self) -> None:
+        self._check(self.lib.cb_reset_kernel_times(self.handle))
+
+    def kernel_times(self) -> dict:
+        arr = (B.cb_kernel_time * 32)()
+        n = C.c_int32()
+        self._check(self.lib.cb_kernel_times(self.handle, arr, 32, C.byref(n)))
+        return {arr[i].name.decode(): dict(launches=arr[i].launches, total_ms=arr[i].total_ms,
+                                           flops=arr[i].flops, bytes=arr[i].bytes)
+                for i in range(n.value)}
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        self._check(self.lib.cb_get_stream(self.handle, C.byref(s)))
+        return s.value or 0
+
+
+# ---------------------------------------------------------------- model API
+
+@dataclass
+class ForwardResult:
+    """Forward outputs. The reference's ForwardResult (full_model.rs:121-129)
+    also carries backward caches; training is not part of this engine."""
+    loss: float
+    per_token_loss: Optional[np.ndarray] = None
+
+
+def forward_only_ws(cfg: ModelConfig, kernels: CompiledKernels, weights: ModelWeights,
+                    tokens, targets, softcap: float = 0.0,
+                    ws: Optional[ModelForwardWorkspace] = None) -> float:
+    """Mean next-token cross-entropy (full_model.rs:378). tokens/targets hold one
+    or more sequences of cfg.seq back to back."""
+    if kernels.cfg != cfg:
+        raise ValueError("kernels were compiled for a different config")
+    kernels.load_weights(weights)
+    return kernels.forward_loss(tokens, targets, softcap)
+
+
+forward_ws = forward_only_ws
+
+
+def forward(cfg: ModelConfig, kernels: CompiledKernels, weights: ModelWeights, tokens,
+            targets, softcap: float = 0.0) -> ForwardResult:
+    kernels.load_weights(weights)
+    loss, ptl = kernels.forward_loss(tokens, targets, softcap, per_token=True)
+    return ForwardResult(loss, ptl)
+
+
+def forward_losses(cfg: ModelConfig, kernels: CompiledKernels, weights: ModelWeights, tokens,
+                   targets, softcap: float = 0.0) -> np.ndarray:
+    """Per-position losses (full_model.rs:1603)."""
+    kernels.load_weights(weights)
+    return kernels.forward_loss(tokens, targets, softcap, per_token=True)[1]
+
+
+class ForwardScheduler:
+    """Sequence-parallel forward workers (multistream.rs:54-161): one
+    CompiledKernels per worker (here: per GPU), each on its own host thread,
+    pulling whole sequences; results return in request order. No communication
+    between workers."""
+
+    def __init__(self, cfg: ModelConfig, weights: ModelWeights, devices: Sequence[int],
+                 max_batch: int = 1):
+        self.cfg = cfg
+        self.workers = [CompiledKernels(cfg, d, max_batch) for d in devices]
+        for w in self.workers:
+            w.load_weights(weights)
+
+    def run_batch(self, requests: Sequence[tuple], softcap: float = 0.0) -> list:
+        """requests: [(tokens, targets)] one sequence each -> [loss] in order."""
+        out = [None] * len(requests)
+        errors = []
+        lock = threading.Lock()
+        nxt = [0]
+
+        def work(k: CompiledKernels):
+            while True:
+                with lock:
+                    i = nxt[0]
+                    nxt[0] += 1
+                if i >= len(requests):
+                    return
+                try:
+                    out[i] = k.forward_loss(requests[i][0], requests[i][1], softcap)
+                except Exception as e:  # propagate after join
+                    errors.append(e)
+                    return
+
+        threads = [threading.Thread(target=work, args=(k,)) for k in self.workers]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return out
+
+    def close(self) -> None:
+        for w in self.workers:
+            w.close()

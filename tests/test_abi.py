@@ -1,0 +1,104 @@
+"""CPU tests of the C ABI boundary and the host-side API (no GPU needed)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from rustane_b200 import bridge as B
+from rustane_b200.model import CONFIGS, ModelConfig
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "cuda_bridge.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(cb_\w+)\(", text, re.M)))
+
+
+def test_header_declares_exported_list():
+    assert header_functions() == sorted(B.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(bridge_lib):
+    for name in header_functions():
+        assert hasattr(bridge_lib, name), name
+
+
+def test_version(bridge_lib):
+    assert b"sm_100a" in bridge_lib.cb_version()
+
+
+def test_device_count(bridge_lib):
+    n = C.c_int32(-1)
+    assert bridge_lib.cb_device_count(C.byref(n)) == B.CB_OK
+    assert n.value >= 0
+
+
+def _create(cfg_tuple, max_batch=1):
+    lib = B.load_library()
+    h = C.c_void_p()
+    cfg = B.cb_model_config(*cfg_tuple)
+    return lib.cb_create(C.byref(cfg), 0, max_batch, C.byref(h)), h
+
+
+@pytest.mark.parametrize("bad", [
+    (1536, 4096, 12, 12, 64, 512, 20, 8192),   # hd != 128
+    (1500, 4096, 12, 12, 128, 512, 20, 8192),  # dim not a multiple of 256
+    (1536, 4096, 12, 5, 128, 512, 20, 8192),   # heads % kv_heads
+    (1536, 4096, 12, 12, 128, 500, 20, 8192),  # seq % 64
+    (1536, 4096, 12, 12, 128, 512, 0, 8192),   # no layers
+    (1536, 4000, 12, 12, 128, 512, 20, 8192),  # hidden % 64
+])
+def test_create_rejects_invalid_config(bridge_lib, bad):
+    rc, h = _create(bad)
+    assert rc == B.CB_ERR_INVALID_ARG
+    assert not h.value
+    assert bridge_lib.cb_create_error()
+
+
+def test_create_rejects_bad_batch(bridge_lib):
+    rc, _ = _create((256, 512, 2, 2, 128, 64, 1, 512), max_batch=0)
+    assert rc == B.CB_ERR_INVALID_ARG
+
+
+def test_create_without_gpu_fails_loudly(bridge_lib):
+    n = C.c_int32()
+    bridge_lib.cb_device_count(C.byref(n))
+    if n.value > 0:
+        pytest.skip("a GPU is present")
+    rc, h = _create((256, 512, 2, 2, 128, 64, 1, 512))
+    assert rc == B.CB_ERR_UNSUPPORTED
+    assert b"no CUDA device" in bridge_lib.cb_create_error()
+
+
+def test_null_context_calls_are_rejected(bridge_lib):
+    assert bridge_lib.cb_destroy(None) == B.CB_OK
+    assert bridge_lib.cb_init_weights(None, 0, 0, 0.02) == B.CB_ERR_INVALID_ARG
+    assert bridge_lib.cb_forward_loss(None, None, None, 1, 0.0, None, None) == B.CB_ERR_INVALID_ARG
+    assert bridge_lib.cb_gemm_f16(None, None, None, 128, 128, 64, 0, 0, None) == B.CB_ERR_INVALID_ARG
+    assert bridge_lib.cb_last_error(None) == b"null context"
+
+
+def test_python_api_raises_without_gpu(bridge_lib):
+    n = C.c_int32()
+    bridge_lib.cb_device_count(C.byref(n))
+    if n.value > 0:
+        pytest.skip("a GPU is present")
+    from rustane_b200 import CompiledKernels, CudaBridgeError
+    with pytest.raises(CudaBridgeError):
+        CompiledKernels.compile_forward_only(ModelConfig.gpt_karpathy())
+
+
+def test_param_counts_match_reference_presets():
+    # model.rs doc comments: 600M ~579M, gpt_karpathy 48.8M incl. embedding
+    assert abs(ModelConfig.target_600m().param_count() / 1e6 - 579) < 1
+    assert CONFIGS["600m-A"] == ModelConfig.target_600m()
+
+
+def test_flop_model_matches_survey():
+    cfg = CONFIGS["600m-A"]
+    tflop_fwd = cfg.forward_flops_per_token() * 512 / 1e12
+    assert abs(tflop_fwd - 0.6088) < 0.001
+    c4 = CONFIGS["32B"]
+    assert abs(c4.forward_flops_per_token() * 32768 / 1e12 - 2161.0) < 1.0
