@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Forward + loss throughput of the rustane transformer on B200.
+
+Workload (default): 600m-A (1536d / 4096h / 20L / 12 heads x 128, vocab 8192,
+tied head), seq 512, global batch 64 sequences of uniform random tokens,
+sharded by sequence over the GPUs (no communication; total work fixed:
+strong scaling). Weights ~N(0, 0.02) generated on the device, RMSNorm gains 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line. Phases (ours):
+  1. timed region (value): K forwards from device-resident tokens through
+     cb_forward_loss_async (CUDA graph), CUDA events on the bridge's stream,
+     barrier + synchronize on both sides, max over ranks;
+  2. profiled pass: the same K forwards with CUDA events around every kernel
+     (per-kernel durations for the roofline);
+  3. e2e pass: K calls of the public host API cb_forward_loss with pinned host
+     tokens/targets (H2D copy + forward + D2H loss inside the timed region);
+  4. CPU baseline (rank 0, N = 1): the CPU oracle on a bounded sample.
+--impl reference times the reference's forward math on the host cores (the CPU
+restatement under oracle/; the Rust reference cannot be built here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "forward tokens/sec (ms/forward, seq512) at 1/2/4/8 B200; % of fp16 TC peak"
+GEMM_CLASSES = ("gemm_qkv_rope", "gemm_o_residual", "gemm_w13_swiglu", "gemm_w2_residual",
+                "gemm_lmhead_ce")
+# DRAM bytes per GEMM launch measured by ncu (profiles/gemm_tc_600m-A_dram.md):
+# sum over the 101 GEMM launches of one forward at 8 sequences, scaled x8 to the
+# 64-sequence workload, divided by 101. None until measured.
+GEMM_TRAFFIC_PER_LAUNCH = None
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", default="600m-A")
+    p.add_argument("--global-batch", type=int, default=64)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--cpu-budget-s", type=float, default=12.0,
+                   help="CPU-baseline sample budget (seconds of oracle work)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during a region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.6)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def make_tokens(cfg, n_seq, seed, rank):
+    rng = np.random.default_rng([seed, rank])
+    tok = rng.integers(0, cfg.vocab, n_seq * cfg.seq, dtype=np.int64).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, n_seq * cfg.seq, dtype=np.int64).astype(np.uint32)
+    return tok, tgt
+
+
+def cpu_oracle_sample(cfg, seed, tok, tgt, budget_s):
+    """Time the CPU oracle on whole sequences until budget_s is spent."""
+    from oracle import oracle
+    model = oracle.OracleModel(cfg, seed=seed, scheme=oracle.SCHEME_NORMAL, sigma=0.02)
+    threads = oracle.max_threads()
+    n_done, elapsed, losses = 0, 0.0, []
+    n_avail = tok.size // cfg.seq
+    while n_done < n_avail and (n_done == 0 or elapsed < budget_s):
+        s = slice(n_done * cfg.seq, (n_done + 1) * cfg.seq)
+        t0 = time.perf_counter()
+        loss, _, _ = model.forward(tok[s], tgt[s])
+        elapsed += time.perf_counter() - t0
+        losses.append(loss)
+        n_done += 1
+    return dict(seqs=n_done, seconds=elapsed, threads=threads, losses=losses)
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """Reference arm: the reference's forward math on the host CPU cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from rustane_b200.model import CONFIGS
+    from oracle import oracle
+    cfg = CONFIGS[args.config]
+    tok, tgt = make_tokens(cfg, 1, args.seed, 0)
+    model = oracle.OracleModel(cfg, seed=args.seed, scheme=oracle.SCHEME_NORMAL, sigma=0.02)
+    threads = oracle.max_threads()
+    for _ in range(args.warmup):
+        model.forward(tok, tgt)
+    t0 = time.perf_counter()
+    loss = None
+    for _ in range(args.steps):
+        loss, _, _ = model.forward(tok, tgt)
+    dt = time.perf_counter() - t0
+    value = args.steps * cfg.seq / dt
+    sample = (f"one {cfg.seq}-token sequence of the {args.config} forward+loss per step "
+              f"(fp32 CPU restatement of the reference math, {threads} threads, "
+              f"{cpu_model_name()})")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} forward+loss, seq {cfg.seq}", "seq_len": cfg.seq,
+                   "global_batch": args.global_batch, "sample_per_step": 1},
+        "loss": loss,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
+    from rustane_b200.model import CONFIGS
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+
+    cfg = CONFIGS[args.config]
+    if args.global_batch % world:
+        raise SystemExit("global batch must divide evenly over the GPUs")
+    per = args.global_batch // world
+    T = per * cfg.seq
+    kern = CompiledKernels(cfg, local, per)
+    kern.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
+    tok_np, tgt_np = make_tokens(cfg, per, args.seed, rank)
+    d_tok = torch.from_numpy(tok_np.view(np.int32)).cuda()
+    d_tgt = torch.from_numpy(tgt_np.view(np.int32)).cuda()
+    d_loss = torch.zeros(1, dtype=torch.float32, device="cuda")
+    sptr = kern.stream()
+    stream = torch.cuda.ExternalStream(sptr)
+
+    def step():
+        kern.forward_loss_async(d_tok.data_ptr(), d_tgt.data_ptr(), per, 0.0, d_loss.data_ptr(),
+                                0, sptr)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def mean_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item()) / world
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    kern.check_device_error()
+
+    # ---- 1. timed region (CUDA graph replays, device-resident inputs)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    kern.check_device_error()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    loss = mean_over_ranks(float(d_loss.item()))
+    ms_step = ms_total / args.steps
+    tokens_total = args.global_batch * cfg.seq * args.steps
+    value = tokens_total / (ms_total / 1e3)
+
+    # ---- 2. profiled pass: CUDA events around every kernel
+    kern.set_profiling(True)
+    kern.reset_kernel_times()
+    barrier()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    times = kern.kernel_times()
+    kern.set_profiling(False)
+    barrier()
+
+    # ---- 3. e2e through the public host API (pinned host buffers)
+    e2e = None
+    if not args.no_e2e:
+        h_tok = torch.from_numpy(tok_np.view(np.int32)).pin_memory()
+        h_tgt = torch.from_numpy(tgt_np.view(np.int32)).pin_memory()
+        tok_view = h_tok.numpy().view(np.uint32)
+        tgt_view = h_tgt.numpy().view(np.uint32)
+        kern.forward_loss(tok_view, tgt_view)  # warm the path
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            kern.forward_loss(tok_view, tgt_view)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+        e2e = {"value": tokens_total / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(tok_view.nbytes + tgt_view.nbytes) * world,
+               "d2h_bytes_per_step": 4 * world, "ms_per_step": e2e_ms / args.steps}
+
+    # ---- roofline of the dominant kernel (the tcgen05 GEMM, all its launches)
+    peaks, peak_kind = load_peaks()
+    g_launch = sum(times[c]["launches"] for c in GEMM_CLASSES if c in times)
+    g_ms = sum(times[c]["total_ms"] for c in GEMM_CLASSES if c in times)
+    g_flops = sum(times[c]["flops"] for c in GEMM_CLASSES if c in times)
+    all_ms = sum(v["total_ms"] for v in times.values())
+    peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+    roofline = {
+        "kernel": "gemm_tn_kernel (tcgen05, all 5 fused-epilogue GEMMs)",
+        "bound": "tensor", "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
+        "frac": round(achieved / peak_tf, 4), "peak_source": f"bf16_tflops_sustained ({peak_kind})",
+        "flops_per_launch": g_flops / max(g_launch, 1),
+        "ms_per_launch": g_ms / max(g_launch, 1),
+        "share_of_step": round(g_ms / all_ms, 4) if all_ms > 0 else None,
+        "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+    }
+    flops_fwd = cfg.forward_flops_per_token() * args.global_batch * cfg.seq
+    kernels = {k: {"launches": v["launches"], "ms": round(v["total_ms"], 3),
+                   "share": round(v["total_ms"] / all_ms, 4) if all_ms else None,
+                   "tflops": round(v["flops"] / (v["total_ms"] / 1e3) / 1e12, 1)
+                   if v["flops"] and v["total_ms"] else None,
+                   "gbs": round(v["bytes"] / (v["total_ms"] / 1e3) / 1e9, 1)
+                   if v["total_ms"] else None}
+               for k, v in times.items()}
+
+    # ---- 4. CPU baseline on the host cores (rank 0 at N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_oracle_sample(cfg, args.seed, tok_np, tgt_np, args.cpu_budget_s)
+        cpu_val = r["seqs"] * cfg.seq / r["seconds"]
+        gpu_seq_losses = kern.forward_loss(tok_np[:r["seqs"] * cfg.seq],
+                                           tgt_np[:r["seqs"] * cfg.seq])
+        cpu = {"value": cpu_val, "unit": "tokens/s", "cores": r["threads"], "kind": "port",
+               "sample": (f"{r['seqs']} x {cfg.seq}-token sequences of the bench workload "
+                          f"(same weights and tokens), fp32 CPU oracle, {r['threads']} threads, "
+                          f"{cpu_model_name()}"),
+               "parity": {"loss_cpu": float(np.mean(r["losses"])), "loss_gpu": gpu_seq_losses,
+                          "rel": abs(gpu_seq_losses - float(np.mean(r["losses"])))
+                          / float(np.mean(r["losses"]))}}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (uniform random tokens, N(0,0.02) weights generated on device)",
+            "config": {
+                "workload": (f"{args.config} forward+loss ({cfg.dim}d/{cfg.hidden}h/"
+                             f"{cfg.nlayers}L/{cfg.heads}x128, vocab {cfg.vocab}, tied head), "
+                             f"seq {cfg.seq}, global batch {args.global_batch}"),
+                "global_batch": args.global_batch, "seq_len": cfg.seq,
+                "parallelism": f"dp{world} (sequence sharding, no communication)",
+                "per_gpu_batch": per,
+                "l2": "no flush: every step reads >1.1 GB of weights and >1 GB of "
+                      "activations, well above the 126 MB L2",
+            },
+            "loss": loss,
+            "tflops": flops_fwd / (ms_step / 1e3) / 1e12,
+            "frac_of_peak_forward": round(flops_fwd / (ms_step / 1e3) / 1e12 / peak_tf, 4),
+            "roofline": roofline,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(sum(v["launches"] for v in times.values())),
+            "clocks": clk,
+            "ms_per_step_profiled": all_ms / args.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+    kern.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -81,13 +81,22 @@ def _kat(name):
 @pytest.mark.parametrize("name,cfg_key", [("600m-A", "600m-A"), ("7B", "7B"), ("13B", "13B")])
 def test_reference_init_known_answer_full_depth(bridge_lib, name, cfg_key):
     """The reference's own init and benchmark tokens at full depth reproduce
-    the published forward loss."""
+    the published forward loss.
+
+    Bound: 5e-5 relative. Under this init every layer is an identity and the
+    loss is dominated by each token's self-logit, a dim-long dot product of
+    all-positive terms (about 10 at dim 5120). Tensor-core fp32 accumulation
+    truncates instead of rounding, which biases such sums low by ~2e-5
+    relative at 13B (test_gemm_positive_sum_bias_matches_cublas shows cuBLAS
+    has the same bias); the oracle and the published values accumulate with
+    round-to-nearest on the CPU."""
     cfg = CONFIGS[cfg_key]
     tok, tgt = reference_tokens(cfg.seq, cfg.vocab)
     with CompiledKernels(cfg, 0, 1) as k:
         w = ModelWeights.random(cfg)
         loss = forward_only_ws(cfg, k, w, tok, tgt, 0.0)
-    assert abs(loss - _kat(name)["loss"]) <= 1e-4, loss
+    ref = _kat(name)["loss"]
+    assert abs(loss - ref) / ref <= 5e-5, loss
 
 
 def test_host_f32_upload_matches_device_init(bridge_lib):

@@ -61,3 +61,27 @@ def test_attention_matches_torch(bridge_lib, batch, heads, seq):
     ref = ref.transpose(1, 2).reshape(batch * seq, heads * 128)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=3e-3)
+
+
+def test_gemm_positive_sum_bias_matches_cublas(bridge_lib):
+    """Long all-positive dot products: our tcgen05 GEMM and cuBLAS show the same
+    small low bias against float64 (tensor-core fp32 accumulation truncates)."""
+    M, N, K = 512, 512, 5120
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.rand(M, K, device="cuda", generator=g).half()
+    b = torch.rand(N, K, device="cuda", generator=g).half()
+    ref = a.double() @ b.double().T
+    ours = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_gemm_f16(_ptr(a), _ptr(b), _ptr(ours), M, N, K, 1, 0, _stream()) == 0
+    torch.cuda.synchronize()
+    rel_ours = ((ours.double() - ref) / ref).mean().item()
+    # cuBLAS fp16 GEMM with fp32 accumulation and fp32 output (when torch exposes it)
+    try:
+        cub = torch.mm(a, b.T, out_dtype=torch.float32)
+    except (TypeError, RuntimeError):
+        cub = None
+    assert abs(rel_ours) < 2e-4
+    if cub is not None:
+        rel_cub = ((cub.double() - ref) / ref).mean().item()
+        print(f"mean relative error vs float64: ours {rel_ours:.3e}, cuBLAS {rel_cub:.3e}")
+        assert abs(rel_ours - rel_cub) < max(5e-5, 0.5 * abs(rel_cub))
