@@ -177,6 +177,18 @@ cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t 
 cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out,
                            int32_t batch, int32_t heads, int32_t seq, void* stream);
 
+/* Tied LM head + next-token cross-entropy on device buffers (the model's final
+ * step: full_model.rs:436-471). xf [T, dim] fp16 (final-normalised activations),
+ * embed [vocab, dim] fp16, targets [T] u32. Logits = xf * embed^T, softcapped when
+ * softcap > 0, are reduced on chip to per-token losses; the [T, vocab] logits are
+ * never written. per_token_loss (device [T] f32) and loss (device f32 scalar, mean)
+ * are each nullable. A target >= vocab yields NaN for that token. dim % 64 == 0,
+ * vocab % 32 == 0, 16-byte aligned pointers. Scratch of about T*vocab/32 bytes comes
+ * from the stream-ordered allocator (cudaMallocAsync) and is released on `stream`. */
+cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* targets,
+                            int32_t T, int32_t dim, int32_t vocab, float softcap,
+                            float* per_token_loss, float* loss, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -412,6 +412,82 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
 
 int launches_per_forward(const cb_ctx* c) { return 7 * c->cfg.nlayers + 4; }
 
+// ---------------------------------------------------------- standalone LM head + CE
+struct LmCeScratch {
+  float2* part;       // [T, nparts]
+  float* tgt;         // [T]
+  float* tok;         // [T]   (used when the caller passes no per-token buffer)
+  float* blocks;      // [ceil(T / ROW_WARPS)]
+  float* loss;        // [1]   (used when the caller passes no loss buffer)
+};
+
+int lm_ce_block_n(int vocab) { return (vocab % 256 == 0) ? 256 : 128; }
+int lm_ce_nparts(int vocab) { return (vocab + lm_ce_block_n(vocab) - 1) / lm_ce_block_n(vocab); }
+
+size_t lm_ce_scratch_bytes(int T, int vocab) {
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t nb = (size_t)(T + ROW_WARPS - 1) / ROW_WARPS;
+  return up((size_t)T * lm_ce_nparts(vocab) * sizeof(float2)) + 2 * up((size_t)T * 4) +
+         up(nb * 4) + up(4);
+}
+
+LmCeScratch lm_ce_carve(void* base, int T, int vocab) {
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  uint8_t* p = static_cast<uint8_t*>(base);
+  LmCeScratch s;
+  s.part = reinterpret_cast<float2*>(p);
+  p += up((size_t)T * lm_ce_nparts(vocab) * sizeof(float2));
+  s.tgt = reinterpret_cast<float*>(p);
+  p += up((size_t)T * 4);
+  s.tok = reinterpret_cast<float*>(p);
+  p += up((size_t)T * 4);
+  s.blocks = reinterpret_cast<float*>(p);
+  p += up((size_t)(T + ROW_WARPS - 1) / ROW_WARPS * 4);
+  s.loss = reinterpret_cast<float*>(p);
+  return s;
+}
+
+bool lm_ce_args_ok(const void* xf, const void* embed, const uint32_t* targets, int T, int d,
+                   int V) {
+  if (!xf || !embed || !targets || T <= 0 || d <= 0 || V <= 0) return false;
+  if (d % 64 != 0 || V % 32 != 0) return false;
+  return (((uintptr_t)xf | (uintptr_t)embed) & 15) == 0;
+}
+
+// Enqueue the fused head: GEMM with the cross-entropy epilogue, per-token combine,
+// fixed-order mean. Target logits start as NaN so an out-of-range target shows.
+cudaError_t lm_ce_enqueue(const void* xf, const void* embed, const uint32_t* targets, int T,
+                          int d, int V, float softcap, float* per_token_loss, float* loss,
+                          const LmCeScratch& s, cudaStream_t st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  ensure_attrs(dev);
+  const int sms = num_sms_of(dev);
+  const int bn = lm_ce_block_n(V);
+  const int nparts = lm_ce_nparts(V);
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, xf, d, T, 1, 128) || !make_tmap(&tb, embed, d, V, 1, bn))
+    return cudaErrorInvalidValue;
+  e = cudaMemsetAsync(s.tgt, 0xFF, (size_t)T * 4, st);
+  if (e != cudaSuccess) return e;
+  EpiCrossEntropy ep{};
+  ep.part = s.part;
+  ep.nparts = nparts;
+  ep.targets = targets;
+  ep.tgt_logit = s.tgt;
+  ep.softcap = softcap;
+  e = launch_gemm(bn, ta, tb, tb, T, V, d, 0, ep, nullptr, sms, st);
+  if (e != cudaSuccess) return e;
+  const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
+  float* tok = per_token_loss ? per_token_loss : s.tok;
+  ce_finalize_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(s.part, nparts, s.tgt, tok, s.blocks,
+                                                            T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  loss_mean_kernel<<<1, 256, 0, st>>>(s.blocks, row_blocks, T, loss ? loss : s.loss);
+  return cudaGetLastError();
+}
+
 void harvest(cb_ctx* c) {
   if (!c->pending_harvest) return;
   c->pending_harvest = false;
@@ -951,6 +1027,22 @@ cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* ou
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
       static_cast<__half*>(out), seq, heads, heads, 1.4426950408889634f / sqrtf(128.0f));
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* targets,
+                            int32_t T, int32_t dim, int32_t vocab, float softcap,
+                            float* per_token_loss, float* loss, void* stream) {
+  if (!lm_ce_args_ok(xf, embed, targets, T, dim, vocab)) return CB_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  if (cudaMallocAsync(&scratch, lm_ce_scratch_bytes(T, vocab), st) != cudaSuccess)
+    return CB_ERR_OUT_OF_MEMORY;
+  const LmCeScratch s = lm_ce_carve(scratch, T, vocab);
+  cudaError_t e = lm_ce_enqueue(xf, embed, targets, T, dim, vocab, softcap, per_token_loss, loss,
+                                s, st);
+  cudaError_t e2 = cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess || e2 != cudaSuccess) return CB_ERR_CUDA;
+  return CB_OK;
 }
 
 }  // extern "C"

@@ -85,3 +85,47 @@ def test_gemm_positive_sum_bias_matches_cublas(bridge_lib):
         rel_cub = ((cub.double() - ref) / ref).mean().item()
         print(f"mean relative error vs float64: ours {rel_ours:.3e}, cuBLAS {rel_cub:.3e}")
         assert abs(rel_ours - rel_cub) < max(5e-5, 0.5 * abs(rel_cub))
+
+
+def _lm_head_ce_torch(xf, emb, tgt, softcap):
+    z = xf.float() @ emb.float().T
+    if softcap > 0:
+        z = softcap * torch.tanh(z / softcap)
+    return torch.logsumexp(z, -1) - z.gather(1, tgt.long()[:, None])[:, 0]
+
+
+@pytest.mark.parametrize("T,d,V,softcap", [(512, 1536, 8192, 0.0), (300, 256, 1024, 15.0),
+                                           (1024, 512, 4000, 0.0)])
+def test_lm_head_ce_matches_torch(bridge_lib, T, d, V, softcap):
+    g = torch.Generator(device="cuda").manual_seed(T + V)
+    xf = torch.randn(T, d, device="cuda", generator=g).half()
+    emb = (torch.randn(V, d, device="cuda", generator=g) * 0.02).half()
+    tgt = torch.randint(0, V, (T,), device="cuda", generator=g).to(torch.int32)
+    ptl = torch.empty(T, device="cuda", dtype=torch.float32)
+    loss = torch.empty(1, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, d, V, softcap,
+                                        _ptr(ptl), _ptr(loss), _stream()) == 0
+    ref = _lm_head_ce_torch(xf, emb, tgt, softcap)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(ptl, ref, rtol=1e-4, atol=1e-4)
+    assert abs(loss.item() - ref.mean().item()) < 1e-4
+    # nullable outputs
+    assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, d, V, softcap,
+                                        None, _ptr(loss), _stream()) == 0
+    torch.cuda.synchronize()
+    assert abs(loss.item() - ref.mean().item()) < 1e-4
+
+
+def test_lm_head_ce_bad_target_is_nan(bridge_lib):
+    T, d, V = 128, 256, 1024
+    xf = torch.randn(T, d, device="cuda").half()
+    emb = torch.randn(V, d, device="cuda").half()
+    tgt = torch.zeros(T, device="cuda", dtype=torch.int32)
+    tgt[5] = V
+    ptl = torch.empty(T, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, d, V, 0.0, _ptr(ptl),
+                                        None, _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.isnan(ptl[5]) and torch.isfinite(ptl[:5]).all()
+    assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, 100, V, 0.0, _ptr(ptl),
+                                        None, _stream()) == B.CB_ERR_INVALID_ARG
