@@ -189,6 +189,24 @@ cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* t
                             int32_t T, int32_t dim, int32_t vocab, float softcap,
                             float* per_token_loss, float* loss, void* stream);
 
+/* cb_lm_head_ce_f16 for callers that cannot allocate device memory during the call:
+ * engines that reserve all device memory for their own pool up front and forbid
+ * cudaMalloc afterwards, and latency-critical loops where cudaMalloc/cudaFree would
+ * synchronise the device. Same arguments, same results; it calls no allocator.
+ * Scratch is one fixed array of about 8.1 MiB compiled into this library (a static
+ * __device__ array): every GPU that loads the library holds it until the process exits.
+ * Limits: T <= 8192 and vocab <= 16384; larger sizes return CB_ERR_INVALID_ARG (split
+ * the tokens into chunks of at most 8192).
+ * The first call on a device looks up the array's device address with that device
+ * current; make that first call before any stream capture on the device.
+ * All calls share the one array and it keeps the last call's contents: calls that
+ * overlap on the GPU (other streams or threads on the same device) race, so the
+ * caller must serialise them.
+ * No counterpart in the reference (its head and loss run on the CPU). */
+cb_status cb_lm_head_ce_f16_noalloc(const void* xf, const void* embed, const uint32_t* targets,
+                                    int32_t T, int32_t dim, int32_t vocab, float softcap,
+                                    float* per_token_loss, float* loss, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,7 @@ EXPORTED = [
     "cb_check_device_error", "cb_sampled_logits", "cb_set_profiling", "cb_kernel_times",
     "cb_reset_kernel_times", "cb_get_stream", "cb_last_error", "cb_create_error",
     "cb_gemm_f16", "cb_attention_f16", "cb_lm_head_ce_f16",
+    "cb_lm_head_ce_f16_noalloc",
 ]
 
 
@@ -100,6 +101,7 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp]),
         "cb_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
         "cb_lm_head_ce_f16": (i32, [vp, vp, vp, i32, i32, i32, f32, vp, vp, vp]),
+        "cb_lm_head_ce_f16_noalloc": (i32, [vp, vp, vp, i32, i32, i32, f32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

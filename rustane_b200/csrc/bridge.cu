@@ -1046,3 +1046,70 @@ cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* t
 }
 
 }  // extern "C"
+
+// ============================================================================
+// LM head + cross-entropy without any device allocation.
+//
+// Some callers cannot allocate device memory while they run: engines that carve
+// all device memory into their own pool at start-up and forbid cudaMalloc in the
+// steady state, and latency-critical loops where cudaMalloc/cudaFree would
+// synchronise the whole device and stall other streams. This variant of
+// cb_lm_head_ce_f16 takes its scratch (the per-tile max/sum-exp partials, the
+// target logits, the per-block loss sums) from one fixed array compiled into
+// this library instead of from an allocator.
+//
+// The array is a file-scope static __device__ array of NOALLOC_SCRATCH_BYTES:
+// every GPU that loads this library holds it until the process exits. Host code
+// may not pass the array's name to a kernel (on the host it is only a stand-in
+// symbol), so the first call on each device looks up its device address with
+// cudaGetSymbolAddress, with that device current, and caches it.
+namespace {
+
+constexpr int NOALLOC_MAX_TOKENS = 8192;
+constexpr int NOALLOC_MAX_VOCAB = 16384;
+// Partials for 8192 tokens x 128 tiles (vocab 16384 with 128-wide tiles) plus
+// target logits, per-token losses, block sums and the mean: 8.07 MiB, rounded up.
+constexpr size_t NOALLOC_SCRATCH_BYTES = 8u * 1024u * 1024u + 128u * 1024u;
+
+static __device__ __align__(256) unsigned char g_lm_ce_scratch[NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of g_lm_ce_scratch on the current device (looked up once per device).
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_lm_ce_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" cb_status cb_lm_head_ce_f16_noalloc(const void* xf, const void* embed,
+                                               const uint32_t* targets, int32_t T, int32_t dim,
+                                               int32_t vocab, float softcap,
+                                               float* per_token_loss, float* loss,
+                                               void* stream) {
+  if (!lm_ce_args_ok(xf, embed, targets, T, dim, vocab)) return CB_ERR_INVALID_ARG;
+  if (T > NOALLOC_MAX_TOKENS || vocab > NOALLOC_MAX_VOCAB ||
+      lm_ce_scratch_bytes(T, vocab) > NOALLOC_SCRATCH_BYTES)
+    return CB_ERR_INVALID_ARG;
+  void* base = nullptr;
+  if (noalloc_scratch(&base) != cudaSuccess) return CB_ERR_CUDA;
+  // Every scratch word the kernels read is written earlier in the same call (the
+  // target logits are reset to NaN first), so leftovers of a previous call are harmless.
+  const LmCeScratch s = lm_ce_carve(base, T, vocab);
+  cudaError_t e = lm_ce_enqueue(xf, embed, targets, T, dim, vocab, softcap, per_token_loss, loss,
+                                s, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
