@@ -167,8 +167,10 @@ const char* cb_create_error(void);
  * micro-benchmarks; they sit below the model API). -------------------------- */
 
 /* C[M,N] = A[M,K] * B[N,K]^T with fp16 A/B (K contiguous) on the tcgen05 GEMM.
- * out_f32 = 0: C is fp16; 1: C is f32. K % 64 == 0, N % 32 == 0, 16-byte
- * aligned pointers. Enqueued on `stream` (NULL = default stream). */
+ * out_f32 = 0: C is fp16; 1: C is f32. block_n selects the tile: 0 = automatic,
+ * 128 or 256 = one CTA per 128 x block_n tile, 2 = a CTA pair per 256 x 256 tile
+ * (needs N % 256 == 0, else 128 is used). K % 64 == 0, N % 32 == 0, 16-byte aligned
+ * pointers. Enqueued on `stream` (NULL = default stream). */
 cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N, int32_t K,
                       int32_t out_f32, int32_t block_n, void* stream);
 

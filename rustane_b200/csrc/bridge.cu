@@ -77,6 +77,9 @@ bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t k, uint64_t rows, uin
 }
 
 // ------------------------------------------------------------ GEMM launch
+// Tile modes of the tcgen05 GEMM.
+enum GemmMode { GM_SINGLE128 = 0, GM_SINGLE256 = 1, GM_PAIR = 2 };
+
 template <int BN, class Epi>
 void set_gemm_attr() {
   cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -87,6 +90,8 @@ template <class Epi>
 void set_gemm_attrs_for() {
   set_gemm_attr<128, Epi>();
   set_gemm_attr<256, Epi>();
+  cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       GemmCfg<256, true>::SMEM_BYTES);
 }
 
 void set_all_kernel_attrs() {
@@ -100,50 +105,110 @@ void set_all_kernel_attrs() {
                        ATT_SMEM);
 }
 
-// Attributes are per device; remember which devices are done.
-void ensure_attrs(int device) {
+struct DeviceInfo {
+  int sms = 148;
+  int pair_clusters = 74;  // CTA pairs of the GEMM that fit on the device at once
+};
+
+// Per-device kernel attributes and occupancy, set up once per device.
+const DeviceInfo& device_info(int device) {
   static std::mutex mu;
+  static DeviceInfo info[64];
   static uint64_t done = 0;
   std::lock_guard<std::mutex> lk(mu);
-  if (device >= 0 && device < 64 && (done & (1ull << device))) return;
-  set_all_kernel_attrs();
-  if (device >= 0 && device < 64) done |= (1ull << device);
+  if (device < 0 || device >= 64) return info[0];
+  if (!(done & (1ull << device))) {
+    set_all_kernel_attrs();
+    DeviceInfo d;
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
+    d.pair_clusters = d.sms / 2;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(d.sms & ~1, 1, 1);
+    lc.blockDim = dim3(GEMM_THREADS, 1, 1);
+    lc.dynamicSmemBytes = GemmCfg<256, true>::SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    lc.attrs = &attr;
+    lc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tn_pair_kernel<EpiStoreF16>, &lc) ==
+            cudaSuccess &&
+        n > 0)
+      d.pair_clusters = n;
+    cudaGetLastError();
+    info[device] = d;
+    done |= (1ull << device);
+  }
+  return info[device];
 }
 
-int num_sms_of(int device) {
-  int n = 148;
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
-  return n;
-}
+void ensure_attrs(int device) { (void)device_info(device); }
+
+int num_sms_of(int device) { return device_info(device).sms; }
 
 template <int BN, class Epi>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                           int bz, const Epi& epi, int* err, int num_sms, cudaStream_t st) {
+                           int bz, const Epi& epi, int* err, int units, cudaStream_t st) {
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
+  const int grid = tiles < units ? tiles : units;
   gemm_tn_kernel<BN, Epi><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K,
                                                                                bz, epi, err);
   return cudaGetLastError();
 }
 
-// Tile width choice: the one whose last wave is fullest; ties go to 256 (less
-// operand traffic per FLOP).
-int pick_bn(int M, int N, int num_sms) {
-  auto eff = [&](int bn) {
-    long tiles = (long)((M + 127) / 128) * ((N + bn - 1) / bn);
-    long waves = (tiles + num_sms - 1) / num_sms;
-    return (double)tiles / (double)(waves * num_sms);
-  };
-  if (N % 256 != 0) return 128;
-  return eff(128) > eff(256) * 1.15 ? 128 : 256;
+template <class Epi>
+cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
+                             int K, int bz, const Epi& epi, int* err, int clusters,
+                             cudaStream_t st) {
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int pairs = tiles < clusters ? tiles : clusters;
+  gemm_tn_pair_kernel<Epi><<<2 * pairs, GEMM_THREADS, GemmCfg<256, true>::SMEM_BYTES, st>>>(
+      ta, tb_half, M, N, K, bz, epi, err);
+  return cudaGetLastError();
 }
 
+// Tile mode for an M x N GEMM: the best of (last-wave fill) x (per-tile operand
+// efficiency). A CTA pair moves the fewest operand bytes per FLOP; 128-wide tiles
+// fill small problems better. CB_GEMM_MODE=pair|256|128 forces one mode.
+int pick_mode(int M, int N, const DeviceInfo& di) {
+  static const int forced = [] {
+    const char* e = getenv("CB_GEMM_MODE");
+    if (!e) return -1;
+    if (!strcmp(e, "pair")) return (int)GM_PAIR;
+    if (!strcmp(e, "256")) return (int)GM_SINGLE256;
+    if (!strcmp(e, "128")) return (int)GM_SINGLE128;
+    return -1;
+  }();
+  auto fill = [](long tiles, long units) {
+    long waves = (tiles + units - 1) / units;
+    return (double)tiles / (double)(waves * units);
+  };
+  const bool n256 = (N % 256) == 0;
+  if (forced == GM_SINGLE128 || (!n256 && forced != -1)) return GM_SINGLE128;
+  if (forced >= 0) return forced;
+  const double s_pair = n256 ? fill((long)((M + 255) / 256) * (N / 256), di.pair_clusters) : 0.0;
+  const double s_256 = n256 ? 0.85 * fill((long)((M + 127) / 128) * (N / 256), di.sms) : 0.0;
+  const double s_128 = 0.78 * fill((long)((M + 127) / 128) * ((N + 127) / 128), di.sms);
+  if (s_pair >= s_256 && s_pair >= s_128) return GM_PAIR;
+  return s_256 >= s_128 ? GM_SINGLE256 : GM_SINGLE128;
+}
+
+int mode_block_n(int mode) { return mode == GM_SINGLE128 ? 128 : 256; }
+
+// tb128: B tensor map with 128-row boxes (single 128-wide tiles and CTA pairs);
+// tb256: 256-row boxes (single 256-wide tiles).
 template <class Epi>
-cudaError_t launch_gemm(int bn, const CUtensorMap& ta, const CUtensorMap& tb128,
+cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
-                        int* err, int num_sms, cudaStream_t st) {
-  if (bn == 128) return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, num_sms, st);
-  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, num_sms, st);
+                        int* err, const DeviceInfo& di, cudaStream_t st) {
+  if (mode == GM_PAIR)
+    return launch_gemm_pair(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters, st);
+  if (mode == GM_SINGLE128)
+    return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, di.sms, st);
+  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, di.sms, st);
 }
 
 // ------------------------------------------------------------ kernel classes
@@ -325,10 +390,11 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(K_EMBED_NORM, 0, Td * 4 + Td * d * (2 + 4 + 2));
 
-  const int bn_qkv = pick_bn(T, c->n_qkv, c->num_sms);
-  const int bn_o = pick_bn(T, d, c->num_sms);
-  const int bn_13 = pick_bn(T, 2 * hid, c->num_sms);
-  const int bn_2 = pick_bn(T, d, c->num_sms);
+  const DeviceInfo& di = device_info(c->device);
+  const int m_qkv = pick_mode(T, c->n_qkv, di);
+  const int m_o = pick_mode(T, d, di);
+  const int m_13 = pick_mode(T, 2 * hid, di);
+  const int m_2 = pick_mode(T, d, di);
   const double attn_flops = 2.0 * 2.0 * (double)batch * cfg.heads * 128.0 * S * (S + 1) / 2.0;
 
   for (int l = 0; l < L; ++l) {
@@ -340,8 +406,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     }
     {
       EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, cfg.heads, cfg.kv_heads};
-      e = launch_gemm(bn_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
-                      c->dev_err, c->num_sms, st);
+      e = launch_gemm(m_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
+                      c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
@@ -356,8 +422,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     }
     {
       EpiResidual ep{c->x, d, alpha};
-      e = launch_gemm(bn_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], T, d, c->q_dim, l, ep,
-                      c->dev_err, c->num_sms, st);
+      e = launch_gemm(m_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], T, d, c->q_dim, l, ep,
+                      c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_O, 2.0 * Td * d * c->q_dim,
            Td * c->q_dim * 2 + (double)d * c->q_dim * 2 + Td * d * 8);
@@ -368,15 +434,15 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     mark(K_RMSNORM, 0, Td * d * 6);
     {
       EpiSwiglu ep{c->g, hid};
-      e = launch_gemm(bn_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
-                      c->dev_err, c->num_sms, st);
+      e = launch_gemm(m_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
+                      c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
     {
       EpiResidual ep{c->x, d, alpha};
-      e = launch_gemm(bn_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err,
-                      c->num_sms, st);
+      e = launch_gemm(m_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err, di,
+                      st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W2, 2.0 * Td * d * hid, Td * hid * 2 + (double)d * hid * 2 + Td * d * 8);
     }
@@ -386,8 +452,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(K_RMSNORM, 0, Td * d * 6);
 
-  const int bn_head = pick_bn(T, V, c->num_sms);
-  const int nparts = (V + bn_head - 1) / bn_head;
+  const int m_head = pick_mode(T, V, di);
+  const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
   {
     EpiCrossEntropy ep{};
     ep.part = c->ce_part;
@@ -395,8 +461,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     ep.targets = c->targets;
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
-    e = launch_gemm(bn_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
-                    c->dev_err, c->num_sms, st);
+    e = launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
+                    c->dev_err, di, st);
     if (e != cudaSuccess) return e;
     mark(K_GEMM_HEAD, 2.0 * Td * V * d, Td * d * 2 + (double)V * d * 2 + Td * nparts * 8 + Td * 8);
   }
@@ -462,12 +528,15 @@ cudaError_t lm_ce_enqueue(const void* xf, const void* embed, const uint32_t* tar
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  ensure_attrs(dev);
-  const int sms = num_sms_of(dev);
-  const int bn = lm_ce_block_n(V);
+  const DeviceInfo& di = device_info(dev);
+  // 256-wide tiles (CTA pair or single CTA) when the vocab allows, else 128-wide:
+  // the partial count always equals lm_ce_nparts(V).
+  const int mode = (V % 256 == 0) ? (pick_mode(T, V, di) == GM_PAIR ? GM_PAIR : GM_SINGLE256)
+                                  : GM_SINGLE128;
   const int nparts = lm_ce_nparts(V);
-  CUtensorMap ta, tb;
-  if (!make_tmap(&ta, xf, d, T, 1, 128) || !make_tmap(&tb, embed, d, V, 1, bn))
+  CUtensorMap ta, tb128, tb256;
+  if (!make_tmap(&ta, xf, d, T, 1, 128) || !make_tmap(&tb128, embed, d, V, 1, 128) ||
+      !make_tmap(&tb256, embed, d, V, 1, 256))
     return cudaErrorInvalidValue;
   e = cudaMemsetAsync(s.tgt, 0xFF, (size_t)T * 4, st);
   if (e != cudaSuccess) return e;
@@ -477,7 +546,7 @@ cudaError_t lm_ce_enqueue(const void* xf, const void* embed, const uint32_t* tar
   ep.targets = targets;
   ep.tgt_logit = s.tgt;
   ep.softcap = softcap;
-  e = launch_gemm(bn, ta, tb, tb, T, V, d, 0, ep, nullptr, sms, st);
+  e = launch_gemm(mode, ta, tb128, tb256, T, V, d, 0, ep, nullptr, di, st);
   if (e != cudaSuccess) return e;
   const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
   float* tok = per_token_loss ? per_token_loss : s.tok;
@@ -931,9 +1000,9 @@ cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, fl
   if (e == cudaSuccess && !make_tmap(&ta, ctx->samp_a, d, n_pad, 1, 128)) e = cudaErrorInvalidValue;
   if (e == cudaSuccess) {
     EpiStoreF32 ep{ctx->samp_out, V, ctx->last_softcap};
-    const int bn = (V % 256 == 0) ? 256 : 128;
-    e = launch_gemm(bn, ta, ctx->tm_embed[0], ctx->tm_embed[1], n_pad, V, d, 0, ep, ctx->dev_err,
-                    ctx->num_sms, st);
+    const DeviceInfo& di = device_info(ctx->device);
+    e = launch_gemm(pick_mode(n_pad, V, di), ta, ctx->tm_embed[0], ctx->tm_embed[1], n_pad, V, d,
+                    0, ep, ctx->dev_err, di, st);
   }
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(logits_out, ctx->samp_out, (size_t)n_rows * V * sizeof(float),
@@ -995,22 +1064,25 @@ cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t 
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return CB_ERR_INVALID_ARG;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
-  ensure_attrs(dev);
-  const int sms = num_sms_of(dev);
-  int bn = block_n;
-  if (bn != 128 && bn != 256) bn = pick_bn(M, N, sms);
-  if (bn == 256 && N % 256 != 0) bn = 128;
-  CUtensorMap ta, tb;
-  if (!make_tmap(&ta, A, K, M, 1, 128) || !make_tmap(&tb, B, K, N, 1, bn))
+  const DeviceInfo& di = device_info(dev);
+  int mode;
+  if (block_n == 128) mode = GM_SINGLE128;
+  else if (block_n == 256) mode = GM_SINGLE256;
+  else if (block_n == 2) mode = GM_PAIR;
+  else mode = pick_mode(M, N, di);
+  if (mode != GM_SINGLE128 && N % 256 != 0) mode = GM_SINGLE128;
+  CUtensorMap ta, tb128, tb256;
+  if (!make_tmap(&ta, A, K, M, 1, 128) || !make_tmap(&tb128, B, K, N, 1, 128) ||
+      !make_tmap(&tb256, B, K, N, 1, 256))
     return CB_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (out_f32) {
     EpiStoreF32 ep{static_cast<float*>(C), N, 0.f};
-    e = launch_gemm(bn, ta, tb, tb, M, N, K, 0, ep, nullptr, sms, st);
+    e = launch_gemm(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di, st);
   } else {
     EpiStoreF16 ep{static_cast<__half*>(C), N};
-    e = launch_gemm(bn, ta, tb, tb, M, N, K, 0, ep, nullptr, sms, st);
+    e = launch_gemm(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di, st);
   }
   return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }

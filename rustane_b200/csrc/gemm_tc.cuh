@@ -2,16 +2,14 @@
 // fp32 accumulation in TMEM), with the forward pass's fusions applied in the
 // epilogue while the accumulator is still in registers.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0, lane 0 : TMA producer. 128x64 A tile + BNx64 B tile per stage,
+// Roles (320 threads, one CTA per SM; the kernel body at the end of this file):
+//   warp 0, lane 0 : TMA producer. 128x64 A tile + (BN or BN/2)x64 B tile per stage,
 //                    128-byte swizzle, mbarrier expect-tx completion.
 //   warp 1         : allocates TMEM (2 x BN columns: double-buffered
-//                    accumulator); lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
+//                    accumulator); lane 0 issues tcgen05.mma (K=16 steps)
 //                    and tcgen05.commit to release smem stages / hand over
 //                    finished accumulators.
-//   warps 2..5     : epilogue. Warp w reads TMEM lanes 32*(w%4)..+31, i.e. each
-//                    thread owns one output row of the tile and walks its BN
-//                    columns in chunks of 32 (tcgen05.ld 32x32b.x32).
+//   warps 2..9     : epilogue, two groups of four that take alternate tiles.
 // Tiles are visited n-fastest so CTAs running at the same time share A rows
 // and the weight matrix (B) stays resident in L2.
 //
@@ -38,15 +36,20 @@ namespace cb {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
-template <int BN>
+// PAIR: a two-CTA cluster computes a 256 x BN tile (each CTA 128 rows, half of B).
+template <int BN, bool PAIR = false>
 struct GemmCfg {
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
+  static constexpr int TILE_M = PAIR ? 2 * GEMM_BM : GEMM_BM;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B each CTA loads
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int B_BYTES = B_ROWS * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (STAGE_BYTES <= 32768) ? 6 : 4;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
@@ -54,11 +57,18 @@ struct GemmCfg {
 
 // ------------------------------------------------------------------ epilogues
 
+// Epilogue interface: begin_row(row, valid); prefetch(row, col0, Pre&) issues the
+// global loads a chunk needs (one chunk ahead of its use); chunk(row, col0, v, Pre)
+// consumes 32 accumulator columns of one row; end_row(row, n_blk).
+struct NoPre {};
+
 struct EpiStoreF16 {
+  using Pre = NoPre;
   __half* out;
   int ldo;
   __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
     uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -74,11 +84,13 @@ struct EpiStoreF16 {
 };
 
 struct EpiStoreF32 {
+  using Pre = NoPre;
   float* out;
   int ldo;
   float softcap;  // > 0: out = softcap * tanh(acc / softcap)
   __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
     float4* dst = reinterpret_cast<float4*>(out + (size_t)row * ldo + col0);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -99,6 +111,9 @@ struct EpiStoreF32 {
 // Columns [0, q_dim) -> Q, [q_dim, q_dim+kv_dim) -> K, rest -> V. Head dim 128.
 // Output layout [batch, heads, seq, 128] (row = b*seq + s).
 struct EpiQkvRope {
+  struct Pre {
+    float4 cs[8];  // (cos, sin) of the chunk's 16 frequency pairs
+  };
   __half* q;
   __half* k;
   __half* v;
@@ -107,7 +122,14 @@ struct EpiQkvRope {
   int heads;
   int kv_heads;
   __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32]) {
+  __device__ __forceinline__ void prefetch(int row, int col0, Pre& p) {
+    if (col0 >= (heads + kv_heads) * 128) return;  // V columns are not rotated
+    const int s = row % seq;
+    const float4* rs = reinterpret_cast<const float4*>(rope + (size_t)s * 64 + ((col0 & 127) >> 1));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p.cs[i] = __ldg(rs + i);
+  }
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32], const Pre& p) {
     const int q_dim = heads * 128;
     const int kv_dim = kv_heads * 128;
     int b = row / seq;
@@ -133,19 +155,22 @@ struct EpiQkvRope {
     int d0 = c & 127;
     float o[32];
     if (rot) {
-      const float2* rs = rope + (size_t)s * 64 + (d0 >> 1);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float2 cs = rs[i];
-        float a = acc[2 * i], bb = acc[2 * i + 1];
-        o[2 * i] = a * cs.x - bb * cs.y;
-        o[2 * i + 1] = bb * cs.x + a * cs.y;
+      for (int i = 0; i < 8; ++i) {
+        const float4 cs = p.cs[i];  // pairs 2i and 2i+1: (cos, sin, cos, sin)
+        float a = acc[4 * i], bb = acc[4 * i + 1];
+        o[4 * i] = a * cs.x - bb * cs.y;
+        o[4 * i + 1] = bb * cs.x + a * cs.y;
+        a = acc[4 * i + 2];
+        bb = acc[4 * i + 3];
+        o[4 * i + 2] = a * cs.z - bb * cs.w;
+        o[4 * i + 3] = bb * cs.z + a * cs.w;
       }
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = acc[i];
     }
-    uint4* p = reinterpret_cast<uint4*>(dst + (((size_t)b * nh + h) * seq + s) * 128 + d0);
+    uint4* ptr = reinterpret_cast<uint4*>(dst + (((size_t)b * nh + h) * seq + s) * 128 + d0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint4 w;
@@ -153,28 +178,37 @@ struct EpiQkvRope {
       w.y = pack_half2(o[8 * j + 2], o[8 * j + 3]);
       w.z = pack_half2(o[8 * j + 4], o[8 * j + 5]);
       w.w = pack_half2(o[8 * j + 6], o[8 * j + 7]);
-      p[j] = w;
+      ptr[j] = w;
     }
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
 
-// x[row, col] += alpha * acc   (fp32 residual stream, updated in place)
+// x[row, col] += alpha * acc   (fp32 residual stream, updated in place; the chunk's
+// 32 residual values are loaded one chunk ahead)
 struct EpiResidual {
+  struct Pre {
+    float4 r[8];
+  };
   float* x;
   int ldx;
   float alpha;
   __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
-    float4* p = reinterpret_cast<float4*>(x + (size_t)row * ldx + col0);
+  __device__ __forceinline__ void prefetch(int row, int col0, Pre& p) {
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * ldx + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p.r[j] = src[j];
+  }
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre& p) {
+    float4* dst = reinterpret_cast<float4*>(x + (size_t)row * ldx + col0);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float4 r = p[j];
+      float4 r = p.r[j];
       r.x += alpha * v[4 * j + 0];
       r.y += alpha * v[4 * j + 1];
       r.z += alpha * v[4 * j + 2];
       r.w += alpha * v[4 * j + 3];
-      p[j] = r;
+      dst[j] = r;
     }
   }
   __device__ __forceinline__ void end_row(int, int) {}
@@ -183,10 +217,12 @@ struct EpiResidual {
 // B rows interleave W1 and W3 columns: row 2j = W1[:, j], row 2j+1 = W3[:, j].
 // g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
 struct EpiSwiglu {
+  using Pre = NoPre;
   __half* g;
   int ldg;
   __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
     float o[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -211,6 +247,7 @@ struct EpiSwiglu {
 // (max_z, sum exp(z - max_z)) over the tile's logits z (softcapped if
 // softcap > 0) and, for the tile holding targets[row], that logit.
 struct EpiCrossEntropy {
+  using Pre = NoPre;
   float2* part;      // [M, nparts]
   int nparts;
   const uint32_t* targets;
@@ -224,7 +261,8 @@ struct EpiCrossEntropy {
     s = 0.f;
     tgt = valid ? (int)targets[row] : -1;
   }
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32]) {
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
     float z[32];
     float cm = -CUDART_INF_F;
 #pragma unroll
@@ -257,13 +295,28 @@ struct EpiCrossEntropy {
 };
 
 // ------------------------------------------------------------------ kernel
+//
+// One body, two modes:
+//   PAIR = false : one CTA computes a 128 x BN tile (tcgen05.mma.cta_group::1, M = 128).
+//   PAIR = true  : a cluster of two CTAs computes a 256 x 256 tile with
+//                  tcgen05.mma.cta_group::2 (M = 256) issued by the even CTA. Each CTA
+//                  loads its own 128 rows of A and its own 128 rows of B (no multicast);
+//                  both loads count on the even CTA's `full` barrier; the even CTA's
+//                  commits release both CTAs' stages and accumulators (multicast commit).
+//                  Per SM this moves 32 KB of operands per 4.2 MFLOP instead of 48 KB.
+// Epilogue: warps 2..9 form two groups of four; group g drains accumulator buffer g,
+// so consecutive tiles' epilogues overlap. In each group warp w reads TMEM lanes
+// 32*(w%4)..+31: one thread per output row, BN columns in chunks of 32, the next
+// chunk's TMEM load in flight while the current one is processed.
 
-template <int BN, class Epi>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, int b_z, Epi epi, int* err) {
-  using Cfg = GemmCfg<BN>;
+template <int BN, bool PAIR, class Epi>
+__device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
+                                             int M, int N, int K, int b_z, const Epi& epi,
+                                             int* err) {
+  using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int TILE_M = Cfg::TILE_M;
+  constexpr int NC = BN / 32;  // TMEM chunks per row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -278,7 +331,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int m_tiles = (M + TILE_M - 1) / TILE_M;
   const int n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
@@ -290,54 +346,71 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], (PAIR ? 2 : 1) * 4);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(tmA);
+    tma_prefetch_desc(tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
+      // ---------------- TMA producer (both CTAs of a pair)
       const uint64_t pol_a = policy_evict_first();
       const uint64_t pol_b = policy_evict_last();
-      uint32_t it = 0;  // loads issued
+      uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * GEMM_BM;
-        const int n0 = (tile % n_tiles) * BN;
+      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
+        const int m0 = (tile / n_tiles) * TILE_M + (int)rank * GEMM_BM;
+        const int n0 = (tile % n_tiles) * BN + (int)rank * Cfg::B_ROWS;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-          tma_load_3d(sA + s * Cfg::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m0, 0, pol_a);
-          tma_load_3d(sB + s * Cfg::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n0, b_z, pol_b);
+          if (PAIR) {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+            tma_load_3d_pair(sA + s * Cfg::A_BYTES, tmA, bar, kb * GEMM_BK, m0, 0, pol_a);
+            tma_load_3d_pair(sB + s * Cfg::B_BYTES, tmB, bar, kb * GEMM_BK, n0, b_z, pol_b);
+          } else {
+            mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+            tma_load_3d(sA + s * Cfg::A_BYTES, tmA, &full[s], kb * GEMM_BK, m0, 0, pol_a);
+            tma_load_3d(sB + s * Cfg::B_BYTES, tmB, &full[s], kb * GEMM_BK, n0, b_z, pol_b);
+          }
         }
       }
-      // Drain: wait (bounded) for the copies this thread may still have in flight.
-      uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, err);
+      // Drain: wait (bounded) for copies still in flight. The even CTA's full
+      // barriers count both CTAs' bytes, so it drains for the pair.
+      if (rank == 0) {
+        uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
+        for (uint32_t j = first; j < it; ++j)
+          mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, err);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      constexpr uint32_t idesc = umma_idesc_f16(GEMM_BM, BN);
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (the even CTA of a pair)
+      constexpr uint32_t idesc = umma_idesc_f16(TILE_M, BN);
       uint32_t it = 0;
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -350,63 +423,110 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            umma_f16_ss(d_tmem, sw128_kmajor_desc(a_addr + k * 32),
-                        sw128_kmajor_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+            const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
+            const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
+            const uint32_t accum = (kb | k) != 0;
+            if (PAIR) umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
+            else umma_f16_ss(d_tmem, ad, bd, idesc, accum);
           }
-          umma_commit(&empty[s]);
+          if (PAIR) umma_commit_pair_mc(&empty[s], 0x3);
+          else umma_commit(&empty[s]);
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if (PAIR) umma_commit_pair_mc(&tfull[acc], 0x3);
+        else umma_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1u;
       }
-      // Drain: all MMAs issued by this thread complete before TMEM is released.
-      umma_commit(drain);
+      // Drain: every MMA issued here completes before TMEM (and the peer's smem) is released.
+      if (PAIR) umma_commit_pair_mc(drain, 0x1);
+      else umma_commit(drain);
       mbar_wait(drain, 0, err);
     }
   } else {
-    // ---------------- epilogue warps 2..5
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    int acc = 0;
-    uint32_t acc_ph = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    // ---------------- epilogue: warps 2..5 drain accumulator 0, warps 6..9 accumulator 1
+    const int group = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const uint32_t tempty_addr =
+        PAIR ? mapa_shared(smem_u32(&tempty[group]), 0) : smem_u32(&tempty[group]);
+    uint32_t ph = 0;
+    int it = 0;
+    for (int tile = unit; tile < num_tiles; tile += n_units, ++it) {
+      if ((it & 1) != group) continue;
       const int m_blk = tile / n_tiles;
       const int n_blk = tile % n_tiles;
-      if (!mbar_wait(&tfull[acc], acc_ph, err)) break;
+      if (!mbar_wait(&tfull[group], ph, err)) break;
+      ph ^= 1u;
       tc_fence_after();
-      const int row = m_blk * GEMM_BM + quad * 32 + lane;
+      const int row = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32 + lane;
       const bool row_ok = row < M;
       Epi e = epi;
       e.begin_row(row, row_ok);
-      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(group * BN);
+      uint32_t ra[32], rb[32];
+      typename Epi::Pre pa, pb;
+      const int col_base = n_blk * BN;
+      if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
+      tmem_ld_32x32b_x32(t_row, ra);
+      tmem_ld_wait_regs(ra);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = n_blk * BN + c * 32;
-        if (row_ok && col0 < N) {
+      for (int c = 0; c < NC; c += 2) {
+        const int col_a = col_base + c * 32, col_b = col_a + 32;
+        tmem_ld_32x32b_x32(t_row + (c + 1) * 32, rb);
+        if (row_ok && col_b < N) e.prefetch(row, col_b, pb);
+        if (row_ok && col_a < N) {
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          e.chunk(row, col0, v);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
+          e.chunk(row, col_a, v, pa);
         }
+        tmem_ld_wait_regs(rb);
+        if (c + 2 < NC) {
+          tmem_ld_32x32b_x32(t_row + (c + 2) * 32, ra);
+          if (row_ok && col_b + 32 < N) e.prefetch(row, col_b + 32, pa);
+        }
+        if (row_ok && col_b < N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rb[i]);
+          e.chunk(row, col_b, v, pb);
+        }
+        if (c + 2 < NC) tmem_ld_wait_regs(ra);
       }
       if (row_ok) e.end_row(row, n_blk);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_ph ^= 1u;
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(tempty_addr);
+        else mbar_arrive(&tempty[group]);
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  __syncwarp();
+  if (PAIR) cluster_sync();  // the peer's smem and barriers stay alive until both are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+}
+
+template <int BN, class Epi>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, int b_z, Epi epi, int* err) {
+  gemm_tn_body<BN, false, Epi>(&tmA, &tmB, M, N, K, b_z, epi, err);
+}
+
+template <class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int b_z,
+                        Epi epi, int* err) {
+  gemm_tn_body<256, true, Epi>(&tmA, &tmB, M, N, K, b_z, epi, err);
 }
 
 }  // namespace cb

@@ -27,6 +27,11 @@ def _stream():
     (1024, 4608, 1536, 0),      # QKV shape, automatic tile choice
     (512, 1536, 4096, 0),       # down-projection shape
     (4096, 8192, 1536, 256),
+    (256, 256, 64, 2),          # one CTA-pair tile
+    (200, 512, 192, 2),         # ragged M: the odd CTA of the pair is out of bounds
+    (1000, 1536, 1536, 2),
+    (4096, 8192, 1536, 2),
+    (32768, 4608, 1536, 0),     # full 600m-A QKV shape, automatic choice
 ])
 def test_gemm_matches_torch(bridge_lib, M, N, K, bn):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
