@@ -30,6 +30,7 @@
 
 #include "cuda_bridge.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemm_tc.cuh"
 #include "ptx.cuh"
 #include "rowwise.cuh"
@@ -76,6 +77,21 @@ bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t k, uint64_t rows, uin
   return r == CUDA_SUCCESS;
 }
 
+// fp16 matrix [rows][128] (row stride 256 B) tiled as 64 x box_rows boxes, 128B swizzle
+// (Q/K/V of the tcgen05 attention).
+bool make_tmap_qkv(CUtensorMap* map, const void* ptr, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {128, rows};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------ GEMM launch
 // Tile modes of the tcgen05 GEMM.
 enum GemmMode { GM_SINGLE128 = 0, GM_SINGLE256 = 1, GM_PAIR = 2 };
@@ -99,10 +115,12 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiStoreF32>();
   set_gemm_attrs_for<EpiQkvRope>();
   set_gemm_attrs_for<EpiResidual>();
+  set_gemm_attrs_for<EpiScaledF16>();
   set_gemm_attrs_for<EpiSwiglu>();
   set_gemm_attrs_for<EpiCrossEntropy>();
   cudaFuncSetAttribute(attn_fwd_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        ATT_SMEM);
+  cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
 }
 
 struct DeviceInfo {
@@ -211,6 +229,37 @@ cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb12
   return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, di.sms, st);
 }
 
+// Causal attention: tcgen05 kernel when seq is a multiple of 128 (tensor maps given),
+// otherwise the mma.sync kernel.
+cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
+                             const __half* q, const __half* k, const __half* v, __half* out,
+                             int batch, int heads, int kv_heads, int seq, int* err,
+                             cudaStream_t st) {
+  const float scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
+  if (tq && seq % FA_BQ == 0) {
+    dim3 grid(seq / FA_BQ, heads, batch);
+    attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, out, seq, heads,
+                                                          kv_heads, scale_log2, err);
+  } else {
+    dim3 grid(seq / ATT_BQ, heads, batch);
+    attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(q, k, v, out, seq, heads,
+                                                                kv_heads, scale_log2);
+  }
+  return cudaGetLastError();
+}
+
+// x += delta; xn = rmsnorm(x) * gamma (rows kept in registers up to 2048 wide).
+cudaError_t launch_add_rmsnorm(float* x, const __half* delta, const float* gamma, __half* xn,
+                               int T, int d, cudaStream_t st) {
+  const int blocks = (T + ROW_WARPS - 1) / ROW_WARPS, threads = ROW_WARPS * 32;
+  if (d <= 512) add_rmsnorm_kernel<2><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 1024) add_rmsnorm_kernel<4><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 1536) add_rmsnorm_kernel<6><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 2048) add_rmsnorm_kernel<8><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else add_rmsnorm_long_kernel<<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------ kernel classes
 enum KClass {
   K_EMBED_NORM = 0,
@@ -225,9 +274,9 @@ enum KClass {
   K_LOSS_MEAN,
   K_NUM
 };
-const char* kclass_name[K_NUM] = {"embed_rmsnorm",   "rmsnorm",          "gemm_qkv_rope",
-                                  "attention",       "gemm_o_residual",  "gemm_w13_swiglu",
-                                  "gemm_w2_residual", "gemm_lmhead_ce",  "ce_finalize",
+const char* kclass_name[K_NUM] = {"embed_rmsnorm", "add_rmsnorm",   "gemm_qkv_rope",
+                                  "attention",     "gemm_o",        "gemm_w13_swiglu",
+                                  "gemm_w2",       "gemm_lmhead_ce", "ce_finalize",
                                   "loss_mean"};
 
 struct KStat {
@@ -265,6 +314,7 @@ struct cb_ctx {
   __half* v = nullptr;
   __half* attn = nullptr;      // [T, q_dim]
   __half* g = nullptr;         // [T, hidden]
+  __half* delta = nullptr;     // [T, dim] alpha * (O or down projection), added by add_rmsnorm
   float2* ce_part = nullptr;   // [T, vocab/128]
   float* tgt_logit = nullptr;  // [T]
   float* tok_loss = nullptr;   // [T]
@@ -279,6 +329,7 @@ struct cb_ctx {
 
   // tensor maps (A operands sized for max_batch; B per weight kind, both tile widths)
   CUtensorMap tm_xn, tm_attn, tm_g;
+  CUtensorMap tm_q, tm_k, tm_v;  // attention operands ([B*H*S, 128] rows)
   CUtensorMap tm_wqkv[2], tm_wo[2], tm_w13[2], tm_w2[2], tm_embed[2];  // [0]=BN128 [1]=BN256
 
   // graphs
@@ -347,7 +398,7 @@ void free_ctx(cb_ctx* c) {
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   c->graphs.clear();
   for (auto e : c->events) cudaEventDestroy(e);
-  void* ptrs[] = {c->embed, c->wqkv, c->wo,        c->w13,      c->w2,       c->gamma,
+  void* ptrs[] = {c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
@@ -397,12 +448,12 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   const int m_2 = pick_mode(T, d, di);
   const double attn_flops = 2.0 * 2.0 * (double)batch * cfg.heads * 128.0 * S * (S + 1) / 2.0;
 
+  const double norm_bytes = Td * d * (4 + 2 + 4 + 2);
   for (int l = 0; l < L; ++l) {
-    if (l > 0) {
-      rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma + (size_t)l * 2 * d,
-                                                            c->xn, T, d);
-      if ((e = cudaGetLastError()) != cudaSuccess) return e;
-      mark(K_RMSNORM, 0, Td * d * 6);
+    if (l > 0) {  // residual add of the previous layer's down projection + RMSNorm(gamma1)
+      e = launch_add_rmsnorm(c->x, c->delta, c->gamma + (size_t)l * 2 * d, c->xn, T, d, st);
+      if (e != cudaSuccess) return e;
+      mark(K_RMSNORM, 0, norm_bytes);
     }
     {
       EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, cfg.heads, cfg.kv_heads};
@@ -413,25 +464,22 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
     }
     {
-      dim3 grid(S / ATT_BQ, cfg.heads, batch);
-      attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(
-          c->q, c->k, c->v, c->attn, S, cfg.heads, cfg.kv_heads,
-          1.4426950408889634f / sqrtf(128.0f));
-      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      e = launch_attention(&c->tm_q, &c->tm_k, &c->tm_v, c->q, c->k, c->v, c->attn, batch,
+                           cfg.heads, cfg.kv_heads, S, c->dev_err, st);
+      if (e != cudaSuccess) return e;
       mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
     }
     {
-      EpiResidual ep{c->x, d, alpha};
+      EpiScaledF16 ep{c->delta, d, alpha};
       e = launch_gemm(m_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], T, d, c->q_dim, l, ep,
                       c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_O, 2.0 * Td * d * c->q_dim,
-           Td * c->q_dim * 2 + (double)d * c->q_dim * 2 + Td * d * 8);
+           Td * c->q_dim * 2 + (double)d * c->q_dim * 2 + Td * d * 2);
     }
-    rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma + (size_t)l * 2 * d + d,
-                                                          c->xn, T, d);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    mark(K_RMSNORM, 0, Td * d * 6);
+    e = launch_add_rmsnorm(c->x, c->delta, c->gamma + (size_t)l * 2 * d + d, c->xn, T, d, st);
+    if (e != cudaSuccess) return e;
+    mark(K_RMSNORM, 0, norm_bytes);
     {
       EpiSwiglu ep{c->g, hid};
       e = launch_gemm(m_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
@@ -440,17 +488,17 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
     {
-      EpiResidual ep{c->x, d, alpha};
+      EpiScaledF16 ep{c->delta, d, alpha};
       e = launch_gemm(m_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err, di,
                       st);
       if (e != cudaSuccess) return e;
-      mark(K_GEMM_W2, 2.0 * Td * d * hid, Td * hid * 2 + (double)d * hid * 2 + Td * d * 8);
+      mark(K_GEMM_W2, 2.0 * Td * d * hid, Td * hid * 2 + (double)d * hid * 2 + Td * d * 2);
     }
   }
 
-  rmsnorm_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->x, c->gamma_final, c->xn, T, d);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  mark(K_RMSNORM, 0, Td * d * 6);
+  e = launch_add_rmsnorm(c->x, c->delta, c->gamma_final, c->xn, T, d, st);
+  if (e != cudaSuccess) return e;
+  mark(K_RMSNORM, 0, norm_bytes);
 
   const int m_head = pick_mode(T, V, di);
   const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
@@ -693,6 +741,7 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   CREATE_CUDA(dmalloc(&ctx->v, T * ctx->kv_dim));
   CREATE_CUDA(dmalloc(&ctx->attn, T * ctx->q_dim));
   CREATE_CUDA(dmalloc(&ctx->g, T * hid));
+  CREATE_CUDA(dmalloc(&ctx->delta, T * d));
   CREATE_CUDA(dmalloc(&ctx->ce_part, T * ((V + 127) / 128)));
   CREATE_CUDA(dmalloc(&ctx->tgt_logit, T));
   CREATE_CUDA(dmalloc(&ctx->tok_loss, T));
@@ -725,6 +774,9 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   ok &= make_tmap(&ctx->tm_xn, ctx->xn, d, T, 1, 128);
   ok &= make_tmap(&ctx->tm_attn, ctx->attn, ctx->q_dim, T, 1, 128);
   ok &= make_tmap(&ctx->tm_g, ctx->g, hid, T, 1, 128);
+  ok &= make_tmap_qkv(&ctx->tm_q, ctx->q, T * cfg->heads, FA_BQ);
+  ok &= make_tmap_qkv(&ctx->tm_k, ctx->k, T * cfg->kv_heads, FA_BKV);
+  ok &= make_tmap_qkv(&ctx->tm_v, ctx->v, T * cfg->kv_heads, FA_BKV);
   for (int i = 0; i < 2; ++i) {
     const uint32_t bn = i ? 256 : 128;
     ok &= make_tmap(&ctx->tm_wqkv[i], ctx->wqkv, d, ctx->n_qkv, L, bn);
@@ -1094,11 +1146,15 @@ cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* ou
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
   ensure_attrs(dev);
-  dim3 grid(seq / ATT_BQ, heads, batch);
-  attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
-      static_cast<__half*>(out), seq, heads, heads, 1.4426950408889634f / sqrtf(128.0f));
-  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+  const uint64_t rows = (uint64_t)batch * heads * seq;
+  CUtensorMap tq, tk, tv;
+  const bool tc = seq % FA_BQ == 0 && make_tmap_qkv(&tq, q, rows, FA_BQ) &&
+                  make_tmap_qkv(&tk, k, rows, FA_BKV) && make_tmap_qkv(&tv, v, rows, FA_BKV);
+  cudaError_t e = launch_attention(tc ? &tq : nullptr, &tk, &tv, static_cast<const __half*>(q),
+                                   static_cast<const __half*>(k), static_cast<const __half*>(v),
+                                   static_cast<__half*>(out), batch, heads, heads, seq, nullptr,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
 cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* targets,

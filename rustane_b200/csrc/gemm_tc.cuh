@@ -18,7 +18,8 @@
 //   EpiStoreF32   fp32 store with optional softcap (sampled-logit dump)
 //   EpiQkvRope    Q/K/V split + RoPE on interleaved pairs, head-major store
 //                 (crates/engine/src/kernels/sdpa_fwd.rs:24-60,117-150,213-221)
-//   EpiResidual   x += alpha * acc (crates/engine/src/layer.rs:4471, ffn_fused.rs:144-154)
+//   EpiScaledF16  delta = alpha * acc for the residual add (layer.rs:4471, ffn_fused.rs:144-154)
+//   EpiResidual   x += alpha * acc in place (kept for direct use)
 //   EpiSwiglu     g = silu(h1) * h3 from interleaved W1/W3 columns
 //                 (crates/engine/src/kernels/ffn_fused.rs:79-80,105-107)
 //   EpiCrossEntropy  per-(row, N-tile) running max / sum-exp and target logit
@@ -209,6 +210,31 @@ struct EpiResidual {
       r.z += alpha * v[4 * j + 2];
       r.w += alpha * v[4 * j + 3];
       dst[j] = r;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// delta[row, col] = fp16(alpha * acc): the O-proj / down-proj output handed to the
+// next add_rmsnorm kernel, which adds it to the fp32 residual stream. Write-only, so
+// the epilogue never waits on global loads.
+struct EpiScaledF16 {
+  using Pre = NoPre;
+  __half* out;
+  int ldo;
+  float alpha;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_half2(alpha * v[8 * j + 0], alpha * v[8 * j + 1]);
+      w.y = pack_half2(alpha * v[8 * j + 2], alpha * v[8 * j + 3]);
+      w.z = pack_half2(alpha * v[8 * j + 4], alpha * v[8 * j + 5]);
+      w.w = pack_half2(alpha * v[8 * j + 6], alpha * v[8 * j + 7]);
+      dst[j] = w;
     }
   }
   __device__ __forceinline__ void end_row(int, int) {}

@@ -185,6 +185,46 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
       : "memory");
 }
 
+// Each thread of the warp stores 32 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Generic-proxy shared-memory writes become visible to the async proxy (UMMA, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tiled TMA load (c0 innermost, elements; must be 16-byte aligned).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Shared-memory descriptor for an MN-major operand in the 128-byte-swizzled layout
+// TMA writes: 64 fp16 along MN per 128-byte row, rows along K, 8-row atoms of
+// 1024 B (SBO); the next 64-wide MN block starts `lbo_bytes` further on (LBO).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo_bytes) {
+  return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo_bytes >> 4) << 16) |
+         (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
 // ------------------------------------------------------ clusters / CTA pairs
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -278,6 +318,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
          | (0u << 7) | (0u << 10)         // A, B format: f16
          | ((uint32_t)(N >> 3) << 17)     // N / 8
          | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+// Instruction descriptor, kind::f16: A=B=fp16, D=fp32, A K-major, B MN-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_bmn(int M, int N) {
+  return umma_idesc_f16(M, N) | (1u << 16);
 }
 
 // -------------------------------------------------- legacy warp MMA (attention)

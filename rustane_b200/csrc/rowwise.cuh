@@ -6,6 +6,7 @@
 //                          (crates/engine/src/cpu/embedding.rs:8-17,
 //                           cpu/rmsnorm.rs:149-183, EPS = 1e-5 at :10)
 //   rmsnorm_kernel       : Xn = X * rinv * gamma (fp32 in, fp16 out)
+//   add_rmsnorm_kernel   : X += delta (the scaled O / down projection), then the norm
 //   ce_finalize_kernel   : per-token loss from the LM-head epilogue partials,
 //                          loss_t = log(sum_v e^{z_v - m}) + m - z_tgt
 //                          (crates/engine/src/cpu/cross_entropy.rs:58-96)
@@ -101,6 +102,92 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
     ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z +
           b.w * b.w;
+  }
+  ss = warp_sum(ss);
+  const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  __half* o = xn + (size_t)row * dim;
+  for (int c = lane * 8; c < dim; c += 256) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    float f[8] = {a.x * rinv * g0.x, a.y * rinv * g0.y, a.z * rinv * g0.z, a.w * rinv * g0.w,
+                  b.x * rinv * g1.x, b.y * rinv * g1.y, b.z * rinv * g1.z, b.w * rinv * g1.w};
+    *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
+  }
+}
+
+// Residual add + RMSNorm, the reference's vsma + rmsnorm pair (layer.rs:4932-4940,
+// cpu/rmsnorm.rs:149-183): x += delta (fp16 projection output already scaled by
+// alpha), then xn = x * rinv * gamma. One warp per row; rows of up to NREG*256
+// elements stay in registers between the two passes.
+template <int NREG>
+__global__ void add_rmsnorm_kernel(float* __restrict__ x, const __half* __restrict__ delta,
+                                   const float* __restrict__ gamma, __half* __restrict__ xn,
+                                   int T, int dim) {
+  const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  float* xr = x + (size_t)row * dim;
+  const __half* dr = delta + (size_t)row * dim;
+  float keep[NREG][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < NREG; ++it) {
+    const int c = it * 256 + lane * 8;
+    if (c < dim) {
+      const float4 a = *reinterpret_cast<const float4*>(xr + c);
+      const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+      float dv[8];
+      h8_to_f8(*reinterpret_cast<const uint4*>(dr + c), dv);
+      float* f = keep[it];
+      f[0] = a.x + dv[0]; f[1] = a.y + dv[1]; f[2] = a.z + dv[2]; f[3] = a.w + dv[3];
+      f[4] = b.x + dv[4]; f[5] = b.y + dv[5]; f[6] = b.z + dv[6]; f[7] = b.w + dv[7];
+      *reinterpret_cast<float4*>(xr + c) = make_float4(f[0], f[1], f[2], f[3]);
+      *reinterpret_cast<float4*>(xr + c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+  }
+  ss = warp_sum(ss);
+  const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  __half* o = xn + (size_t)row * dim;
+#pragma unroll
+  for (int it = 0; it < NREG; ++it) {
+    const int c = it * 256 + lane * 8;
+    if (c < dim) {
+      const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+      const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = keep[it][i] * rinv * gg[i];
+      *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
+    }
+  }
+}
+
+// Same for rows longer than the register budget: the second pass re-reads x (L2-hot).
+__global__ void add_rmsnorm_long_kernel(float* __restrict__ x, const __half* __restrict__ delta,
+                                        const float* __restrict__ gamma, __half* __restrict__ xn,
+                                        int T, int dim) {
+  const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  float* xr = x + (size_t)row * dim;
+  const __half* dr = delta + (size_t)row * dim;
+  float ss = 0.f;
+  for (int c = lane * 8; c < dim; c += 256) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    float dv[8];
+    h8_to_f8(*reinterpret_cast<const uint4*>(dr + c), dv);
+    float f[8] = {a.x + dv[0], a.y + dv[1], a.z + dv[2], a.w + dv[3],
+                  b.x + dv[4], b.y + dv[5], b.z + dv[6], b.w + dv[7]};
+    *reinterpret_cast<float4*>(xr + c) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(xr + c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
   }
   ss = warp_sum(ss);
   const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
