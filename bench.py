@@ -118,13 +118,6 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-def make_tokens(cfg, n_seq, seed, rank):
-    rng = np.random.default_rng([seed, rank])
-    tok = rng.integers(0, cfg.vocab, n_seq * cfg.seq, dtype=np.int64).astype(np.uint32)
-    tgt = rng.integers(0, cfg.vocab, n_seq * cfg.seq, dtype=np.int64).astype(np.uint32)
-    return tok, tgt
-
-
 def cpu_oracle_sample(cfg, seed, tok, tgt, budget_s):
     """Time the CPU oracle on whole sequences until budget_s is spent."""
     from oracle import oracle
@@ -158,9 +151,10 @@ def run_reference(args):
     if rank != 0:
         return
     from rustane_b200.model import CONFIGS
+    from rustane_b200.sharding import global_tokens
     from oracle import oracle
     cfg = CONFIGS[args.config]
-    tok, tgt = make_tokens(cfg, 1, args.seed, 0)
+    tok, tgt = global_tokens(cfg.vocab, cfg.seq, 1, args.seed)
     model = oracle.OracleModel(cfg, seed=args.seed, scheme=oracle.SCHEME_NORMAL, sigma=0.02)
     threads = oracle.max_threads()
     for _ in range(args.warmup):
@@ -200,6 +194,8 @@ def main():
     import torch.distributed as dist
     from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
     from rustane_b200.model import CONFIGS
+    from rustane_b200.sharding import (global_tokens, rank_shard, reduce_max, reduce_mean,
+                                       shard_sequences)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -214,13 +210,11 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     cfg = CONFIGS[args.config]
-    if args.global_batch % world:
-        raise SystemExit("global batch must divide evenly over the GPUs")
-    per = args.global_batch // world
-    T = per * cfg.seq
+    per = shard_sequences(args.global_batch, world)
     kern = CompiledKernels(cfg, local, per)
     kern.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
-    tok_np, tgt_np = make_tokens(cfg, per, args.seed, rank)
+    all_tok, all_tgt = global_tokens(cfg.vocab, cfg.seq, args.global_batch, args.seed)
+    tok_np, tgt_np = rank_shard(all_tok, all_tgt, cfg.seq, rank, per)
     d_tok = torch.from_numpy(tok_np.view(np.int32)).cuda()
     d_tgt = torch.from_numpy(tgt_np.view(np.int32)).cuda()
     d_loss = torch.zeros(1, dtype=torch.float32, device="cuda")
@@ -236,18 +230,10 @@ def main():
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(x, device="cuda")
 
     def mean_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item()) / world
+        return reduce_mean(x, device="cuda")
 
     for _ in range(args.warmup):
         step()
