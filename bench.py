@@ -118,9 +118,19 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def host_threads() -> int:
+    """Every core this process may run on (torchrun's OMP_NUM_THREADS=1 is ignored
+    on purpose: the CPU legs use the whole host)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_oracle_sample(cfg, seed, tok, tgt, budget_s):
     """Time the CPU oracle on whole sequences until budget_s is spent."""
     from oracle import oracle
+    oracle.set_threads(host_threads())
     model = oracle.OracleModel(cfg, seed=seed, scheme=oracle.SCHEME_NORMAL, sigma=0.02)
     threads = oracle.max_threads()
     n_done, elapsed, losses = 0, 0.0, []
@@ -155,6 +165,7 @@ def run_reference(args):
     from oracle import oracle
     cfg = CONFIGS[args.config]
     tok, tgt = global_tokens(cfg.vocab, cfg.seq, 1, args.seed)
+    oracle.set_threads(host_threads())
     model = oracle.OracleModel(cfg, seed=args.seed, scheme=oracle.SCHEME_NORMAL, sigma=0.02)
     threads = oracle.max_threads()
     for _ in range(args.warmup):
