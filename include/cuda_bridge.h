@@ -104,6 +104,28 @@ cb_status cb_device_count(int32_t* count);
 cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batch,
                     cb_ctx** out);
 
+/* Tensor-parallel context (Megatron split of one model over tp_world GPUs, one
+ * process or thread per rank), the CUDA counterpart of the reference's
+ * head-sharded attention and hidden-sharded FFN (layer.rs:972-1003, 1906-2053,
+ * 4943-5139): rank r holds a near-even share of the kv heads (with their query
+ * heads) for Wq/Wk/Wv (column-parallel) and Wo (row-parallel), and of the hidden
+ * width in 64-column blocks for W1/W3 (column) and W2 (row). The row-parallel
+ * partial outputs are summed with an NCCL all-reduce where the reference summed
+ * shard outputs on the CPU (layer.rs:5121, 2018). Embedding, norms, residual and
+ * the LM head + loss are replicated. Every rank passes the same 128-byte NCCL
+ * unique id (from cb_nccl_unique_id on one rank) and must run the same sequence
+ * of calls. NCCL is loaded at run time ($CB_NCCL_LIB or libnccl.so.2). */
+cb_status cb_create_tp(const cb_model_config* cfg, int32_t device, int32_t max_batch,
+                       int32_t tp_rank, int32_t tp_world, const void* nccl_unique_id,
+                       cb_ctx** out);
+
+/* Writes a fresh 128-byte NCCL unique id to `out` (for cb_create_tp). */
+cb_status cb_nccl_unique_id(void* out);
+
+/* info[8] = {tp_rank, tp_world, local heads, local kv heads, local hidden,
+ *            first head, first kv head, first hidden column} of a context. */
+cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info);
+
 /* Frees every device resource of the context. NULL is accepted. */
 cb_status cb_destroy(cb_ctx* ctx);
 

@@ -8,11 +8,11 @@ from .model import CONFIGS, ModelConfig, custom_config
 from .bridge import CudaBridgeError, CB_INIT_NORMAL, CB_INIT_REFERENCE, load_library
 from .engine import (CompiledKernels, ForwardResult, ForwardScheduler, LayerWeights,
                      ModelForwardWorkspace, ModelWeights, forward, forward_losses,
-                     forward_only_ws, forward_ws)
+                     forward_only_ws, forward_ws, nccl_unique_id)
 
 __all__ = [
     "CONFIGS", "ModelConfig", "custom_config", "CudaBridgeError", "CB_INIT_NORMAL",
     "CB_INIT_REFERENCE", "load_library", "CompiledKernels", "ForwardResult", "ForwardScheduler",
     "LayerWeights", "ModelForwardWorkspace", "ModelWeights", "forward", "forward_losses",
-    "forward_only_ws", "forward_ws",
+    "forward_only_ws", "forward_ws", "nccl_unique_id",
 ]

@@ -25,6 +25,17 @@ NVCC_FLAGS = [
 ]
 
 
+def nccl_dirs():
+    """(include dir, library file) of the NCCL that ships with torch, if present."""
+    try:
+        import nvidia.nccl  # namespace package from the nvidia-nccl wheel
+        base = Path(list(nvidia.nccl.__path__)[0])
+    except Exception:
+        return None, None
+    inc, lib = base / "include", base / "lib" / "libnccl.so.2"
+    return (inc if (inc / "nccl.h").exists() else None), (lib if lib.exists() else None)
+
+
 def nvcc_path() -> str:
     cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
     p = Path(cuda) / "bin" / "nvcc"
@@ -41,8 +52,14 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_build():
         return LIB
-    cmd = [nvcc_path(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}",
-           "-o", str(LIB), *map(str, SOURCES)]
+    inc, nccl_lib = nccl_dirs()
+    if inc is None:
+        raise RuntimeError("nccl.h not found (the nvidia-nccl wheel provides it)")
+    extra = [f"-I{inc}"]
+    if nccl_lib is not None:
+        extra.append(f'-DCB_NCCL_DEFAULT_PATH="{nccl_lib}"')
+    cmd = [nvcc_path(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}", *extra,
+           "-o", str(LIB), *map(str, SOURCES), "-ldl"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -18,6 +18,8 @@
 //   ce_finalize -> per-token loss; loss_mean           cpu/cross_entropy.rs:58-96; full_model.rs:471
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdio>
@@ -90,6 +92,64 @@ bool make_tmap_qkv(CUtensorMap* map, const void* ptr, uint64_t rows, uint32_t bo
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------ NCCL (loaded on demand)
+// Only tensor-parallel contexts need NCCL, so the library resolves it at run time:
+// $CB_NCCL_LIB, else the copy this library was built against (CB_NCCL_DEFAULT_PATH),
+// else whatever libnccl.so.2 the dynamic loader finds (the one torch loaded, if any).
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclCommAbort) abort = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  decltype(&ncclCommGetAsyncError) async_error = nullptr;
+  std::string why;
+  bool ok() const { return all_reduce != nullptr; }
+};
+
+const NcclApi& nccl_api() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    std::vector<std::string> names;
+    if (const char* e = getenv("CB_NCCL_LIB")) names.push_back(e);
+#ifdef CB_NCCL_DEFAULT_PATH
+    names.push_back(CB_NCCL_DEFAULT_PATH);
+#endif
+    names.push_back("libnccl.so.2");
+    void* h = nullptr;
+    for (const auto& n : names)
+      if ((h = dlopen(n.c_str(), RTLD_NOW | RTLD_GLOBAL)) != nullptr) break;
+    if (!h) {
+      api.why = "libnccl.so.2 not found (set CB_NCCL_LIB)";
+      return;
+    }
+    NcclApi a;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    if (!a.get_unique_id || !a.init_rank || !a.all_reduce || !a.destroy || !a.abort ||
+        !a.error_string || !a.async_error) {
+      api.why = "libnccl.so.2 lacks a required symbol";
+      return;
+    }
+    api = a;
+  });
+  return api;
+}
+
+// Near-even split of `n` units over `world` ranks: the first n % world ranks get one more.
+void split_even(int n, int world, int rank, int* begin, int* count) {
+  const int base = n / world, extra = n % world;
+  *count = base + (rank < extra ? 1 : 0);
+  *begin = rank * base + (rank < extra ? rank : extra);
 }
 
 // ------------------------------------------------------------ GEMM launch
@@ -249,14 +309,20 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
 }
 
 // x += delta; xn = rmsnorm(x) * gamma (rows kept in registers up to 2048 wide).
-cudaError_t launch_add_rmsnorm(float* x, const __half* delta, const float* gamma, __half* xn,
+template <typename DT>
+cudaError_t launch_add_rmsnorm(float* x, const DT* delta, const float* gamma, __half* xn,
                                int T, int d, cudaStream_t st) {
   const int blocks = (T + ROW_WARPS - 1) / ROW_WARPS, threads = ROW_WARPS * 32;
-  if (d <= 512) add_rmsnorm_kernel<2><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
-  else if (d <= 1024) add_rmsnorm_kernel<4><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
-  else if (d <= 1536) add_rmsnorm_kernel<6><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
-  else if (d <= 2048) add_rmsnorm_kernel<8><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
-  else add_rmsnorm_long_kernel<<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  if (d <= 512)
+    add_rmsnorm_kernel<2, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 1024)
+    add_rmsnorm_kernel<4, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 1536)
+    add_rmsnorm_kernel<6, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else if (d <= 2048)
+    add_rmsnorm_kernel<8, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+  else
+    add_rmsnorm_long_kernel<DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
   return cudaGetLastError();
 }
 
@@ -272,12 +338,13 @@ enum KClass {
   K_GEMM_HEAD,
   K_CE_FINAL,
   K_LOSS_MEAN,
+  K_ALLREDUCE,
   K_NUM
 };
 const char* kclass_name[K_NUM] = {"embed_rmsnorm", "add_rmsnorm",   "gemm_qkv_rope",
                                   "attention",     "gemm_o",        "gemm_w13_swiglu",
                                   "gemm_w2",       "gemm_lmhead_ce", "ce_finalize",
-                                  "loss_mean"};
+                                  "loss_mean",     "nccl_allreduce"};
 
 struct KStat {
   int64_t launches = 0;
@@ -292,7 +359,13 @@ struct cb_ctx {
   int device = 0;
   int max_batch = 0;
   int num_sms = 148;
-  int q_dim = 0, kv_dim = 0, n_qkv = 0;
+  // this rank's share (the whole model unless tensor-parallel)
+  int heads_l = 0, kv_heads_l = 0, hidden_l = 0;
+  int q_dim = 0, kv_dim = 0, n_qkv = 0;  // local: heads_l*128, kv_heads_l*128, q+2kv
+  int q_off = 0, kv_off = 0, hid_off = 0;  // offsets of the share in the full model
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
+  float* delta32 = nullptr;  // [T, dim] fp32 partial projections, all-reduced across ranks
   cudaStream_t stream = nullptr;
   std::string err;
   bool weights_ready = false;
@@ -379,15 +452,21 @@ cudaError_t dmalloc(T** p, size_t n) {
 
 size_t wqkv_layer_elems(const cb_ctx* c) { return (size_t)c->n_qkv * c->cfg.dim; }
 size_t wo_layer_elems(const cb_ctx* c) { return (size_t)c->cfg.dim * c->q_dim; }
-size_t w13_layer_elems(const cb_ctx* c) { return (size_t)2 * c->cfg.hidden * c->cfg.dim; }
-size_t w2_layer_elems(const cb_ctx* c) { return (size_t)c->cfg.dim * c->cfg.hidden; }
+size_t w13_layer_elems(const cb_ctx* c) { return (size_t)2 * c->hidden_l * c->cfg.dim; }
+size_t w2_layer_elems(const cb_ctx* c) { return (size_t)c->cfg.dim * c->hidden_l; }
 
 ShapeInfo shape_of(const cb_ctx* c) {
   ShapeInfo s;
   s.dim = c->cfg.dim;
-  s.hidden = c->cfg.hidden;
+  s.hidden = c->hidden_l;
   s.q_dim = c->q_dim;
   s.kv_dim = c->kv_dim;
+  s.hidden_g = c->cfg.hidden;
+  s.q_dim_g = c->cfg.heads * 128;
+  s.kv_dim_g = c->cfg.kv_heads * 128;
+  s.q_off = c->q_off;
+  s.kv_off = c->kv_off;
+  s.hid_off = c->hid_off;
   s.vocab = c->cfg.vocab;
   return s;
 }
@@ -398,7 +477,8 @@ void free_ctx(cb_ctx* c) {
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   c->graphs.clear();
   for (auto e : c->events) cudaEventDestroy(e);
-  void* ptrs[] = {c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
+  if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
+  void* ptrs[] = {c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
@@ -415,10 +495,11 @@ void free_ctx(cb_ctx* c) {
 // CUDA events bracket every launch (eager mode only).
 cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof) {
   const cb_model_config& cfg = c->cfg;
-  const int S = cfg.seq, d = cfg.dim, hid = cfg.hidden, V = cfg.vocab, L = cfg.nlayers;
+  const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
   const int T = batch * S;
   const float alpha = 1.0f / sqrtf(2.0f * (float)L);  // layer.rs:4420
   const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
+  const bool tp = c->tp_world > 1;
   int ev = 0;
   auto mark = [&](int cls, double flops, double bytes) {
     if (!prof) return;
@@ -446,40 +527,57 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   const int m_o = pick_mode(T, d, di);
   const int m_13 = pick_mode(T, 2 * hid, di);
   const int m_2 = pick_mode(T, d, di);
-  const double attn_flops = 2.0 * 2.0 * (double)batch * cfg.heads * 128.0 * S * (S + 1) / 2.0;
+  const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
+  const double norm_bytes = Td * d * (4 + (tp ? 4 : 2) + 4 + 2);
 
-  const double norm_bytes = Td * d * (4 + 2 + 4 + 2);
+  // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer; under
+  // tensor parallelism the fp32 partials are summed across ranks (NCCL all-reduce).
+  auto project = [&](int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
+                     const CUtensorMap& tb256, int K, int layer, int cls) -> cudaError_t {
+    cudaError_t r;
+    if (tp) {
+      EpiScaledF32 ep{c->delta32, d, alpha};
+      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st);
+    } else {
+      EpiScaledF16 ep{c->delta, d, alpha};
+      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st);
+    }
+    if (r != cudaSuccess) return r;
+    mark(cls, 2.0 * Td * d * K, Td * K * 2 + (double)d * K * 2 + Td * d * (tp ? 4 : 2));
+    if (tp) {
+      ncclResult_t nr = nccl_api().all_reduce(c->delta32, c->delta32, (size_t)T * d, ncclFloat32,
+                                              ncclSum, c->comm, st);
+      if (nr != ncclSuccess) return cudaErrorUnknown;
+      mark(K_ALLREDUCE, 0, Td * d * 4);
+    }
+    return cudaSuccess;
+  };
+  auto add_norm = [&](const float* gamma) -> cudaError_t {
+    cudaError_t r = tp ? launch_add_rmsnorm(c->x, c->delta32, gamma, c->xn, T, d, st)
+                       : launch_add_rmsnorm(c->x, c->delta, gamma, c->xn, T, d, st);
+    if (r == cudaSuccess) mark(K_RMSNORM, 0, norm_bytes);
+    return r;
+  };
+
   for (int l = 0; l < L; ++l) {
     if (l > 0) {  // residual add of the previous layer's down projection + RMSNorm(gamma1)
-      e = launch_add_rmsnorm(c->x, c->delta, c->gamma + (size_t)l * 2 * d, c->xn, T, d, st);
-      if (e != cudaSuccess) return e;
-      mark(K_RMSNORM, 0, norm_bytes);
+      if ((e = add_norm(c->gamma + (size_t)l * 2 * d)) != cudaSuccess) return e;
     }
     {
-      EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, cfg.heads, cfg.kv_heads};
+      EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, c->heads_l, c->kv_heads_l};
       e = launch_gemm(m_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
                       c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
     }
-    {
-      e = launch_attention(&c->tm_q, &c->tm_k, &c->tm_v, c->q, c->k, c->v, c->attn, batch,
-                           cfg.heads, cfg.kv_heads, S, c->dev_err, st);
-      if (e != cudaSuccess) return e;
-      mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
-    }
-    {
-      EpiScaledF16 ep{c->delta, d, alpha};
-      e = launch_gemm(m_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], T, d, c->q_dim, l, ep,
-                      c->dev_err, di, st);
-      if (e != cudaSuccess) return e;
-      mark(K_GEMM_O, 2.0 * Td * d * c->q_dim,
-           Td * c->q_dim * 2 + (double)d * c->q_dim * 2 + Td * d * 2);
-    }
-    e = launch_add_rmsnorm(c->x, c->delta, c->gamma + (size_t)l * 2 * d + d, c->xn, T, d, st);
+    e = launch_attention(&c->tm_q, &c->tm_k, &c->tm_v, c->q, c->k, c->v, c->attn, batch,
+                         c->heads_l, c->kv_heads_l, S, c->dev_err, st);
     if (e != cudaSuccess) return e;
-    mark(K_RMSNORM, 0, norm_bytes);
+    mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
+    e = project(m_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O);
+    if (e != cudaSuccess) return e;
+    if ((e = add_norm(c->gamma + (size_t)l * 2 * d + d)) != cudaSuccess) return e;
     {
       EpiSwiglu ep{c->g, hid};
       e = launch_gemm(m_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
@@ -487,18 +585,10 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
-    {
-      EpiScaledF16 ep{c->delta, d, alpha};
-      e = launch_gemm(m_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err, di,
-                      st);
-      if (e != cudaSuccess) return e;
-      mark(K_GEMM_W2, 2.0 * Td * d * hid, Td * hid * 2 + (double)d * hid * 2 + Td * d * 2);
-    }
+    e = project(m_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2);
+    if (e != cudaSuccess) return e;
   }
-
-  e = launch_add_rmsnorm(c->x, c->delta, c->gamma_final, c->xn, T, d, st);
-  if (e != cudaSuccess) return e;
-  mark(K_RMSNORM, 0, norm_bytes);
+  if ((e = add_norm(c->gamma_final)) != cudaSuccess) return e;
 
   const int m_head = pick_mode(T, V, di);
   const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
@@ -524,7 +614,9 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   return cudaSuccess;
 }
 
-int launches_per_forward(const cb_ctx* c) { return 7 * c->cfg.nlayers + 4; }
+int launches_per_forward(const cb_ctx* c) {
+  return (c->tp_world > 1 ? 9 : 7) * c->cfg.nlayers + 4;  // + 2 all-reduces per layer
+}
 
 // ---------------------------------------------------------- standalone LM head + CE
 struct LmCeScratch {
@@ -663,7 +755,10 @@ const char* cb_last_error(const cb_ctx* ctx) {
   return ctx->err.c_str();
 }
 
-cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batch, cb_ctx** out) {
+// Shared constructor of cb_create (tp_world == 1) and cb_create_tp.
+static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t max_batch,
+                            int32_t tp_rank, int32_t tp_world, const void* nccl_id,
+                            cb_ctx** out) {
   g_create_error.clear();
   if (!out) {
     g_create_error = "null output pointer";
@@ -699,12 +794,41 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
     return CB_ERR_UNSUPPORTED;
   }
 
+  if (tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) {
+    g_create_error = "bad tensor-parallel rank/world";
+    return CB_ERR_INVALID_ARG;
+  }
+  if (tp_world > cfg->kv_heads || tp_world > cfg->hidden / 64) {
+    g_create_error = "tensor-parallel world larger than the kv heads or hidden blocks";
+    return CB_ERR_INVALID_ARG;
+  }
+  if (tp_world > 1 && !nccl_api().ok()) {
+    g_create_error = "NCCL unavailable: " + nccl_api().why;
+    return CB_ERR_NCCL;
+  }
+
   cb_ctx* ctx = new cb_ctx();
   ctx->cfg = *cfg;
   ctx->device = device;
   ctx->max_batch = max_batch;
-  ctx->q_dim = cfg->heads * 128;
-  ctx->kv_dim = cfg->kv_heads * 128;
+  ctx->tp_rank = tp_rank;
+  ctx->tp_world = tp_world;
+  {
+    // Megatron split: kv heads (with their query heads) and 64-column hidden blocks
+    // are divided as evenly as possible, e.g. 52 heads over 8 ranks = 7,7,7,7,6,6,6,6.
+    const int grp = cfg->heads / cfg->kv_heads;
+    int kv0, nkv, b0, nb;
+    split_even(cfg->kv_heads, tp_world, tp_rank, &kv0, &nkv);
+    split_even(cfg->hidden / 64, tp_world, tp_rank, &b0, &nb);
+    ctx->kv_heads_l = nkv;
+    ctx->heads_l = nkv * grp;
+    ctx->hidden_l = nb * 64;
+    ctx->kv_off = kv0 * 128;
+    ctx->q_off = kv0 * grp * 128;
+    ctx->hid_off = b0 * 64;
+  }
+  ctx->q_dim = ctx->heads_l * 128;
+  ctx->kv_dim = ctx->kv_heads_l * 128;
   ctx->n_qkv = ctx->q_dim + 2 * ctx->kv_dim;
 
   auto bail = [&](cb_status code, const std::string& m) {
@@ -725,7 +849,7 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   CREATE_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
   ensure_attrs(device);
 
-  const int L = cfg->nlayers, d = cfg->dim, hid = cfg->hidden, V = cfg->vocab, S = cfg->seq;
+  const int L = cfg->nlayers, d = cfg->dim, hid = ctx->hidden_l, V = cfg->vocab, S = cfg->seq;
   const size_t T = ctx->T_max();
   CREATE_CUDA(dmalloc(&ctx->embed, (size_t)V * d));
   CREATE_CUDA(dmalloc(&ctx->wqkv, (size_t)L * wqkv_layer_elems(ctx)));
@@ -742,6 +866,7 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   CREATE_CUDA(dmalloc(&ctx->attn, T * ctx->q_dim));
   CREATE_CUDA(dmalloc(&ctx->g, T * hid));
   CREATE_CUDA(dmalloc(&ctx->delta, T * d));
+  if (tp_world > 1) CREATE_CUDA(dmalloc(&ctx->delta32, T * d));
   CREATE_CUDA(dmalloc(&ctx->ce_part, T * ((V + 127) / 128)));
   CREATE_CUDA(dmalloc(&ctx->tgt_logit, T));
   CREATE_CUDA(dmalloc(&ctx->tok_loss, T));
@@ -774,9 +899,9 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   ok &= make_tmap(&ctx->tm_xn, ctx->xn, d, T, 1, 128);
   ok &= make_tmap(&ctx->tm_attn, ctx->attn, ctx->q_dim, T, 1, 128);
   ok &= make_tmap(&ctx->tm_g, ctx->g, hid, T, 1, 128);
-  ok &= make_tmap_qkv(&ctx->tm_q, ctx->q, T * cfg->heads, FA_BQ);
-  ok &= make_tmap_qkv(&ctx->tm_k, ctx->k, T * cfg->kv_heads, FA_BKV);
-  ok &= make_tmap_qkv(&ctx->tm_v, ctx->v, T * cfg->kv_heads, FA_BKV);
+  ok &= make_tmap_qkv(&ctx->tm_q, ctx->q, T * ctx->heads_l, FA_BQ);
+  ok &= make_tmap_qkv(&ctx->tm_k, ctx->k, T * ctx->kv_heads_l, FA_BKV);
+  ok &= make_tmap_qkv(&ctx->tm_v, ctx->v, T * ctx->kv_heads_l, FA_BKV);
   for (int i = 0; i < 2; ++i) {
     const uint32_t bn = i ? 256 : 128;
     ok &= make_tmap(&ctx->tm_wqkv[i], ctx->wqkv, d, ctx->n_qkv, L, bn);
@@ -787,11 +912,64 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
   }
   if (!ok) return bail(CB_ERR_UNSUPPORTED, "tensor map encoding failed");
 
+  if (tp_world > 1) {
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof(id));
+    ncclResult_t nr = nccl_api().init_rank(&ctx->comm, tp_world, id, tp_rank);
+    if (nr != ncclSuccess) {
+      ctx->comm = nullptr;
+      return bail(CB_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl_api().error_string(nr));
+    }
+  }
+
   const int nev = launches_per_forward(ctx) + 1;
   ctx->events.resize(nev);
   for (int i = 0; i < nev; ++i) CREATE_CUDA(cudaEventCreate(&ctx->events[i]));
 #undef CREATE_CUDA
   *out = ctx;
+  return CB_OK;
+}
+
+cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batch, cb_ctx** out) {
+  return create_ctx(cfg, device, max_batch, 0, 1, nullptr, out);
+}
+
+cb_status cb_create_tp(const cb_model_config* cfg, int32_t device, int32_t max_batch,
+                       int32_t tp_rank, int32_t tp_world, const void* nccl_unique_id,
+                       cb_ctx** out) {
+  if (tp_world > 1 && !nccl_unique_id) {
+    g_create_error = "null NCCL unique id";
+    return CB_ERR_INVALID_ARG;
+  }
+  return create_ctx(cfg, device, max_batch, tp_rank, tp_world, nccl_unique_id, out);
+}
+
+cb_status cb_nccl_unique_id(void* out) {
+  if (!out) return CB_ERR_INVALID_ARG;
+  if (!nccl_api().ok()) {
+    g_create_error = "NCCL unavailable: " + nccl_api().why;
+    return CB_ERR_NCCL;
+  }
+  ncclUniqueId id;
+  ncclResult_t nr = nccl_api().get_unique_id(&id);
+  if (nr != ncclSuccess) {
+    g_create_error = std::string("ncclGetUniqueId: ") + nccl_api().error_string(nr);
+    return CB_ERR_NCCL;
+  }
+  std::memcpy(out, &id, sizeof(id));
+  return CB_OK;
+}
+
+cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info) {
+  if (!ctx || !info) return CB_ERR_INVALID_ARG;
+  info[0] = ctx->tp_rank;
+  info[1] = ctx->tp_world;
+  info[2] = ctx->heads_l;
+  info[3] = ctx->kv_heads_l;
+  info[4] = ctx->hidden_l;
+  info[5] = ctx->q_off / 128;
+  info[6] = ctx->kv_off / 128;
+  info[7] = ctx->hid_off;
   return CB_OK;
 }
 
@@ -828,9 +1006,9 @@ cb_status cb_init_weights(cb_ctx* ctx, uint64_t seed, int32_t scheme, float sigm
     init_weight_kernel<<<grid, block, 0, st>>>(ctx->wo + l * wo_layer_elems(ctx), ST_WO, l,
                                                cfg.dim, ctx->q_dim, s, p);
     init_weight_kernel<<<grid, block, 0, st>>>(ctx->w13 + l * w13_layer_elems(ctx), ST_W13, l,
-                                               2 * cfg.hidden, cfg.dim, s, p);
+                                               2 * ctx->hidden_l, cfg.dim, s, p);
     init_weight_kernel<<<grid, block, 0, st>>>(ctx->w2 + l * w2_layer_elems(ctx), ST_W2, l,
-                                               cfg.dim, cfg.hidden, s, p);
+                                               cfg.dim, ctx->hidden_l, s, p);
   }
   fill_f32_kernel<<<grid, block, 0, st>>>(ctx->gamma, (size_t)cfg.nlayers * 2 * cfg.dim, 1.0f);
   fill_f32_kernel<<<grid, block, 0, st>>>(ctx->gamma_final, (size_t)cfg.dim, 1.0f);
@@ -853,9 +1031,11 @@ cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamm
   }
   CB_CUDA(cudaSetDevice(ctx->device));
   const ShapeInfo s = shape_of(ctx);
-  const size_t d = cfg.dim, hid = cfg.hidden, V = cfg.vocab;
-  size_t stage_n = std::max(std::max(V * d, d * hid), std::max(d * (size_t)ctx->q_dim,
-                                                               d * (size_t)ctx->kv_dim));
+  // Host tensors are the full model (reference orientation); each rank copies the
+  // slice it owns out of the staged f32 tensor.
+  const size_t d = cfg.dim, hid = cfg.hidden, V = cfg.vocab, hid_l = ctx->hidden_l;
+  const size_t qd_g = (size_t)cfg.heads * 128, kvd_g = (size_t)cfg.kv_heads * 128;
+  size_t stage_n = std::max(std::max(V * d, d * hid), std::max(d * qd_g, d * kvd_g));
   float* stage = nullptr;
   CB_CUDA(cudaMalloc(&stage, stage_n * sizeof(float)));
   cudaStream_t st = ctx->stream;
@@ -872,15 +1052,15 @@ cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamm
   for (int l = 0; ok && l < cfg.nlayers; ++l) {
     const cb_layer_weights_f32& w = layers[l];
     __half* qkv = ctx->wqkv + l * wqkv_layer_elems(ctx);
-    ok = ok && up(w.wq, d * ctx->q_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WQ);
-    ok = ok && up(w.wk, d * ctx->kv_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WK);
-    ok = ok && up(w.wv, d * ctx->kv_dim, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WV);
-    ok = ok && up(w.wo, d * ctx->q_dim, ctx->wo + l * wo_layer_elems(ctx), ST_WO, (int)d,
+    ok = ok && up(w.wq, d * qd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WQ);
+    ok = ok && up(w.wk, d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WK);
+    ok = ok && up(w.wv, d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WV);
+    ok = ok && up(w.wo, d * qd_g, ctx->wo + l * wo_layer_elems(ctx), ST_WO, (int)d,
                   ctx->q_dim, CB_T_WO);
     __half* w13 = ctx->w13 + l * w13_layer_elems(ctx);
-    ok = ok && up(w.w1, d * hid, w13, ST_W13, 2 * (int)hid, (int)d, CB_T_W1);
-    ok = ok && up(w.w3, d * hid, w13, ST_W13, 2 * (int)hid, (int)d, CB_T_W3);
-    ok = ok && up(w.w2, d * hid, ctx->w2 + l * w2_layer_elems(ctx), ST_W2, (int)d, (int)hid,
+    ok = ok && up(w.w1, d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W1);
+    ok = ok && up(w.w3, d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W3);
+    ok = ok && up(w.w2, d * hid, ctx->w2 + l * w2_layer_elems(ctx), ST_W2, (int)d, (int)hid_l,
                   CB_T_W2);
     ok = ok && cudaMemcpy(ctx->gamma + (size_t)l * 2 * d, w.gamma1, d * sizeof(float),
                           cudaMemcpyHostToDevice) == cudaSuccess;

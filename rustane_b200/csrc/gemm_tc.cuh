@@ -240,6 +240,25 @@ struct EpiScaledF16 {
   __device__ __forceinline__ void end_row(int, int) {}
 };
 
+// delta[row, col] = alpha * acc in fp32: the tensor-parallel partial O / down
+// projection that is all-reduced across ranks before the residual add.
+struct EpiScaledF32 {
+  using Pre = NoPre;
+  float* out;
+  int ldo;
+  float alpha;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
+    float4* dst = reinterpret_cast<float4*>(out + (size_t)row * ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      dst[j] = make_float4(alpha * v[4 * j], alpha * v[4 * j + 1], alpha * v[4 * j + 2],
+                           alpha * v[4 * j + 3]);
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
 // B rows interleave W1 and W3 columns: row 2j = W1[:, j], row 2j+1 = W3[:, j].
 // g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
 struct EpiSwiglu {

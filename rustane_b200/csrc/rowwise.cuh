@@ -117,19 +117,29 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   }
 }
 
+__device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
+  h8_to_f8(*reinterpret_cast<const uint4*>(p), f);
+}
+__device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
 // Residual add + RMSNorm, the reference's vsma + rmsnorm pair (layer.rs:4932-4940,
-// cpu/rmsnorm.rs:149-183): x += delta (fp16 projection output already scaled by
-// alpha), then xn = x * rinv * gamma. One warp per row; rows of up to NREG*256
-// elements stay in registers between the two passes.
-template <int NREG>
-__global__ void add_rmsnorm_kernel(float* __restrict__ x, const __half* __restrict__ delta,
+// cpu/rmsnorm.rs:149-183): x += delta (projection output already scaled by alpha;
+// fp16, or fp32 after a tensor-parallel all-reduce), then xn = x * rinv * gamma.
+// One warp per row; rows of up to NREG*256 elements stay in registers.
+template <int NREG, typename DT>
+__global__ void add_rmsnorm_kernel(float* __restrict__ x, const DT* __restrict__ delta,
                                    const float* __restrict__ gamma, __half* __restrict__ xn,
                                    int T, int dim) {
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   float* xr = x + (size_t)row * dim;
-  const __half* dr = delta + (size_t)row * dim;
+  const DT* dr = delta + (size_t)row * dim;
   float keep[NREG][8];
   float ss = 0.f;
 #pragma unroll
@@ -139,7 +149,7 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const __half* __restri
       const float4 a = *reinterpret_cast<const float4*>(xr + c);
       const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
       float dv[8];
-      h8_to_f8(*reinterpret_cast<const uint4*>(dr + c), dv);
+      load8(dr + c, dv);
       float* f = keep[it];
       f[0] = a.x + dv[0]; f[1] = a.y + dv[1]; f[2] = a.z + dv[2]; f[3] = a.w + dv[3];
       f[4] = b.x + dv[4]; f[5] = b.y + dv[5]; f[6] = b.z + dv[6]; f[7] = b.w + dv[7];
@@ -168,20 +178,21 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const __half* __restri
 }
 
 // Same for rows longer than the register budget: the second pass re-reads x (L2-hot).
-__global__ void add_rmsnorm_long_kernel(float* __restrict__ x, const __half* __restrict__ delta,
+template <typename DT>
+__global__ void add_rmsnorm_long_kernel(float* __restrict__ x, const DT* __restrict__ delta,
                                         const float* __restrict__ gamma, __half* __restrict__ xn,
                                         int T, int dim) {
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   float* xr = x + (size_t)row * dim;
-  const __half* dr = delta + (size_t)row * dim;
+  const DT* dr = delta + (size_t)row * dim;
   float ss = 0.f;
   for (int c = lane * 8; c < dim; c += 256) {
     const float4 a = *reinterpret_cast<const float4*>(xr + c);
     const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
     float dv[8];
-    h8_to_f8(*reinterpret_cast<const uint4*>(dr + c), dv);
+    load8(dr + c, dv);
     float f[8] = {a.x + dv[0], a.y + dv[1], a.z + dv[2], a.w + dv[3],
                   b.x + dv[4], b.y + dv[5], b.z + dv[6], b.w + dv[7]};
     *reinterpret_cast<float4*>(xr + c) = make_float4(f[0], f[1], f[2], f[3]);

@@ -9,7 +9,8 @@
 //   gamma [L, 2, dim] fp32, gamma_final [dim] fp32
 // Element (r, c) of a storage tensor maps back to one element of a reference
 // tensor (orientation of crates/engine/src/layer.rs:52-63); both the on-device
-// generator and the host-f32 upload use that mapping.
+// generator and the host-f32 upload use that mapping, so a tensor-parallel rank
+// generates exactly its slice of the single-GPU model.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -20,8 +21,13 @@ namespace cb {
 
 enum StoreKind : int { ST_EMBED = 0, ST_QKV = 1, ST_WO = 2, ST_W13 = 3, ST_W2 = 4 };
 
+// Local (this rank's) and global sizes. Under tensor parallelism a rank holds
+// q heads [q_off/128, +q_dim/128), kv heads [kv_off/128, +kv_dim/128) and hidden
+// columns [hid_off, +hidden); single-GPU contexts have zero offsets and local == global.
 struct ShapeInfo {
-  int dim, hidden, q_dim, kv_dim, vocab;
+  int dim, hidden, q_dim, kv_dim, vocab;          // local
+  int hidden_g, q_dim_g, kv_dim_g;                // global (reference tensor shapes)
+  int q_off, kv_off, hid_off;                     // this rank's offsets
 };
 
 struct RefElem {
@@ -39,24 +45,27 @@ __host__ __device__ __forceinline__ RefElem ref_of_storage(int st, int r, int c,
       break;
     case ST_QKV:
       if (r < s.q_dim) {
-        e.kind = CB_T_WQ; e.idx = (uint64_t)c * s.q_dim + r; e.len = (uint64_t)s.dim * s.q_dim;
+        e.kind = CB_T_WQ; e.idx = (uint64_t)c * s.q_dim_g + s.q_off + r;
+        e.len = (uint64_t)s.dim * s.q_dim_g;
       } else if (r < s.q_dim + s.kv_dim) {
-        e.kind = CB_T_WK; e.idx = (uint64_t)c * s.kv_dim + (r - s.q_dim);
-        e.len = (uint64_t)s.dim * s.kv_dim;
+        e.kind = CB_T_WK; e.idx = (uint64_t)c * s.kv_dim_g + s.kv_off + (r - s.q_dim);
+        e.len = (uint64_t)s.dim * s.kv_dim_g;
       } else {
-        e.kind = CB_T_WV; e.idx = (uint64_t)c * s.kv_dim + (r - s.q_dim - s.kv_dim);
-        e.len = (uint64_t)s.dim * s.kv_dim;
+        e.kind = CB_T_WV; e.idx = (uint64_t)c * s.kv_dim_g + s.kv_off + (r - s.q_dim - s.kv_dim);
+        e.len = (uint64_t)s.dim * s.kv_dim_g;
       }
       break;
-    case ST_WO:
-      e.kind = CB_T_WO; e.idx = (uint64_t)c * s.dim + r; e.len = (uint64_t)s.q_dim * s.dim;
+    case ST_WO:  // storage (n, k) = Wo[q_off + k, n]
+      e.kind = CB_T_WO; e.idx = (uint64_t)(s.q_off + c) * s.dim + r;
+      e.len = (uint64_t)s.q_dim_g * s.dim;
       break;
-    case ST_W13:
-      e.kind = (r & 1) ? CB_T_W3 : CB_T_W1; e.idx = (uint64_t)c * s.hidden + (r >> 1);
-      e.len = (uint64_t)s.dim * s.hidden;
+    case ST_W13:  // row 2j / 2j+1 = W1 / W3 column hid_off + j
+      e.kind = (r & 1) ? CB_T_W3 : CB_T_W1; e.idx = (uint64_t)c * s.hidden_g + s.hid_off + (r >> 1);
+      e.len = (uint64_t)s.dim * s.hidden_g;
       break;
-    default:  // ST_W2
-      e.kind = CB_T_W2; e.idx = (uint64_t)r * s.hidden + c; e.len = (uint64_t)s.dim * s.hidden;
+    default:  // ST_W2: storage (n, k) = W2[n, hid_off + k]
+      e.kind = CB_T_W2; e.idx = (uint64_t)r * s.hidden_g + s.hid_off + c;
+      e.len = (uint64_t)s.dim * s.hidden_g;
       break;
   }
   return e;

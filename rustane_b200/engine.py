@@ -105,13 +105,22 @@ class CompiledKernels:
     """Owns one cb_ctx: device weights, workspace and captured forward graphs
     for `max_batch` sequences on one GPU. Not thread-safe (one per thread)."""
 
-    def __init__(self, cfg: ModelConfig, device: int = 0, max_batch: int = 1):
+    def __init__(self, cfg: ModelConfig, device: int = 0, max_batch: int = 1,
+                 tp_rank: int = 0, tp_world: int = 1, nccl_id: Optional[bytes] = None):
         self.lib = B.load_library()
         self.cfg = cfg
         self.device = device
         self.max_batch = max_batch
+        self.tp_rank, self.tp_world = tp_rank, tp_world
         h = C.c_void_p()
-        B.check(self.lib.cb_create(C.byref(_cfg_struct(cfg)), device, max_batch, C.byref(h)))
+        if tp_world == 1:
+            B.check(self.lib.cb_create(C.byref(_cfg_struct(cfg)), device, max_batch, C.byref(h)))
+        else:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("tensor parallelism needs the 128-byte NCCL unique id")
+            buf = C.create_string_buffer(bytes(nccl_id), 128)
+            B.check(self.lib.cb_create_tp(C.byref(_cfg_struct(cfg)), device, max_batch, tp_rank,
+                                          tp_world, buf, C.byref(h)))
         self._h = h
         self._loaded_generation: Optional[int] = None
 
@@ -228,10 +237,24 @@ class CompiledKernels:
                                            flops=arr[i].flops, bytes=arr[i].bytes)
                 for i in range(n.value)}
 
+    def tp_info(self) -> dict:
+        a = (C.c_int32 * 8)()
+        self._check(self.lib.cb_tp_info(self.handle, a))
+        keys = ("rank", "world", "heads", "kv_heads", "hidden", "head0", "kv_head0", "hidden0")
+        return dict(zip(keys, list(a)))
+
     def stream(self) -> int:
         s = C.c_void_p()
         self._check(self.lib.cb_get_stream(self.handle, C.byref(s)))
         return s.value or 0
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id for CompiledKernels(..., tp_world > 1)."""
+    lib = B.load_library()
+    buf = C.create_string_buffer(128)
+    B.check(lib.cb_nccl_unique_id(buf))
+    return buf.raw
 
 
 # ---------------------------------------------------------------- model API
