@@ -176,6 +176,7 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiQkvRope>();
   set_gemm_attrs_for<EpiResidual>();
   set_gemm_attrs_for<EpiScaledF16>();
+  set_gemm_attrs_for<EpiScaledF32>();
   set_gemm_attrs_for<EpiSwiglu>();
   set_gemm_attrs_for<EpiCrossEntropy>();
   cudaFuncSetAttribute(attn_fwd_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -547,7 +548,10 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if (tp) {
       ncclResult_t nr = nccl_api().all_reduce(c->delta32, c->delta32, (size_t)T * d, ncclFloat32,
                                               ncclSum, c->comm, st);
-      if (nr != ncclSuccess) return cudaErrorUnknown;
+      if (nr != ncclSuccess) {
+        c->err = std::string("ncclAllReduce: ") + nccl_api().error_string(nr);
+        return cudaErrorUnknown;
+      }
       mark(K_ALLREDUCE, 0, Td * d * 4);
     }
     return cudaSuccess;
@@ -920,6 +924,12 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
       ctx->comm = nullptr;
       return bail(CB_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl_api().error_string(nr));
     }
+    // One eager all-reduce so NCCL sets up its connections before any graph capture.
+    nr = nccl_api().all_reduce(ctx->delta32, ctx->delta32, 1, ncclFloat32, ncclSum, ctx->comm,
+                               ctx->stream);
+    if (nr != ncclSuccess)
+      return bail(CB_ERR_NCCL, std::string("ncclAllReduce: ") + nccl_api().error_string(nr));
+    CREATE_CUDA(cudaStreamSynchronize(ctx->stream));
   }
 
   const int nev = launches_per_forward(ctx) + 1;
