@@ -39,11 +39,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "forward tokens/sec (ms/forward, seq512) at 1/2/4/8 B200; % of fp16 TC peak"
-GEMM_CLASSES = ("gemm_qkv_rope", "gemm_o_residual", "gemm_w13_swiglu", "gemm_w2_residual",
-                "gemm_lmhead_ce")
+GEMM_CLASSES = ("gemm_qkv_rope", "gemm_o", "gemm_w13_swiglu", "gemm_w2", "gemm_lmhead_ce")
 # DRAM bytes per GEMM launch measured by ncu (profiles/gemm_tc_600m-A_dram.md):
-# sum over the 101 GEMM launches of one forward at 8 sequences, scaled x8 to the
-# 64-sequence workload, divided by 101. None until measured.
+# the 81 GEMM launches of one forward. None until measured.
 GEMM_TRAFFIC_PER_LAUNCH = None
 
 
@@ -54,7 +52,11 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", default="600m-A")
-    p.add_argument("--global-batch", type=int, default=64)
+    p.add_argument("--global-batch", type=int, default=None,
+                   help="sequences per step for the whole job (default 64; 16 for 32B)")
+    p.add_argument("--tp", action="store_true",
+                   help="tensor parallelism over all ranks (Megatron split, NCCL all-reduce) "
+                        "instead of sequence sharding")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-budget-s", type=float, default=12.0,
                    help="CPU-baseline sample budget (seconds of oracle work)")
@@ -197,13 +199,15 @@ def run_reference(args):
 
 def main():
     args = parse_args()
+    if args.global_batch is None:
+        args.global_batch = 16 if args.config == "32B" else 64
     if args.impl == "reference":
         run_reference(args)
         return
 
     import torch
     import torch.distributed as dist
-    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels, nccl_unique_id
     from rustane_b200.model import CONFIGS
     from rustane_b200.sharding import (global_tokens, rank_shard, reduce_max, reduce_mean,
                                        shard_sequences)
@@ -221,11 +225,19 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     cfg = CONFIGS[args.config]
-    per = shard_sequences(args.global_batch, world)
-    kern = CompiledKernels(cfg, local, per)
-    kern.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
     all_tok, all_tgt = global_tokens(cfg.vocab, cfg.seq, args.global_batch, args.seed)
-    tok_np, tgt_np = rank_shard(all_tok, all_tgt, cfg.seq, rank, per)
+    if args.tp and world > 1:
+        # every rank runs the whole batch on its slice of the model
+        per = args.global_batch
+        nid = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(nid, src=0)
+        kern = CompiledKernels(cfg, local, per, tp_rank=rank, tp_world=world, nccl_id=nid[0])
+        tok_np, tgt_np = all_tok, all_tgt
+    else:
+        per = shard_sequences(args.global_batch, world)
+        kern = CompiledKernels(cfg, local, per)
+        tok_np, tgt_np = rank_shard(all_tok, all_tgt, cfg.seq, rank, per)
+    kern.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
     d_tok = torch.from_numpy(tok_np.view(np.int32)).cuda()
     d_tgt = torch.from_numpy(tgt_np.view(np.int32)).cuda()
     d_loss = torch.zeros(1, dtype=torch.float32, device="cuda")
@@ -302,7 +314,9 @@ def main():
         e2e_ms = max_over_ranks(f0.elapsed_time(f1))
         e2e = {"value": tokens_total / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(tok_view.nbytes + tgt_view.nbytes) * world,
-               "d2h_bytes_per_step": 4 * world, "ms_per_step": e2e_ms / args.steps}
+               "d2h_bytes_per_step": 4 * world, "ms_per_step": e2e_ms / args.steps,
+               "note": ("every TP rank copies the whole batch" if args.tp and world > 1
+                        else "each rank copies its own sequences")}
 
     # ---- roofline of the dominant kernel (the tcgen05 GEMM, all its launches)
     peaks, peak_kind = load_peaks()
@@ -313,7 +327,7 @@ def main():
     peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
     roofline = {
-        "kernel": "gemm_tn_kernel (tcgen05, all 5 fused-epilogue GEMMs)",
+        "kernel": "gemm_tn (tcgen05, all 5 fused-epilogue GEMMs, 81 launches per forward)",
         "bound": "tensor", "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
         "frac": round(achieved / peak_tf, 4), "peak_source": f"bf16_tflops_sustained ({peak_kind})",
         "flops_per_launch": g_flops / max(g_launch, 1),
@@ -332,7 +346,7 @@ def main():
 
     # ---- 4. CPU baseline on the host cores (rank 0 at N = 1)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.dim <= 2048:
         r = cpu_oracle_sample(cfg, args.seed, tok_np, tgt_np, args.cpu_budget_s)
         cpu_val = r["seqs"] * cfg.seq / r["seconds"]
         gpu_seq_losses = kern.forward_loss(tok_np[:r["seqs"] * cfg.seq],
@@ -356,7 +370,9 @@ def main():
                              f"{cfg.nlayers}L/{cfg.heads}x128, vocab {cfg.vocab}, tied head), "
                              f"seq {cfg.seq}, global batch {args.global_batch}"),
                 "global_batch": args.global_batch, "seq_len": cfg.seq,
-                "parallelism": f"dp{world} (sequence sharding, no communication)",
+                "parallelism": (f"tp{world} (Megatron column/row split, NCCL all-reduce after "
+                                "O and down projections)" if args.tp and world > 1 else
+                                f"dp{world} (sequence sharding, no communication)"),
                 "per_gpu_batch": per,
                 "l2": "no flush: every step reads >1.1 GB of weights and >1 GB of "
                       "activations, well above the 126 MB L2",

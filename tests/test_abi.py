@@ -102,3 +102,17 @@ def test_flop_model_matches_survey():
     assert abs(tflop_fwd - 0.6088) < 0.001
     c4 = CONFIGS["32B"]
     assert abs(c4.forward_flops_per_token() * 32768 / 1e12 - 2161.0) < 1.0
+
+
+def test_bench_gemm_classes_exist_in_bridge():
+    """bench.py's roofline sums these kernel classes; each must be a class the
+    bridge reports (a rename must not silently drop a GEMM from the roofline)."""
+    import importlib.util
+    root = Path(__file__).resolve().parents[1]
+    spec = importlib.util.spec_from_file_location("bench_mod", root / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    src = (root / "rustane_b200" / "csrc" / "bridge.cu").read_text()
+    table = src[src.index("kclass_name"):src.index("kclass_name") + 800]
+    for c in bench.GEMM_CLASSES:
+        assert f'"{c}"' in table, c
