@@ -174,7 +174,6 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiStoreF16>();
   set_gemm_attrs_for<EpiStoreF32>();
   set_gemm_attrs_for<EpiQkvRope>();
-  set_gemm_attrs_for<EpiResidual>();
   set_gemm_attrs_for<EpiScaledF16>();
   set_gemm_attrs_for<EpiScaledF32>();
   set_gemm_attrs_for<EpiSwiglu>();
@@ -396,7 +395,7 @@ struct cb_ctx {
   float* loss = nullptr;       // [1]
   uint32_t* tokens = nullptr;  // [T]
   uint32_t* targets = nullptr; // [T]
-  float2* rope = nullptr;      // [S, 64]
+  float2* rope = nullptr;      // [64, S] (cos, sin), pair-major
   int* dev_err = nullptr;      // device error flag
   float* h_loss = nullptr;     // pinned
   int* h_err = nullptr;        // pinned
@@ -886,14 +885,15 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(cudaMemset(ctx->x, 0, T * d * sizeof(float)));
   CREATE_CUDA(cudaMemset(ctx->tgt_logit, 0, T * sizeof(float)));
 
-  // RoPE table: theta = p * 10000^(-2i/128)  (sdpa_fwd.rs:24-39, layer.rs:645-666),
-  // evaluated in double and rounded to f32 (the CPU oracle builds the same table).
+  // RoPE table [64 pairs][S positions]: theta = p * 10000^(-2i/128) (sdpa_fwd.rs:24-39,
+  // layer.rs:645-666), evaluated in double and rounded to f32 (the CPU oracle builds the
+  // same values).
   {
     std::vector<float2> tab((size_t)S * 64);
     for (int p = 0; p < S; ++p)
       for (int i = 0; i < 64; ++i) {
         double th = (double)p * std::pow(10000.0, -2.0 * i / 128.0);
-        tab[(size_t)p * 64 + i] = make_float2((float)std::cos(th), (float)std::sin(th));
+        tab[(size_t)i * S + p] = make_float2((float)std::cos(th), (float)std::sin(th));
       }
     CREATE_CUDA(cudaMemcpy(ctx->rope, tab.data(), tab.size() * sizeof(float2),
                            cudaMemcpyHostToDevice));

@@ -19,7 +19,7 @@
 //   EpiQkvRope    Q/K/V split + RoPE on interleaved pairs, head-major store
 //                 (crates/engine/src/kernels/sdpa_fwd.rs:24-60,117-150,213-221)
 //   EpiScaledF16  delta = alpha * acc for the residual add (layer.rs:4471, ffn_fused.rs:144-154)
-//   EpiResidual   x += alpha * acc in place (kept for direct use)
+//   EpiScaledF32  the same in fp32 (tensor-parallel partials before the all-reduce)
 //   EpiSwiglu     g = silu(h1) * h3 from interleaved W1/W3 columns
 //                 (crates/engine/src/kernels/ffn_fused.rs:79-80,105-107)
 //   EpiCrossEntropy  per-(row, N-tile) running max / sum-exp and target logit
@@ -53,72 +53,120 @@ struct GemmCfg {
   static constexpr int STAGES = (STAGE_BYTES <= 32768) ? 6 : 4;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+  static constexpr int EPI_BUF_BYTES = 4096;  // per epilogue warp (32 rows x 128 B)
+  static constexpr int SMEM_BYTES =
+      STAGES * STAGE_BYTES + 1024 + BAR_BYTES + GEMM_EPI_WARPS * EPI_BUF_BYTES;
 };
 
 // ------------------------------------------------------------------ epilogues
 
-// Epilogue interface: begin_row(row, valid); prefetch(row, col0, Pre&) issues the
-// global loads a chunk needs (one chunk ahead of its use); chunk(row, col0, v, Pre)
-// consumes 32 accumulator columns of one row; end_row(row, n_blk).
+// Epilogue interface:
+//   begin_row(row, valid)          once per tile row
+//   prefetch(row, col0, Pre&)      global loads a chunk needs, issued one chunk ahead
+//   chunk(row, col0, v, Pre, out, dst)
+//                                  consumes 32 accumulator columns of one row and
+//                                  produces OUT_BYTES bytes of output (`out`, in 16-byte
+//                                  pieces) for the contiguous destination segment `dst`
+//   end_row(row, n_blk)
+// OUT_BYTES = 0: the epilogue writes nothing per chunk (the cross-entropy partials are
+// written in end_row). The kernel stores `out` through warp_store_rows: each warp's 32
+// row segments are staged in shared memory and written back so every store instruction
+// covers whole 16-byte-aligned row segments, instead of one 16-byte piece of 32
+// different rows (4-8x fewer L1 wavefronts).
 struct NoPre {};
+
+__device__ __forceinline__ uint4 pack8_f16(const float* f) {
+  uint4 w;
+  w.x = pack_half2(f[0], f[1]);
+  w.y = pack_half2(f[2], f[3]);
+  w.z = pack_half2(f[4], f[5]);
+  w.w = pack_half2(f[6], f[7]);
+  return w;
+}
+
+// Warp-cooperative transposed store of 32 row segments of NB bytes (32, 64 or 128):
+// lane L owns row L's segment (out[0 .. NB/16)) and its address; `wbuf` is this warp's
+// 32*NB-byte shared buffer. Pieces are XOR-swizzled so both phases are conflict-free.
+template <int NB>
+__device__ __forceinline__ void warp_store_rows(uint8_t* wbuf, const uint4 (&out)[8],
+                                                uint8_t* dst, bool ok) {
+  constexpr int Q = NB / 16;       // 16-byte pieces per row
+  constexpr int RPI = 32 / Q;      // rows covered by one store instruction
+  const int lane = threadIdx.x & 31;
+  const int sw = (lane / (8 / Q)) & (Q - 1);
+#pragma unroll
+  for (int j = 0; j < Q; ++j)
+    *reinterpret_cast<uint4*>(wbuf + lane * NB + ((j ^ sw) << 4)) = out[j];
+  __syncwarp();
+  const unsigned long long my = reinterpret_cast<unsigned long long>(ok ? dst : nullptr);
+#pragma unroll
+  for (int k = 0; k < Q; ++k) {
+    const int r = k * RPI + lane / Q;
+    const int j = lane % Q;
+    const unsigned long long base = __shfl_sync(0xffffffffu, my, r);
+    const int swr = (r / (8 / Q)) & (Q - 1);
+    const uint4 x = *reinterpret_cast<const uint4*>(wbuf + r * NB + ((j ^ swr) << 4));
+    if (base) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(base) + (j << 4)) = x;
+  }
+  __syncwarp();
+}
 
 struct EpiStoreF16 {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 64;
   __half* out;
   int ldo;
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
-    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col0);
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_half2(v[8 * j + 0], v[8 * j + 1]);
-      w.y = pack_half2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = pack_half2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = pack_half2(v[8 * j + 6], v[8 * j + 7]);
-      dst[j] = w;
-    }
+    for (int j = 0; j < 4; ++j) o[j] = pack8_f16(v + 8 * j);
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
 
 struct EpiStoreF32 {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 128;
   float* out;
   int ldo;
   float softcap;  // > 0: out = softcap * tanh(acc / softcap)
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
-    float4* dst = reinterpret_cast<float4*>(out + (size_t)row * ldo + col0);
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       if (softcap > 0.f) {
-        float inv = 1.0f / softcap;
+        const float inv = 1.0f / softcap;
         w.x = softcap * tanhf(w.x * inv);
         w.y = softcap * tanhf(w.y * inv);
         w.z = softcap * tanhf(w.z * inv);
         w.w = softcap * tanhf(w.w * inv);
       }
-      dst[j] = w;
+      o[j] = *reinterpret_cast<const uint4*>(&w);
     }
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
 
 // Columns [0, q_dim) -> Q, [q_dim, q_dim+kv_dim) -> K, rest -> V. Head dim 128.
-// Output layout [batch, heads, seq, 128] (row = b*seq + s).
+// Output layout [batch, heads, seq, 128] (row = b*seq + s). RoPE on Q and K rotates
+// pairs (2i, 2i+1) by theta = s * 10000^(-2i/128); the (cos, sin) table is
+// pair-major [64][seq] so the lanes of a warp (consecutive positions) read it contiguously.
 struct EpiQkvRope {
   struct Pre {
-    float4 cs[8];  // (cos, sin) of the chunk's 16 frequency pairs
+    float2 cs[16];  // (cos, sin) of the chunk's 16 frequency pairs
   };
+  static constexpr int OUT_BYTES = 64;
   __half* q;
   __half* k;
   __half* v;
-  const float2* rope;  // [seq, 64] (cos, sin) of theta = s * 10000^(-2i/128)
+  const float2* rope;  // [64][seq]
   int seq;
   int heads;
   int kv_heads;
@@ -126,91 +174,50 @@ struct EpiQkvRope {
   __device__ __forceinline__ void prefetch(int row, int col0, Pre& p) {
     if (col0 >= (heads + kv_heads) * 128) return;  // V columns are not rotated
     const int s = row % seq;
-    const float4* rs = reinterpret_cast<const float4*>(rope + (size_t)s * 64 + ((col0 & 127) >> 1));
+    const float2* rs = rope + (size_t)((col0 & 127) >> 1) * seq + s;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) p.cs[i] = __ldg(rs + i);
+    for (int i = 0; i < 16; ++i) p.cs[i] = __ldg(rs + (size_t)i * seq);
   }
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32], const Pre& p) {
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32], const Pre& p,
+                                        uint4 (&o)[8], uint8_t*& dst) {
     const int q_dim = heads * 128;
     const int kv_dim = kv_heads * 128;
-    int b = row / seq;
-    int s = row - b * seq;
-    __half* dst;
+    const int b = row / seq;
+    const int s = row - b * seq;
+    __half* base;
     int c = col0;
     bool rot = true;
     int nh;
     if (c < q_dim) {
-      dst = q;
+      base = q;
       nh = heads;
     } else if (c < q_dim + kv_dim) {
-      dst = k;
+      base = k;
       c -= q_dim;
       nh = kv_heads;
     } else {
-      dst = v;
+      base = v;
       c -= q_dim + kv_dim;
       nh = kv_heads;
       rot = false;
     }
-    int h = c >> 7;
-    int d0 = c & 127;
-    float o[32];
+    const int h = c >> 7;
+    const int d0 = c & 127;
+    float r[32];
     if (rot) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 cs = p.cs[i];  // pairs 2i and 2i+1: (cos, sin, cos, sin)
-        float a = acc[4 * i], bb = acc[4 * i + 1];
-        o[4 * i] = a * cs.x - bb * cs.y;
-        o[4 * i + 1] = bb * cs.x + a * cs.y;
-        a = acc[4 * i + 2];
-        bb = acc[4 * i + 3];
-        o[4 * i + 2] = a * cs.z - bb * cs.w;
-        o[4 * i + 3] = bb * cs.z + a * cs.w;
+      for (int i = 0; i < 16; ++i) {
+        const float a = acc[2 * i], bb = acc[2 * i + 1];
+        r[2 * i] = a * p.cs[i].x - bb * p.cs[i].y;
+        r[2 * i + 1] = bb * p.cs[i].x + a * p.cs[i].y;
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = acc[i];
+      for (int i = 0; i < 32; ++i) r[i] = acc[i];
     }
-    uint4* ptr = reinterpret_cast<uint4*>(dst + (((size_t)b * nh + h) * seq + s) * 128 + d0);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_half2(o[8 * j + 0], o[8 * j + 1]);
-      w.y = pack_half2(o[8 * j + 2], o[8 * j + 3]);
-      w.z = pack_half2(o[8 * j + 4], o[8 * j + 5]);
-      w.w = pack_half2(o[8 * j + 6], o[8 * j + 7]);
-      ptr[j] = w;
-    }
-  }
-  __device__ __forceinline__ void end_row(int, int) {}
-};
-
-// x[row, col] += alpha * acc   (fp32 residual stream, updated in place; the chunk's
-// 32 residual values are loaded one chunk ahead)
-struct EpiResidual {
-  struct Pre {
-    float4 r[8];
-  };
-  float* x;
-  int ldx;
-  float alpha;
-  __device__ __forceinline__ void begin_row(int, bool) {}
-  __device__ __forceinline__ void prefetch(int row, int col0, Pre& p) {
-    const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * ldx + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) p.r[j] = src[j];
-  }
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre& p) {
-    float4* dst = reinterpret_cast<float4*>(x + (size_t)row * ldx + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 r = p.r[j];
-      r.x += alpha * v[4 * j + 0];
-      r.y += alpha * v[4 * j + 1];
-      r.z += alpha * v[4 * j + 2];
-      r.w += alpha * v[4 * j + 3];
-      dst[j] = r;
-    }
+    for (int j = 0; j < 4; ++j) o[j] = pack8_f16(r + 8 * j);
+    dst = reinterpret_cast<uint8_t*>(base + (((size_t)b * nh + h) * seq + s) * 128 + d0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
@@ -220,22 +227,20 @@ struct EpiResidual {
 // the epilogue never waits on global loads.
 struct EpiScaledF16 {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 64;
   __half* out;
   int ldo;
   float alpha;
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
-    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col0);
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    float r[32];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_half2(alpha * v[8 * j + 0], alpha * v[8 * j + 1]);
-      w.y = pack_half2(alpha * v[8 * j + 2], alpha * v[8 * j + 3]);
-      w.z = pack_half2(alpha * v[8 * j + 4], alpha * v[8 * j + 5]);
-      w.w = pack_half2(alpha * v[8 * j + 6], alpha * v[8 * j + 7]);
-      dst[j] = w;
-    }
+    for (int i = 0; i < 32; ++i) r[i] = alpha * v[i];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pack8_f16(r + 8 * j);
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
@@ -244,17 +249,21 @@ struct EpiScaledF16 {
 // projection that is all-reduced across ranks before the residual add.
 struct EpiScaledF32 {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 128;
   float* out;
   int ldo;
   float alpha;
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
-    float4* dst = reinterpret_cast<float4*>(out + (size_t)row * ldo + col0);
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      dst[j] = make_float4(alpha * v[4 * j], alpha * v[4 * j + 1], alpha * v[4 * j + 2],
-                           alpha * v[4 * j + 3]);
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = make_float4(alpha * v[4 * j], alpha * v[4 * j + 1], alpha * v[4 * j + 2],
+                                   alpha * v[4 * j + 3]);
+      o[j] = *reinterpret_cast<const uint4*>(&w);
+    }
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
@@ -263,27 +272,22 @@ struct EpiScaledF32 {
 // g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
 struct EpiSwiglu {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 32;
   __half* g;
   int ldg;
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
-    float o[16];
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    float r[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      float h1 = v[2 * j], h3 = v[2 * j + 1];
-      o[j] = h1 / (1.0f + __expf(-h1)) * h3;
+      const float h1 = v[2 * j], h3 = v[2 * j + 1];
+      r[j] = h1 / (1.0f + __expf(-h1)) * h3;
     }
-    uint4* p = reinterpret_cast<uint4*>(g + (size_t)row * ldg + (col0 >> 1));
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      uint4 w;
-      w.x = pack_half2(o[8 * j + 0], o[8 * j + 1]);
-      w.y = pack_half2(o[8 * j + 2], o[8 * j + 3]);
-      w.z = pack_half2(o[8 * j + 4], o[8 * j + 5]);
-      w.w = pack_half2(o[8 * j + 6], o[8 * j + 7]);
-      p[j] = w;
-    }
+    o[0] = pack8_f16(r);
+    o[1] = pack8_f16(r + 8);
+    dst = reinterpret_cast<uint8_t*>(g + (size_t)row * ldg + (col0 >> 1));
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
@@ -293,6 +297,7 @@ struct EpiSwiglu {
 // softcap > 0) and, for the tile holding targets[row], that logit.
 struct EpiCrossEntropy {
   using Pre = NoPre;
+  static constexpr int OUT_BYTES = 0;
   float2* part;      // [M, nparts]
   int nparts;
   const uint32_t* targets;
@@ -307,7 +312,8 @@ struct EpiCrossEntropy {
     tgt = valid ? (int)targets[row] : -1;
   }
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&) {
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&)[8], uint8_t*&) {
     float z[32];
     float cm = -CUDART_INF_F;
 #pragma unroll
@@ -317,7 +323,7 @@ struct EpiCrossEntropy {
       z[i] = t;
       cm = fmaxf(cm, t);
     }
-    unsigned rel = (unsigned)(tgt - col0);
+    const unsigned rel = (unsigned)(tgt - col0);
     if (rel < 32u) {
       float zt = z[0];
 #pragma unroll
@@ -373,6 +379,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint8_t* epi_bufs = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -508,35 +515,37 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       Epi e = epi;
       e.begin_row(row, row_ok);
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(group * BN);
-      uint32_t ra[32], rb[32];
       typename Epi::Pre pa, pb;
+      uint8_t* wbuf = epi_bufs + (warp - 2) * Cfg::EPI_BUF_BYTES;
+      // One chunk: TMEM -> registers, epilogue math, warp-cooperative store. Global
+      // operands (Pre) are loaded one chunk ahead; the TMEM load latency is covered by
+      // the other epilogue group. col < N is warp-uniform.
+      auto do_chunk = [&](int c, const typename Epi::Pre& pre) {
+        const int col = n_blk * BN + c * 32;
+        if (col >= N) return;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait_regs(r);
+        uint4 outv[8];
+        uint8_t* dst = nullptr;
+        if (row_ok) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          e.chunk(row, col, v, pre, outv, dst);
+        }
+        if constexpr (Epi::OUT_BYTES > 0)
+          warp_store_rows<(Epi::OUT_BYTES > 0 ? Epi::OUT_BYTES : 16)>(wbuf, outv, dst, row_ok);
+      };
       const int col_base = n_blk * BN;
       if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
-      tmem_ld_32x32b_x32(t_row, ra);
-      tmem_ld_wait_regs(ra);
 #pragma unroll 1
       for (int c = 0; c < NC; c += 2) {
-        const int col_a = col_base + c * 32, col_b = col_a + 32;
-        tmem_ld_32x32b_x32(t_row + (c + 1) * 32, rb);
+        const int col_b = col_base + (c + 1) * 32;
         if (row_ok && col_b < N) e.prefetch(row, col_b, pb);
-        if (row_ok && col_a < N) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
-          e.chunk(row, col_a, v, pa);
-        }
-        tmem_ld_wait_regs(rb);
-        if (c + 2 < NC) {
-          tmem_ld_32x32b_x32(t_row + (c + 2) * 32, ra);
-          if (row_ok && col_b + 32 < N) e.prefetch(row, col_b + 32, pa);
-        }
-        if (row_ok && col_b < N) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rb[i]);
-          e.chunk(row, col_b, v, pb);
-        }
-        if (c + 2 < NC) tmem_ld_wait_regs(ra);
+        do_chunk(c, pa);
+        if (c + 2 < NC && row_ok && col_b + 32 < N) e.prefetch(row, col_b + 32, pa);
+        do_chunk(c + 1, pb);
       }
       if (row_ok) e.end_row(row, n_blk);
       tc_fence_before();
