@@ -6,18 +6,20 @@
 // One CTA = 128 queries of one (batch, head); 96 KB of shared memory and 256 TMEM
 // columns, so two CTAs share an SM. 192 threads:
 //   warp 0 lane 0 : TMA producer. Q tile once (128 x 128), then per 64-key tile j:
-//                   K_j (double-buffered) and V_j (single buffer), 128-byte swizzle.
+//                   K_j and V_j (both double-buffered), 128-byte swizzle.
 //   warp 1        : TMEM owner; lane 0 issues the UMMAs:
 //                     S_j = Q K_j^T   (M=128, N=64, K=128; A and B K-major) into one of
 //                                      two TMEM S buffers, S_{j+1} issued before P_j is
 //                                      ready so it overlaps the softmax of tile j
-//                     O  += P_j V_j   (M=128, N=128, K=64; P K-major from smem,
-//                                      V MN-major straight from its TMA tile)
+//                     O  += P_j V_j   (M=128, N=128, K=64; P read from TMEM, where it
+//                                      overwrites S_j, V MN-major from its TMA tile)
 //   warps 2..5    : softmax, one thread per query row (TMEM lane): reads its 64 scores,
 //                   applies the causal mask on the diagonal tiles, updates the running
-//                   max / sum in base 2, rescales its O row in TMEM when the max grows,
-//                   writes P (fp16) into the swizzled A-operand tile, and at the end
-//                   divides O by the row sum and stores the output row.
+//                   max / sum in base 2 (exponentials split between the MUFU and an FMA
+//                   polynomial), rescales its O row in TMEM only when the max grows past
+//                   the reference max by 2^8, writes P (fp16, packed in pairs) over its
+//                   S row in TMEM, and at the end divides O by the row sum and stores
+//                   the output row.
 // Layout: q, k, v are [batch, heads, seq, 128] fp16 (rows of a [batch*heads*seq, 128]
 // matrix for the tensor maps); out is [batch*seq, heads*128] fp16. seq % 128 == 0.
 #pragma once
@@ -36,11 +38,39 @@ constexpr int FA_THREADS = 192;
 // shared memory map (bytes from the 1024-aligned base)
 constexpr int FA_Q_OFF = 0;             // 2 x 16 KB: head dims 0-63 | 64-127, [128 rows][128 B]
 constexpr int FA_K_OFF = 32768;         // 2 buffers x (2 x 8 KB), [64 keys][128 B]
-constexpr int FA_V_OFF = 65536;         // 2 x 8 KB: head dims 0-63 | 64-127, [64 keys][128 B]
-constexpr int FA_P_OFF = 81920;         // 16 KB: [128 rows][64 keys] fp16
+constexpr int FA_V_OFF = 65536;         // 2 buffers x (2 x 8 KB): head dims 0-63 | 64-127
 constexpr int FA_BAR_OFF = 98304;
 constexpr int FA_SMEM = FA_BAR_OFF + 256 + 1024;
-constexpr uint32_t FA_TMEM_COLS = 256;  // S0 [0,64) S1 [64,128) O [128,256)
+constexpr uint32_t FA_TMEM_COLS = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
+
+// 2^x on the special-function unit (MUFU); 2^-inf = +0.
+__device__ __forceinline__ float exp2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x for x <= 0 on the FMA pipe, to share the softmax exponentials with the MUFU:
+// x = n + f with n = floor(x), f in [0, 1); 2^f by a degree-4 polynomial (a weighted
+// least-squares fit to 2^f on [0, 1), max relative error 2.6e-6, below the fp16
+// rounding of P); 2^n added to the exponent bits. Returns 0 below -126 (masked keys).
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float n = floorf(xc);
+  const float f = xc - n;
+  float p = 0.013534540310502052f;
+  p = fmaf(p, f, 0.05201074853539467f);
+  p = fmaf(p, f, 0.24144317209720612f);
+  p = fmaf(p, f, 0.69300377368927f);
+  p = fmaf(p, f, 1.0000026226043701f);
+  const float r = __int_as_float(__float_as_int(p) + ((int)n << 23));
+  return x < -126.0f ? 0.0f : r;
+}
+
+// The O accumulator and row sum keep a stale reference max until the running max
+// exceeds it by this much (base-2 log): P values stay <= 2^8, and most tiles skip
+// the TMEM read-scale-write of O.
+constexpr float FA_RESCALE_THRESHOLD = 8.0f;
 
 __global__ void __launch_bounds__(FA_THREADS, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -54,13 +84,13 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 12;
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -78,8 +108,10 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
     mbar_init(&k_full[1], 1);
     mbar_init(&k_empty[0], 1);
     mbar_init(&k_empty[1], 1);
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
+    mbar_init(&v_full[0], 1);
+    mbar_init(&v_full[1], 1);
+    mbar_init(&v_empty[0], 1);
+    mbar_init(&v_empty[1], 1);
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 4);
@@ -118,10 +150,12 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       bool ok = load_k(0);
       for (int j = 0; j < n_kv && ok; ++j) {
         if (j + 1 < n_kv && !load_k(j + 1)) break;
-        if (!mbar_wait(v_empty, (j & 1) ^ 1u, err)) break;
-        mbar_arrive_expect_tx(v_full, 16384);
-        tma_load_2d(smem + FA_V_OFF, &tmV, v_full, 0, kv_row0 + j * FA_BKV);
-        tma_load_2d(smem + FA_V_OFF + 8192, &tmV, v_full, 64, kv_row0 + j * FA_BKV);
+        const int vb = j & 1;
+        if (!mbar_wait(&v_empty[vb], ((j >> 1) & 1) ^ 1u, err)) break;
+        mbar_arrive_expect_tx(&v_full[vb], 16384);
+        uint8_t* vdst = smem + FA_V_OFF + vb * 16384;
+        tma_load_2d(vdst, &tmV, &v_full[vb], 0, kv_row0 + j * FA_BKV);
+        tma_load_2d(vdst + 8192, &tmV, &v_full[vb], 64, kv_row0 + j * FA_BKV);
       }
     }
   } else if (warp == 1) {
@@ -132,7 +166,6 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       const uint32_t q_addr = smem_u32(smem + FA_Q_OFF);
       const uint32_t k_addr = smem_u32(smem + FA_K_OFF);
       const uint32_t v_addr = smem_u32(smem + FA_V_OFF);
-      const uint32_t p_addr = smem_u32(smem + FA_P_OFF);
       auto issue_s = [&](int j) -> bool {
         const int kb = j & 1;
         if (!mbar_wait(&k_full[kb], (j >> 1) & 1, err)) return false;
@@ -152,15 +185,18 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       bool ok = mbar_wait(q_full, 0, err) && issue_s(0);
       for (int j = 0; j < n_kv && ok; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        const int vb = j & 1;
         if (!mbar_wait(p_full, j & 1, err)) break;
-        if (!mbar_wait(v_full, j & 1, err)) break;
+        if (!mbar_wait(&v_full[vb], (j >> 1) & 1, err)) break;
         tc_fence_after();
+        const uint32_t p_tmem = t_s0 + (uint32_t)(vb * FA_BKV);  // P_j over S_j's columns
 #pragma unroll
-        for (int k = 0; k < FA_BKV / 16; ++k) {  // keys in steps of 16
-          umma_f16_ss(t_o, sw128_kmajor_desc(p_addr + k * 32),
-                      sw128_mnmajor_desc(v_addr + k * 2048, 8192), idesc_pv, (j | k) != 0);
+        for (int k = 0; k < FA_BKV / 16; ++k) {  // keys in steps of 16 (8 packed columns)
+          umma_f16_ts(t_o, p_tmem + k * 8,
+                      sw128_mnmajor_desc(v_addr + vb * 16384 + k * 2048, 8192), idesc_pv,
+                      (j | k) != 0);
         }
-        umma_commit(v_empty);
+        umma_commit(&v_empty[vb]);
         umma_commit(pv_done);
       }
       umma_commit(drain);
@@ -172,7 +208,6 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int q_idx = qt * FA_BQ + r;
-    uint8_t* p_row = smem + FA_P_OFF + r * 128;
     float m_run = -CUDART_INF_F, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -184,11 +219,13 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       tmem_ld_32x32b_x32(t_s0 + lane_off + (uint32_t)(kb * FA_BKV + 32), sb);
       tmem_ld_wait_regs(sa);
       tmem_ld_wait_regs(sb);
+      // Raw scores; the scale (> 0) commutes with max, so it is folded into the
+      // exponent argument. Reductions use 8 independent accumulators (short chains).
       float s[64];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        s[i] = __uint_as_float(sa[i]) * scale_log2;
-        s[32 + i] = __uint_as_float(sb[i]) * scale_log2;
+        s[i] = __uint_as_float(sa[i]);
+        s[32 + i] = __uint_as_float(sb[i]);
       }
       const int key0 = j * FA_BKV;
       if (key0 + FA_BKV - 1 > q_idx) {  // diagonal tile: mask keys after the query
@@ -196,24 +233,47 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
         for (int i = 0; i < 64; ++i)
           if (key0 + i > q_idx) s[i] = -CUDART_INF_F;
       }
-      float mx = s[0];
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
-      const float m_new = fmaxf(m_run, mx);
-      float sum = 0.f;
+      for (int a = 0; a < 8; ++a) m8[a] = s[a];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = exp2f(s[i] - m_new);
-        sum += s[i];
+      for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
+      // Lazy rescaling: move the reference max only when it is exceeded by the threshold.
+      float corr = 1.0f;
+      bool need = false;
+      if (j == 0) {
+        m_run = mx;  // tile 0 always holds key 0 <= every query, so mx is finite
+      } else if (mx > m_run + FA_RESCALE_THRESHOLD) {
+        need = true;
+        corr = exp2_mufu(m_run - mx);
+        m_run = mx;
+        l_run *= corr;
       }
-      const float corr = exp2f(m_run - m_new);
-      l_run = l_run * corr + sum;
-      m_run = m_new;
+      const float neg_m = -m_run;
+      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        s[i] = exp2_mufu(fmaf(s[i], scale_log2, neg_m));
+        s[i + 1] = exp2_fma(fmaf(s[i + 1], scale_log2, neg_m));
+        l8[(i >> 1) & 7] += s[i] + s[i + 1];
+      }
+      const float sum = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      l_run += sum;
+      // P_j (fp16 pairs) over the first 32 columns of this row of S_j. PV_{j-1} reads
+      // the other buffer, and S_{j+2} is issued after PV_j, so nothing else uses them.
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+        tmem_st_32x32b_x32(t_s0 + lane_off + (uint32_t)(kb * FA_BKV), pk);
+      }
       if (j > 0) {
-        // P_{j-1} has been consumed and O holds P_{0..j-1} V: rescale it if needed.
+        // O holds P_{0..j-1} V once PV_{j-1} is done: rescale it if needed.
         if (!mbar_wait(pv_done, (j - 1) & 1, err)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, corr != 1.0f)) {
+        if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -223,20 +283,9 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
             tmem_st_32x32b_x32(t_o + lane_off + c * 32, o);
           }
-          tmem_st_wait();
         }
       }
-      // P row -> swizzled K-major A tile (16-byte chunk c of row r at c ^ (r & 7)).
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = pack_half2(s[8 * c + 0], s[8 * c + 1]);
-        w.y = pack_half2(s[8 * c + 2], s[8 * c + 3]);
-        w.z = pack_half2(s[8 * c + 4], s[8 * c + 5]);
-        w.w = pack_half2(s[8 * c + 6], s[8 * c + 7]);
-        *reinterpret_cast<uint4*>(p_row + ((c ^ (r & 7)) << 4)) = w;
-      }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
