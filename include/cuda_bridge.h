@@ -189,7 +189,11 @@ const char* cb_create_error(void);
  * micro-benchmarks; they sit below the model API). -------------------------- */
 
 /* C[M,N] = A[M,K] * B[N,K]^T with fp16 A/B (K contiguous) on the tcgen05 GEMM.
- * out_f32 = 0: C is fp16; 1: C is f32. block_n selects the tile: 0 = automatic,
+ * out_f32 = 0: C is fp16; 1: C is f32; 2: C is f32 and is accumulated into
+ * (C += A * B^T), with K split in two halves whose partial tiles are added
+ * atomically (the split-K path of the row-parallel projections; the order of the
+ * two adds is not fixed, so results may differ in the last bit between calls).
+ * block_n selects the tile: 0 = automatic,
  * 128 or 256 = one CTA per 128 x block_n tile, 2 = a CTA pair per 256 x 256 tile
  * (needs N % 256 == 0, else 128 is used). K % 64 == 0, N % 32 == 0, 16-byte aligned
  * pointers. Enqueued on `stream` (NULL = default stream). */

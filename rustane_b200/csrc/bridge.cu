@@ -176,6 +176,7 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiQkvRope>();
   set_gemm_attrs_for<EpiScaledF16>();
   set_gemm_attrs_for<EpiScaledF32>();
+  set_gemm_attrs_for<EpiScaledF32Add>();
   set_gemm_attrs_for<EpiSwiglu>();
   set_gemm_attrs_for<EpiCrossEntropy>();
   cudaFuncSetAttribute(attn_fwd_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -229,22 +230,23 @@ int num_sms_of(int device) { return device_info(device).sms; }
 
 template <int BN, class Epi>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                           int bz, const Epi& epi, int* err, int units, cudaStream_t st) {
-  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+                           int bz, const Epi& epi, int* err, int units, int splits,
+                           cudaStream_t st) {
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
-  gemm_tn_kernel<BN, Epi><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K,
-                                                                               bz, epi, err);
+  gemm_tn_kernel<BN, Epi><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(
+      ta, tb, M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
 
 template <class Epi>
 cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
-                             int K, int bz, const Epi& epi, int* err, int clusters,
+                             int K, int bz, const Epi& epi, int* err, int clusters, int splits,
                              cudaStream_t st) {
-  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
   gemm_tn_pair_kernel<Epi><<<2 * pairs, GEMM_THREADS, GemmCfg<256, true>::SMEM_BYTES, st>>>(
-      ta, tb_half, M, N, K, bz, epi, err);
+      ta, tb_half, M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
 
@@ -281,12 +283,47 @@ int mode_block_n(int mode) { return mode == GM_SINGLE128 ? 128 : 256; }
 template <class Epi>
 cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
-                        int* err, const DeviceInfo& di, cudaStream_t st) {
+                        int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1) {
   if (mode == GM_PAIR)
-    return launch_gemm_pair(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters, st);
+    return launch_gemm_pair(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters, splits, st);
   if (mode == GM_SINGLE128)
-    return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, di.sms, st);
-  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, di.sms, st);
+    return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st);
+  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st);
+}
+
+// Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
+// accumulate: split-K = 2 doubles the work units when the tiles alone leave the last
+// wave mostly empty (few tokens per GPU). CB_GEMM_SPLIT=1|2 forces the split.
+void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* splits) {
+  static const int forced_split = [] {
+    const char* e = getenv("CB_GEMM_SPLIT");
+    return e ? atoi(e) : 0;
+  }();
+  auto fill = [](long tiles, long units) {
+    long waves = (tiles + units - 1) / units;
+    return (double)tiles / (double)(waves * units);
+  };
+  const bool n256 = (N % 256) == 0;
+  const long kb = (K + GEMM_BK - 1) / GEMM_BK;
+  double best = -1.0;
+  for (int sp = 1; sp <= 2; ++sp) {
+    if (forced_split && sp != forced_split) continue;
+    // The zeroing and the fp32 atomics cost about as much as a 16-k-block half saves:
+    // only long reductions (the down projection) split.
+    if (!forced_split && sp == 2 && kb < 32) continue;
+    const double sp_cost = sp == 2 ? 0.93 : 1.0;  // zeroing + fp32 atomics
+    struct Cand { int mode; double score; };
+    const Cand cands[3] = {
+        {GM_PAIR, n256 ? fill((long)((M + 255) / 256) * (N / 256) * sp, di.pair_clusters) : 0.0},
+        {GM_SINGLE256, n256 ? 0.85 * fill((long)((M + 127) / 128) * (N / 256) * sp, di.sms) : 0.0},
+        {GM_SINGLE128, 0.78 * fill((long)((M + 127) / 128) * ((N + 127) / 128) * sp, di.sms)}};
+    for (const Cand& c : cands)
+      if (c.score * sp_cost > best) {
+        best = c.score * sp_cost;
+        *mode = c.mode;
+        *splits = sp;
+      }
+  }
 }
 
 // Causal attention: tcgen05 kernel when seq is a multiple of 128 (tensor maps given),
@@ -524,18 +561,26 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
 
   const DeviceInfo& di = device_info(c->device);
   const int m_qkv = pick_mode(T, c->n_qkv, di);
-  const int m_o = pick_mode(T, d, di);
+  int m_o, s_o, m_2, s_2;
+  pick_projection(T, d, c->q_dim, di, &m_o, &s_o);
+  pick_projection(T, d, hid, di, &m_2, &s_2);
   const int m_13 = pick_mode(T, 2 * hid, di);
-  const int m_2 = pick_mode(T, d, di);
   const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
-  const double norm_bytes = Td * d * (4 + (tp ? 4 : 2) + 4 + 2);
 
-  // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer; under
-  // tensor parallelism the fp32 partials are summed across ranks (NCCL all-reduce).
-  auto project = [&](int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
+  // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer. fp16
+  // by default; fp32 when K is split in two (atomic adds into a zeroed buffer) or under
+  // tensor parallelism, where the fp32 partials are summed across ranks (NCCL).
+  bool delta_f32 = false;
+  auto project = [&](int mode, int splits, const CUtensorMap& ta, const CUtensorMap& tb128,
                      const CUtensorMap& tb256, int K, int layer, int cls) -> cudaError_t {
     cudaError_t r;
-    if (tp) {
+    delta_f32 = tp || splits > 1;
+    if (splits > 1) {
+      r = cudaMemsetAsync(c->delta32, 0, (size_t)T * d * sizeof(float), st);
+      if (r != cudaSuccess) return r;
+      EpiScaledF32Add ep{c->delta32, d, alpha};
+      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, splits);
+    } else if (tp) {
       EpiScaledF32 ep{c->delta32, d, alpha};
       r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st);
     } else {
@@ -543,7 +588,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
       r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st);
     }
     if (r != cudaSuccess) return r;
-    mark(cls, 2.0 * Td * d * K, Td * K * 2 + (double)d * K * 2 + Td * d * (tp ? 4 : 2));
+    mark(cls, 2.0 * Td * d * K,
+         Td * K * 2 + (double)d * K * 2 + Td * d * (delta_f32 ? 4 * splits : 2));
     if (tp) {
       ncclResult_t nr = nccl_api().all_reduce(c->delta32, c->delta32, (size_t)T * d, ncclFloat32,
                                               ncclSum, c->comm, st);
@@ -556,9 +602,9 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     return cudaSuccess;
   };
   auto add_norm = [&](const float* gamma) -> cudaError_t {
-    cudaError_t r = tp ? launch_add_rmsnorm(c->x, c->delta32, gamma, c->xn, T, d, st)
-                       : launch_add_rmsnorm(c->x, c->delta, gamma, c->xn, T, d, st);
-    if (r == cudaSuccess) mark(K_RMSNORM, 0, norm_bytes);
+    cudaError_t r = delta_f32 ? launch_add_rmsnorm(c->x, c->delta32, gamma, c->xn, T, d, st)
+                              : launch_add_rmsnorm(c->x, c->delta, gamma, c->xn, T, d, st);
+    if (r == cudaSuccess) mark(K_RMSNORM, 0, Td * d * (4 + (delta_f32 ? 4 : 2) + 4 + 2));
     return r;
   };
 
@@ -578,7 +624,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
                          c->heads_l, c->kv_heads_l, S, c->dev_err, st);
     if (e != cudaSuccess) return e;
     mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
-    e = project(m_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O);
+    e = project(m_o, s_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O);
     if (e != cudaSuccess) return e;
     if ((e = add_norm(c->gamma + (size_t)l * 2 * d + d)) != cudaSuccess) return e;
     {
@@ -588,7 +634,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
-    e = project(m_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2);
+    e = project(m_2, s_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2);
     if (e != cudaSuccess) return e;
   }
   if ((e = add_norm(c->gamma_final)) != cudaSuccess) return e;
@@ -869,7 +915,7 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(dmalloc(&ctx->attn, T * ctx->q_dim));
   CREATE_CUDA(dmalloc(&ctx->g, T * hid));
   CREATE_CUDA(dmalloc(&ctx->delta, T * d));
-  if (tp_world > 1) CREATE_CUDA(dmalloc(&ctx->delta32, T * d));
+  CREATE_CUDA(dmalloc(&ctx->delta32, T * d));
   CREATE_CUDA(dmalloc(&ctx->ce_part, T * ((V + 127) / 128)));
   CREATE_CUDA(dmalloc(&ctx->tgt_logit, T));
   CREATE_CUDA(dmalloc(&ctx->tok_loss, T));
@@ -1302,7 +1348,7 @@ cb_status cb_get_stream(cb_ctx* ctx, void** stream) {
 cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N, int32_t K,
                       int32_t out_f32, int32_t block_n, void* stream) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return CB_ERR_INVALID_ARG;
-  if (K % 64 != 0 || N % 32 != 0) return CB_ERR_INVALID_ARG;
+  if (K % 64 != 0 || N % 32 != 0 || out_f32 < 0 || out_f32 > 2) return CB_ERR_INVALID_ARG;
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return CB_ERR_INVALID_ARG;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
@@ -1319,7 +1365,10 @@ cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t 
     return CB_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (out_f32) {
+  if (out_f32 == 2) {
+    EpiScaledF32Add ep{static_cast<float*>(C), N, 1.f};
+    e = launch_gemm(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di, st, K >= 128 ? 2 : 1);
+  } else if (out_f32) {
     EpiStoreF32 ep{static_cast<float*>(C), N, 0.f};
     e = launch_gemm(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di, st);
   } else {

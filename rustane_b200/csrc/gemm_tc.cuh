@@ -75,6 +75,11 @@ struct GemmCfg {
 // different rows (4-8x fewer L1 wavefronts).
 struct NoPre {};
 
+template <class Epi, class = void>
+struct EpiAtomic { static constexpr bool value = false; };
+template <class Epi>
+struct EpiAtomic<Epi, decltype(void(Epi::ATOMIC))> { static constexpr bool value = Epi::ATOMIC; };
+
 __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   uint4 w;
   w.x = pack_half2(f[0], f[1]);
@@ -87,7 +92,7 @@ __device__ __forceinline__ uint4 pack8_f16(const float* f) {
 // Warp-cooperative transposed store of 32 row segments of NB bytes (32, 64 or 128):
 // lane L owns row L's segment (out[0 .. NB/16)) and its address; `wbuf` is this warp's
 // 32*NB-byte shared buffer. Pieces are XOR-swizzled so both phases are conflict-free.
-template <int NB>
+template <int NB, bool ATOMIC_ADD = false>
 __device__ __forceinline__ void warp_store_rows(uint8_t* wbuf, const uint4 (&out)[8],
                                                 uint8_t* dst, bool ok) {
   constexpr int Q = NB / 16;       // 16-byte pieces per row
@@ -106,7 +111,13 @@ __device__ __forceinline__ void warp_store_rows(uint8_t* wbuf, const uint4 (&out
     const unsigned long long base = __shfl_sync(0xffffffffu, my, r);
     const int swr = (r / (8 / Q)) & (Q - 1);
     const uint4 x = *reinterpret_cast<const uint4*>(wbuf + r * NB + ((j ^ swr) << 4));
-    if (base) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(base) + (j << 4)) = x;
+    if (base) {
+      uint8_t* p = reinterpret_cast<uint8_t*>(base) + (j << 4);
+      if constexpr (ATOMIC_ADD)  // four fp32 lanes added in L2 (sm_90+ vector atomic)
+        atomicAdd(reinterpret_cast<float4*>(p), *reinterpret_cast<const float4*>(&x));
+      else
+        *reinterpret_cast<uint4*>(p) = x;
+    }
   }
   __syncwarp();
 }
@@ -268,6 +279,31 @@ struct EpiScaledF32 {
   __device__ __forceinline__ void end_row(int, int) {}
 };
 
+// delta[row, col] += alpha * acc (fp32 vector atomics into a zeroed buffer): the
+// split-K form of the O / down projection, used when the tile count alone fills the
+// GPU poorly. Exactly two K halves add onto zero, so the sum is order-independent.
+struct EpiScaledF32Add {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 128;
+  static constexpr bool ATOMIC = true;
+  float* out;
+  int ldo;
+  float alpha;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = make_float4(alpha * v[4 * j], alpha * v[4 * j + 1], alpha * v[4 * j + 2],
+                                   alpha * v[4 * j + 3]);
+      o[j] = *reinterpret_cast<const uint4*>(&w);
+    }
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
 // B rows interleave W1 and W3 columns: row 2j = W1[:, j], row 2j+1 = W3[:, j].
 // g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
 struct EpiSwiglu {
@@ -362,8 +398,8 @@ struct EpiCrossEntropy {
 
 template <int BN, bool PAIR, class Epi>
 __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
-                                             int M, int N, int K, int b_z, const Epi& epi,
-                                             int* err) {
+                                             int M, int N, int K, int b_z, int splits,
+                                             const Epi& epi, int* err) {
   using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int TILE_M = Cfg::TILE_M;
@@ -388,8 +424,11 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int m_tiles = (M + TILE_M - 1) / TILE_M;
   const int n_tiles = (N + BN - 1) / BN;
-  const int num_tiles = m_tiles * n_tiles;
-  const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
+  // Work unit = (tile, K split): unit u covers tile u / splits and k-blocks
+  // [split * kb_per, ...) of it. splits > 1 only with an accumulating epilogue.
+  const int num_tiles = m_tiles * n_tiles * splits;
+  const int kb_total = (K + GEMM_BK - 1) / GEMM_BK;
+  const int kb_per = (kb_total + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -427,10 +466,13 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       const uint64_t pol_b = policy_evict_last();
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
+      for (int u = unit; u < num_tiles && ok; u += n_units) {
+        const int tile = u / splits;
+        const int kb0 = (u % splits) * kb_per;
+        const int kb1 = min(kb0 + kb_per, kb_total);
         const int m0 = (tile / n_tiles) * TILE_M + (int)rank * GEMM_BM;
         const int n0 = (tile % n_tiles) * BN + (int)rank * Cfg::B_ROWS;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, err)) { ok = false; break; }
@@ -462,11 +504,13 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
+      for (int u = unit; u < num_tiles && ok; u += n_units) {
+        const int kb0 = (u % splits) * kb_per;
+        const int kb1 = min(kb0 + kb_per, kb_total);
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&full[s], ph, err)) { ok = false; break; }
@@ -477,7 +521,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
           for (int k = 0; k < GEMM_BK / 16; ++k) {
             const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
             const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
-            const uint32_t accum = (kb | k) != 0;
+            const uint32_t accum = (kb != kb0) || (k != 0);
             if (PAIR) umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
             else umma_f16_ss(d_tmem, ad, bd, idesc, accum);
           }
@@ -503,8 +547,9 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         PAIR ? mapa_shared(smem_u32(&tempty[group]), 0) : smem_u32(&tempty[group]);
     uint32_t ph = 0;
     int it = 0;
-    for (int tile = unit; tile < num_tiles; tile += n_units, ++it) {
+    for (int u = unit; u < num_tiles; u += n_units, ++it) {
       if ((it & 1) != group) continue;
+      const int tile = u / splits;
       const int m_blk = tile / n_tiles;
       const int n_blk = tile % n_tiles;
       if (!mbar_wait(&tfull[group], ph, err)) break;
@@ -535,7 +580,8 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
           e.chunk(row, col, v, pre, outv, dst);
         }
         if constexpr (Epi::OUT_BYTES > 0)
-          warp_store_rows<(Epi::OUT_BYTES > 0 ? Epi::OUT_BYTES : 16)>(wbuf, outv, dst, row_ok);
+          warp_store_rows<(Epi::OUT_BYTES > 0 ? Epi::OUT_BYTES : 16), EpiAtomic<Epi>::value>(
+              wbuf, outv, dst, row_ok);
       };
       const int col_base = n_blk * BN;
       if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
@@ -571,16 +617,16 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
 template <int BN, class Epi>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, int b_z, Epi epi, int* err) {
-  gemm_tn_body<BN, false, Epi>(&tmA, &tmB, M, N, K, b_z, epi, err);
+                   int M, int N, int K, int b_z, int splits, Epi epi, int* err) {
+  gemm_tn_body<BN, false, Epi>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
 }
 
 template <class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int b_z,
-                        Epi epi, int* err) {
-  gemm_tn_body<256, true, Epi>(&tmA, &tmB, M, N, K, b_z, epi, err);
+                        int splits, Epi epi, int* err) {
+  gemm_tn_body<256, true, Epi>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
 }
 
 }  // namespace cb

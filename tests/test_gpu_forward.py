@@ -129,6 +129,44 @@ def test_gamma_is_applied(bridge_lib):
     assert abs(loss - l_ref) / l_ref <= LOSS_RTOL
 
 
+_SPLIT_CHILD = """
+import json, sys
+import numpy as np
+from oracle.oracle import OracleModel, SCHEME_NORMAL
+from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
+from rustane_b200.model import custom_config
+cfg = custom_config(512, 1024, 4, 2, 128, 2048).replace(kv_heads=2)
+rng = np.random.default_rng(7)
+tok = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+tgt = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+ref = OracleModel(cfg, seed=5, scheme=SCHEME_NORMAL, sigma=0.05).forward(tok, tgt, 0.0)[0]
+with CompiledKernels(cfg, 0, 2) as k:
+    k.init_weights(5, CB_INIT_NORMAL, 0.05)
+    a = k.forward_loss(tok, tgt)
+    b = k.forward_loss(tok, tgt)
+print(json.dumps({"ref": ref, "a": a, "b": b}))
+"""
+
+
+@pytest.mark.parametrize("split", ["1", "2"])
+def test_forced_projection_split_parity(bridge_lib, split):
+    """The O and down projections with K split in two (atomic fp32 accumulation into a
+    zeroed buffer) give the oracle's loss, and, with exactly two partial sums per
+    element, the same bits on every call. The split is forced through CB_GEMM_SPLIT,
+    read once per process, hence the child process."""
+    import os
+    import subprocess
+    import sys
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, CB_GEMM_SPLIT=split)
+    r = subprocess.run([sys.executable, "-c", _SPLIT_CHILD], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["a"] == out["b"]
+    assert abs(out["a"] - out["ref"]) / abs(out["ref"]) <= LOSS_RTOL, out
+
+
 def test_deterministic_and_batch_consistent(bridge_lib):
     cfg = custom_config(512, 1024, 4, 2, 256, 2048)
     tok, tgt = _tokens(cfg, 4, 12)

@@ -47,6 +47,26 @@ def test_gemm_matches_torch(bridge_lib, M, N, K, bn):
     torch.testing.assert_close(c16.float(), ref, rtol=2e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("M,N,K,bn", [
+    (128, 128, 128, 128),       # two k-blocks: one per half
+    (300, 256, 192, 256),       # odd k-block count: halves of 2 and 1, ragged M
+    (4096, 1536, 1536, 2),      # the O projection at 4096 tokens per GPU
+    (4096, 1536, 4096, 0),      # the down projection, automatic tile
+    (1000, 1536, 4096, 2),      # ragged M on the CTA pair
+])
+def test_gemm_split_k_accumulates(bridge_lib, M, N, K, bn):
+    """out_f32 = 2: C += A * B^T with the K range split across two work units per tile."""
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + K)
+    a = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.25).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.25).half()
+    c0 = torch.randn(M, N, device="cuda", generator=g)
+    ref = c0 + a.float() @ b.float().T
+    c = c0.clone()
+    assert bridge_lib.cb_gemm_f16(_ptr(a), _ptr(b), _ptr(c), M, N, K, 2, bn, _stream()) == 0
+    torch.cuda.synchronize()
+    torch.testing.assert_close(c, ref, rtol=1e-4, atol=1e-3)
+
+
 def test_gemm_rejects_bad_shapes(bridge_lib):
     a = torch.zeros(128, 96, device="cuda", dtype=torch.float16)
     assert bridge_lib.cb_gemm_f16(_ptr(a), _ptr(a), _ptr(a), 128, 128, 96, 0, 0, None) == \
