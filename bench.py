@@ -40,9 +40,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "forward tokens/sec (ms/forward, seq512) at 1/2/4/8 B200; % of fp16 TC peak"
 GEMM_CLASSES = ("gemm_qkv_rope", "gemm_o", "gemm_w13_swiglu", "gemm_w2", "gemm_lmhead_ce")
-# DRAM bytes per GEMM launch measured by ncu (profiles/gemm_tc_600m-A_dram.md):
-# the 81 GEMM launches of one forward. None until measured.
-GEMM_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch, averaged
+# over the 81 GEMM launches of one forward, from one ncu capture of this bench's own
+# workload (profiles/gemm_tc_600m-A_b64_dram.md), keyed by (config, sequences per GPU).
+GEMM_TRAFFIC_PER_LAUNCH = {("600m-A", 64): 400.07e6}
+GEMM_TRAFFIC_SOURCE = "profiles/gemm_tc_600m-A_b64_dram.md"
 
 
 def parse_args():
@@ -62,6 +64,10 @@ def parse_args():
                    help="CPU-baseline sample budget (seconds of oracle work)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", choices=("forward", "validate", "rstk-load"), default="forward",
+                   help="forward: the headline forward+loss step; validate: the evaluation "
+                        "loop over an HBM-resident uint16 token file (val_loss + val_bpb); "
+                        "rstk-load: RSTK checkpoint file -> fp16 device weights (1 GPU)")
     return p.parse_args()
 
 
@@ -197,12 +203,112 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_io_workload(args):
+    """The evaluation-path rows on one GPU (host wall clock around synchronous
+    public calls, i.e. end to end): `validate` times cb_eval_windows over a
+    synthetic uint16 token file (uniform ids, 0-byte special tokens) resident in
+    HBM; `rstk-load` times cb_load_rstk of a synthetic N(0, 0.02) checkpoint
+    (page-cache warm, as after a save) and, beside it, the f32 host-array upload."""
+    import tempfile
+
+    import torch
+    from rustane_b200 import (CB_INIT_NORMAL, CompiledKernels, DeviceTokens, LayerWeights,
+                              ModelWeights, TokenBytes)
+    from rustane_b200.checkpoint import save_checkpoint
+    from rustane_b200.model import CONFIGS
+
+    if args.gpus != 1:
+        raise SystemExit("--workload validate / rstk-load run on one GPU")
+    torch.cuda.set_device(0)
+    torch.zeros(1, device="cuda")  # the CUDA context exists before any timed call
+    cfg = CONFIGS[args.config]
+    rng = np.random.default_rng(args.seed)
+    tmp = Path(tempfile.mkdtemp(prefix="rustane_bench_"))
+    clocks = ClockSampler(0)
+    if args.workload == "validate":
+        batch = args.global_batch
+        n_tok = 64 << 20  # 128 MB token file (larger than L2)
+        path = tmp / "val.bin"
+        path.write_bytes(rng.integers(0, cfg.vocab, n_tok, dtype=np.uint16).tobytes())
+        table = rng.integers(1, 9, cfg.vocab).astype(np.int32)
+        table[:4] = 0
+        tb = TokenBytes(table)
+        t0 = time.perf_counter()
+        data = DeviceTokens.open(path, 0)
+        t_open = time.perf_counter() - t0
+        k = CompiledKernels(cfg, 0, batch)
+        k.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
+        windows = batch * args.steps
+        k.eval_windows(data, tb, 0, batch * args.warmup)
+        clocks.start()
+        t0 = time.perf_counter()
+        tot = k.eval_windows(data, tb, 0, windows)
+        dt = time.perf_counter() - t0
+        clk = clocks.stop()
+        line = {
+            "metric": "validation tokens/s (cb_eval_windows: windows gathered from an "
+                      "HBM-resident uint16 token file, val_loss and val_bpb sums on device)",
+            "value": tot["tokens"] / dt, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "dtype": "fp16", "data": "synthetic uniform token ids",
+            "config": {"workload": f"{args.config} validate, {batch} windows of seq "
+                                   f"{cfg.seq} per forward, {windows} windows",
+                       "token_file_tokens": n_tok,
+                       "token_file_load_gbs": n_tok * 2 / t_open / 1e9},
+            "val_loss": tot["loss_sum"] / tot["tokens"],
+            "val_bpb": tot["nats"] / (np.log(2) * tot["bytes"]), "clocks": clk,
+        }
+        data.close()
+    else:
+        d, h = cfg.dim, cfg.hidden
+        qd, kvd = cfg.heads * cfg.hd, cfg.kv_heads * cfg.hd
+
+        def f(*shape):
+            return (rng.standard_normal(shape, dtype=np.float32) * 0.02)
+
+        layers = [LayerWeights(wq=f(d, qd), wk=f(d, kvd), wv=f(d, kvd), wo=f(qd, d),
+                               w1=f(d, h), w3=f(d, h), w2=f(d, h), gamma1=np.ones(d, np.float32),
+                               gamma2=np.ones(d, np.float32)) for _ in range(cfg.nlayers)]
+        w = ModelWeights.from_arrays(f(cfg.vocab, d), layers, np.ones(d, np.float32))
+        path = save_checkpoint(cfg, w, 1, tmp)
+        nbytes = path.stat().st_size
+        k = CompiledKernels(cfg, 0, 1)
+        for _ in range(args.warmup):
+            k.load_checkpoint(path)
+        clocks.start()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            k.load_checkpoint(path)
+        dt = (time.perf_counter() - t0) / args.steps
+        clk = clocks.stop()
+        t0 = time.perf_counter()
+        k.load_weights(w)
+        dt_host = time.perf_counter() - t0
+        line = {
+            "metric": "RSTK checkpoint load GB/s (cb_load_rstk: f32 file -> fp16 device "
+                      "weights, pinned double-buffered streaming)",
+            "value": nbytes / dt / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "dtype": "f32->fp16", "data": "synthetic N(0, 0.02) checkpoint, page cache warm",
+            "config": {"workload": f"{args.config} RSTK checkpoint", "file_bytes": nbytes,
+                       "host_array_upload_gbs": nbytes / dt_host / 1e9},
+            "clocks": clk,
+        }
+    k.close()
+    import shutil
+    shutil.rmtree(tmp, ignore_errors=True)
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.global_batch is None:
         args.global_batch = 16 if args.config == "32B" else 64
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload != "forward":
+        run_io_workload(args)
         return
 
     import torch
@@ -333,7 +439,9 @@ def main():
         "flops_per_launch": g_flops / max(g_launch, 1),
         "ms_per_launch": g_ms / max(g_launch, 1),
         "share_of_step": round(g_ms / all_ms, 4) if all_ms > 0 else None,
-        "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+        "traffic": None if args.tp else GEMM_TRAFFIC_PER_LAUNCH.get((args.config, per)),
+        "traffic_unit": "bytes per launch",
+        "traffic_source": GEMM_TRAFFIC_SOURCE,
     }
     flops_fwd = cfg.forward_flops_per_token() * args.global_batch * cfg.seq
     kernels = {k: {"launches": v["launches"], "ms": round(v["total_ms"], 3),

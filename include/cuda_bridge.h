@@ -170,6 +170,66 @@ cb_status cb_check_device_error(cb_ctx* ctx);
  * the last forward's softcap applied. Synchronous. */
 cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, float* logits_out);
 
+/* ---- Checkpoints and token data (the training binary's I/O:
+ * crates/engine/src/bin/train.rs, crates/engine/src/data.rs). ---------------- */
+
+/* Loads an RSTK checkpoint (the format written by save_checkpoint,
+ * train.rs:238-273, read by load_checkpoint, train.rs:297-346) straight into the
+ * context's fp16 device weights: a 28-byte header (magic "RSTK", then u32 LE
+ * version, step, dim, nlayers, vocab, seq) followed by f32 LE tensors in the
+ * order embed, gamma_final, then per layer wq, wk, wv, wo, w1, w3, w2, gamma1,
+ * gamma2 (reference orientation, as cb_load_weights_f32). The file is streamed
+ * through pinned chunks; no host copy of the model is made. Where the reference
+ * panics (bad magic) or misreads (header dims that differ from the config, a
+ * short file) this returns CB_ERR_INVALID_ARG. Bytes after the last tensor are
+ * ignored, as in the reference. step_out (nullable) receives the header step.
+ * Tensor-parallel contexts keep their own slice of each tensor. Synchronous. */
+cb_status cb_load_rstk(cb_ctx* ctx, const char* path, uint32_t* step_out);
+
+/* A uint16 token array resident in one device's HBM: the B200 form of TokenData
+ * (data.rs:11-44), which memory-maps the file. A file of 1e9 tokens takes 2 GB. */
+typedef struct cb_tokens cb_tokens;
+
+/* Reads a flat uint16 LE token file (data.rs:17-28; n = file bytes / 2) into
+ * device memory on `device`. On failure *out is NULL and cb_create_error()
+ * describes it. */
+cb_status cb_tokens_open(const char* path, int32_t device, cb_tokens** out);
+/* The same from host memory (n tokens). */
+cb_status cb_tokens_from_host(const uint16_t* tokens, int64_t n, int32_t device,
+                              cb_tokens** out);
+cb_status cb_tokens_len(const cb_tokens* data, int64_t* n);
+cb_status cb_tokens_close(cb_tokens* data);
+
+/* One forward over `batch` windows of a device token array: sequence b has
+ * tokens data[positions[b] .. + seq) and targets data[positions[b] + 1 .. + seq]
+ * (train.rs:556-558 `tokens(pos, seq)`, `tokens(pos + 1, seq)`). positions is a
+ * host array of `batch` offsets with positions[b] + seq + 1 <= n. The windows
+ * are gathered on the device; the data never returns to the host. Token ids >=
+ * vocab give CB_ERR_INVALID_ARG. Outputs as cb_forward_loss. Synchronous. */
+cb_status cb_forward_loss_windows(cb_ctx* ctx, const cb_tokens* data, const int64_t* positions,
+                                  int32_t batch, float softcap, float* loss_out,
+                                  float* per_token_loss);
+
+/* Sums of an evaluation pass (all accumulated on the device, fixed order). */
+typedef struct cb_eval_totals {
+  double loss_sum;   /* sum of the per-token losses */
+  double nats;       /* sum of the losses whose target has a positive byte length */
+  int64_t bytes;     /* sum of those byte lengths */
+  int64_t tokens;    /* positions evaluated */
+} cb_eval_totals;
+
+/* The evaluation loop of validate (train.rs:197-236) for validation steps
+ * [step_begin, step_end): step vs evaluates the window at
+ * pos = (vs * seq) % (n - seq - 1), up to max_batch windows per forward. With
+ * token_bytes (host int32 [n_token_bytes], TokenBytes of data.rs:47-73; nullable)
+ * the byte-weighted nats of compute_bpb (data.rs:75-91) are summed as well. The
+ * caller forms val_loss = loss_sum / tokens and val_bpb = nats / (ln 2 * bytes);
+ * data-parallel callers split the step range across ranks and add the totals.
+ * Synchronous. */
+cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* token_bytes,
+                          int32_t n_token_bytes, int64_t step_begin, int64_t step_end,
+                          float softcap, cb_eval_totals* out);
+
 /* Per-kernel-class CUDA-event timing of forwards run while enabled. */
 cb_status cb_set_profiling(cb_ctx* ctx, int32_t enable);
 cb_status cb_kernel_times(cb_ctx* ctx, cb_kernel_time* out, int32_t max_entries,

@@ -9,10 +9,14 @@ from .bridge import CudaBridgeError, CB_INIT_NORMAL, CB_INIT_REFERENCE, load_lib
 from .engine import (CompiledKernels, ForwardResult, ForwardScheduler, LayerWeights,
                      ModelForwardWorkspace, ModelWeights, forward, forward_losses,
                      forward_only_ws, forward_ws, nccl_unique_id)
+from .checkpoint import load_checkpoint, save_checkpoint
+from .data import (DeviceTokens, TokenBytes, TokenData, compute_bpb, random_position,
+                   validate)
 
 __all__ = [
     "CONFIGS", "ModelConfig", "custom_config", "CudaBridgeError", "CB_INIT_NORMAL",
     "CB_INIT_REFERENCE", "load_library", "CompiledKernels", "ForwardResult", "ForwardScheduler",
     "LayerWeights", "ModelForwardWorkspace", "ModelWeights", "forward", "forward_losses",
-    "forward_only_ws", "forward_ws", "nccl_unique_id",
+    "forward_only_ws", "forward_ws", "nccl_unique_id", "load_checkpoint", "save_checkpoint",
+    "DeviceTokens", "TokenBytes", "TokenData", "compute_bpb", "random_position", "validate",
 ]

@@ -42,7 +42,8 @@ EXPORTED = [
     "cb_check_device_error", "cb_sampled_logits", "cb_set_profiling", "cb_kernel_times",
     "cb_reset_kernel_times", "cb_get_stream", "cb_last_error", "cb_create_error",
     "cb_gemm_f16", "cb_attention_f16", "cb_lm_head_ce_f16",
-    "cb_lm_head_ce_f16_noalloc",
+    "cb_lm_head_ce_f16_noalloc", "cb_load_rstk", "cb_tokens_open", "cb_tokens_from_host",
+    "cb_tokens_len", "cb_tokens_close", "cb_forward_loss_windows", "cb_eval_windows",
 ]
 
 
@@ -67,6 +68,11 @@ class cb_kernel_time(C.Structure):
                 ("flops", C.c_double), ("bytes", C.c_double)]
 
 
+class cb_eval_totals(C.Structure):
+    _fields_ = [("loss_sum", C.c_double), ("nats", C.c_double), ("bytes", C.c_int64),
+                ("tokens", C.c_int64)]
+
+
 _lib = None
 
 
@@ -80,7 +86,7 @@ def load_library(path: Path | None = None) -> C.CDLL:
         raise RuntimeError(
             f"{p} not found: build the CUDA bridge first (python -m rustane_b200.build)")
     lib = C.CDLL(str(p))
-    vp, i32, u64, f32 = C.c_void_p, C.c_int32, C.c_uint64, C.c_float
+    vp, i32, i64, u64, f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_float
     pf, pu32, pi32 = C.POINTER(C.c_float), C.POINTER(C.c_uint32), C.POINTER(C.c_int32)
     sig = {
         "cb_version": (C.c_char_p, []),
@@ -107,6 +113,13 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
         "cb_lm_head_ce_f16": (i32, [vp, vp, vp, i32, i32, i32, f32, vp, vp, vp]),
         "cb_lm_head_ce_f16_noalloc": (i32, [vp, vp, vp, i32, i32, i32, f32, vp, vp, vp]),
+        "cb_load_rstk": (i32, [vp, C.c_char_p, pu32]),
+        "cb_tokens_open": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
+        "cb_tokens_from_host": (i32, [C.POINTER(C.c_uint16), i64, i32, C.POINTER(vp)]),
+        "cb_tokens_len": (i32, [vp, C.POINTER(i64)]),
+        "cb_tokens_close": (i32, [vp]),
+        "cb_forward_loss_windows": (i32, [vp, vp, C.POINTER(i64), i32, f32, pf, pf]),
+        "cb_eval_windows": (i32, [vp, vp, pi32, i32, i64, i64, f32, C.POINTER(cb_eval_totals)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

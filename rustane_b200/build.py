@@ -59,7 +59,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if nccl_lib is not None:
         extra.append(f'-DCB_NCCL_DEFAULT_PATH="{nccl_lib}"')
     cmd = [nvcc_path(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}", *extra,
-           "-o", str(LIB), *map(str, SOURCES), "-ldl"]
+           "-o", str(LIB), *map(str, SOURCES), "-ldl", "-lpthread"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -19,10 +19,15 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
+#include <errno.h>
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <nccl.h>
 
 #include <cmath>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -34,6 +39,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "gemm_tc.cuh"
+#include "io.cuh"
 #include "ptx.cuh"
 #include "rowwise.cuh"
 #include "weights.cuh"
@@ -432,6 +438,7 @@ struct cb_ctx {
   float* loss = nullptr;       // [1]
   uint32_t* tokens = nullptr;  // [T]
   uint32_t* targets = nullptr; // [T]
+  int64_t* eval_pos = nullptr; // [max_batch] window offsets into a cb_tokens array
   float2* rope = nullptr;      // [64, S] (cos, sin), pair-major
   int* dev_err = nullptr;      // device error flag
   float* h_loss = nullptr;     // pinned
@@ -515,7 +522,7 @@ void free_ctx(cb_ctx* c) {
   c->graphs.clear();
   for (auto e : c->events) cudaEventDestroy(e);
   if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
-  void* ptrs[] = {c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
+  void* ptrs[] = {c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
@@ -923,6 +930,7 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(dmalloc(&ctx->loss, 1));
   CREATE_CUDA(dmalloc(&ctx->tokens, T));
   CREATE_CUDA(dmalloc(&ctx->targets, T));
+  CREATE_CUDA(dmalloc(&ctx->eval_pos, (size_t)ctx->max_batch));
   CREATE_CUDA(dmalloc(&ctx->rope, (size_t)S * 64));
   CREATE_CUDA(dmalloc(&ctx->dev_err, 1));
   CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_loss), sizeof(float)));
@@ -1074,64 +1082,405 @@ cb_status cb_init_weights(cb_ctx* ctx, uint64_t seed, int32_t scheme, float sigm
   return CB_OK;
 }
 
+// Uploads the model's f32 tensors in checkpoint order (train.rs:260-268): embed,
+// gamma_final, then per layer wq, wk, wv, wo, w1, w3, w2, gamma1, gamma2.
+// fetch(dst, n) enqueues on ctx->stream the copy of the source's next n floats into
+// the device buffer dst. Matrices pass through one device staging buffer and are
+// rounded to fp16 into their storage slots (each tensor-parallel rank keeps its own
+// slice); gains are copied as they are. Returns false with ctx->err set on failure.
+static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStream_t st);
+
+extern "C++" {
+template <class Fetch>
+bool upload_model(cb_ctx* ctx, Fetch&& fetch) {
+  const cb_model_config& cfg = ctx->cfg;
+  const ShapeInfo s = shape_of(ctx);
+  const size_t d = cfg.dim, hid = cfg.hidden, V = cfg.vocab, hid_l = ctx->hidden_l;
+  const size_t qd_g = (size_t)cfg.heads * 128, kvd_g = (size_t)cfg.kv_heads * 128;
+  const size_t stage_n = std::max(std::max(V * d, d * hid), std::max(d * qd_g, d * kvd_g));
+  float* stage = nullptr;
+  if (cudaMalloc(&stage, stage_n * sizeof(float)) != cudaSuccess) {
+    ctx->err = "staging allocation failed";
+    return false;
+  }
+  cudaStream_t st = ctx->stream;
+  const int grid = ctx->num_sms * 8, block = 256;
+  auto mat = [&](size_t n, __half* dst, int kind, int rows, int cols, int sub) -> bool {
+    if (!fetch(stage, n)) return false;
+    load_weight_kernel<<<grid, block, 0, st>>>(dst, kind, rows, cols, s, sub, stage);
+    return cudaGetLastError() == cudaSuccess;
+  };
+  bool ok = mat(V * d, ctx->embed, ST_EMBED, (int)V, (int)d, -1) && fetch(ctx->gamma_final, d);
+  for (int l = 0; ok && l < cfg.nlayers; ++l) {
+    __half* qkv = ctx->wqkv + l * wqkv_layer_elems(ctx);
+    __half* w13 = ctx->w13 + l * w13_layer_elems(ctx);
+    ok = mat(d * qd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WQ) &&
+         mat(d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WK) &&
+         mat(d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WV) &&
+         mat(d * qd_g, ctx->wo + l * wo_layer_elems(ctx), ST_WO, (int)d, ctx->q_dim, CB_T_WO) &&
+         mat(d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W1) &&
+         mat(d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W3) &&
+         mat(d * hid, ctx->w2 + l * w2_layer_elems(ctx), ST_W2, (int)d, (int)hid_l, CB_T_W2) &&
+         fetch(ctx->gamma + (size_t)l * 2 * d, d) && fetch(ctx->gamma + (size_t)l * 2 * d + d, d);
+  }
+  const cudaError_t e = cudaStreamSynchronize(st);
+  cudaFree(stage);
+  if (ok && e != cudaSuccess) {
+    ctx->err = std::string("weight upload: ") + cudaGetErrorString(e);
+    ok = false;
+  }
+  return ok;
+}
+}  // extern "C++"
+
+// Number of f32 values of a checkpoint's tensors (train.rs:303-331).
+static uint64_t rstk_floats(const cb_model_config& c) {
+  const uint64_t d = c.dim, qd = (uint64_t)c.heads * 128, kvd = (uint64_t)c.kv_heads * 128;
+  const uint64_t per_layer = d * qd + 2 * d * kvd + qd * d + 3 * d * (uint64_t)c.hidden + 2 * d;
+  return (uint64_t)c.vocab * d + d + (uint64_t)c.nlayers * per_layer;
+}
+
 cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamma_final,
                               const cb_layer_weights_f32* layers) {
   if (!ctx) return CB_ERR_INVALID_ARG;
   if (!embed || !gamma_final || !layers)
     return fail(ctx, CB_ERR_INVALID_ARG, "null weight pointer");
   const cb_model_config& cfg = ctx->cfg;
+  std::vector<const float*> src = {embed, gamma_final};
   for (int l = 0; l < cfg.nlayers; ++l) {
     const cb_layer_weights_f32& w = layers[l];
-    if (!w.wq || !w.wk || !w.wv || !w.wo || !w.w1 || !w.w3 || !w.w2 || !w.gamma1 || !w.gamma2)
-      return fail(ctx, CB_ERR_INVALID_ARG, "null pointer in layer " + std::to_string(l));
+    const float* p[9] = {w.wq, w.wk, w.wv, w.wo, w.w1, w.w3, w.w2, w.gamma1, w.gamma2};
+    for (const float* q : p) {
+      if (!q) return fail(ctx, CB_ERR_INVALID_ARG, "null pointer in layer " + std::to_string(l));
+      src.push_back(q);
+    }
   }
   CB_CUDA(cudaSetDevice(ctx->device));
-  const ShapeInfo s = shape_of(ctx);
-  // Host tensors are the full model (reference orientation); each rank copies the
-  // slice it owns out of the staged f32 tensor.
-  const size_t d = cfg.dim, hid = cfg.hidden, V = cfg.vocab, hid_l = ctx->hidden_l;
-  const size_t qd_g = (size_t)cfg.heads * 128, kvd_g = (size_t)cfg.kv_heads * 128;
-  size_t stage_n = std::max(std::max(V * d, d * hid), std::max(d * qd_g, d * kvd_g));
-  float* stage = nullptr;
-  CB_CUDA(cudaMalloc(&stage, stage_n * sizeof(float)));
-  cudaStream_t st = ctx->stream;
-  const int grid = ctx->num_sms * 8, block = 256;
-  cb_status rc = CB_OK;
-  auto up = [&](const float* src, size_t n, __half* dst, int kind, int rows, int cols,
-                int sub) -> bool {
-    if (cudaMemcpyAsync(stage, src, n * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess)
-      return false;
-    load_weight_kernel<<<grid, block, 0, st>>>(dst, kind, rows, cols, s, sub, stage);
-    return cudaStreamSynchronize(st) == cudaSuccess;
+  size_t next = 0;
+  auto fetch = [&](float* dst, size_t n) -> bool {
+    if (cudaMemcpyAsync(dst, src[next++], n * sizeof(float), cudaMemcpyHostToDevice,
+                        ctx->stream) == cudaSuccess)
+      return true;
+    ctx->err = "host-to-device copy failed";
+    return false;
   };
-  bool ok = up(embed, V * d, ctx->embed, ST_EMBED, (int)V, (int)d, -1);
-  for (int l = 0; ok && l < cfg.nlayers; ++l) {
-    const cb_layer_weights_f32& w = layers[l];
-    __half* qkv = ctx->wqkv + l * wqkv_layer_elems(ctx);
-    ok = ok && up(w.wq, d * qd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WQ);
-    ok = ok && up(w.wk, d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WK);
-    ok = ok && up(w.wv, d * kvd_g, qkv, ST_QKV, ctx->n_qkv, (int)d, CB_T_WV);
-    ok = ok && up(w.wo, d * qd_g, ctx->wo + l * wo_layer_elems(ctx), ST_WO, (int)d,
-                  ctx->q_dim, CB_T_WO);
-    __half* w13 = ctx->w13 + l * w13_layer_elems(ctx);
-    ok = ok && up(w.w1, d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W1);
-    ok = ok && up(w.w3, d * hid, w13, ST_W13, 2 * (int)hid_l, (int)d, CB_T_W3);
-    ok = ok && up(w.w2, d * hid, ctx->w2 + l * w2_layer_elems(ctx), ST_W2, (int)d, (int)hid_l,
-                  CB_T_W2);
-    ok = ok && cudaMemcpy(ctx->gamma + (size_t)l * 2 * d, w.gamma1, d * sizeof(float),
-                          cudaMemcpyHostToDevice) == cudaSuccess;
-    ok = ok && cudaMemcpy(ctx->gamma + (size_t)l * 2 * d + d, w.gamma2, d * sizeof(float),
-                          cudaMemcpyHostToDevice) == cudaSuccess;
-  }
-  ok = ok && cudaMemcpy(ctx->gamma_final, gamma_final, d * sizeof(float),
-                        cudaMemcpyHostToDevice) == cudaSuccess;
-  cudaError_t e = cudaGetLastError();
-  cudaFree(stage);
-  if (!ok || e != cudaSuccess) {
-    rc = fail(ctx, CB_ERR_CUDA, std::string("weight upload failed: ") + cudaGetErrorString(e));
-    return rc;
-  }
+  if (!upload_model(ctx, fetch)) return fail(ctx, CB_ERR_CUDA, "weight upload failed: " + ctx->err);
   ctx->weights_ready = true;
+  return CB_OK;
+}
+
+namespace {
+struct Fd {
+  int fd = -1;
+  explicit Fd(const char* path) : fd(open(path, O_RDONLY | O_CLOEXEC)) {}
+  ~Fd() {
+    if (fd >= 0) close(fd);
+  }
+};
+uint32_t le32(const unsigned char* p) {
+  return (uint32_t)p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24;
+}
+}  // namespace
+
+cb_status cb_load_rstk(cb_ctx* ctx, const char* path, uint32_t* step_out) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (!path) return fail(ctx, CB_ERR_INVALID_ARG, "null path");
+  Fd f(path);
+  if (f.fd < 0) return fail(ctx, CB_ERR_INVALID_ARG, std::string("open ") + path + ": " + strerror(errno));
+  struct stat sb;
+  if (fstat(f.fd, &sb) != 0 || !S_ISREG(sb.st_mode))
+    return fail(ctx, CB_ERR_INVALID_ARG, std::string(path) + " is not a regular file");
+  unsigned char h[28];
+  if (sb.st_size < 28 || pread(f.fd, h, 28, 0) != 28)
+    return fail(ctx, CB_ERR_INVALID_ARG, "checkpoint shorter than its 28-byte header");
+  if (std::memcmp(h, "RSTK", 4) != 0) return fail(ctx, CB_ERR_INVALID_ARG, "bad checkpoint magic");
+  const uint32_t step = le32(h + 8), dim = le32(h + 12), nl = le32(h + 16), vocab = le32(h + 20);
+  const cb_model_config& cfg = ctx->cfg;
+  if (dim != (uint32_t)cfg.dim || nl != (uint32_t)cfg.nlayers || vocab != (uint32_t)cfg.vocab)
+    return fail(ctx, CB_ERR_INVALID_ARG,
+                "checkpoint header dim/nlayers/vocab " + std::to_string(dim) + "/" +
+                    std::to_string(nl) + "/" + std::to_string(vocab) + " differ from the config");
+  const uint64_t need = 28 + 4 * rstk_floats(cfg);
+  if ((uint64_t)sb.st_size < need)
+    return fail(ctx, CB_ERR_INVALID_ARG,
+                "checkpoint truncated: " + std::to_string(sb.st_size) + " bytes, need " +
+                    std::to_string(need));
+  CB_CUDA(cudaSetDevice(ctx->device));
+  FileStreamer fs(f.fd, ctx->stream);
+  if (!fs.ok()) return fail(ctx, CB_ERR_OUT_OF_MEMORY, fs.error());
+  uint64_t off = 28;
+  auto fetch = [&](float* dst, size_t n) -> bool {
+    const bool ok = fs.copy(dst, off, (uint64_t)n * 4);
+    off += (uint64_t)n * 4;
+    if (!ok) ctx->err = fs.error();
+    return ok;
+  };
+  ctx->weights_ready = false;
+  const bool ok = upload_model(ctx, fetch) && fs.finish();
+  if (!ok) return fail(ctx, CB_ERR_CUDA, "checkpoint load failed: " + (fs.ok() ? ctx->err : fs.error()));
+  if (step_out) *step_out = step;
+  ctx->weights_ready = true;
+  return CB_OK;
+}
+
+struct cb_tokens {
+  int device = 0;
+  int64_t n = 0;
+  uint16_t* data = nullptr;
+};
+
+static cb_status tokens_alloc(int64_t n, int32_t device, cb_tokens** out) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    g_create_error = "no CUDA device";
+    return CB_ERR_UNSUPPORTED;
+  }
+  if (device < 0 || device >= count) {
+    g_create_error = "device index out of range";
+    return CB_ERR_INVALID_ARG;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    g_create_error = "cudaSetDevice failed";
+    return CB_ERR_CUDA;
+  }
+  cb_tokens* t = new cb_tokens;
+  t->device = device;
+  t->n = n;
+  if (cudaMalloc(&t->data, std::max<size_t>(16, (size_t)n * 2)) != cudaSuccess) {
+    delete t;
+    g_create_error = "device allocation of the token array failed";
+    return CB_ERR_OUT_OF_MEMORY;
+  }
+  *out = t;
+  return CB_OK;
+}
+
+cb_status cb_tokens_open(const char* path, int32_t device, cb_tokens** out) {
+  g_create_error.clear();
+  if (!out) {
+    g_create_error = "null output pointer";
+    return CB_ERR_INVALID_ARG;
+  }
+  *out = nullptr;
+  if (!path) {
+    g_create_error = "null path";
+    return CB_ERR_INVALID_ARG;
+  }
+  Fd f(path);
+  struct stat sb;
+  if (f.fd < 0 || fstat(f.fd, &sb) != 0) {
+    g_create_error = std::string("open ") + path + ": " + strerror(errno);
+    return CB_ERR_INVALID_ARG;
+  }
+  if (!S_ISREG(sb.st_mode)) {
+    g_create_error = std::string(path) + " is not a regular file";
+    return CB_ERR_INVALID_ARG;
+  }
+  const int64_t n = (int64_t)sb.st_size / 2;  // data.rs:23 n_tokens = len / 2
+  cb_tokens* t = nullptr;
+  cb_status rc = tokens_alloc(n, device, &t);
+  if (rc != CB_OK) return rc;
+  cudaStream_t st;
+  if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+    cb_tokens_close(t);
+    g_create_error = "stream creation failed";
+    return CB_ERR_CUDA;
+  }
+  bool ok;
+  std::string why;
+  {
+    FileStreamer fs(f.fd, st);
+    ok = fs.ok() && fs.copy(t->data, 0, (uint64_t)n * 2) && fs.finish();
+    why = fs.error();
+  }
+  cudaStreamDestroy(st);
+  if (!ok) {
+    cb_tokens_close(t);
+    g_create_error = "token file load failed: " + why;
+    return CB_ERR_CUDA;
+  }
+  *out = t;
+  return CB_OK;
+}
+
+cb_status cb_tokens_from_host(const uint16_t* tokens, int64_t n, int32_t device,
+                              cb_tokens** out) {
+  g_create_error.clear();
+  if (!out || (!tokens && n > 0) || n < 0) {
+    g_create_error = "bad token array arguments";
+    return CB_ERR_INVALID_ARG;
+  }
+  *out = nullptr;
+  cb_tokens* t = nullptr;
+  cb_status rc = tokens_alloc(n, device, &t);
+  if (rc != CB_OK) return rc;
+  if (n > 0 && cudaMemcpy(t->data, tokens, (size_t)n * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cb_tokens_close(t);
+    g_create_error = "token upload failed";
+    return CB_ERR_CUDA;
+  }
+  *out = t;
+  return CB_OK;
+}
+
+cb_status cb_tokens_len(const cb_tokens* data, int64_t* n) {
+  if (!data || !n) return CB_ERR_INVALID_ARG;
+  *n = data->n;
+  return CB_OK;
+}
+
+cb_status cb_tokens_close(cb_tokens* data) {
+  if (!data) return CB_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(data->device);
+  cudaFree(data->data);
+  cudaSetDevice(prev);
+  delete data;
+  return CB_OK;
+}
+
+// Gathers `batch` windows (positions already on the device in ctx->eval_pos + first)
+// into the context's token/target buffers and runs one forward, all on ctx->stream.
+static cb_status windows_forward(cb_ctx* ctx, const cb_tokens* data, size_t first, int32_t batch,
+                                 float softcap) {
+  const int S = ctx->cfg.seq;
+  const int64_t total = (int64_t)batch * S;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)ctx->num_sms * 8);
+  gather_windows_kernel<<<grid, 256, 0, ctx->stream>>>(data->data, data->n, ctx->eval_pos + first,
+                                                       batch, S, ctx->cfg.vocab, ctx->tokens,
+                                                       ctx->targets, ctx->dev_err);
+  CB_CUDA(cudaGetLastError());
+  return run_forward(ctx, batch, softcap, ctx->stream);
+}
+
+static cb_status read_device_error(cb_ctx* ctx) {
+  CB_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost,
+                          ctx->stream));
+  CB_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (*ctx->h_err != 0) {
+    const int code = *ctx->h_err;
+    cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
+                code == DEV_ERR_BAD_TOKEN ? "token id out of range in the token data"
+                                          : "device error flag " + std::to_string(code));
+  }
+  return CB_OK;
+}
+
+static cb_status check_windows(cb_ctx* ctx, const cb_tokens* data) {
+  if (!ctx->weights_ready) return fail(ctx, CB_ERR_NOT_READY, "weights are not loaded");
+  if (!data) return fail(ctx, CB_ERR_INVALID_ARG, "null token data");
+  if (data->device != ctx->device)
+    return fail(ctx, CB_ERR_INVALID_ARG, "token data lives on another device");
+  return CB_OK;
+}
+
+cb_status cb_forward_loss_windows(cb_ctx* ctx, const cb_tokens* data, const int64_t* positions,
+                                  int32_t batch, float softcap, float* loss_out,
+                                  float* per_token_loss) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  cb_status rc = check_windows(ctx, data);
+  if (rc != CB_OK) return rc;
+  if (!positions || !loss_out) return fail(ctx, CB_ERR_INVALID_ARG, "null positions/loss_out");
+  if (batch <= 0 || batch > ctx->max_batch)
+    return fail(ctx, CB_ERR_INVALID_ARG, "batch " + std::to_string(batch) + " outside [1, " +
+                                             std::to_string(ctx->max_batch) + "]");
+  const int S = ctx->cfg.seq;
+  for (int b = 0; b < batch; ++b)
+    if (positions[b] < 0 || positions[b] + S + 1 > data->n)
+      return fail(ctx, CB_ERR_INVALID_ARG,
+                  "window " + std::to_string(b) + " at " + std::to_string(positions[b]) +
+                      " runs past the token data");
+  CB_CUDA(cudaSetDevice(ctx->device));
+  CB_CUDA(cudaMemcpyAsync(ctx->eval_pos, positions, (size_t)batch * 8, cudaMemcpyHostToDevice,
+                          ctx->stream));
+  rc = windows_forward(ctx, data, 0, batch, softcap);
+  if (rc != CB_OK) return rc;
+  const size_t T = (size_t)batch * S;
+  CB_CUDA(cudaMemcpyAsync(ctx->h_loss, ctx->loss, sizeof(float), cudaMemcpyDeviceToHost,
+                          ctx->stream));
+  if (per_token_loss)
+    CB_CUDA(cudaMemcpyAsync(per_token_loss, ctx->tok_loss, T * sizeof(float),
+                            cudaMemcpyDeviceToHost, ctx->stream));
+  rc = read_device_error(ctx);
+  if (rc != CB_OK) return rc;
+  *loss_out = *ctx->h_loss;
+  return CB_OK;
+}
+
+cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* token_bytes,
+                          int32_t n_token_bytes, int64_t step_begin, int64_t step_end,
+                          float softcap, cb_eval_totals* out) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  cb_status rc = check_windows(ctx, data);
+  if (rc != CB_OK) return rc;
+  if (!out) return fail(ctx, CB_ERR_INVALID_ARG, "null output");
+  if (step_begin < 0 || step_end < step_begin)
+    return fail(ctx, CB_ERR_INVALID_ARG, "bad step range");
+  if (token_bytes && n_token_bytes <= 0)
+    return fail(ctx, CB_ERR_INVALID_ARG, "empty token_bytes table");
+  const int S = ctx->cfg.seq;
+  const int64_t max_pos = data->n - S - 1;  // train.rs:207
+  if (max_pos <= 0)
+    return fail(ctx, CB_ERR_INVALID_ARG, "token data shorter than seq + 2 tokens");
+  CB_CUDA(cudaSetDevice(ctx->device));
+  const int64_t steps = step_end - step_begin;
+  std::memset(out, 0, sizeof(*out));
+  if (steps == 0) return CB_OK;
+  int32_t* d_bytes = nullptr;
+  EvalSums* d_sums = nullptr;
+  int64_t* d_pos = nullptr;
+  std::vector<int64_t> pos((size_t)steps);
+  for (int64_t i = 0; i < steps; ++i) pos[(size_t)i] = ((step_begin + i) * S) % max_pos;  // :209
+  auto cleanup = [&] {
+    cudaFree(d_bytes);
+    cudaFree(d_sums);
+    cudaFree(d_pos);
+  };
+  if (cudaMalloc(&d_sums, sizeof(EvalSums)) != cudaSuccess ||
+      cudaMalloc(&d_pos, (size_t)steps * 8) != cudaSuccess ||
+      (token_bytes && cudaMalloc(&d_bytes, (size_t)n_token_bytes * 4) != cudaSuccess)) {
+    cleanup();
+    return fail(ctx, CB_ERR_OUT_OF_MEMORY, "evaluation buffers");
+  }
+  cudaStream_t st = ctx->stream;
+  cudaError_t e = cudaMemsetAsync(d_sums, 0, sizeof(EvalSums), st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_pos, pos.data(), (size_t)steps * 8, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && token_bytes)
+    e = cudaMemcpyAsync(d_bytes, token_bytes, (size_t)n_token_bytes * 4, cudaMemcpyHostToDevice,
+                        st);
+  if (e != cudaSuccess) {
+    cleanup();
+    return fail(ctx, CB_ERR_CUDA, std::string("evaluation setup: ") + cudaGetErrorString(e));
+  }
+  int64_t* saved_pos = ctx->eval_pos;
+  ctx->eval_pos = d_pos;
+  for (int64_t first = 0; first < steps && rc == CB_OK; first += ctx->max_batch) {
+    const int32_t b = (int32_t)std::min<int64_t>(ctx->max_batch, steps - first);
+    rc = windows_forward(ctx, data, (size_t)first, b, softcap);
+    if (rc == CB_OK) {
+      eval_accumulate_kernel<<<1, EVAL_THREADS, 0, st>>>(ctx->tok_loss, ctx->targets, d_bytes,
+                                                         n_token_bytes, b * S, d_sums);
+      if (cudaGetLastError() != cudaSuccess) rc = fail(ctx, CB_ERR_CUDA, "evaluation launch");
+    }
+  }
+  ctx->eval_pos = saved_pos;
+  EvalSums h{};
+  if (rc == CB_OK) {
+    e = cudaMemcpyAsync(&h, d_sums, sizeof(h), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) rc = fail(ctx, CB_ERR_CUDA, "evaluation read-back");
+  }
+  if (rc == CB_OK) rc = read_device_error(ctx);
+  cudaStreamSynchronize(st);
+  cleanup();
+  if (rc != CB_OK) return rc;
+  out->loss_sum = h.loss_sum;
+  out->nats = h.nats;
+  out->bytes = h.bytes;
+  out->tokens = h.tokens;
   return CB_OK;
 }
 

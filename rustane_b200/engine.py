@@ -186,6 +186,14 @@ class CompiledKernels:
                                                      _fptr(w.gamma_final), arr))
         self._loaded_generation = w.generation
 
+    def load_checkpoint(self, path) -> int:
+        """Stream an RSTK checkpoint (train.rs:238-346) into the device weights;
+        returns the step recorded in its header."""
+        step = C.c_uint32()
+        self._check(self.lib.cb_load_rstk(self.handle, str(path).encode(), C.byref(step)))
+        self._loaded_generation = None
+        return step.value
+
     # ---- forward
     def _tokens(self, tokens, targets):
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
@@ -211,6 +219,31 @@ class CompiledKernels:
         self._check(self.lib.cb_forward_loss_async(
             self.handle, C.c_void_p(d_tokens), C.c_void_p(d_targets), batch, softcap,
             C.c_void_p(d_loss), C.c_void_p(d_per_token or None), C.c_void_p(stream or None)))
+
+    def forward_loss_windows(self, data, positions, softcap: float = 0.0,
+                             per_token: bool = False):
+        """Forward over windows of a DeviceTokens array: sequence b has tokens
+        data[positions[b]:+seq] and targets data[positions[b]+1:+seq+1]."""
+        pos = np.ascontiguousarray(np.asarray(positions, dtype=np.int64).reshape(-1))
+        loss = C.c_float()
+        ptl = np.empty(pos.size * self.cfg.seq, np.float32) if per_token else None
+        self._check(self.lib.cb_forward_loss_windows(
+            self.handle, data.handle, pos.ctypes.data_as(C.POINTER(C.c_int64)), pos.size,
+            softcap, C.byref(loss), _fptr(ptl) if ptl is not None else None))
+        return (loss.value, ptl) if per_token else loss.value
+
+    def eval_windows(self, data, token_bytes, step_begin: int, step_end: int,
+                     softcap: float = 0.0) -> dict:
+        """Device sums of validation steps [step_begin, step_end) (train.rs:197-236)."""
+        tb = None
+        if token_bytes is not None:
+            tb = np.ascontiguousarray(token_bytes.bytes, dtype=np.int32)
+        out = B.cb_eval_totals()
+        self._check(self.lib.cb_eval_windows(
+            self.handle, data.handle,
+            tb.ctypes.data_as(C.POINTER(C.c_int32)) if tb is not None else None,
+            tb.size if tb is not None else 0, step_begin, step_end, softcap, C.byref(out)))
+        return dict(loss_sum=out.loss_sum, nats=out.nats, bytes=out.bytes, tokens=out.tokens)
 
     def check_device_error(self) -> None:
         self._check(self.lib.cb_check_device_error(self.handle))
