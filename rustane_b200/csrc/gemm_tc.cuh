@@ -462,7 +462,10 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs of a pair)
-      const uint64_t pol_a = policy_evict_first();
+      // Both operands are re-read by other tiles (A by every n-tile of its row block, B
+      // by every m-block): keep both in L2. Evict-first on A let the streaming outputs
+      // push A out before its last n-tile (A read ~2.2x from DRAM, 1.6 % slower).
+      const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
       uint32_t it = 0;
       bool ok = true;
