@@ -260,10 +260,34 @@ const char* cb_create_error(void);
 cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N, int32_t K,
                       int32_t out_f32, int32_t block_n, void* stream);
 
+/* cb_gemm_f16 with either operand stored transposed, the GEMMs of a backward pass:
+ * layout bit 0 set = A is stored [K][M] (M contiguous), bit 1 = B is stored [K][N].
+ * C[M,N] = A * B^T as in cb_gemm_f16 (out_f32 0, 1 or 2 as there). An operand stored
+ * transposed needs its M (or N) % 64 == 0; a K-major one needs K % 8 == 0. */
+cb_status cb_gemm_f16_layout(const void* A, const void* B, void* C, int32_t M, int32_t N,
+                             int32_t K, int32_t layout, int32_t out_f32, int32_t block_n,
+                             void* stream);
+
 /* Causal attention: q/k/v [batch, heads, seq, 128] fp16 -> out [batch*seq,
  * heads*128] fp16, scale 1/sqrt(128). seq % 64 == 0. */
 cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out,
                            int32_t batch, int32_t heads, int32_t seq, void* stream);
+
+/* cb_attention_f16 that also writes lse [batch, heads, seq] (f32): the base-2
+ * log-sum-exp of each query's scaled scores, lse = log2 sum_k 2^(s_k log2(e)/sqrt(128)),
+ * which the backward pass needs. kv_heads divides heads (grouped-query attention). */
+cb_status cb_attention_fwd_lse_f16(const void* q, const void* k, const void* v, void* out,
+                                   float* lse, int32_t batch, int32_t heads, int32_t kv_heads,
+                                   int32_t seq, void* stream);
+
+/* Backward of causal attention (no RoPE): q [batch, heads, seq, 128], k/v [batch,
+ * kv_heads, seq, 128], o and dout [batch*seq, heads*128] fp16, lse from
+ * cb_attention_fwd_lse_f16 -> dqkv [batch*seq, (heads + 2 kv_heads)*128] fp16 holding
+ * dQ, dK, dV side by side per token (the layout of the QKV projection's output
+ * gradient). Scratch comes from cudaMallocAsync; returns after the stream finishes. */
+cb_status cb_attention_bwd_f16(const void* q, const void* k, const void* v, const void* o,
+                               const void* dout, const float* lse, void* dqkv, int32_t batch,
+                               int32_t heads, int32_t kv_heads, int32_t seq, void* stream);
 
 /* Tied LM head + next-token cross-entropy on device buffers (the model's final
  * step: full_model.rs:436-471). xf [T, dim] fp16 (final-normalised activations),

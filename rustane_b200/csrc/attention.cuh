@@ -44,7 +44,7 @@ __device__ __forceinline__ void att_load_tile(uint32_t s_base, const __half* g, 
 __global__ void __launch_bounds__(ATT_THREADS)
     attn_fwd_causal_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                            const __half* __restrict__ v, __half* __restrict__ out, int seq,
-                           int heads, int kv_heads, float scale_log2) {
+                           int heads, int kv_heads, float scale_log2, float* __restrict__ lse) {
   extern __shared__ __align__(128) uint8_t att_smem[];
   const uint32_t sQ = smem_u32(att_smem);
   const uint32_t sK0 = sQ + ATT_BQ * 256;
@@ -187,6 +187,9 @@ __global__ void __launch_bounds__(ATT_THREADS)
     float l = l_run[r];
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (lse && tig == 0)  // base-2 log-sum-exp of the scaled scores, for the backward pass
+      lse[((size_t)b * heads + h) * seq + qt * ATT_BQ + warp * 16 + g + 8 * r] =
+          m_run[r] + log2f(l);
     l_run[r] = 1.0f / l;
   }
   const int q_row = qt * ATT_BQ + warp * 16 + g;

@@ -76,7 +76,8 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, __half* __restrict__ out, int seq,
-                       int heads, int kv_heads, float scale_log2, int* err) {
+                       int heads, int kv_heads, float scale_log2, float* __restrict__ lse,
+                       int* err) {
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -293,6 +294,9 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
     if (ok && mbar_wait(pv_done, (n_kv - 1) & 1, err)) {
       tc_fence_after();
       const float inv = 1.0f / l_run;
+      // Log-sum-exp of the scaled scores in base 2 (lse2 = log2 sum_k 2^(s_k c)), kept
+      // for the backward pass: P = 2^(s c - lse2).
+      if (lse) lse[q_row0 + r] = m_run + log2f(l_run);
       __half* dst = out + ((size_t)b * seq + q_idx) * ((size_t)heads * 128) + h * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {

@@ -38,6 +38,7 @@
 #include "cuda_bridge.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "attention_bwd.cuh"
 #include "gemm_tc.cuh"
 #include "io.cuh"
 #include "ptx.cuh"
@@ -78,6 +79,21 @@ bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t k, uint64_t rows, uin
   cuuint64_t dims[3] = {k, rows, depth};
   cuuint64_t strides[2] = {k * 2, k * rows * 2};
   cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// MN-major fp16 operand: a row-major [depth][k][mn] array (mn contiguous) read as
+// 64 (mn) x 64 (k) boxes with 128-byte swizzle (the GEMM's MN-major A or B).
+bool make_tmap_mn(CUtensorMap* map, const void* ptr, uint64_t mn, uint64_t k, uint64_t depth) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || mn % 8 != 0) return false;
+  cuuint64_t dims[3] = {mn, k, depth};
+  cuuint64_t strides[2] = {mn * 2, mn * k * 2};
+  cuuint32_t box[3] = {64, 64, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -162,18 +178,18 @@ void split_even(int n, int world, int rank, int* begin, int* count) {
 // Tile modes of the tcgen05 GEMM.
 enum GemmMode { GM_SINGLE128 = 0, GM_SINGLE256 = 1, GM_PAIR = 2 };
 
-template <int BN, class Epi>
+template <int BN, class Epi, int LAYOUT>
 void set_gemm_attr() {
-  cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       GemmCfg<BN>::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi, LAYOUT>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM_BYTES);
 }
 
-template <class Epi>
+template <class Epi, int LAYOUT = 0>
 void set_gemm_attrs_for() {
-  set_gemm_attr<128, Epi>();
-  set_gemm_attr<256, Epi>();
-  cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       GemmCfg<256, true>::SMEM_BYTES);
+  set_gemm_attr<128, Epi, LAYOUT>();
+  set_gemm_attr<256, Epi, LAYOUT>();
+  cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi, LAYOUT>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<256, true>::SMEM_BYTES);
 }
 
 void set_all_kernel_attrs() {
@@ -183,11 +199,21 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiScaledF16>();
   set_gemm_attrs_for<EpiScaledF32>();
   set_gemm_attrs_for<EpiScaledF32Add>();
+  set_gemm_attrs_for<EpiStoreF16, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiStoreF32, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiScaledF32Add, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiStoreF16, GEMM_A_MN>();
+  set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN>();
+  set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN>();
+  set_gemm_attrs_for<EpiStoreF16, GEMM_A_MN | GEMM_B_MN>();
+  set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
+  set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwiglu>();
   set_gemm_attrs_for<EpiCrossEntropy>();
   cudaFuncSetAttribute(attn_fwd_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        ATT_SMEM);
   cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+  cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_SMEM);
 }
 
 struct DeviceInfo {
@@ -234,24 +260,24 @@ void ensure_attrs(int device) { (void)device_info(device); }
 
 int num_sms_of(int device) { return device_info(device).sms; }
 
-template <int BN, class Epi>
+template <int BN, class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                            int bz, const Epi& epi, int* err, int units, int splits,
                            cudaStream_t st) {
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
-  gemm_tn_kernel<BN, Epi><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(
+  gemm_tn_kernel<BN, Epi, LAYOUT><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(
       ta, tb, M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
 
-template <class Epi>
+template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
                              int K, int bz, const Epi& epi, int* err, int clusters, int splits,
                              cudaStream_t st) {
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
-  gemm_tn_pair_kernel<Epi><<<2 * pairs, GEMM_THREADS, GemmCfg<256, true>::SMEM_BYTES, st>>>(
+  gemm_tn_pair_kernel<Epi, LAYOUT><<<2 * pairs, GEMM_THREADS, GemmCfg<256, true>::SMEM_BYTES, st>>>(
       ta, tb_half, M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
@@ -286,15 +312,19 @@ int mode_block_n(int mode) { return mode == GM_SINGLE128 ? 128 : 256; }
 
 // tb128: B tensor map with 128-row boxes (single 128-wide tiles and CTA pairs);
 // tb256: 256-row boxes (single 256-wide tiles).
-template <class Epi>
+// tb128 is B's tensor map with 128-row boxes (1-CTA 128-wide tiles and the CTA pair's
+// halves), tb256 the one with 256-row boxes. For an MN-major B (LAYOUT & GEMM_B_MN) both
+// are the same 64 x 64-box map.
+template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
                         int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1) {
   if (mode == GM_PAIR)
-    return launch_gemm_pair(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters, splits, st);
+    return launch_gemm_pair<Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters,
+                                         splits, st);
   if (mode == GM_SINGLE128)
-    return launch_gemm_bn<128>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st);
-  return launch_gemm_bn<256>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st);
+    return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st);
+  return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st);
 }
 
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
@@ -337,17 +367,40 @@ void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* 
 cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
                              const __half* q, const __half* k, const __half* v, __half* out,
                              int batch, int heads, int kv_heads, int seq, int* err,
-                             cudaStream_t st) {
+                             cudaStream_t st, float* lse = nullptr) {
   const float scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
   if (tq && seq % FA_BQ == 0) {
     dim3 grid(seq / FA_BQ, heads, batch);
     attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, out, seq, heads,
-                                                          kv_heads, scale_log2, err);
+                                                          kv_heads, scale_log2, lse, err);
   } else {
     dim3 grid(seq / ATT_BQ, heads, batch);
     attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(q, k, v, out, seq, heads,
-                                                                kv_heads, scale_log2);
+                                                                kv_heads, scale_log2, lse);
   }
+  return cudaGetLastError();
+}
+
+// Attention backward: D = rowsum(dO o O), the key-block kernel (dK, dV into dqkv; dQ
+// accumulated in dq32, which this zeroes first), then dQ into dqkv.
+cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half* v,
+                                 const __half* o, const __half* dout, const float* lse2,
+                                 float* dsum, float* dq32, const float2* rope, __half* dqkv,
+                                 int batch, int heads, int kv_heads, int seq, int sms,
+                                 cudaStream_t st) {
+  const int T = batch * seq;
+  const int q_dim = heads * 128, n_qkv = q_dim + 2 * kv_heads * 128;
+  const float scale = 1.0f / sqrtf(128.0f);
+  const float scale_log2 = 1.4426950408889634f * scale;
+  cudaError_t e = cudaMemsetAsync(dq32, 0, (size_t)T * q_dim * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  attn_bwd_dsum_kernel<<<(T * heads + 7) / 8, 256, 0, st>>>(o, dout, dsum, T, seq, heads);
+  dim3 grid(seq / AB_BK, kv_heads, batch);
+  attn_bwd_kernel<<<grid, AB_THREADS, AB_SMEM, st>>>(q, k, v, dout, lse2, dsum, rope, dq32, dqkv,
+                                                     seq, heads, kv_heads, scale_log2, scale);
+  const size_t pairs = (size_t)T * q_dim / 2;
+  const int blocks = (int)std::min<size_t>((pairs + 255) / 256, (size_t)sms * 16);
+  attn_bwd_dq_kernel<<<blocks, 256, 0, st>>>(dq32, rope, dqkv, T, seq, heads, n_qkv, scale);
   return cudaGetLastError();
 }
 
@@ -1727,6 +1780,66 @@ cb_status cb_gemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t 
   return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
+extern "C++" {
+template <int LAYOUT>
+static cudaError_t gemm_layout_launch(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
+                                      const CUtensorMap& tb256, void* C, int M, int N, int K,
+                                      int out_mode, const DeviceInfo& di, cudaStream_t st) {
+  if (out_mode == 2) {
+    EpiScaledF32Add ep{static_cast<float*>(C), N, 1.f};
+    return launch_gemm<EpiScaledF32Add, LAYOUT>(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr,
+                                                di, st, K >= 128 ? 2 : 1);
+  }
+  if (out_mode == 1) {
+    EpiStoreF32 ep{static_cast<float*>(C), N, 0.f};
+    return launch_gemm<EpiStoreF32, LAYOUT>(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di,
+                                            st);
+  }
+  EpiStoreF16 ep{static_cast<__half*>(C), N};
+  return launch_gemm<EpiStoreF16, LAYOUT>(mode, ta, tb128, tb256, M, N, K, 0, ep, nullptr, di, st);
+}
+}  // extern "C++"
+
+cb_status cb_gemm_f16_layout(const void* A, const void* B, void* C, int32_t M, int32_t N,
+                             int32_t K, int32_t layout, int32_t out_f32, int32_t block_n,
+                             void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || layout < 0 || layout > 3)
+    return CB_ERR_INVALID_ARG;
+  if (N % 32 != 0 || out_f32 < 0 || out_f32 > 2) return CB_ERR_INVALID_ARG;
+  if ((layout & GEMM_A_MN) ? (M % 64 != 0) : (K % 8 != 0)) return CB_ERR_INVALID_ARG;
+  if ((layout & GEMM_B_MN) ? (N % 64 != 0) : (K % 8 != 0)) return CB_ERR_INVALID_ARG;
+  if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return CB_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  const DeviceInfo& di = device_info(dev);
+  int mode;
+  if (block_n == 128) mode = GM_SINGLE128;
+  else if (block_n == 256) mode = GM_SINGLE256;
+  else if (block_n == 2) mode = GM_PAIR;
+  else mode = pick_mode(M, N, di);
+  if (mode != GM_SINGLE128 && N % 256 != 0) mode = GM_SINGLE128;
+  CUtensorMap ta, tb128, tb256;
+  const bool a_ok = (layout & GEMM_A_MN) ? make_tmap_mn(&ta, A, M, K, 1)
+                                         : make_tmap(&ta, A, K, M, 1, 128);
+  bool b_ok;
+  if (layout & GEMM_B_MN) {
+    b_ok = make_tmap_mn(&tb128, B, N, K, 1);
+    tb256 = tb128;
+  } else {
+    b_ok = make_tmap(&tb128, B, K, N, 1, 128) && make_tmap(&tb256, B, K, N, 1, 256);
+  }
+  if (!a_ok || !b_ok) return CB_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (layout) {
+    case 1: e = gemm_layout_launch<1>(mode, ta, tb128, tb256, C, M, N, K, out_f32, di, st); break;
+    case 2: e = gemm_layout_launch<2>(mode, ta, tb128, tb256, C, M, N, K, out_f32, di, st); break;
+    case 3: e = gemm_layout_launch<3>(mode, ta, tb128, tb256, C, M, N, K, out_f32, di, st); break;
+    default: e = gemm_layout_launch<0>(mode, ta, tb128, tb256, C, M, N, K, out_f32, di, st);
+  }
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
 cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out, int32_t batch,
                            int32_t heads, int32_t seq, void* stream) {
   if (!q || !k || !v || !out || batch <= 0 || heads <= 0 || seq <= 0 || seq % 64 != 0)
@@ -1742,6 +1855,60 @@ cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* ou
                                    static_cast<const __half*>(k), static_cast<const __half*>(v),
                                    static_cast<__half*>(out), batch, heads, heads, seq, nullptr,
                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+cb_status cb_attention_fwd_lse_f16(const void* q, const void* k, const void* v, void* out,
+                                   float* lse, int32_t batch, int32_t heads, int32_t kv_heads,
+                                   int32_t seq, void* stream) {
+  if (!q || !k || !v || !out || !lse || batch <= 0 || heads <= 0 || kv_heads <= 0 ||
+      heads % kv_heads != 0 || seq <= 0 || seq % 64 != 0)
+    return CB_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  ensure_attrs(dev);
+  CUtensorMap tq, tk, tv;
+  const bool tc = seq % FA_BQ == 0 &&
+                  make_tmap_qkv(&tq, q, (uint64_t)batch * heads * seq, FA_BQ) &&
+                  make_tmap_qkv(&tk, k, (uint64_t)batch * kv_heads * seq, FA_BKV) &&
+                  make_tmap_qkv(&tv, v, (uint64_t)batch * kv_heads * seq, FA_BKV);
+  cudaError_t e = launch_attention(tc ? &tq : nullptr, &tk, &tv, static_cast<const __half*>(q),
+                                   static_cast<const __half*>(k), static_cast<const __half*>(v),
+                                   static_cast<__half*>(out), batch, heads, kv_heads, seq, nullptr,
+                                   static_cast<cudaStream_t>(stream), lse);
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+cb_status cb_attention_bwd_f16(const void* q, const void* k, const void* v, const void* o,
+                               const void* dout, const float* lse, void* dqkv, int32_t batch,
+                               int32_t heads, int32_t kv_heads, int32_t seq, void* stream) {
+  if (!q || !k || !v || !o || !dout || !lse || !dqkv || batch <= 0 || heads <= 0 ||
+      kv_heads <= 0 || heads % kv_heads != 0 || seq <= 0 || seq % 64 != 0)
+    return CB_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  ensure_attrs(dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t T = (size_t)batch * seq;
+  // identity rotation: plain attention gradients
+  std::vector<float2> tab((size_t)seq * 64, make_float2(1.f, 0.f));
+  void* scratch = nullptr;
+  const size_t rope_b = tab.size() * sizeof(float2), dsum_b = T * heads * 4,
+               dq_b = T * heads * 128 * 4;
+  if (cudaMallocAsync(&scratch, rope_b + dsum_b + dq_b, st) != cudaSuccess) return CB_ERR_OUT_OF_MEMORY;
+  char* sp = static_cast<char*>(scratch);
+  float2* rope = reinterpret_cast<float2*>(sp);
+  float* dsum = reinterpret_cast<float*>(sp + rope_b);
+  float* dq32 = reinterpret_cast<float*>(sp + rope_b + dsum_b);
+  cudaError_t e = cudaMemcpyAsync(rope, tab.data(), rope_b, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    e = launch_attention_bwd(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                             static_cast<const __half*>(v), static_cast<const __half*>(o),
+                             static_cast<const __half*>(dout), lse, dsum, dq32, rope,
+                             static_cast<__half*>(dqkv), batch, heads, kv_heads, seq,
+                             device_info(dev).sms, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // the host table must outlive the copy
+  cudaFreeAsync(scratch, st);
   return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 

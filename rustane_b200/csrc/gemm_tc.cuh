@@ -396,7 +396,18 @@ struct EpiCrossEntropy {
 // 32*(w%4)..+31: one thread per output row, BN columns in chunks of 32, the next
 // chunk's TMEM load in flight while the current one is processed.
 
-template <int BN, bool PAIR, class Epi>
+// Operand layouts (the LAYOUT template argument): bit 0 set = A is MN-major (stored
+// [K][M], M contiguous: A = X^T of a row-major X), bit 1 = B is MN-major ([K][N]).
+// Backward GEMMs use them: dX = dY * W reads W as stored (B MN-major) and
+// dW = dY^T * X reads both activations as stored (A and B MN-major).
+// An MN-major operand is loaded as 64 (MN) x 64 (K) boxes, 8 KB each, laid side by
+// side along MN; its UMMA descriptor uses LBO = 8 KB between MN blocks and SBO =
+// 1 KB between 8-row K groups, and each K = 16 step advances 2 KB.
+constexpr int GEMM_A_MN = 1;
+constexpr int GEMM_B_MN = 2;
+constexpr int MN_BOX_BYTES = 64 * 64 * 2;
+
+template <int BN, bool PAIR, class Epi, int LAYOUT = 0>
 __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
                                              int M, int N, int K, int b_z, int splits,
                                              const Epi& epi, int* err) {
@@ -479,15 +490,42 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, err)) { ok = false; break; }
+          uint8_t* a_dst = sA + s * Cfg::A_BYTES;
+          uint8_t* b_dst = sB + s * Cfg::B_BYTES;
+          const int k0 = kb * GEMM_BK;
           if (PAIR) {
             if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
             const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
-            tma_load_3d_pair(sA + s * Cfg::A_BYTES, tmA, bar, kb * GEMM_BK, m0, 0, pol_a);
-            tma_load_3d_pair(sB + s * Cfg::B_BYTES, tmB, bar, kb * GEMM_BK, n0, b_z, pol_b);
+            if constexpr (LAYOUT & GEMM_A_MN) {
+#pragma unroll
+              for (int j = 0; j < GEMM_BM / 64; ++j)
+                tma_load_3d_pair(a_dst + j * MN_BOX_BYTES, tmA, bar, m0 + 64 * j, k0, 0, pol_a);
+            } else {
+              tma_load_3d_pair(a_dst, tmA, bar, k0, m0, 0, pol_a);
+            }
+            if constexpr (LAYOUT & GEMM_B_MN) {
+#pragma unroll
+              for (int j = 0; j < Cfg::B_ROWS / 64; ++j)
+                tma_load_3d_pair(b_dst + j * MN_BOX_BYTES, tmB, bar, n0 + 64 * j, k0, b_z, pol_b);
+            } else {
+              tma_load_3d_pair(b_dst, tmB, bar, k0, n0, b_z, pol_b);
+            }
           } else {
             mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-            tma_load_3d(sA + s * Cfg::A_BYTES, tmA, &full[s], kb * GEMM_BK, m0, 0, pol_a);
-            tma_load_3d(sB + s * Cfg::B_BYTES, tmB, &full[s], kb * GEMM_BK, n0, b_z, pol_b);
+            if constexpr (LAYOUT & GEMM_A_MN) {
+#pragma unroll
+              for (int j = 0; j < GEMM_BM / 64; ++j)
+                tma_load_3d(a_dst + j * MN_BOX_BYTES, tmA, &full[s], m0 + 64 * j, k0, 0, pol_a);
+            } else {
+              tma_load_3d(a_dst, tmA, &full[s], k0, m0, 0, pol_a);
+            }
+            if constexpr (LAYOUT & GEMM_B_MN) {
+#pragma unroll
+              for (int j = 0; j < Cfg::B_ROWS / 64; ++j)
+                tma_load_3d(b_dst + j * MN_BOX_BYTES, tmB, &full[s], n0 + 64 * j, k0, b_z, pol_b);
+            } else {
+              tma_load_3d(b_dst, tmB, &full[s], k0, n0, b_z, pol_b);
+            }
           }
         }
       }
@@ -502,7 +540,9 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (the even CTA of a pair)
-      constexpr uint32_t idesc = umma_idesc_f16(TILE_M, BN);
+      constexpr uint32_t idesc = umma_idesc_f16(TILE_M, BN) |
+                                 ((LAYOUT & GEMM_A_MN) ? (1u << 15) : 0u) |
+                                 ((LAYOUT & GEMM_B_MN) ? (1u << 16) : 0u);
       uint32_t it = 0;
       int acc = 0;
       uint32_t acc_ph = 0;
@@ -522,8 +562,12 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
           const uint32_t b_addr = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
-            const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
+            const uint64_t ad = (LAYOUT & GEMM_A_MN)
+                                    ? sw128_mnmajor_desc(a_addr + k * 2048, MN_BOX_BYTES)
+                                    : sw128_kmajor_desc(a_addr + k * 32);
+            const uint64_t bd = (LAYOUT & GEMM_B_MN)
+                                    ? sw128_mnmajor_desc(b_addr + k * 2048, MN_BOX_BYTES)
+                                    : sw128_kmajor_desc(b_addr + k * 32);
             const uint32_t accum = (kb != kb0) || (k != 0);
             if (PAIR) umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
             else umma_f16_ss(d_tmem, ad, bd, idesc, accum);
@@ -617,19 +661,19 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   }
 }
 
-template <int BN, class Epi>
+template <int BN, class Epi, int LAYOUT = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, int b_z, int splits, Epi epi, int* err) {
-  gemm_tn_body<BN, false, Epi>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
+  gemm_tn_body<BN, false, Epi, LAYOUT>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
 }
 
-template <class Epi>
+template <class Epi, int LAYOUT = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int b_z,
                         int splits, Epi epi, int* err) {
-  gemm_tn_body<256, true, Epi>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
+  gemm_tn_body<256, true, Epi, LAYOUT>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
 }
 
 }  // namespace cb

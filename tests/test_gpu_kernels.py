@@ -1,6 +1,7 @@
 """GPU tests of the individual kernels through the C ABI, against plain
 PyTorch fp32 references of the same op."""
 import ctypes as C
+import math
 
 import pytest
 import torch
@@ -65,6 +66,37 @@ def test_gemm_split_k_accumulates(bridge_lib, M, N, K, bn):
     assert bridge_lib.cb_gemm_f16(_ptr(a), _ptr(b), _ptr(c), M, N, K, 2, bn, _stream()) == 0
     torch.cuda.synchronize()
     torch.testing.assert_close(c, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("layout", [1, 2, 3])
+@pytest.mark.parametrize("M,N,K,bn", [
+    (128, 128, 64, 128),
+    (256, 256, 200, 2),          # ragged K (zero-filled boxes)
+    (320, 512, 1000, 256),       # ragged M on a 1-CTA tile, K not a multiple of 64
+    (1536, 1536, 4096, 0),       # a weight-gradient shape: K = tokens
+    (4096, 4608, 1536, 2),       # dX of the QKV projection: B = Wqkv as stored
+])
+def test_gemm_transposed_operands(bridge_lib, layout, M, N, K, bn):
+    """cb_gemm_f16_layout: A stored [K][M] (bit 0) and/or B stored [K][N] (bit 1)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + layout)
+    a = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.25).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.25).half()
+    ref = a.float() @ b.float().T
+    a_arg = a.t().contiguous() if layout & 1 else a
+    b_arg = b.t().contiguous() if layout & 2 else b
+    c32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_gemm_f16_layout(_ptr(a_arg), _ptr(b_arg), _ptr(c32), M, N, K, layout, 1,
+                                         bn, _stream()) == 0
+    c16 = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    assert bridge_lib.cb_gemm_f16_layout(_ptr(a_arg), _ptr(b_arg), _ptr(c16), M, N, K, layout, 0,
+                                         bn, _stream()) == 0
+    acc = torch.ones(M, N, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_gemm_f16_layout(_ptr(a_arg), _ptr(b_arg), _ptr(acc), M, N, K, layout, 2,
+                                         bn, _stream()) == 0
+    torch.cuda.synchronize()
+    torch.testing.assert_close(c32, ref, rtol=1e-4, atol=1e-3)
+    torch.testing.assert_close(c16.float(), ref, rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(acc, ref + 1, rtol=1e-4, atol=1e-3)
 
 
 def test_gemm_rejects_bad_shapes(bridge_lib):
@@ -154,3 +186,49 @@ def test_lm_head_ce_bad_target_is_nan(bridge_lib):
     assert torch.isnan(ptl[5]) and torch.isfinite(ptl[:5]).all()
     assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, 100, V, 0.0, _ptr(ptl),
                                         None, _stream()) == B.CB_ERR_INVALID_ARG
+
+
+def _attn_ref(q, k, v, group):
+    """float32 causal attention with autograd (K/V heads repeated for GQA)."""
+    kk = k.repeat_interleave(group, dim=1)
+    vv = v.repeat_interleave(group, dim=1)
+    return torch.nn.functional.scaled_dot_product_attention(q, kk, vv, is_causal=True)
+
+
+@pytest.mark.parametrize("batch,heads,kv_heads,seq", [
+    (1, 1, 1, 64), (2, 3, 3, 128), (1, 4, 2, 256), (2, 2, 1, 512), (1, 2, 2, 192)])
+def test_attention_backward_matches_torch(bridge_lib, batch, heads, kv_heads, seq):
+    g = torch.Generator(device="cuda").manual_seed(seq * 3 + heads + kv_heads)
+    q = torch.randn(batch, heads, seq, 128, device="cuda", generator=g).half()
+    k = torch.randn(batch, kv_heads, seq, 128, device="cuda", generator=g).half()
+    v = torch.randn(batch, kv_heads, seq, 128, device="cuda", generator=g).half()
+    dout = (torch.randn(batch * seq, heads * 128, device="cuda", generator=g) * 0.1).half()
+    T = batch * seq
+    out = torch.empty(T, heads * 128, device="cuda", dtype=torch.float16)
+    lse = torch.empty(batch, heads, seq, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_attention_fwd_lse_f16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse),
+                                               batch, heads, kv_heads, seq, _stream()) == 0
+    n_qkv = (heads + 2 * kv_heads) * 128
+    dqkv = torch.empty(T, n_qkv, device="cuda", dtype=torch.float16)
+    assert bridge_lib.cb_attention_bwd_f16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(dout),
+                                           _ptr(lse), _ptr(dqkv), batch, heads, kv_heads, seq,
+                                           _stream()) == 0
+    qf, kf, vf = (t.float().requires_grad_() for t in (q, k, v))
+    ref = _attn_ref(qf, kf, vf, heads // kv_heads)
+    # lse against the float32 scores: log2 sum_k 2^(s_k log2(e) / sqrt(128))
+    s = (qf.detach() @ kf.detach().repeat_interleave(heads // kv_heads, 1).transpose(-1, -2))
+    s = s / 128 ** 0.5
+    mask = torch.ones(seq, seq, device="cuda", dtype=torch.bool).triu(1)
+    lse_ref = torch.logsumexp(s.masked_fill(mask, float("-inf")), dim=-1) / math.log(2)
+    do4 = dout.float().reshape(batch, seq, heads, 128).transpose(1, 2)
+    ref.backward(do4)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(lse, lse_ref, rtol=0, atol=2e-3)
+    d = dqkv.float().reshape(batch, seq, heads + 2 * kv_heads, 128).transpose(1, 2)
+    dq, dk, dv = d[:, :heads], d[:, heads:heads + kv_heads], d[:, heads + kv_heads:]
+    for got, want in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
+        err = (got - want).abs().max().item()
+        scale = want.abs().max().item()
+        assert err <= 2e-2 * scale + 1e-3, (err, scale)
+        cos = torch.nn.functional.cosine_similarity(got.flatten(), want.flatten(), dim=0).item()
+        assert cos >= 0.999, cos
