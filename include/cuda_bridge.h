@@ -230,6 +230,45 @@ cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* tok
                           int32_t n_token_bytes, int64_t step_begin, int64_t step_end,
                           float softcap, cb_eval_totals* out);
 
+/* ---- Training step: the backward pass (crates/engine/src/full_model.rs:592-702
+ * backward_ws; layer.rs:6747-7037). ------------------------------------------- */
+
+/* Gradients in the reference orientation, laid out like cb_layer_weights_f32. */
+typedef struct cb_layer_grads_f32 {
+  float* wq;
+  float* wk;
+  float* wv;
+  float* wo;
+  float* w1;
+  float* w3;
+  float* w2;
+  float* gamma1;
+  float* gamma2;
+} cb_layer_grads_f32;
+
+/* Allocates what the training step needs on the context's device: every layer's
+ * saved activations for max_batch sequences, backward scratch and fp32 gradients
+ * for all weights (zeroed). Not available on tensor-parallel contexts. */
+cb_status cb_enable_training(cb_ctx* ctx);
+
+/* Zeroes the gradients (ModelGrads::zero_out, full_model.rs:152). */
+cb_status cb_zero_grads(cb_ctx* ctx);
+
+/* One training step for `batch` sequences (host tokens/targets as cb_forward_loss):
+ * the forward (loss_out = mean loss) followed by the backward, which ADDS into the
+ * device gradients, as the reference accumulates ModelGrads over micro-batches. The
+ * logits gradient is (softmax - onehot) * loss_scale / seq per position, so each
+ * sequence contributes the gradient of its own mean loss, as `batch` calls of
+ * forward_ws + backward_ws would. Gradients are bit-reproducible run to run.
+ * Synchronous. */
+cb_status cb_forward_backward(cb_ctx* ctx, const uint32_t* tokens, const uint32_t* targets,
+                              int32_t batch, float softcap, float loss_scale, float* loss_out);
+
+/* Copies the accumulated gradients to host f32 buffers in the reference orientation
+ * (d_embed [vocab, dim], d_gamma_final [dim], and cfg.nlayers cb_layer_grads_f32). */
+cb_status cb_get_grads_f32(cb_ctx* ctx, float* d_embed, float* d_gamma_final,
+                           const cb_layer_grads_f32* layers);
+
 /* Per-kernel-class CUDA-event timing of forwards run while enabled. */
 cb_status cb_set_profiling(cb_ctx* ctx, int32_t enable);
 cb_status cb_kernel_times(cb_ctx* ctx, cb_kernel_time* out, int32_t max_entries,

@@ -22,6 +22,19 @@
 // The reference is channel-first [dim, seq]; this restatement is token-major
 // [tokens, dim]; the arithmetic per element is the same.
 //
+// orc_forward_backward adds the backward pass (the training step's gradients):
+//   model backward     full_model.rs:592-702 (backward_ws): dlogits = (softmax -
+//                      onehot) * loss_scale / seq (cross_entropy.rs:58-96), softcap
+//                      derivative (1 - tanh^2), dembed += dl^T x_final, dx_final =
+//                      dl embed, final RMSNorm backward, layers in reverse, embedding
+//                      backward (embedding.rs:34-44)
+//   layer backward     layer.rs:6747-7037 (backward): dffn = alpha dy, dsilu = dffn W2,
+//                      SiLU derivative, dx_ffn = dh1 W1^T + dh3 W3^T, RMSNorm2
+//                      backward + dy, dx2s = alpha dx2, da = dx2s Wo^T, SDPA backward,
+//                      RoPE backward (:7391-7408), dx = dq Wq^T + dk Wk^T + dv Wv^T,
+//                      RMSNorm1 backward + dx2; weight gradients as accumulate_dw
+//   RMSNorm backward   cpu/rmsnorm.rs:190-238
+//
 // Weights come from rustane_b200/csrc/weight_init.h, the generator the CUDA
 // bridge also uses, so both sides see bit-identical fp16-valued weights.
 // Accumulations that the reference does in f32 (norm sums, CE log-sum-exp) are
@@ -159,6 +172,67 @@ void rmsnorm(const float* x, const float* gamma, float* out, int T, int d) {
   }
 }
 
+void rmsnorm_save(const float* x, const float* gamma, float* out, float* rinv_out, int T, int d) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const float* xr = x + (size_t)t * d;
+    double ss = 0.0;
+    for (int i = 0; i < d; ++i) ss += (double)xr[i] * xr[i];
+    const float rinv = (float)(1.0 / sqrt(ss / d + (double)RMS_EPS));
+    rinv_out[t] = rinv;
+    float* o = out + (size_t)t * d;
+    for (int i = 0; i < d; ++i) o[i] = xr[i] * rinv * gamma[i];
+  }
+}
+
+// cpu/rmsnorm.rs:190-238: x_hat = x rinv; dgamma += sum_t dy x_hat;
+// dx = rinv (dy gamma - x_hat mean_d(dy gamma x_hat)). dx = or += (accumulate).
+void rmsnorm_backward(const float* dy, const float* x, const float* gamma, const float* rinv,
+                      float* dx, bool accumulate, float* dgamma, int T, int d) {
+  std::vector<double> dg((size_t)d, 0.0);
+#pragma omp parallel
+  {
+    std::vector<double> dg_local((size_t)d, 0.0);
+#pragma omp for schedule(static)
+    for (int t = 0; t < T; ++t) {
+      const float* dyr = dy + (size_t)t * d;
+      const float* xr = x + (size_t)t * d;
+      double dot = 0.0;
+      for (int i = 0; i < d; ++i) {
+        const double xh = (double)xr[i] * rinv[t];
+        dot += (double)dyr[i] * gamma[i] * xh;
+        dg_local[i] += (double)dyr[i] * xh;
+      }
+      dot /= d;
+      float* o = dx + (size_t)t * d;
+      for (int i = 0; i < d; ++i) {
+        const double xh = (double)xr[i] * rinv[t];
+        const float v = (float)(rinv[t] * ((double)dyr[i] * gamma[i] - xh * dot));
+        o[i] = accumulate ? o[i] + v : v;
+      }
+    }
+#pragma omp critical
+    for (int i = 0; i < d; ++i) dg[i] += dg_local[i];
+  }
+  for (int i = 0; i < d; ++i) dgamma[i] += (float)dg[i];
+}
+
+// out[c][r] = in[r][c]
+void transpose(const float* in, int rows, int cols, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < cols; ++c) out[(size_t)c * rows + r] = in[(size_t)r * cols + c];
+}
+
+// dW[R, N] += X^T dY for X [T, R], dY [T, N] (accumulate_dw of the reference).
+void accumulate_dw(const float* X, int R, const float* dY, int N, int T, float* dW) {
+  std::vector<float> xt((size_t)R * T), tmp((size_t)R * N);
+  transpose(X, T, R, xt.data());
+  sgemm(R, N, T, xt.data(), dY, false, tmp.data());
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)R * N; ++i) dW[i] += tmp[i];
+}
+
 // RoPE table [seq][64] (cos, sin), theta = p * 10000^(-2i/128) (sdpa_fwd.rs:24-39).
 std::vector<float> rope_table(int seq) {
   std::vector<float> tab((size_t)seq * 128);
@@ -185,6 +259,86 @@ void apply_rope(float* m, int T, int ncols, int seq, const std::vector<float>& t
       r[c] = a * cs - b * sn;
       r[c + 1] = b * cs + a * sn;
     }
+  }
+}
+
+// Inverse RoPE (rotation by -theta), layer.rs:7391-7408:
+// (d0, d1) -> (c d0 + s d1, -s d0 + c d1)
+void rope_backward(float* m, int T, int ncols, int seq, const std::vector<float>& tab) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const int p = t % seq;
+    float* r = m + (size_t)t * ncols;
+    for (int c = 0; c < ncols; c += 2) {
+      const int i = (c & 127) >> 1;
+      const float cs = tab[(size_t)p * 128 + 2 * i], sn = tab[(size_t)p * 128 + 2 * i + 1];
+      const float a = r[c], b = r[c + 1];
+      r[c] = cs * a + sn * b;
+      r[c + 1] = -sn * a + cs * b;
+    }
+  }
+}
+
+// Backward of causal attention for one forward: dO [T, qd] -> dQ [T, qd], dK, dV
+// [T, kvd] (written, not accumulated). Scores are recomputed:
+//   P = softmax(S), dV_u += P_u dO_t, dP_u = dO_t . V_u, D_t = sum_u P_u dP_u,
+//   dS_u = P_u (dP_u - D_t), dQ_t = scale sum_u dS_u K_u, dK_u += scale dS_u Q_t.
+void attention_backward(const float* Q, const float* K, const float* V, const float* dO,
+                        float* dQ, float* dK, float* dV, int batch, int seq, int heads,
+                        int kv_heads) {
+  const int qd = heads * 128, kvd = kv_heads * 128, grp = heads / kv_heads;
+  const float scale = 1.0f / sqrtf(128.0f);
+  memset(dK, 0, (size_t)batch * seq * kvd * 4);
+  memset(dV, 0, (size_t)batch * seq * kvd * 4);
+#pragma omp parallel
+  {
+    std::vector<float> p(seq), dp(seq);
+#pragma omp for schedule(dynamic, 1) collapse(2)
+    for (int b = 0; b < batch; ++b)
+      for (int hk = 0; hk < kv_heads; ++hk)
+        for (int h = hk * grp; h < (hk + 1) * grp; ++h)
+          for (int t = 0; t < seq; ++t) {
+            const float* q = Q + ((size_t)b * seq + t) * qd + h * 128;
+            const float* go = dO + ((size_t)b * seq + t) * qd + h * 128;
+            float mx = -INFINITY;
+            for (int u = 0; u <= t; ++u) {
+              const float* k = K + ((size_t)b * seq + u) * kvd + hk * 128;
+              float s = 0.f;
+              for (int i = 0; i < 128; ++i) s += q[i] * k[i];
+              p[u] = s * scale;
+              mx = std::max(mx, p[u]);
+            }
+            double den = 0.0;
+            for (int u = 0; u <= t; ++u) {
+              p[u] = expf(p[u] - mx);
+              den += p[u];
+            }
+            const float inv = (float)(1.0 / den);
+            double Dt = 0.0;
+            for (int u = 0; u <= t; ++u) {
+              p[u] *= inv;
+              const float* v = V + ((size_t)b * seq + u) * kvd + hk * 128;
+              float s = 0.f;
+              for (int i = 0; i < 128; ++i) s += go[i] * v[i];
+              dp[u] = s;
+              Dt += (double)p[u] * s;
+            }
+            float* gq = dQ + ((size_t)b * seq + t) * qd + h * 128;
+            float accq[128];
+            for (int i = 0; i < 128; ++i) accq[i] = 0.f;
+            for (int u = 0; u <= t; ++u) {
+              const float ds = p[u] * (dp[u] - (float)Dt);
+              const float* k = K + ((size_t)b * seq + u) * kvd + hk * 128;
+              float* gk = dK + ((size_t)b * seq + u) * kvd + hk * 128;
+              float* gv = dV + ((size_t)b * seq + u) * kvd + hk * 128;
+              for (int i = 0; i < 128; ++i) {
+                accq[i] += ds * k[i];
+                gk[i] += scale * ds * q[i];
+                gv[i] += p[u] * go[i];
+              }
+            }
+            for (int i = 0; i < 128; ++i) gq[i] = scale * accq[i];
+          }
   }
 }
 
@@ -379,6 +533,190 @@ int orc_forward(const orc_config* cfg, const float* embed, const float* gamma_fi
     if (per_token_loss) per_token_loss[t] = (float)tok_loss[t];
   }
   *loss = (float)(sum / T);
+  return 0;
+}
+
+// Forward + backward of `batch` sequences back to back (the training step's
+// gradients). Gradients ADD into the grad buffers (reference orientation, laid out like
+// the weights), as ModelGrads accumulates over micro-batches; dlogits carry
+// loss_scale / seq per position, i.e. each sequence contributes the gradient of its own
+// mean loss, as `batch` separate reference calls would.
+int orc_forward_backward(const orc_config* cfg, const float* embed, const float* gamma_final,
+                         const orc_layer* layers, const uint32_t* tokens,
+                         const uint32_t* targets, int batch, float softcap, float loss_scale,
+                         float* loss, float* d_embed, float* d_gamma_final,
+                         const orc_layer* grads) {
+  if (!cfg || !embed || !gamma_final || !layers || !tokens || !targets || batch <= 0 || !loss ||
+      !d_embed || !d_gamma_final || !grads)
+    return 1;
+  const int d = cfg->dim, hid = cfg->hidden, V = cfg->vocab, S = cfg->seq, L = cfg->nlayers;
+  const int qd = cfg->heads * cfg->hd, kvd = cfg->kv_heads * cfg->hd;
+  if (cfg->hd != 128) return 2;
+  const int T = batch * S;
+  for (int t = 0; t < T; ++t)
+    if (tokens[t] >= (uint32_t)V || targets[t] >= (uint32_t)V) return 3;
+  const float alpha = 1.0f / sqrtf(2.0f * (float)L);
+  const std::vector<float> rope = rope_table(S);
+  const size_t Td = (size_t)T * d;
+
+  struct Cache {
+    std::vector<float> x, xn, r1, q, k, v, a, x2, x2n, r2, h1, h3, g;
+  };
+  std::vector<Cache> cache(L);
+  std::vector<float> X(Td), O(Td);
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) memcpy(&X[(size_t)t * d], embed + (size_t)tokens[t] * d, d * 4);
+  for (int l = 0; l < L; ++l) {
+    const orc_layer& w = layers[l];
+    Cache& c = cache[l];
+    c.x = X;
+    c.xn.resize(Td);
+    c.r1.resize(T);
+    rmsnorm_save(X.data(), w.gamma1, c.xn.data(), c.r1.data(), T, d);
+    c.q.resize((size_t)T * qd);
+    c.k.resize((size_t)T * kvd);
+    c.v.resize((size_t)T * kvd);
+    sgemm(T, qd, d, c.xn.data(), w.wq, false, c.q.data());
+    sgemm(T, kvd, d, c.xn.data(), w.wk, false, c.k.data());
+    sgemm(T, kvd, d, c.xn.data(), w.wv, false, c.v.data());
+    apply_rope(c.q.data(), T, qd, S, rope);
+    apply_rope(c.k.data(), T, kvd, S, rope);
+    c.a.resize((size_t)T * qd);
+    attention(c.q.data(), c.k.data(), c.v.data(), c.a.data(), batch, S, cfg->heads,
+              cfg->kv_heads);
+    sgemm(T, d, qd, c.a.data(), w.wo, false, O.data());
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)Td; ++i) X[i] = X[i] + alpha * O[i];
+    c.x2 = X;
+    c.x2n.resize(Td);
+    c.r2.resize(T);
+    rmsnorm_save(X.data(), w.gamma2, c.x2n.data(), c.r2.data(), T, d);
+    c.h1.resize((size_t)T * hid);
+    c.h3.resize((size_t)T * hid);
+    c.g.resize((size_t)T * hid);
+    sgemm(T, hid, d, c.x2n.data(), w.w1, false, c.h1.data());
+    sgemm(T, hid, d, c.x2n.data(), w.w3, false, c.h3.data());
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)T * hid; ++i) {
+      const float h1 = c.h1[i];
+      c.g[i] = h1 / (1.0f + expf(-h1)) * c.h3[i];
+    }
+    sgemm(T, d, hid, c.g.data(), w.w2, true, O.data());
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)Td; ++i) X[i] = X[i] + alpha * O[i];
+  }
+  std::vector<float> Xf(Td), rf(T);
+  rmsnorm_save(X.data(), gamma_final, Xf.data(), rf.data(), T, d);
+
+  // LM head + CE + dlogits, in row chunks; dx_final = dl embed, dembed += dl^T Xf
+  std::vector<float> dXf(Td);
+  const float inv_seq = loss_scale / (float)S;
+  double loss_sum = 0.0;
+  const int CH = 512;
+  std::vector<float> Z((size_t)CH * V), dZt((size_t)V * CH), tmp((size_t)V * d);
+  for (int t0 = 0; t0 < T; t0 += CH) {
+    const int n = std::min(CH, T - t0);
+    sgemm(n, V, d, Xf.data() + (size_t)t0 * d, embed, true, Z.data());
+    std::vector<double> part(n);
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < n; ++r) {
+      float* z = Z.data() + (size_t)r * V;
+      if (softcap > 0.f)
+        for (int i = 0; i < V; ++i) z[i] = softcap * tanhf(z[i] / softcap);
+      float mx = -INFINITY;
+      for (int i = 0; i < V; ++i) mx = std::max(mx, z[i]);
+      double se = 0.0;
+      for (int i = 0; i < V; ++i) se += exp((double)z[i] - mx);
+      const int tgt = (int)targets[t0 + r];
+      part[r] = log(se) + mx - z[tgt];
+      for (int i = 0; i < V; ++i) {
+        double pr = exp((double)z[i] - mx) / se;
+        double g = (pr - (i == tgt ? 1.0 : 0.0)) * inv_seq;
+        if (softcap > 0.f) {
+          const double th = z[i] / softcap;  // tanh(raw / softcap)
+          g *= 1.0 - th * th;
+        }
+        z[i] = (float)g;  // z now holds dl
+      }
+    }
+    for (int r = 0; r < n; ++r) loss_sum += part[r];
+    sgemm(n, d, V, Z.data(), embed, false, dXf.data() + (size_t)t0 * d);
+    transpose(Z.data(), n, V, dZt.data());
+    sgemm(V, d, n, dZt.data(), Xf.data() + (size_t)t0 * d, false, tmp.data());
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)V * d; ++i) d_embed[i] += tmp[i];
+  }
+  *loss = (float)(loss_sum / T);
+
+  std::vector<float> dY(Td), dffn(Td), dx2(Td), dx2s(Td), dxa(Td);
+  rmsnorm_backward(dXf.data(), X.data(), gamma_final, rf.data(), dY.data(), false,
+                   d_gamma_final, T, d);
+  std::vector<float> dsilu((size_t)T * hid), dh1((size_t)T * hid), dh3((size_t)T * hid);
+  std::vector<float> da((size_t)T * qd), dq((size_t)T * qd), dk((size_t)T * kvd),
+      dv((size_t)T * kvd);
+  for (int l = L - 1; l >= 0; --l) {
+    const orc_layer& w = layers[l];
+    const orc_layer& gw = grads[l];
+    Cache& c = cache[l];
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)Td; ++i) dffn[i] = alpha * dY[i];
+    sgemm(T, hid, d, dffn.data(), w.w2, false, dsilu.data());  // dffn @ W2
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)T * hid; ++i) {
+      const float h1 = c.h1[i];
+      const float sig = 1.0f / (1.0f + expf(-h1));
+      const float silu = h1 * sig;
+      const float dsil = sig * (1.0f + h1 * (1.0f - sig));
+      dh3[i] = dsilu[i] * silu;
+      dh1[i] = dsilu[i] * c.h3[i] * dsil;
+    }
+    sgemm(T, d, hid, dh1.data(), w.w1, true, dxa.data());  // dh1 @ W1^T
+    {
+      std::vector<float> t3(Td);
+      sgemm(T, d, hid, dh3.data(), w.w3, true, t3.data());
+#pragma omp parallel for schedule(static)
+      for (int64_t i = 0; i < (int64_t)Td; ++i) dxa[i] += t3[i];
+    }
+    accumulate_dw(c.x2n.data(), d, dh1.data(), hid, T, gw.w1);
+    accumulate_dw(c.x2n.data(), d, dh3.data(), hid, T, gw.w3);
+    accumulate_dw(dffn.data(), d, c.g.data(), hid, T, gw.w2);
+    rmsnorm_backward(dxa.data(), c.x2.data(), w.gamma2, c.r2.data(), dx2.data(), false,
+                     gw.gamma2, T, d);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)Td; ++i) {
+      dx2[i] += dY[i];
+      dx2s[i] = alpha * dx2[i];
+    }
+    sgemm(T, qd, d, dx2s.data(), w.wo, true, da.data());  // dx2s @ Wo^T
+    accumulate_dw(c.a.data(), qd, dx2s.data(), d, T, gw.wo);
+    attention_backward(c.q.data(), c.k.data(), c.v.data(), da.data(), dq.data(), dk.data(),
+                       dv.data(), batch, S, cfg->heads, cfg->kv_heads);
+    rope_backward(dq.data(), T, qd, S, rope);
+    rope_backward(dk.data(), T, kvd, S, rope);
+    sgemm(T, d, qd, dq.data(), w.wq, true, dxa.data());
+    {
+      std::vector<float> t3(Td);
+      sgemm(T, d, kvd, dk.data(), w.wk, true, t3.data());
+#pragma omp parallel for schedule(static)
+      for (int64_t i = 0; i < (int64_t)Td; ++i) dxa[i] += t3[i];
+      sgemm(T, d, kvd, dv.data(), w.wv, true, t3.data());
+#pragma omp parallel for schedule(static)
+      for (int64_t i = 0; i < (int64_t)Td; ++i) dxa[i] += t3[i];
+    }
+    accumulate_dw(c.xn.data(), d, dq.data(), qd, T, gw.wq);
+    accumulate_dw(c.xn.data(), d, dk.data(), kvd, T, gw.wk);
+    accumulate_dw(c.xn.data(), d, dv.data(), kvd, T, gw.wv);
+    rmsnorm_backward(dxa.data(), c.x.data(), w.gamma1, c.r1.data(), dY.data(), false,
+                     gw.gamma1, T, d);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)Td; ++i) dY[i] += dx2[i];
+  }
+  // embedding backward (embedding.rs:34-44): dembed[tok] += dy, in position order
+  for (int t = 0; t < T; ++t) {
+    float* dst = d_embed + (size_t)tokens[t] * d;
+    const float* src = dY.data() + (size_t)t * d;
+    for (int i = 0; i < d; ++i) dst[i] += src[i];
+  }
   return 0;
 }
 

@@ -55,6 +55,11 @@ def lib() -> C.CDLL:
         L.orc_forward.argtypes = [C.POINTER(orc_config), pf, pf, C.POINTER(orc_layer),
                                   C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.c_int,
                                   C.c_float, pf, pf, C.POINTER(C.c_int32), C.c_int, pf]
+        L.orc_forward_backward.restype = C.c_int
+        L.orc_forward_backward.argtypes = [C.POINTER(orc_config), pf, pf, C.POINTER(orc_layer),
+                                           C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                           C.c_int, C.c_float, C.c_float, pf, pf, pf,
+                                           C.POINTER(orc_layer)]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_max_threads.restype = C.c_int
         L.orc_f32_to_f16_bits.restype = C.c_uint16
@@ -125,6 +130,28 @@ class OracleModel:
         if rc != 0:
             raise RuntimeError(f"orc_forward failed: {rc}")
         return loss.value, ptl, samp
+
+
+    def forward_backward(self, tokens, targets, softcap: float = 0.0, loss_scale: float = 1.0):
+        """(loss, grads): grads = {"embed", "gamma_final", "layers": [dict]} in the
+        reference orientation, the gradients of one training step (orc_forward_backward)."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.uint32).reshape(-1))
+        g = np.ascontiguousarray(np.asarray(targets, np.uint32).reshape(-1))
+        batch = t.size // self.cfg.seq
+        d_embed = np.zeros_like(self.embed)
+        d_gf = np.zeros_like(self.gamma_final)
+        d_layers = [{k: np.zeros_like(v) for k, v in lw.items()} for lw in self.layers]
+        arr = (orc_layer * self.cfg.nlayers)()
+        for i, lw in enumerate(d_layers):
+            arr[i] = orc_layer(*[_fp(lw[k]) for k in self.LAYER_FIELDS])
+        loss = C.c_float()
+        rc = lib().orc_forward_backward(
+            C.byref(self.c), _fp(self.embed), _fp(self.gamma_final), self._layer_arr,
+            t.ctypes.data_as(C.POINTER(C.c_uint32)), g.ctypes.data_as(C.POINTER(C.c_uint32)),
+            batch, softcap, loss_scale, C.byref(loss), _fp(d_embed), _fp(d_gf), arr)
+        if rc != 0:
+            raise RuntimeError(f"orc_forward_backward failed: {rc}")
+        return loss.value, {"embed": d_embed, "gamma_final": d_gf, "layers": d_layers}
 
 
 def set_threads(n: int) -> None:

@@ -6,9 +6,10 @@ flash attention, vectorised row kernels). There is no CPU fallback.
 """
 from .model import CONFIGS, ModelConfig, custom_config
 from .bridge import CudaBridgeError, CB_INIT_NORMAL, CB_INIT_REFERENCE, load_library
-from .engine import (CompiledKernels, ForwardResult, ForwardScheduler, LayerWeights,
-                     ModelForwardWorkspace, ModelWeights, forward, forward_losses,
-                     forward_only_ws, forward_ws, nccl_unique_id)
+from .engine import (CompiledKernels, ForwardResult, ForwardScheduler, LayerGrads,
+                     LayerWeights, ModelForwardWorkspace, ModelGrads, ModelWeights, forward,
+                     forward_backward, forward_losses, forward_only_ws, forward_ws,
+                     nccl_unique_id)
 from .checkpoint import load_checkpoint, save_checkpoint
 from .data import (DeviceTokens, TokenBytes, TokenData, compute_bpb, random_position,
                    validate)
@@ -17,6 +18,7 @@ __all__ = [
     "CONFIGS", "ModelConfig", "custom_config", "CudaBridgeError", "CB_INIT_NORMAL",
     "CB_INIT_REFERENCE", "load_library", "CompiledKernels", "ForwardResult", "ForwardScheduler",
     "LayerWeights", "ModelForwardWorkspace", "ModelWeights", "forward", "forward_losses",
-    "forward_only_ws", "forward_ws", "nccl_unique_id", "load_checkpoint", "save_checkpoint",
+    "forward_only_ws", "forward_ws", "nccl_unique_id", "LayerGrads", "ModelGrads",
+    "forward_backward", "load_checkpoint", "save_checkpoint",
     "DeviceTokens", "TokenBytes", "TokenData", "compute_bpb", "random_position", "validate",
 ]

@@ -45,6 +45,7 @@ EXPORTED = [
     "cb_attention_bwd_f16", "cb_lm_head_ce_f16",
     "cb_lm_head_ce_f16_noalloc", "cb_load_rstk", "cb_tokens_open", "cb_tokens_from_host",
     "cb_tokens_len", "cb_tokens_close", "cb_forward_loss_windows", "cb_eval_windows",
+    "cb_enable_training", "cb_zero_grads", "cb_forward_backward", "cb_get_grads_f32",
 ]
 
 
@@ -67,6 +68,11 @@ class cb_layer_weights_f32(C.Structure):
 class cb_kernel_time(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_int64), ("total_ms", C.c_double),
                 ("flops", C.c_double), ("bytes", C.c_double)]
+
+
+class cb_layer_grads_f32(C.Structure):
+    _fields_ = [(n, C.POINTER(C.c_float)) for n in
+                ("wq", "wk", "wv", "wo", "w1", "w3", "w2", "gamma1", "gamma2")]
 
 
 class cb_eval_totals(C.Structure):
@@ -124,6 +130,10 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_tokens_close": (i32, [vp]),
         "cb_forward_loss_windows": (i32, [vp, vp, C.POINTER(i64), i32, f32, pf, pf]),
         "cb_eval_windows": (i32, [vp, vp, pi32, i32, i64, i64, f32, C.POINTER(cb_eval_totals)]),
+        "cb_enable_training": (i32, [vp]),
+        "cb_zero_grads": (i32, [vp]),
+        "cb_forward_backward": (i32, [vp, pu32, pu32, i32, f32, f32, pf]),
+        "cb_get_grads_f32": (i32, [vp, pf, pf, C.POINTER(cb_layer_grads_f32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -32,6 +32,8 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
+#include <type_traits>
 #include <utility>
 #include <vector>
 
@@ -206,6 +208,12 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN>();
   set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN>();
   set_gemm_attrs_for<EpiStoreF16, GEMM_A_MN | GEMM_B_MN>();
+  // training step (training.cuh)
+  set_gemm_attrs_for<EpiSwigluSave>();
+  set_gemm_attrs_for<EpiCeBwd>();
+  set_gemm_attrs_for<EpiScaledF32, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiSwigluBwd, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwiglu>();
@@ -404,21 +412,22 @@ cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half*
   return cudaGetLastError();
 }
 
-// x += delta; xn = rmsnorm(x) * gamma (rows kept in registers up to 2048 wide).
+// x = x_in + delta; xn = rmsnorm(x) * gamma (rows kept in registers up to 2048 wide).
+// x_in == x is the in-place update; rinv (nullable) receives 1/rms per row.
 template <typename DT>
-cudaError_t launch_add_rmsnorm(float* x, const DT* delta, const float* gamma, __half* xn,
-                               int T, int d, cudaStream_t st) {
+cudaError_t launch_add_rmsnorm(const float* x_in, float* x, const DT* delta, const float* gamma,
+                               __half* xn, int T, int d, cudaStream_t st, float* rinv = nullptr) {
   const int blocks = (T + ROW_WARPS - 1) / ROW_WARPS, threads = ROW_WARPS * 32;
   if (d <= 512)
-    add_rmsnorm_kernel<2, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+    add_rmsnorm_kernel<2, DT><<<blocks, threads, 0, st>>>(x_in, x, delta, gamma, xn, T, d, rinv);
   else if (d <= 1024)
-    add_rmsnorm_kernel<4, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+    add_rmsnorm_kernel<4, DT><<<blocks, threads, 0, st>>>(x_in, x, delta, gamma, xn, T, d, rinv);
   else if (d <= 1536)
-    add_rmsnorm_kernel<6, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+    add_rmsnorm_kernel<6, DT><<<blocks, threads, 0, st>>>(x_in, x, delta, gamma, xn, T, d, rinv);
   else if (d <= 2048)
-    add_rmsnorm_kernel<8, DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+    add_rmsnorm_kernel<8, DT><<<blocks, threads, 0, st>>>(x_in, x, delta, gamma, xn, T, d, rinv);
   else
-    add_rmsnorm_long_kernel<DT><<<blocks, threads, 0, st>>>(x, delta, gamma, xn, T, d);
+    add_rmsnorm_long_kernel<DT><<<blocks, threads, 0, st>>>(x_in, x, delta, gamma, xn, T, d, rinv);
   return cudaGetLastError();
 }
 
@@ -450,6 +459,9 @@ struct KStat {
 }  // namespace
 
 // ------------------------------------------------------------ context
+struct TrainState;
+void free_train_state(TrainState* t);
+
 struct cb_ctx {
   cb_model_config cfg{};
   int device = 0;
@@ -522,6 +534,9 @@ struct cb_ctx {
   std::vector<double> ev_flops, ev_bytes;
   bool pending_harvest = false;
 
+  // training (cb_enable_training): saved activations, backward scratch, gradients
+  TrainState* train = nullptr;
+
   size_t T_max() const { return (size_t)max_batch * cfg.seq; }
 };
 
@@ -573,6 +588,8 @@ void free_ctx(cb_ctx* c) {
   cudaSetDevice(c->device);
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   c->graphs.clear();
+  free_train_state(c->train);
+  c->train = nullptr;
   for (auto e : c->events) cudaEventDestroy(e);
   if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
   void* ptrs[] = {c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
@@ -662,8 +679,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     return cudaSuccess;
   };
   auto add_norm = [&](const float* gamma) -> cudaError_t {
-    cudaError_t r = delta_f32 ? launch_add_rmsnorm(c->x, c->delta32, gamma, c->xn, T, d, st)
-                              : launch_add_rmsnorm(c->x, c->delta, gamma, c->xn, T, d, st);
+    cudaError_t r = delta_f32 ? launch_add_rmsnorm(c->x, c->x, c->delta32, gamma, c->xn, T, d, st)
+                              : launch_add_rmsnorm(c->x, c->x, c->delta, gamma, c->xn, T, d, st);
     if (r == cudaSuccess) mark(K_RMSNORM, 0, Td * d * (4 + (delta_f32 ? 4 : 2) + 4 + 2));
     return r;
   };
@@ -1996,3 +2013,5 @@ extern "C" cb_status cb_lm_head_ce_f16_noalloc(const void* xf, const void* embed
                                 s, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
+
+#include "training.cuh"

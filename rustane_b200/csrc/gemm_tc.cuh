@@ -80,6 +80,13 @@ struct EpiAtomic { static constexpr bool value = false; };
 template <class Epi>
 struct EpiAtomic<Epi, decltype(void(Epi::ATOMIC))> { static constexpr bool value = Epi::ATOMIC; };
 
+// Epilogues with set_split(k) are told which K split a work unit covers (split-K into
+// separate partial buffers).
+template <class Epi, class = void>
+struct EpiHasSplit { static constexpr bool value = false; };
+template <class Epi>
+struct EpiHasSplit<Epi, decltype(void(&Epi::set_split))> { static constexpr bool value = true; };
+
 __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   uint4 w;
   w.x = pack_half2(f[0], f[1]);
@@ -324,6 +331,142 @@ struct EpiSwiglu {
     o[0] = pack8_f16(r);
     o[1] = pack8_f16(r + 8);
     dst = reinterpret_cast<uint8_t*>(g + (size_t)row * ldg + (col0 >> 1));
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// Training forward of W1/W3: g as EpiSwiglu, and the pre-activations (h1, h3
+// interleaved, as the accumulator holds them) saved in fp16 for the backward pass.
+struct EpiSwigluSave {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 32;
+  __half* g;
+  int ldg;
+  __half* h13;
+  int ldh;
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    float r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float h1 = v[2 * j], h3 = v[2 * j + 1];
+      r[j] = h1 / (1.0f + __expf(-h1)) * h3;
+    }
+    uint4* hs = reinterpret_cast<uint4*>(h13 + (size_t)row * ldh + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hs[j] = pack8_f16(v + 8 * j);
+    o[0] = pack8_f16(r);
+    o[1] = pack8_f16(r + 8);
+    dst = reinterpret_cast<uint8_t*>(g + (size_t)row * ldg + (col0 >> 1));
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// Backward of the SwiGLU gate, fused into dG = (alpha dY) W2 (layer.rs:6760-6771):
+// for hidden column j, sig = 1/(1 + e^-h1), dh3 = dG h1 sig, dh1 = dG h3 sig (1 +
+// h1 (1 - sig)). Writes dh1, dh3 interleaved like the W1/W3 storage rows, the layout
+// the next GEMMs (dX = dH13 W13, dW13 = dH13^T X2n) read. The row's saved (h1, h3) are
+// loaded per chunk (prefetching a chunk ahead would need 64 more registers per thread).
+struct EpiSwigluBwd {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 128;
+  __half* dh13;
+  const __half* h13;
+  int ld;  // 2 * hidden
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    const uint4* src = reinterpret_cast<const uint4*>(h13 + (size_t)row * ld + 2 * col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __ldg(src + i);  // (h1, h3) pairs, fp16
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 hv = o[i];
+      const __half2* hh = reinterpret_cast<const __half2*>(&hv);
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 h = __half22float2(hh[k]);  // (h1, h3) of column 4i + k
+        const float dg = v[4 * i + k];
+        const float sig = 1.0f / (1.0f + __expf(-h.x));
+        const float dh3 = dg * h.x * sig;
+        const float dh1 = dg * h.y * sig * (1.0f + h.x * (1.0f - sig));
+        w[k] = pack_half2(dh1, dh3);
+      }
+      o[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    dst = reinterpret_cast<uint8_t*>(dh13 + (size_t)row * ld + 2 * col0);
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// Gradient of the loss w.r.t. the logits, recomputed from the saved per-token
+// log-sum-exp (tok_loss + target logit): dl = softmax(z) - onehot(target), times the
+// softcap derivative 1 - tanh^2 when softcap > 0 (cross_entropy.rs:58-96,
+// full_model.rs:600-611). fp16 output, unscaled (the 1/seq and loss scale are applied
+// by the GEMMs that consume it, where the values are fp32).
+struct EpiCeBwd {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 64;
+  __half* dl;
+  int ldo;
+  const uint32_t* targets;
+  const float* tok_loss;
+  const float* tgt_logit;
+  float softcap;
+  float lse;
+  int tgt;
+  __device__ __forceinline__ void begin_row(int row, bool valid) {
+    tgt = valid ? (int)targets[row] : -1;
+    lse = valid ? tok_loss[row] + tgt_logit[row] : 0.f;
+  }
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    float r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float z = v[i], der = 1.0f;
+      if (softcap > 0.f) {
+        const float t = tanhf(z / softcap);
+        z = softcap * t;
+        der = 1.0f - t * t;
+      }
+      float g = __expf(z - lse);
+      if (col0 + i == tgt) g -= 1.0f;
+      r[i] = g * der;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pack8_f16(r + 8 * j);
+    dst = reinterpret_cast<uint8_t*>(dl + (size_t)row * ldo + col0);
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// alpha * acc into slice `split` of a [splits][M][ldo] fp32 partial buffer: split-K of
+// the weight-gradient GEMMs (K = tokens), reduced afterwards in a fixed order.
+struct EpiPartialF32 {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 128;
+  float* out;
+  int ldo;
+  float alpha;
+  size_t split_stride;
+  __device__ __forceinline__ void set_split(int s) { out += (size_t)s * split_stride; }
+  __device__ __forceinline__ void begin_row(int, bool) {}
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = make_float4(alpha * v[4 * j], alpha * v[4 * j + 1], alpha * v[4 * j + 2],
+                                   alpha * v[4 * j + 3]);
+      o[j] = *reinterpret_cast<const uint4*>(&w);
+    }
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
 };
@@ -605,6 +748,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       const int row = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32 + lane;
       const bool row_ok = row < M;
       Epi e = epi;
+      if constexpr (EpiHasSplit<Epi>::value) e.set_split(u % splits);
       e.begin_row(row, row_ok);
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(group * BN);
       typename Epi::Pre pa, pb;

@@ -55,7 +55,7 @@ __global__ void embed_rmsnorm_kernel(const uint32_t* __restrict__ tokens,
                                      const __half* __restrict__ embed,
                                      const float* __restrict__ gamma, float* __restrict__ x,
                                      __half* __restrict__ xn, int T, int dim, int vocab,
-                                     int* err) {
+                                     int* err, float* __restrict__ rinv_out = nullptr) {
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -77,6 +77,7 @@ __global__ void embed_rmsnorm_kernel(const uint32_t* __restrict__ tokens,
   }
   ss = warp_sum(ss);
   const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  if (rinv_out && lane == 0) rinv_out[row] = rinv;
   __half* o = xn + (size_t)row * dim;
   for (int c = lane * 8; c < dim; c += 256) {
     float f[8];
@@ -128,16 +129,19 @@ __device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
 }
 
 // Residual add + RMSNorm, the reference's vsma + rmsnorm pair (layer.rs:4932-4940,
-// cpu/rmsnorm.rs:149-183): x += delta (projection output already scaled by alpha;
+// cpu/rmsnorm.rs:149-183): x = x_in + delta (projection output already scaled by alpha;
 // fp16, or fp32 after a tensor-parallel all-reduce), then xn = x * rinv * gamma.
+// x_in == x updates the residual in place (inference); a training forward keeps each
+// layer's residual and passes a new x. rinv_out (nullable) keeps 1/rms per row.
 // One warp per row; rows of up to NREG*256 elements stay in registers.
 template <int NREG, typename DT>
-__global__ void add_rmsnorm_kernel(float* __restrict__ x, const DT* __restrict__ delta,
+__global__ void add_rmsnorm_kernel(const float* x_in, float* x, const DT* __restrict__ delta,
                                    const float* __restrict__ gamma, __half* __restrict__ xn,
-                                   int T, int dim) {
+                                   int T, int dim, float* __restrict__ rinv_out) {
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
+  const float* xi = x_in + (size_t)row * dim;
   float* xr = x + (size_t)row * dim;
   const DT* dr = delta + (size_t)row * dim;
   float keep[NREG][8];
@@ -146,8 +150,8 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const DT* __restrict__
   for (int it = 0; it < NREG; ++it) {
     const int c = it * 256 + lane * 8;
     if (c < dim) {
-      const float4 a = *reinterpret_cast<const float4*>(xr + c);
-      const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+      const float4 a = *reinterpret_cast<const float4*>(xi + c);
+      const float4 b = *reinterpret_cast<const float4*>(xi + c + 4);
       float dv[8];
       load8(dr + c, dv);
       float* f = keep[it];
@@ -161,6 +165,7 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const DT* __restrict__
   }
   ss = warp_sum(ss);
   const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
+  if (rinv_out && lane == 0) rinv_out[row] = rinv;
   __half* o = xn + (size_t)row * dim;
 #pragma unroll
   for (int it = 0; it < NREG; ++it) {
@@ -179,18 +184,19 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const DT* __restrict__
 
 // Same for rows longer than the register budget: the second pass re-reads x (L2-hot).
 template <typename DT>
-__global__ void add_rmsnorm_long_kernel(float* __restrict__ x, const DT* __restrict__ delta,
+__global__ void add_rmsnorm_long_kernel(const float* x_in, float* x, const DT* __restrict__ delta,
                                         const float* __restrict__ gamma, __half* __restrict__ xn,
-                                        int T, int dim) {
+                                        int T, int dim, float* __restrict__ rinv_out) {
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
+  const float* xi = x_in + (size_t)row * dim;
   float* xr = x + (size_t)row * dim;
   const DT* dr = delta + (size_t)row * dim;
   float ss = 0.f;
   for (int c = lane * 8; c < dim; c += 256) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + c);
-    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    const float4 a = *reinterpret_cast<const float4*>(xi + c);
+    const float4 b = *reinterpret_cast<const float4*>(xi + c + 4);
     float dv[8];
     load8(dr + c, dv);
     float f[8] = {a.x + dv[0], a.y + dv[1], a.z + dv[2], a.w + dv[3],

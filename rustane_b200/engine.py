@@ -85,6 +85,52 @@ class ModelWeights:
                    gamma_final=np.ascontiguousarray(gamma_final, np.float32))
 
 
+@dataclass
+class LayerGrads:
+    """Host f32 layer gradients, reference orientation (layer.rs:66-76)."""
+    dwq: np.ndarray
+    dwk: np.ndarray
+    dwv: np.ndarray
+    dwo: np.ndarray
+    dw1: np.ndarray
+    dw3: np.ndarray
+    dw2: np.ndarray
+    dgamma1: np.ndarray
+    dgamma2: np.ndarray
+
+
+@dataclass
+class ModelGrads:
+    """Host f32 gradients of all weights (full_model.rs:26-30)."""
+    dembed: np.ndarray
+    layers: list
+    dgamma_final: np.ndarray
+
+    @classmethod
+    def zeros(cls, cfg: ModelConfig) -> "ModelGrads":
+        d, h = cfg.dim, cfg.hidden
+        qd, kvd = cfg.heads * cfg.hd, cfg.kv_heads * cfg.hd
+        z = lambda *s: np.zeros(s, np.float32)  # noqa: E731
+        return cls(z(cfg.vocab, d),
+                   [LayerGrads(z(d, qd), z(d, kvd), z(d, kvd), z(qd, d), z(d, h), z(d, h),
+                               z(d, h), z(d), z(d)) for _ in range(cfg.nlayers)], z(d))
+
+    def zero_out(self) -> None:
+        """ModelGrads::zero_out (full_model.rs:152)."""
+        self.dembed[...] = 0
+        self.dgamma_final[...] = 0
+        for lg in self.layers:
+            for a in vars(lg).values():
+                a[...] = 0
+
+    def add_(self, other: "ModelGrads") -> None:
+        self.dembed += other.dembed
+        self.dgamma_final += other.dgamma_final
+        for a, b in zip(self.layers, other.layers):
+            for k in vars(a):
+                getattr(a, k)[...] += getattr(b, k)
+
+
 class ModelForwardWorkspace:
     """Accepted for API compatibility. The device workspace lives inside
     CompiledKernels (sized by its max_batch); nothing is allocated here."""
@@ -186,6 +232,40 @@ class CompiledKernels:
                                                      _fptr(w.gamma_final), arr))
         self._loaded_generation = w.generation
 
+    # ---- training (backward pass)
+    def enable_training(self) -> None:
+        """Allocate saved activations, backward scratch and gradients on the device."""
+        if not getattr(self, "_training", False):
+            self._check(self.lib.cb_enable_training(self.handle))
+            self._training = True
+
+    def zero_grads(self) -> None:
+        self._check(self.lib.cb_zero_grads(self.handle))
+
+    def forward_backward(self, tokens, targets, softcap: float = 0.0,
+                         loss_scale: float = 1.0) -> float:
+        """One training step: returns the mean loss; gradients accumulate on the device."""
+        self.enable_training()
+        t, g, batch = self._tokens(tokens, targets)
+        loss = C.c_float()
+        self._check(self.lib.cb_forward_backward(
+            self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)),
+            g.ctypes.data_as(C.POINTER(C.c_uint32)), batch, softcap, loss_scale, C.byref(loss)))
+        return loss.value
+
+    def grads(self, out: Optional["ModelGrads"] = None) -> "ModelGrads":
+        """The accumulated device gradients in the reference orientation (host f32)."""
+        cfg = self.cfg
+        if out is None:
+            out = ModelGrads.zeros(cfg)
+        arr = (B.cb_layer_grads_f32 * cfg.nlayers)()
+        for i, lg in enumerate(out.layers):
+            arr[i] = B.cb_layer_grads_f32(*[_fptr(getattr(lg, k)) for k in (
+                "dwq", "dwk", "dwv", "dwo", "dw1", "dw3", "dw2", "dgamma1", "dgamma2")])
+        self._check(self.lib.cb_get_grads_f32(self.handle, _fptr(out.dembed),
+                                              _fptr(out.dgamma_final), arr))
+        return out
+
     def load_checkpoint(self, path) -> int:
         """Stream an RSTK checkpoint (train.rs:238-346) into the device weights;
         returns the step recorded in its header."""
@@ -280,6 +360,23 @@ class CompiledKernels:
         s = C.c_void_p()
         self._check(self.lib.cb_get_stream(self.handle, C.byref(s)))
         return s.value or 0
+
+
+def forward_backward(cfg: ModelConfig, kernels: "CompiledKernels", weights: ModelWeights,
+                     tokens, targets, softcap: float = 0.0, loss_scale: float = 1.0,
+                     grads: Optional[ModelGrads] = None) -> float:
+    """forward_ws followed by backward_ws (full_model.rs:494, 592-702): returns the loss
+    and ADDS this call's gradients into `grads` (host, reference orientation), as the
+    reference accumulates ModelGrads across micro-batches. The device keeps its own
+    running sum too (CompiledKernels.grads / zero_grads)."""
+    kernels.load_weights(weights)
+    kernels.enable_training()
+    if grads is None:
+        return kernels.forward_backward(tokens, targets, softcap, loss_scale)
+    kernels.zero_grads()
+    loss = kernels.forward_backward(tokens, targets, softcap, loss_scale)
+    grads.add_(kernels.grads())
+    return loss
 
 
 def nccl_unique_id() -> bytes:

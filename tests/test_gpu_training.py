@@ -1,0 +1,171 @@
+"""GPU tests of the training step (forward with saved activations + backward) through
+the C ABI, against the CPU oracle's backward (oracle/forward_ref.cpp
+orc_forward_backward, itself checked against float64 autograd in test_oracle.py).
+
+Tolerances: the GPU keeps activations and activation gradients in fp16 with fp32
+accumulation, the oracle is fp32 throughout. Each gradient tensor must reach cosine
+similarity >= 0.999 with the oracle's and a max-abs error <= 3e-2 of its largest
+element; the loss matches within 1e-3 relative (the forward's own bound)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle.oracle import OracleModel, SCHEME_NORMAL
+from rustane_b200 import (CompiledKernels, CudaBridgeError, LayerWeights, ModelGrads,
+                          ModelWeights, forward_backward)
+from rustane_b200 import bridge as B
+from rustane_b200.model import custom_config
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.999
+MAXABS_REL = 3e-2
+
+
+def _model(cfg, seed, sigma=0.05):
+    ora = OracleModel(cfg, seed=seed, scheme=SCHEME_NORMAL, sigma=sigma)
+    rng = np.random.default_rng(seed + 100)
+    for lw in ora.layers:  # non-unit gains
+        lw["gamma1"][:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+        lw["gamma2"][:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+    ora.gamma_final[:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+    w = ModelWeights.from_arrays(ora.embed, [LayerWeights(**lw) for lw in ora.layers],
+                                 ora.gamma_final)
+    return ora, w
+
+
+def _tokens(cfg, batch, seed):
+    rng = np.random.default_rng(seed)
+    return (rng.integers(0, cfg.vocab, batch * cfg.seq).astype(np.uint32),
+            rng.integers(0, cfg.vocab, batch * cfg.seq).astype(np.uint32))
+
+
+def _pairs(g: ModelGrads, ref: dict):
+    yield "embed", g.dembed, ref["embed"]
+    yield "gamma_final", g.dgamma_final, ref["gamma_final"]
+    names = dict(dwq="wq", dwk="wk", dwv="wv", dwo="wo", dw1="w1", dw3="w3", dw2="w2",
+                 dgamma1="gamma1", dgamma2="gamma2")
+    for l, (lg, lr) in enumerate(zip(g.layers, ref["layers"])):
+        for k, rk in names.items():
+            yield f"layer{l}.{rk}", getattr(lg, k), lr[rk]
+
+
+def _check_grads(g: ModelGrads, ref: dict):
+    for name, got, want in _pairs(g, ref):
+        got = got.astype(np.float64).ravel()
+        want = want.astype(np.float64).ravel()
+        scale = np.abs(want).max()
+        assert scale > 0, name
+        cos = got @ want / (np.linalg.norm(got) * np.linalg.norm(want))
+        err = np.abs(got - want).max()
+        assert cos >= COS_MIN, (name, cos)
+        assert err <= MAXABS_REL * scale, (name, err, scale)
+
+
+@pytest.mark.parametrize("kv_heads,softcap,loss_scale", [(2, 0.0, 1.0), (1, 15.0, 8.0)])
+def test_training_step_matches_oracle(bridge_lib, kv_heads, softcap, loss_scale):
+    cfg = custom_config(512, 1024, 2, 2, 128, 1024).replace(kv_heads=kv_heads)
+    ora, w = _model(cfg, seed=5)
+    tok, tgt = _tokens(cfg, 3, 7)
+    l_ref, g_ref = ora.forward_backward(tok, tgt, softcap, loss_scale)
+    with CompiledKernels(cfg, 0, 3) as k:
+        k.load_weights(w)
+        k.enable_training()
+        loss = k.forward_backward(tok, tgt, softcap, loss_scale)
+        g = k.grads()
+        l_fwd = k.forward_loss(tok, tgt, softcap)
+    assert abs(loss - l_ref) / l_ref <= 1e-3, (loss, l_ref)
+    assert abs(loss - l_fwd) <= 1e-5 * l_fwd
+    _check_grads(g, g_ref)
+
+
+def test_training_600m_shape_two_layers(bridge_lib):
+    """The 600m-A layer shape (1536 / 4096 / 12 heads, seq 512, vocab 8192) at 2 layers."""
+    cfg = custom_config(1536, 4096, 12, 2, 512, 8192)
+    ora, w = _model(cfg, seed=9, sigma=0.02)
+    tok, tgt = _tokens(cfg, 2, 3)
+    l_ref, g_ref = ora.forward_backward(tok, tgt)
+    with CompiledKernels(cfg, 0, 2) as k:
+        k.load_weights(w)
+        loss = k.forward_backward(tok, tgt)
+        g = k.grads()
+    assert abs(loss - l_ref) / l_ref <= 1e-3
+    _check_grads(g, g_ref)
+
+
+def test_gradients_accumulate_zero_and_reproduce(bridge_lib):
+    cfg = custom_config(256, 512, 2, 2, 128, 512)
+    _, w = _model(cfg, seed=2)
+    tok, tgt = _tokens(cfg, 2, 4)
+    with CompiledKernels(cfg, 0, 2) as k:
+        k.load_weights(w)
+        k.enable_training()
+        l1 = k.forward_backward(tok, tgt)
+        g1 = k.grads()
+        l2 = k.forward_backward(tok, tgt)
+        g2 = k.grads()
+        assert l1 == l2
+        for (_, a, _), (_, b, _) in zip(_pairs(g1, _flat_ref(g1)), _pairs(g2, _flat_ref(g2))):
+            np.testing.assert_allclose(b, 2 * a, rtol=1e-5, atol=1e-9)
+        k.zero_grads()
+        z = k.grads()
+        assert not np.any(z.dembed) and not np.any(z.layers[1].dw2)
+        k.forward_backward(tok, tgt)
+        g3 = k.grads()
+    # a fresh context gives bit-identical gradients
+    with CompiledKernels(cfg, 0, 2) as k2:
+        k2.load_weights(w)
+        k2.forward_backward(tok, tgt)
+        g4 = k2.grads()
+    for (name, a1, _), (_, a3, _), (_, a4, _) in zip(_pairs(g1, _flat_ref(g1)),
+                                                      _pairs(g3, _flat_ref(g3)),
+                                                      _pairs(g4, _flat_ref(g4))):
+        assert np.array_equal(a1, a3), name  # the same step onto zeroed gradients
+        assert np.array_equal(a3, a4), name  # and in a fresh context
+
+
+def _flat_ref(g: ModelGrads) -> dict:
+    names = dict(dwq="wq", dwk="wk", dwv="wv", dwo="wo", dw1="w1", dw3="w3", dw2="w2",
+                 dgamma1="gamma1", dgamma2="gamma2")
+    return {"embed": g.dembed, "gamma_final": g.dgamma_final,
+            "layers": [{v: getattr(lg, k) for k, v in names.items()} for lg in g.layers]}
+
+
+def test_batch_gradient_is_sum_of_sequences(bridge_lib):
+    """Two sequences in one step give the sum of their separate steps' gradients, as
+    two reference calls accumulating into one ModelGrads would."""
+    cfg = custom_config(256, 512, 2, 1, 128, 512)
+    _, w = _model(cfg, seed=3)
+    tok, tgt = _tokens(cfg, 2, 5)
+    S = cfg.seq
+    with CompiledKernels(cfg, 0, 2) as k:
+        both = ModelGrads.zeros(cfg)
+        forward_backward(cfg, k, w, tok, tgt, grads=both)
+        split = ModelGrads.zeros(cfg)
+        forward_backward(cfg, k, w, tok[:S], tgt[:S], grads=split)
+        forward_backward(cfg, k, w, tok[S:], tgt[S:], grads=split)
+    for (name, a, _), (_, b, _) in zip(_pairs(both, _flat_ref(both)),
+                                       _pairs(split, _flat_ref(split))):
+        scale = np.abs(b).max()
+        assert np.abs(a - b).max() <= 1e-3 * scale + 1e-9, name
+
+
+def test_training_errors(bridge_lib):
+    cfg = custom_config(256, 512, 2, 1, 128, 512)
+    lib = B.load_library()
+    with CompiledKernels(cfg, 0, 1) as k:
+        loss = C.c_float()
+        tok = np.zeros(cfg.seq, np.uint32)
+        p = tok.ctypes.data_as(C.POINTER(C.c_uint32))
+        assert lib.cb_forward_backward(k.handle, p, p, 1, 0.0, 1.0, C.byref(loss)) == \
+            B.CB_ERR_NOT_READY
+        assert lib.cb_zero_grads(k.handle) == B.CB_ERR_NOT_READY
+        k.init_weights(0, B.CB_INIT_NORMAL, 0.02)
+        k.enable_training()
+        bad = tok.copy()
+        bad[5] = cfg.vocab
+        with pytest.raises(CudaBridgeError) as e:
+            k.forward_backward(bad, tok)
+        assert e.value.status == B.CB_ERR_INVALID_ARG
+        assert np.isfinite(k.forward_backward(tok, tok))

@@ -181,3 +181,103 @@ def test_init_loss_near_log_vocab(oracle_lib):
     loss = m.forward(tok, tgt)[0]
     assert 0 < loss < 20
     assert abs(loss - np.log(8192)) < 0.5
+
+
+def _torch_params64(m: OracleModel):
+    f = lambda a: torch.tensor(np.asarray(a, np.float64), requires_grad=True)  # noqa: E731
+    return {"embed": f(m.embed), "gamma_final": f(m.gamma_final),
+            "layers": [{k: f(v) for k, v in lw.items()} for lw in m.layers]}
+
+
+def _torch_seq_loss64(cfg, P, tokens, targets, softcap=0.0):
+    """Sum over sequences of each sequence's mean token loss, float64 autograd."""
+    S = cfg.seq
+    tok = torch.from_numpy(np.asarray(tokens, np.int64)).view(-1, S)
+    x = P["embed"][tok]
+    alpha = 1.0 / np.sqrt(2.0 * cfg.nlayers)
+    p = torch.arange(S, dtype=torch.float64)[:, None]
+    i = torch.arange(64, dtype=torch.float64)[None, :]
+    th = p * torch.pow(torch.tensor(10000.0, dtype=torch.float64), -2.0 * i / 128.0)
+    cos, sin = torch.cos(th), torch.sin(th)
+
+    def norm(v, g):
+        return v / torch.sqrt((v * v).mean(-1, keepdim=True) + 1e-5) * g
+
+    def rope(v):
+        B_ = v.shape[0]
+        v = v.view(B_, S, -1, 64, 2)
+        a, b = v[..., 0], v[..., 1]
+        c, s = cos[None, :, None, :], sin[None, :, None, :]
+        return torch.stack([a * c - b * s, b * c + a * s], -1).view(B_, S, -1)
+
+    for lw in P["layers"]:
+        xn = norm(x, lw["gamma1"])
+        q, k, v = rope(xn @ lw["wq"]), rope(xn @ lw["wk"]), xn @ lw["wv"]
+        B_ = q.shape[0]
+        q = q.view(B_, S, cfg.heads, 128).transpose(1, 2)
+        k = k.view(B_, S, cfg.kv_heads, 128).transpose(1, 2).repeat_interleave(cfg.gqa_ratio, 1)
+        v = v.view(B_, S, cfg.kv_heads, 128).transpose(1, 2).repeat_interleave(cfg.gqa_ratio, 1)
+        sc = q @ k.transpose(-1, -2) / np.sqrt(128.0)
+        sc = sc.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool), 1), float("-inf"))
+        a = (torch.softmax(sc, -1) @ v).transpose(1, 2).reshape(B_, S, -1)
+        x = x + alpha * (a @ lw["wo"])
+        xn = norm(x, lw["gamma2"])
+        h1, h3 = xn @ lw["w1"], xn @ lw["w3"]
+        x = x + alpha * ((h1 * torch.sigmoid(h1) * h3) @ lw["w2"].T)
+    z = norm(x, P["gamma_final"]) @ P["embed"].T
+    if softcap > 0:
+        z = softcap * torch.tanh(z / softcap)
+    tgt = torch.from_numpy(np.asarray(targets, np.int64)).view(-1, S)
+    ptl = torch.logsumexp(z, -1) - torch.gather(z, -1, tgt[..., None])[..., 0]
+    return ptl.mean(-1).sum(), ptl.mean().item()
+
+
+def _grad_close(got, want, rtol):
+    """Max-abs error relative to the tensor's largest gradient."""
+    want = want.detach().numpy()
+    scale = max(np.abs(want).max(), 1e-12)
+    err = np.abs(got.astype(np.float64) - want).max()
+    assert err <= rtol * scale, (err, scale)
+
+
+@pytest.mark.parametrize("softcap,kv_heads", [(0.0, 2), (12.0, 1)])
+def test_oracle_backward_matches_float64_autograd(oracle_lib, softcap, kv_heads):
+    """orc_forward_backward (the reference's backward restated in fp32) against float64
+    autograd of the same forward, with non-unit gains and GQA."""
+    cfg = custom_config(256, 512, 2, 2, 64, 384).replace(kv_heads=kv_heads)
+    m = OracleModel(cfg, seed=11, scheme=SCHEME_NORMAL, sigma=0.08)
+    rng = np.random.default_rng(3)
+    for lw in m.layers:
+        lw["gamma1"][:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+        lw["gamma2"][:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+        lw["wo"][:] = 0.08 * rng.standard_normal(lw["wo"].shape)
+        lw["w2"][:] = 0.08 * rng.standard_normal(lw["w2"].shape)
+    m.gamma_final[:] = 1 + 0.2 * rng.standard_normal(cfg.dim)
+    tok = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+    loss_scale = 4.0
+    loss, g = m.forward_backward(tok, tgt, softcap, loss_scale)
+    P = _torch_params64(m)
+    total, mean = _torch_seq_loss64(cfg, P, tok, tgt, softcap)
+    (loss_scale * total).backward()
+    assert abs(loss - mean) / mean < 1e-5
+    _grad_close(g["embed"], P["embed"].grad, 1e-4)
+    _grad_close(g["gamma_final"], P["gamma_final"].grad, 1e-4)
+    for gl, pl in zip(g["layers"], P["layers"]):
+        for k in OracleModel.LAYER_FIELDS:
+            _grad_close(gl[k], pl[k].grad, 1e-4)
+
+
+def test_oracle_backward_accumulates(oracle_lib):
+    """Two sequences in one call give the sum of the two single-sequence gradients."""
+    cfg = custom_config(256, 512, 2, 1, 64, 256)
+    m = OracleModel(cfg, seed=2, scheme=SCHEME_NORMAL, sigma=0.05)
+    rng = np.random.default_rng(8)
+    tok = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, 2 * cfg.seq).astype(np.uint32)
+    _, g2 = m.forward_backward(tok, tgt)
+    _, ga = m.forward_backward(tok[:64], tgt[:64])
+    _, gb = m.forward_backward(tok[64:], tgt[64:])
+    np.testing.assert_allclose(g2["embed"], ga["embed"] + gb["embed"], rtol=1e-4, atol=1e-7)
+    np.testing.assert_allclose(g2["layers"][0]["w1"], ga["layers"][0]["w1"] + gb["layers"][0]["w1"],
+                               rtol=1e-4, atol=1e-7)
