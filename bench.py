@@ -64,8 +64,10 @@ def parse_args():
                    help="CPU-baseline sample budget (seconds of oracle work)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=("forward", "validate", "rstk-load"), default="forward",
-                   help="forward: the headline forward+loss step; validate: the evaluation "
+    p.add_argument("--workload", choices=("forward", "train", "validate", "rstk-load"),
+                   default="forward",
+                   help="forward: the headline forward+loss step; train: one training step "
+                        "(forward + backward into fp32 gradients); validate: the evaluation "
                         "loop over an HBM-resident uint16 token file (val_loss + val_bpb); "
                         "rstk-load: RSTK checkpoint file -> fp16 device weights (1 GPU)")
     return p.parse_args()
@@ -300,12 +302,103 @@ def run_io_workload(args):
     print(json.dumps(line), flush=True)
 
 
+def run_train_workload(args):
+    """Training step throughput (forward + backward, gradients accumulated on the
+    device), sequence-sharded over the GPUs like the forward (data parallel: each rank
+    trains on its share of the batch; the gradient all-reduce of a data-parallel
+    optimizer step is not part of this step). The timed region is K graph replays of
+    cb_forward_backward with host tokens (H2D + step + D2H of the loss each step), CUDA
+    events on the context's stream, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
+    from rustane_b200.model import CONFIGS
+    from rustane_b200.sharding import global_tokens, rank_shard, reduce_max, shard_sequences
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    cfg = CONFIGS[args.config]
+    per = shard_sequences(args.global_batch, world)
+    all_tok, all_tgt = global_tokens(cfg.vocab, cfg.seq, args.global_batch, args.seed)
+    tok, tgt = rank_shard(all_tok, all_tgt, cfg.seq, rank, per)
+    tok = np.ascontiguousarray(tok)
+    tgt = np.ascontiguousarray(tgt)
+    kern = CompiledKernels(cfg, local, per)
+    kern.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
+    kern.enable_training()
+    stream = torch.cuda.ExternalStream(kern.stream())
+    for _ in range(args.warmup):
+        loss = kern.forward_backward(tok, tgt)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        loss = kern.forward_backward(tok, tgt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = reduce_max(e0.elapsed_time(e1), device="cuda") / args.steps
+    clk = clocks.stop() if clocks else None
+    tokens = args.global_batch * cfg.seq
+    flops = cfg.train_flops_per_token() * tokens
+    peaks, peak_kind = load_peaks()
+    peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    tf = flops / (ms / 1e3) / 1e12 / world
+    if rank == 0:
+        line = {
+            "metric": "training tokens/sec (forward + backward into fp32 gradients, seq512)",
+            "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16", "data": "synthetic (uniform random tokens, N(0,0.02) weights)",
+            "config": {"workload": f"{args.config} training step, global batch "
+                                   f"{args.global_batch} x seq {cfg.seq}",
+                       "global_batch": args.global_batch, "seq_len": cfg.seq,
+                       "parallelism": f"dp{world} (sequence sharding; no gradient all-reduce)",
+                       "l2": "no flush: every step moves tens of GB, far above the 126 MB L2"},
+            "loss": loss,
+            "tflops_per_gpu": round(tf, 1),
+            "roofline": {"kernel": "whole training step (GEMMs, attention, row kernels)",
+                         "bound": "tensor", "achieved": round(tf, 2), "peak": peak_tf,
+                         "unit": "TFLOP/s", "frac": round(tf / peak_tf, 4),
+                         "peak_source": f"bf16_tflops_sustained ({peak_kind})",
+                         "flops_per_token": cfg.train_flops_per_token(), "traffic": None},
+            "e2e": {"value": tokens / (ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(tok.nbytes + tgt.nbytes) * world,
+                    "d2h_bytes_per_step": 4 * world,
+                    "note": "the timed calls are the public host API (cb_forward_backward)"},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    kern.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.global_batch is None:
         args.global_batch = 16 if args.config == "32B" else 64
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "train":
+        run_train_workload(args)
         return
     if args.workload != "forward":
         run_io_workload(args)

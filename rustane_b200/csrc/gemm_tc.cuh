@@ -129,6 +129,40 @@ __device__ __forceinline__ void warp_store_rows(uint8_t* wbuf, const uint4 (&out
   __syncwarp();
 }
 
+// The inverse of warp_store_rows: lane L receives the NB-byte segment at src of row L
+// (src = nullptr: zeros) in in[0 .. NB/16); the warp's loads are coalesced over whole
+// row segments and transposed through the warp's shared buffer.
+template <int NB>
+__device__ __forceinline__ void warp_load_rows(uint8_t* wbuf, const uint8_t* src,
+                                               uint4 (&in)[8]) {
+  constexpr int Q = NB / 16;
+  constexpr int RPI = 32 / Q;
+  const int lane = threadIdx.x & 31;
+  const unsigned long long my = reinterpret_cast<unsigned long long>(src);
+#pragma unroll
+  for (int k = 0; k < Q; ++k) {
+    const int r = k * RPI + lane / Q;
+    const int j = lane % Q;
+    const unsigned long long base = __shfl_sync(0xffffffffu, my, r);
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (base) x = __ldg(reinterpret_cast<const uint4*>(base) + j);
+    const int swr = (r / (8 / Q)) & (Q - 1);
+    *reinterpret_cast<uint4*>(wbuf + r * NB + ((j ^ swr) << 4)) = x;
+  }
+  __syncwarp();
+  const int sw = (lane / (8 / Q)) & (Q - 1);
+#pragma unroll
+  for (int j = 0; j < Q; ++j) in[j] = *reinterpret_cast<const uint4*>(wbuf + lane * NB + ((j ^ sw) << 4));
+  __syncwarp();
+}
+
+// Epilogues with IN_BYTES > 0 read a row segment per chunk: the kernel loads it with
+// warp_load_rows (from in_src(row, col)) into the chunk's output array before chunk().
+template <class Epi, class = void>
+struct EpiInBytes { static constexpr int value = 0; };
+template <class Epi>
+struct EpiInBytes<Epi, decltype(void(Epi::IN_BYTES))> { static constexpr int value = Epi::IN_BYTES; };
+
 struct EpiStoreF16 {
   using Pre = NoPre;
   static constexpr int OUT_BYTES = 64;
@@ -367,21 +401,22 @@ struct EpiSwigluSave {
 // Backward of the SwiGLU gate, fused into dG = (alpha dY) W2 (layer.rs:6760-6771):
 // for hidden column j, sig = 1/(1 + e^-h1), dh3 = dG h1 sig, dh1 = dG h3 sig (1 +
 // h1 (1 - sig)). Writes dh1, dh3 interleaved like the W1/W3 storage rows, the layout
-// the next GEMMs (dX = dH13 W13, dW13 = dH13^T X2n) read. The row's saved (h1, h3) are
-// loaded per chunk (prefetching a chunk ahead would need 64 more registers per thread).
+// the next GEMMs (dX = dH13 W13, dW13 = dH13^T X2n) read. The row's saved (h1, h3)
+// pairs of the chunk (128 B) arrive in o[] (IN_BYTES: loaded by the kernel, coalesced).
 struct EpiSwigluBwd {
   using Pre = NoPre;
   static constexpr int OUT_BYTES = 128;
+  static constexpr int IN_BYTES = 128;
   __half* dh13;
   const __half* h13;
   int ld;  // 2 * hidden
+  __device__ __forceinline__ const uint8_t* in_src(int row, int col0) const {
+    return reinterpret_cast<const uint8_t*>(h13 + (size_t)row * ld + 2 * col0);
+  }
   __device__ __forceinline__ void begin_row(int, bool) {}
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
   __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
                                         uint4 (&o)[8], uint8_t*& dst) {
-    const uint4* src = reinterpret_cast<const uint4*>(h13 + (size_t)row * ld + 2 * col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = __ldg(src + i);  // (h1, h3) pairs, fp16
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint4 hv = o[i];
@@ -764,6 +799,9 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         tmem_ld_wait_regs(r);
         uint4 outv[8];
         uint8_t* dst = nullptr;
+        if constexpr (EpiInBytes<Epi>::value > 0)
+          warp_load_rows<(EpiInBytes<Epi>::value > 0 ? EpiInBytes<Epi>::value : 16)>(
+              wbuf, row_ok ? e.in_src(row, col) : nullptr, outv);
         if (row_ok) {
           float v[32];
 #pragma unroll

@@ -81,6 +81,105 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
   }
 }
 
+// RMSNorm backward with the gain gradient fused (rows of up to NREG * 256 elements):
+// each block handles RB_ROWS rows (8 per warp); every lane keeps the dy * x_hat sums of
+// its columns in registers, the block adds its warps' sums in warp order through shared
+// memory and writes one partial row part[blockIdx.x][dim] (reduced by
+// dgamma_reduce_kernel in block order: deterministic).
+constexpr int RB_ROWS = 64;
+
+template <int NREG>
+__global__ void __launch_bounds__(ROW_WARPS * 32)
+    rmsnorm_bwd_dg_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                          const float* __restrict__ gamma, const float* __restrict__ rinv,
+                          const float* __restrict__ dres, float* __restrict__ dx,
+                          __half* __restrict__ dx_h, float alpha_h, int T, int dim,
+                          float* __restrict__ part) {
+  __shared__ float red[NREG * 256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float dg[NREG][8];
+#pragma unroll
+  for (int it = 0; it < NREG; ++it)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dg[it][i] = 0.f;
+  for (int rr = 0; rr < RB_ROWS / ROW_WARPS; ++rr) {
+    const int row = blockIdx.x * RB_ROWS + rr * ROW_WARPS + warp;
+    if (row >= T) break;
+    const float* dr = dy + (size_t)row * dim;
+    const float* xr = x + (size_t)row * dim;
+    const float ri = rinv[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int it = 0; it < NREG; ++it) {  // pass 1: dot and the gain gradient
+      const int c = it * 256 + lane * 8;
+      if (c < dim) {
+        float a[8], b[8], gm[8];
+        load8(dr + c, a);
+        load8(xr + c, b);
+        load8(gamma + c, gm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xh = b[i] * ri;
+          dot += a[i] * gm[i] * xh;
+          dg[it][i] += a[i] * xh;
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)dim;
+#pragma unroll
+    for (int it = 0; it < NREG; ++it) {  // pass 2 (the row is L1-hot): dx
+      const int c = it * 256 + lane * 8;
+      if (c < dim) {
+        float a[8], b[8], gm[8], r[8];
+        load8(dr + c, a);
+        load8(xr + c, b);
+        load8(gamma + c, gm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = ri * (a[i] * gm[i] - b[i] * ri * dot);
+        if (dres) {
+          float e[8];
+          load8(dres + (size_t)row * dim + c, e);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r[i] += e[i];
+        }
+        float* o = dx + (size_t)row * dim + c;
+        *reinterpret_cast<float4*>(o) = make_float4(r[0], r[1], r[2], r[3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(r[4], r[5], r[6], r[7]);
+        if (dx_h) {
+          float h[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) h[i] = alpha_h * r[i];
+          *reinterpret_cast<uint4*>(dx_h + (size_t)row * dim + c) = f8_to_h8(h);
+        }
+      }
+    }
+  }
+  // block sum of the warps' dgamma partials, in warp order
+  for (int w = 0; w < ROW_WARPS; ++w) {
+    if (warp == w) {
+#pragma unroll
+      for (int it = 0; it < NREG; ++it) {
+        const int c = it * 256 + lane * 8;
+        if (c < dim)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) red[c + i] = (w == 0 ? 0.f : red[c + i]) + dg[it][i];
+      }
+    }
+    __syncthreads();
+  }
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) part[(size_t)blockIdx.x * dim + c] = red[c];
+}
+
+// out[c] += scale * sum_b part[b][c] over `nb` partial rows, in order.
+__global__ void dgamma_reduce_rows_kernel(const float* __restrict__ part, int nb,
+                                          float* __restrict__ out, int dim, float scale) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= dim) return;
+  float acc = 0.f;
+  for (int b = 0; b < nb; ++b) acc += part[(size_t)b * dim + c];
+  out[c] += scale * acc;
+}
+
 constexpr int DGAMMA_SPLITS = 64;
 
 // dgamma[c] = sum_t dy[t][c] x[t][c] rinv[t], first pass: DGAMMA_SPLITS row ranges,
@@ -229,17 +328,40 @@ struct TrainState {
 
 namespace {
 
-// Split count for a weight-gradient GEMM (M x N tiles, K = tokens): double the splits
-// while the work units leave the GPU under two waves and each split keeps >= 1024
+// Tile mode and K split of a weight-gradient GEMM (M x N output, K = tokens): every
+// (mode, splits) candidate gets an estimated time, the FLOPs at a tensor rate scaled by
+// its last-wave fill (and by how fast each tile mode runs these MN-major GEMMs: the CTA
+// pair fastest) plus the split-K partials' DRAM round trip; each split keeps >= 1024
 // k-rows.
-int grad_splits(int mode, int M, int N, int K, const DeviceInfo& di) {
-  const long tiles = mode == GM_PAIR ? (long)((M + 255) / 256) * ((N + 255) / 256)
-                     : mode == GM_SINGLE256 ? (long)((M + 127) / 128) * ((N + 255) / 256)
-                                            : (long)((M + 127) / 128) * ((N + 127) / 128);
-  const long units = mode == GM_PAIR ? di.pair_clusters : di.sms;
-  int s = 1;
-  while (s < 8 && tiles * s < 2 * units && K / (2 * s) >= 1024) s *= 2;
-  return s;
+void pick_grad_gemm(int M, int N, int K, const DeviceInfo& di, size_t max_partial, int* mode,
+                    int* splits) {
+  auto fill = [](long tiles, long units) {
+    const long waves = (tiles + units - 1) / units;
+    return (double)tiles / (double)(waves * units);
+  };
+  const bool n256 = N % 256 == 0;
+  const double flops = 2.0 * M * N * K, tensor = 1.3e15, hbm = 5.0e12;
+  double best = 1e30;
+  *mode = GM_SINGLE128;
+  *splits = 1;
+  for (int sp = 1; sp <= 8; sp *= 2) {
+    if (sp > 1 && (K / sp < 1024 || (size_t)sp * M * N > max_partial)) break;
+    const double extra = sp > 1 ? (double)sp * M * N * 4 * 2 + (double)M * N * 8 : 0.0;
+    struct Cand { int mode; double rate; };
+    const Cand cands[3] = {
+        {GM_PAIR, n256 ? fill((long)((M + 255) / 256) * (N / 256) * sp, di.pair_clusters) : 0.0},
+        {GM_SINGLE256, n256 ? 0.85 * fill((long)((M + 127) / 128) * (N / 256) * sp, di.sms) : 0.0},
+        {GM_SINGLE128, 0.65 * fill((long)((M + 127) / 128) * ((N + 127) / 128) * sp, di.sms)}};
+    for (const Cand& c : cands) {
+      if (c.rate <= 0.0) continue;
+      const double t = flops / (tensor * c.rate) + extra / hbm;
+      if (t < best) {
+        best = t;
+        *mode = c.mode;
+        *splits = sp;
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -294,7 +416,7 @@ static cb_status alloc_train(cb_ctx* c) {
   get(&t->dqkv, T * nq);
   get(&t->dq32, T * qd);
   get(&t->dsum, T * c->heads_l);
-  get(&t->dgam, (size_t)DGAMMA_SPLITS * d);
+  get(&t->dgam, std::max<size_t>(DGAMMA_SPLITS, (T + RB_ROWS - 1) / RB_ROWS) * d);
   const size_t maxw = std::max(std::max(V * d, 2 * h * d), std::max(nq * d, d * qd));
   t->gpart_elems = 8 * maxw;
   get(&t->gpart, t->gpart_elems);
@@ -436,8 +558,8 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
   // weight-gradient GEMM: grad[M][N] += s_w * A^T B over the T tokens (A, B MN-major)
   auto grad_gemm = [&](const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
                        float* grad) -> cudaError_t {
-    const int mode = pick_mode(M, N, di);
-    const int splits = grad_splits(mode, M, N, T, di);
+    int mode, splits;
+    pick_grad_gemm(M, N, T, di, t->gpart_elems, &mode, &splits);
     if (splits == 1) {
       EpiScaledF32Add ep{grad, N, s_w};  // one add per element: order-independent
       return launch_gemm<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>(mode, ta, tb, tb, M, N, T, 0,
@@ -459,8 +581,31 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     dgamma_reduce_kernel<<<(d + 255) / 256, 256, 0, st>>>(t->dgam, out, d, s_w);
     return cudaGetLastError();
   };
+  // RMSNorm backward + residual, with the gain gradient (+= s_w sum_t dy x_hat) into dgam_out
   auto norm_bwd = [&](const float* dy, const float* x, const float* gamma, const float* rinv,
-                      const float* dres, float* dx, __half* dxh) {
+                      const float* dres, float* dx, __half* dxh, float* dgam_out) {
+    const int nb = (T + RB_ROWS - 1) / RB_ROWS, th = ROW_WARPS * 32;
+    bool fused = true;
+    if (d <= 512)
+      rmsnorm_bwd_dg_kernel<2><<<nb, th, 0, st>>>(dy, x, gamma, rinv, dres, dx, dxh, alpha, T, d,
+                                                  t->dgam);
+    else if (d <= 1024)
+      rmsnorm_bwd_dg_kernel<4><<<nb, th, 0, st>>>(dy, x, gamma, rinv, dres, dx, dxh, alpha, T, d,
+                                                  t->dgam);
+    else if (d <= 1536)
+      rmsnorm_bwd_dg_kernel<6><<<nb, th, 0, st>>>(dy, x, gamma, rinv, dres, dx, dxh, alpha, T, d,
+                                                  t->dgam);
+    else if (d <= 2048)
+      rmsnorm_bwd_dg_kernel<8><<<nb, th, 0, st>>>(dy, x, gamma, rinv, dres, dx, dxh, alpha, T, d,
+                                                  t->dgam);
+    else
+      fused = false;
+    if (fused) {
+      dgamma_reduce_rows_kernel<<<(d + 255) / 256, 256, 0, st>>>(t->dgam, nb, dgam_out, d, s_w);
+      return cudaGetLastError();
+    }
+    cudaError_t r = dgamma(dy, x, rinv, dgam_out);
+    if (r != cudaSuccess) return r;
     rmsnorm_bwd_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(dy, x, gamma, rinv, dres, dx, dxh,
                                                               alpha, T, d);
     return cudaGetLastError();
@@ -485,10 +630,9 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
                                              c->dev_err, di, st));
     TRY(grad_gemm(mnmap(t->dl, V, T), mnmap(c->xn, d, T), V, d, t->g_embed));
   }
-  TRY(dgamma(t->dtmp, t->x_last, t->rf, t->g_gamma_final));
   float* dX = t->dxa;
   float* dX2 = t->dxb;
-  TRY(norm_bwd(t->dtmp, t->x_last, c->gamma_final, t->rf, nullptr, dX, t->dxh));
+  TRY(norm_bwd(t->dtmp, t->x_last, c->gamma_final, t->rf, nullptr, dX, t->dxh, t->g_gamma_final));
 
   const CUtensorMap tb_w2 = mnmap(c->w2, hid, d, L);
   const CUtensorMap tb_w13 = mnmap(c->w13, d, 2 * hid, L);
@@ -515,9 +659,8 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     TRY(grad_gemm(tg_dh13, mnmap(t->x2n + lo * d, d, T), 2 * hid, d,
                   t->g_w13 + (size_t)l * 2 * hid * d));
     float* g2 = t->g_gamma + (size_t)l * 2 * d + d;
-    TRY(dgamma(t->dtmp, t->x2 + lo * d, t->r2 + lo, g2));
     TRY(norm_bwd(t->dtmp, t->x2 + lo * d, c->gamma + (size_t)l * 2 * d + d, t->r2 + lo, dX, dX2,
-                 t->dxh));
+                 t->dxh, g2));
     // attention: dA = (alpha dX2) Wo^T; dWo += s (alpha dX2)^T A
     {
       EpiStoreF16 ep{t->da, qd};
@@ -536,9 +679,8 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     TRY(grad_gemm(tg_dqkv, mnmap(t->xn + lo * d, d, T), nq, d,
                   t->g_wqkv + (size_t)l * nq * d));
     float* g1 = t->g_gamma + (size_t)l * 2 * d;
-    TRY(dgamma(t->dtmp, t->x_in + lo * d, t->r1 + lo, g1));
     TRY(norm_bwd(t->dtmp, t->x_in + lo * d, c->gamma + (size_t)l * 2 * d, t->r1 + lo, dX2, dX,
-                 t->dxh));
+                 t->dxh, g1));
   }
   if (!maps_ok) return cudaErrorInvalidValue;
   embed_bwd_kernel<<<(V + ROW_WARPS - 1) / ROW_WARPS, ROW_WARPS * 32, 0, st>>>(

@@ -49,6 +49,17 @@ class ModelConfig:
         return (2.0 * self.linear_params() + 2.0 * self.dim * self.vocab
                 + 2.0 * self.q_dim * (self.seq + 1) * self.nlayers)
 
+    def train_flops_per_token(self) -> float:
+        """Algorithmic FLOPs per token of one training step as this engine runs it:
+        the forward, then for every linear layer the input-gradient and weight-gradient
+        GEMMs (2x its forward FLOPs), for the tied head the logits recompute plus dX and
+        dE (3x), and for attention the recomputed scores, dV, dP, dQ and dK (2.5x its
+        forward FLOPs)."""
+        lin = 2.0 * self.linear_params()
+        head = 2.0 * self.dim * self.vocab
+        attn = 2.0 * self.q_dim * (self.seq + 1) * self.nlayers
+        return (lin + head + attn) + (2.0 * lin + 3.0 * head + 2.5 * attn)
+
     def replace(self, **kw) -> "ModelConfig":
         d = dict(self.__dict__)
         d.update(kw)
