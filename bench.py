@@ -64,12 +64,15 @@ def parse_args():
                    help="CPU-baseline sample budget (seconds of oracle work)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=("forward", "train", "validate", "rstk-load"),
+    p.add_argument("--decode-batch", type=int, default=64,
+                   help="sequences decoded together (--workload decode)")
+    p.add_argument("--workload", choices=("forward", "train", "decode", "validate", "rstk-load"),
                    default="forward",
                    help="forward: the headline forward+loss step; train: one training step "
                         "(forward + backward into fp32 gradients); validate: the evaluation "
                         "loop over an HBM-resident uint16 token file (val_loss + val_bpb); "
-                        "rstk-load: RSTK checkpoint file -> fp16 device weights (1 GPU)")
+                        "rstk-load: RSTK checkpoint file -> fp16 device weights (1 GPU); "
+                        "decode: single-token steps with a KV cache after a prefill (1 GPU)")
     return p.parse_args()
 
 
@@ -302,6 +305,70 @@ def run_io_workload(args):
     print(json.dumps(line), flush=True)
 
 
+def run_decode_workload(args):
+    """Decode throughput: `--decode-batch` sequences prefilled with seq/2 random tokens,
+    then --steps single-token steps through the public cb_decode_step (host tokens in,
+    greedy next tokens and full logits out every step), timed with CUDA events on the
+    context's stream. Roofline: HBM bytes a step must read (every weight once plus the
+    KV cache up to the current position) over the measured time."""
+    import torch
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
+    from rustane_b200.model import CONFIGS
+
+    if args.gpus != 1:
+        raise SystemExit("--workload decode runs on one GPU")
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[args.config]
+    B = args.decode_batch
+    plen = cfg.seq // 2
+    if args.warmup + args.steps > cfg.seq - plen:
+        raise SystemExit("warmup + steps must fit in the second half of the sequence window")
+    rng = np.random.default_rng(args.seed)
+    k = CompiledKernels(cfg, 0, B)
+    k.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
+    k.prefill(rng.integers(0, cfg.vocab, (B, plen)).astype(np.uint32))
+    cur = np.zeros(B, np.uint32)
+    for _ in range(args.warmup):
+        _, cur = k.decode_step(cur)
+    stream = torch.cuda.ExternalStream(k.stream())
+    pos0 = k.decode_position()
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, cur = k.decode_step(cur)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    weight_bytes = 2.0 * (cfg.linear_params() + cfg.vocab * cfg.dim)
+    mean_keys = pos0 + (args.steps + 1) / 2.0
+    kv_bytes = 2.0 * 2 * cfg.nlayers * B * cfg.kv_heads * 128 * mean_keys
+    gbs = (weight_bytes + kv_bytes) / (ms / 1e3) / 1e9
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("hbm_gbs", 6450.0))
+    line = {
+        "metric": "decode tokens/sec (single-token steps with a KV cache)",
+        "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "fp16", "data": "synthetic (random prompt tokens, N(0,0.02) weights)",
+        "config": {"workload": f"{args.config} decode, {B} sequences, positions "
+                               f"{pos0}..{pos0 + args.steps - 1} of {cfg.seq}",
+                   "batch": B, "prompt_len": plen},
+        "roofline": {"kernel": "whole decode step", "bound": "hbm", "achieved": round(gbs, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "peak_source": f"hbm_gbs ({peak_kind})",
+                     "bytes_per_step": weight_bytes + kv_bytes, "traffic": None},
+        "e2e": {"value": B / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B * (cfg.vocab + 1)},
+        "clocks": clk,
+    }
+    k.close()
+    print(json.dumps(line), flush=True)
+
+
 def run_train_workload(args):
     """Training step throughput (forward + backward, gradients accumulated on the
     device), sequence-sharded over the GPUs like the forward (data parallel: each rank
@@ -399,6 +466,9 @@ def main():
         return
     if args.workload == "train":
         run_train_workload(args)
+        return
+    if args.workload == "decode":
+        run_decode_workload(args)
         return
     if args.workload != "forward":
         run_io_workload(args)

@@ -269,6 +269,29 @@ cb_status cb_forward_backward(cb_ctx* ctx, const uint32_t* tokens, const uint32_
 cb_status cb_get_grads_f32(cb_ctx* ctx, float* d_embed, float* d_gamma_final,
                            const cb_layer_grads_f32* layers);
 
+/* ---- Single-token decode with a KV cache (the intent of the reference's
+ * metal-decode crate, crates/metal-decode/src/lib.rs:1-4, a placeholder there). -- */
+
+/* Runs the forward over `batch` prompts of `len` tokens each (host u32 [batch*len],
+ * 1 <= len <= cfg.seq) and keeps every layer's K and V in the context's KV cache
+ * (allocated on first use: 2 * L * max_batch * kv_heads * seq * 128 fp16). logits_out
+ * (nullable, host f32 [batch, vocab]) receives the logits of each prompt's last
+ * position (softcap applied when > 0). The next decode step writes position len.
+ * Synchronous. */
+cb_status cb_prefill(cb_ctx* ctx, const uint32_t* tokens, int32_t batch, int32_t len,
+                     float softcap, float* logits_out);
+
+/* Advances all `batch` sequences (batch = the prefill's) by one token: tokens (host u32
+ * [batch]) are the tokens at the current position; logits_out (nullable, host f32
+ * [batch, vocab]) receives the next-token logits and next_out (nullable, host u32
+ * [batch]) the greedy choice (largest logit, lowest id on ties). Fails once the position
+ * reaches cfg.seq. Synchronous. */
+cb_status cb_decode_step(cb_ctx* ctx, const uint32_t* tokens, int32_t batch, float* logits_out,
+                         uint32_t* next_out);
+
+/* Position the next cb_decode_step writes (0 before any prefill). */
+cb_status cb_decode_position(const cb_ctx* ctx, int32_t* pos);
+
 /* Per-kernel-class CUDA-event timing of forwards run while enabled. */
 cb_status cb_set_profiling(cb_ctx* ctx, int32_t enable);
 cb_status cb_kernel_times(cb_ctx* ctx, cb_kernel_time* out, int32_t max_entries,

@@ -46,6 +46,7 @@ EXPORTED = [
     "cb_lm_head_ce_f16_noalloc", "cb_load_rstk", "cb_tokens_open", "cb_tokens_from_host",
     "cb_tokens_len", "cb_tokens_close", "cb_forward_loss_windows", "cb_eval_windows",
     "cb_enable_training", "cb_zero_grads", "cb_forward_backward", "cb_get_grads_f32",
+    "cb_prefill", "cb_decode_step", "cb_decode_position",
 ]
 
 
@@ -134,6 +135,9 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_zero_grads": (i32, [vp]),
         "cb_forward_backward": (i32, [vp, pu32, pu32, i32, f32, f32, pf]),
         "cb_get_grads_f32": (i32, [vp, pf, pf, C.POINTER(cb_layer_grads_f32)]),
+        "cb_prefill": (i32, [vp, pu32, i32, i32, f32, pf]),
+        "cb_decode_step": (i32, [vp, pu32, i32, pf, pu32]),
+        "cb_decode_position": (i32, [vp, pi32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -214,6 +214,7 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiScaledF32, GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwigluBwd, GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
+  set_gemm_attrs_for<EpiPartialF32>();  // decode (decode.cuh)
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwiglu>();
@@ -461,6 +462,8 @@ struct KStat {
 // ------------------------------------------------------------ context
 struct TrainState;
 void free_train_state(TrainState* t);
+struct DecodeState;
+void free_decode_state(DecodeState* s);
 
 struct cb_ctx {
   cb_model_config cfg{};
@@ -536,6 +539,8 @@ struct cb_ctx {
 
   // training (cb_enable_training): saved activations, backward scratch, gradients
   TrainState* train = nullptr;
+  // decode (cb_prefill / cb_decode_step): KV cache and single-token buffers
+  DecodeState* decode = nullptr;
 
   size_t T_max() const { return (size_t)max_batch * cfg.seq; }
 };
@@ -590,6 +595,8 @@ void free_ctx(cb_ctx* c) {
   c->graphs.clear();
   free_train_state(c->train);
   c->train = nullptr;
+  free_decode_state(c->decode);
+  c->decode = nullptr;
   for (auto e : c->events) cudaEventDestroy(e);
   if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
   void* ptrs[] = {c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
@@ -605,9 +612,19 @@ void free_ctx(cb_ctx* c) {
   delete c;
 }
 
+// Per-layer destination of K and V (the decode KV cache): layer l's [batch, kv_heads,
+// seq, 128] blocks at k + l * layer_stride and v + l * layer_stride.
+struct KvDest {
+  __half* k;
+  __half* v;
+  size_t layer_stride;
+};
+
 // Enqueue one forward for `batch` sequences on `st`. When `prof` is set,
-// CUDA events bracket every launch (eager mode only).
-cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof) {
+// CUDA events bracket every launch (eager mode only). With `kv`, every layer's roped K
+// and V are kept (prefill of the decode cache) instead of reusing one buffer.
+cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof,
+                            const KvDest* kv = nullptr) {
   const cb_model_config& cfg = c->cfg;
   const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
   const int T = batch * S;
@@ -689,16 +706,22 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if (l > 0) {  // residual add of the previous layer's down projection + RMSNorm(gamma1)
       if ((e = add_norm(c->gamma + (size_t)l * 2 * d)) != cudaSuccess) return e;
     }
+    __half* kl = kv ? kv->k + (size_t)l * kv->layer_stride : c->k;
+    __half* vl = kv ? kv->v + (size_t)l * kv->layer_stride : c->v;
     {
-      EpiQkvRope ep{c->q, c->k, c->v, c->rope, S, c->heads_l, c->kv_heads_l};
+      EpiQkvRope ep{c->q, kl, vl, c->rope, S, c->heads_l, c->kv_heads_l};
       e = launch_gemm(m_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
                       c->dev_err, di, st);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
     }
-    e = launch_attention(&c->tm_q, &c->tm_k, &c->tm_v, c->q, c->k, c->v, c->attn, batch,
-                         c->heads_l, c->kv_heads_l, S, c->dev_err, st);
+    CUtensorMap tk = c->tm_k, tv = c->tm_v;
+    if (kv && !(make_tmap_qkv(&tk, kl, (uint64_t)T * c->kv_heads_l, FA_BKV) &&
+                make_tmap_qkv(&tv, vl, (uint64_t)T * c->kv_heads_l, FA_BKV)))
+      return cudaErrorInvalidValue;
+    e = launch_attention(&c->tm_q, &tk, &tv, c->q, kl, vl, c->attn, batch, c->heads_l,
+                         c->kv_heads_l, S, c->dev_err, st);
     if (e != cudaSuccess) return e;
     mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
     e = project(m_o, s_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O);
@@ -2015,3 +2038,4 @@ extern "C" cb_status cb_lm_head_ce_f16_noalloc(const void* xf, const void* embed
 }
 
 #include "training.cuh"
+#include "decode.cuh"

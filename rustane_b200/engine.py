@@ -266,6 +266,45 @@ class CompiledKernels:
                                               _fptr(out.dgamma_final), arr))
         return out
 
+    # ---- decode (KV cache)
+    def prefill(self, prompts, softcap: float = 0.0) -> np.ndarray:
+        """Run `batch` prompts of equal length (array [batch, len]) into the KV cache;
+        returns the logits of each prompt's last position, [batch, vocab]."""
+        p = np.ascontiguousarray(np.asarray(prompts, dtype=np.uint32))
+        if p.ndim == 1:
+            p = p[None, :]
+        batch, length = p.shape
+        out = np.empty((batch, self.cfg.vocab), np.float32)
+        self._check(self.lib.cb_prefill(self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                        batch, length, softcap, _fptr(out)))
+        return out
+
+    def decode_step(self, tokens):
+        """Feed one token per sequence at the current position; returns (logits
+        [batch, vocab], greedy next tokens [batch])."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        logits = np.empty((t.size, self.cfg.vocab), np.float32)
+        nxt = np.empty(t.size, np.uint32)
+        self._check(self.lib.cb_decode_step(
+            self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, _fptr(logits),
+            nxt.ctypes.data_as(C.POINTER(C.c_uint32))))
+        return logits, nxt
+
+    def decode_position(self) -> int:
+        p = C.c_int32()
+        self._check(self.lib.cb_decode_position(self.handle, C.byref(p)))
+        return p.value
+
+    def generate(self, prompts, n_new: int, softcap: float = 0.0) -> np.ndarray:
+        """Greedy continuation of equal-length prompts: [batch, n_new] new tokens."""
+        first = self.prefill(prompts, softcap)
+        cur = first.argmax(axis=1).astype(np.uint32)
+        out = [cur]
+        for _ in range(n_new - 1):
+            _, cur = self.decode_step(cur)
+            out.append(cur)
+        return np.stack(out, axis=1)
+
     def load_checkpoint(self, path) -> int:
         """Stream an RSTK checkpoint (train.rs:238-346) into the device weights;
         returns the step recorded in its header."""
