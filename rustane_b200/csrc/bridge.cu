@@ -520,8 +520,9 @@ struct cb_ctx {
   // graphs
   std::map<std::pair<int, uint32_t>, cudaGraphExec_t> graphs;
 
-  // last forward (for sampled logits)
+  // last forward (for sampled logits): its final fp32 residual stream
   int last_batch = 0;
+  const float* x_final = nullptr;
   float last_softcap = 0.f;
 
   // sampled-logit buffers
@@ -1610,6 +1611,7 @@ static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStre
   }
   ctx->last_batch = batch;
   ctx->last_softcap = softcap;
+  ctx->x_final = ctx->x;
   return CB_OK;
 }
 
@@ -1723,7 +1725,8 @@ cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, fl
   CB_CUDA(cudaMalloc(&d_rows, n_rows * sizeof(int32_t)));
   cudaError_t e = cudaMemcpyAsync(d_rows, rows, n_rows * sizeof(int32_t), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) {
-    gather_rows_kernel<<<n_pad, 128, 0, st>>>(ctx->xn, d_rows, n_rows, n_pad, d, ctx->samp_a);
+    gather_norm_rows_kernel<<<n_pad, 128, 0, st>>>(ctx->x_final, d_rows, ctx->gamma_final, n_rows,
+                                                   n_pad, d, ctx->samp_a);
     e = cudaGetLastError();
   }
   CUtensorMap ta;

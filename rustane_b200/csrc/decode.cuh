@@ -466,6 +466,7 @@ cb_status cb_prefill(cb_ctx* ctx, const uint32_t* tokens, int32_t batch, int32_t
   if (rc != CB_OK) return rc;
   ctx->last_batch = batch;
   ctx->last_softcap = softcap;
+  ctx->x_final = ctx->x;
   if (logits_out) {
     std::vector<int32_t> rows(batch);
     for (int b = 0; b < batch; ++b) rows[b] = b * S + len - 1;

@@ -267,6 +267,33 @@ __global__ void loss_mean_kernel(const float* __restrict__ block_sums, int nbloc
 }
 
 // Copy selected rows of src [*, dim] fp16 into dst [n, dim] (zero rows past n up to n_pad).
+// dst[r] = fp16(RMSNorm(x[rows[r]]) * gamma) for r < n, zero rows up to n_pad: the
+// final-norm output of selected positions, rebuilt from the fp32 residual stream.
+__global__ void gather_norm_rows_kernel(const float* __restrict__ x,
+                                        const int32_t* __restrict__ rows,
+                                        const float* __restrict__ gamma, int n, int n_pad,
+                                        int dim, __half* __restrict__ dst) {
+  const int r = blockIdx.x;
+  if (r >= n_pad) return;
+  __shared__ float red[32];
+  __half* out = dst + (size_t)r * dim;
+  if (r >= n) {
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) out[c] = __float2half_rn(0.f);
+    return;
+  }
+  const float* xr = x + (size_t)rows[r] * dim;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) ss += xr[c] * xr[c];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+  const float rinv = 1.0f / sqrtf(tot / (float)dim + RMS_EPS);
+  for (int c = threadIdx.x; c < dim; c += blockDim.x)
+    out[c] = __float2half_rn(xr[c] * rinv * gamma[c]);
+}
+
 __global__ void gather_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ rows,
                                    int n, int n_pad, int dim, __half* __restrict__ dst) {
   const int r = blockIdx.x;

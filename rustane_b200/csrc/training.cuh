@@ -757,6 +757,7 @@ cb_status cb_forward_backward(cb_ctx* ctx, const uint32_t* tokens, const uint32_
   CB_CUDA(cudaGraphLaunch(it->second, st));
   ctx->last_batch = batch;
   ctx->last_softcap = softcap;
+  ctx->x_final = t->x_last;
   CB_CUDA(cudaMemcpyAsync(ctx->h_loss, ctx->loss, sizeof(float), cudaMemcpyDeviceToHost, st));
   rc = read_device_error(ctx);
   if (rc != CB_OK) return rc;
