@@ -125,6 +125,7 @@ bool make_tmap_qkv(CUtensorMap* map, const void* ptr, uint64_t rows, uint32_t bo
 struct NcclApi {
   decltype(&ncclGetUniqueId) get_unique_id = nullptr;
   decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclCommDestroy) destroy = nullptr;
   decltype(&ncclCommAbort) abort = nullptr;
@@ -154,6 +155,8 @@ const NcclApi& nccl_api() {
     NcclApi a;
     a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.init_rank_config =
+        reinterpret_cast<decltype(a.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
     a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
     a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
@@ -179,6 +182,12 @@ void split_even(int n, int world, int rank, int* begin, int* count) {
 // ------------------------------------------------------------ GEMM launch
 // Tile modes of the tcgen05 GEMM.
 enum GemmMode { GM_SINGLE128 = 0, GM_SINGLE256 = 1, GM_PAIR = 2 };
+
+// Tensor parallelism: the forward runs in TP chunks of sequences so that one chunk's
+// all-reduce (on its own stream, NCCL capped at TP_COMM_SMS CTAs) overlaps the next
+// chunk's GEMMs (which then use all but TP_COMM_SMS SMs).
+constexpr int TP_MAX_CHUNKS = 8;
+constexpr int TP_COMM_SMS = 16;
 
 template <int BN, class Epi, int LAYOUT>
 void set_gemm_attr() {
@@ -476,6 +485,8 @@ struct cb_ctx {
   int q_off = 0, kv_off = 0, hid_off = 0;  // offsets of the share in the full model
   int tp_rank = 0, tp_world = 1;
   ncclComm_t comm = nullptr;
+  cudaStream_t comm_stream = nullptr;           // tensor parallel: the all-reduces' stream
+  cudaEvent_t tp_ev[4 * 8] = {};                // chunk hand-offs between the two streams
   float* delta32 = nullptr;  // [T, dim] fp32 partial projections, all-reduced across ranks
   cudaStream_t stream = nullptr;
   std::string err;
@@ -600,6 +611,9 @@ void free_ctx(cb_ctx* c) {
   c->decode = nullptr;
   for (auto e : c->events) cudaEventDestroy(e);
   if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
+  for (auto ev : c->tp_ev)
+    if (ev) cudaEventDestroy(ev);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
   void* ptrs[] = {c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
@@ -611,6 +625,152 @@ void free_ctx(cb_ctx* c) {
   if (c->h_err) cudaFreeHost(c->h_err);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
+}
+
+// Tensor-parallel forward in chunks of sequences on two streams: the compute stream
+// runs each chunk's QKV, attention and O projection, then (after that chunk's
+// all-reduce) its residual + norm, W1/W3 and down projection; the communication
+// stream all-reduces each chunk's fp32 partial projection as soon as it is written,
+// while the compute stream works on the other chunks. Same math as the one-stream
+// path, chunk by chunk (rows are independent outside attention, and attention stays
+// within a sequence).
+cudaError_t enqueue_forward_tp_chunked(cb_ctx* c, int batch, int chunks, float softcap,
+                                       cudaStream_t st) {
+  const cb_model_config& cfg = c->cfg;
+  const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
+  const int T = batch * S, bc = batch / chunks, Tc = bc * S;
+  const int H = c->heads_l, Hk = c->kv_heads_l, qd = c->q_dim, kvd = c->kv_dim, nq = c->n_qkv;
+  const float alpha = 1.0f / sqrtf(2.0f * (float)L);
+  cudaStream_t cs = c->comm_stream;
+  DeviceInfo dt = device_info(c->device);
+  dt.sms = std::max(1, dt.sms - TP_COMM_SMS);
+  dt.pair_clusters = std::max(1, std::min(dt.pair_clusters, dt.sms / 2));
+  cudaError_t e;
+#define TRYC(...)                                     \
+  do {                                                \
+    if ((e = (__VA_ARGS__)) != cudaSuccess) return e; \
+  } while (0)
+  auto nccl_sum = [&](float* buf, size_t n) -> cudaError_t {
+    ncclResult_t nr = nccl_api().all_reduce(buf, buf, n, ncclFloat32, ncclSum, c->comm, cs);
+    if (nr != ncclSuccess) {
+      c->err = std::string("ncclAllReduce: ") + nccl_api().error_string(nr);
+      return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+  };
+  cudaEvent_t* ev_proj = c->tp_ev;               // projection of chunk j written
+  cudaEvent_t* ev_sum = c->tp_ev + TP_MAX_CHUNKS;  // chunk j's all-reduce done
+  const int m_qkv = pick_mode(Tc, nq, dt), m_o = pick_mode(Tc, d, dt);
+  const int m_13 = pick_mode(Tc, 2 * hid, dt);
+
+  embed_rmsnorm_kernel<<<(T + ROW_WARPS - 1) / ROW_WARPS, ROW_WARPS * 32, 0, st>>>(
+      c->tokens, c->embed, c->gamma, c->x, c->xn, T, d, V, c->dev_err);
+  TRYC(cudaGetLastError());
+  // the communication stream joins the capture here
+  TRYC(cudaEventRecord(c->tp_ev[3 * TP_MAX_CHUNKS], st));
+  TRYC(cudaStreamWaitEvent(cs, c->tp_ev[3 * TP_MAX_CHUNKS], 0));
+  for (int l = 0; l < L; ++l) {
+    // attention half: QKV, attention, O per chunk; O partials all-reduced on cs
+    for (int j = 0; j < chunks; ++j) {
+      const size_t r0 = (size_t)j * Tc;
+      if (l > 0) {  // previous layer's down projection, summed: residual + RMSNorm(gamma1)
+        TRYC(cudaStreamWaitEvent(st, ev_sum[j], 0));
+        TRYC(launch_add_rmsnorm(c->x + r0 * d, c->x + r0 * d, c->delta32 + r0 * d,
+                                c->gamma + (size_t)l * 2 * d, c->xn + r0 * d, Tc, d, st));
+      }
+      __half* qj = c->q + r0 * qd;
+      __half* kj = c->k + r0 * kvd;
+      __half* vj = c->v + r0 * kvd;
+      CUtensorMap ta, tq, tk, tv, to;
+      if (!make_tmap(&ta, c->xn + r0 * d, d, Tc, 1, 128) ||
+          !make_tmap(&to, c->attn + r0 * qd, qd, Tc, 1, 128) ||
+          !make_tmap_qkv(&tq, qj, (uint64_t)Tc * H, FA_BQ) ||
+          !make_tmap_qkv(&tk, kj, (uint64_t)Tc * Hk, FA_BKV) ||
+          !make_tmap_qkv(&tv, vj, (uint64_t)Tc * Hk, FA_BKV))
+        return cudaErrorInvalidValue;
+      {
+        EpiQkvRope ep{qj, kj, vj, c->rope, S, H, Hk};
+        TRYC(launch_gemm(m_qkv, ta, c->tm_wqkv[0], c->tm_wqkv[1], Tc, nq, d, l, ep, c->dev_err,
+                         dt, st));
+      }
+      TRYC(launch_attention(S % FA_BQ == 0 ? &tq : nullptr, &tk, &tv, qj, kj, vj,
+                            c->attn + r0 * qd, bc, H, Hk, S, c->dev_err, st));
+      {
+        EpiScaledF32 ep{c->delta32 + r0 * d, d, alpha};
+        TRYC(launch_gemm(m_o, to, c->tm_wo[0], c->tm_wo[1], Tc, d, qd, l, ep, c->dev_err, dt,
+                         st));
+      }
+      TRYC(cudaEventRecord(ev_proj[j], st));
+      TRYC(cudaStreamWaitEvent(cs, ev_proj[j], 0));
+      TRYC(nccl_sum(c->delta32 + r0 * d, (size_t)Tc * d));
+      TRYC(cudaEventRecord(ev_sum[j], cs));
+    }
+    // FFN half: residual + RMSNorm(gamma2), W1/W3 + SwiGLU, down; partials all-reduced on cs
+    for (int j = 0; j < chunks; ++j) {
+      const size_t r0 = (size_t)j * Tc;
+      TRYC(cudaStreamWaitEvent(st, ev_sum[j], 0));
+      TRYC(launch_add_rmsnorm(c->x + r0 * d, c->x + r0 * d, c->delta32 + r0 * d,
+                              c->gamma + (size_t)l * 2 * d + d, c->xn + r0 * d, Tc, d, st));
+      CUtensorMap ta, tg;
+      if (!make_tmap(&ta, c->xn + r0 * d, d, Tc, 1, 128) ||
+          !make_tmap(&tg, c->g + r0 * hid, hid, Tc, 1, 128))
+        return cudaErrorInvalidValue;
+      {
+        EpiSwiglu ep{c->g + r0 * hid, hid};
+        TRYC(launch_gemm(m_13, ta, c->tm_w13[0], c->tm_w13[1], Tc, 2 * hid, d, l, ep, c->dev_err,
+                         dt, st));
+      }
+      {
+        EpiScaledF32 ep{c->delta32 + r0 * d, d, alpha};
+        TRYC(launch_gemm(m_o, tg, c->tm_w2[0], c->tm_w2[1], Tc, d, hid, l, ep, c->dev_err, dt,
+                         st));
+      }
+      TRYC(cudaEventRecord(ev_proj[j], st));
+      TRYC(cudaStreamWaitEvent(cs, ev_proj[j], 0));
+      TRYC(nccl_sum(c->delta32 + r0 * d, (size_t)Tc * d));
+      TRYC(cudaEventRecord(ev_sum[j], cs));
+    }
+  }
+  for (int j = 0; j < chunks; ++j) {  // last residual + final RMSNorm; joins cs back
+    const size_t r0 = (size_t)j * Tc;
+    TRYC(cudaStreamWaitEvent(st, ev_sum[j], 0));
+    TRYC(launch_add_rmsnorm(c->x + r0 * d, c->x + r0 * d, c->delta32 + r0 * d, c->gamma_final,
+                            c->xn + r0 * d, Tc, d, st));
+  }
+  const DeviceInfo& di = device_info(c->device);
+  const int m_head = pick_mode(T, V, di);
+  const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
+  {
+    EpiCrossEntropy ep{};
+    ep.part = c->ce_part;
+    ep.nparts = nparts;
+    ep.targets = c->targets;
+    ep.tgt_logit = c->tgt_logit;
+    ep.softcap = softcap;
+    TRYC(launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
+                     c->dev_err, di, st));
+  }
+  const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
+  ce_finalize_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->ce_part, nparts, c->tgt_logit,
+                                                            c->tok_loss, c->block_sums, T);
+  TRYC(cudaGetLastError());
+  loss_mean_kernel<<<1, 256, 0, st>>>(c->block_sums, row_blocks, T, c->loss);
+  TRYC(cudaGetLastError());
+#undef TRYC
+  return cudaSuccess;
+}
+
+// Chunks for the tensor-parallel forward: CB_TP_CHUNKS (1 = one stream), else 2 when
+// the batch splits evenly.
+int tp_chunks(const cb_ctx* c, int batch) {
+  static const int forced = [] {
+    const char* e = getenv("CB_TP_CHUNKS");
+    return e ? atoi(e) : 0;
+  }();
+  int n = forced > 0 ? forced : 2;
+  n = std::min(n, TP_MAX_CHUNKS);
+  while (n > 1 && batch % n != 0) --n;
+  return c->tp_world > 1 ? n : 1;
 }
 
 // Per-layer destination of K and V (the decode KV cache): layer l's [batch, kv_heads,
@@ -626,6 +786,10 @@ struct KvDest {
 // and V are kept (prefill of the decode cache) instead of reusing one buffer.
 cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof,
                             const KvDest* kv = nullptr) {
+  if (!prof && !kv && c->tp_world > 1 && c->comm_stream) {
+    const int chunks = tp_chunks(c, batch);
+    if (chunks > 1) return enqueue_forward_tp_chunked(c, batch, chunks, softcap, st);
+  }
   const cb_model_config& cfg = c->cfg;
   const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
   const int T = batch * S;
@@ -1067,7 +1231,21 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   if (tp_world > 1) {
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof(id));
-    ncclResult_t nr = nccl_api().init_rank(&ctx->comm, tp_world, id, tp_rank);
+    // NCCL's all-reduces run beside the GEMMs (tp_chunked_forward): cap them at
+    // TP_COMM_SMS CTAs, the SMs the GEMMs leave free while they overlap.
+    ncclResult_t nr;
+    if (nccl_api().init_rank_config) {
+      ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+      conf.maxCTAs = TP_COMM_SMS;
+      nr = nccl_api().init_rank_config(&ctx->comm, tp_world, id, tp_rank, &conf);
+    } else {
+      nr = nccl_api().init_rank(&ctx->comm, tp_world, id, tp_rank);
+    }
+    if (nr == ncclSuccess) {
+      for (int i = 0; i < 4 * TP_MAX_CHUNKS; ++i)
+        CREATE_CUDA(cudaEventCreateWithFlags(&ctx->tp_ev[i], cudaEventDisableTiming));
+      CREATE_CUDA(cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking));
+    }
     if (nr != ncclSuccess) {
       ctx->comm = nullptr;
       return bail(CB_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl_api().error_string(nr));

@@ -96,3 +96,34 @@ def test_tp2_uneven_split(bridge_lib):
     infos = _check(_run(cfg, 2, 23))
     assert [i["heads"] for i in infos] == [3, 2]
     assert [i["hidden"] for i in infos] == [192, 128]
+
+
+def _tp_rank_env(rank, world, cfg, batch, seed, nccl_id, chunks, out):
+    import os
+    os.environ["CB_TP_CHUNKS"] = str(chunks)  # read on the first forward of the process
+    _tp_rank(rank, world, cfg, batch, seed, nccl_id, out)
+
+
+@needs2
+def test_tp2_two_stream_chunks_equal_one_stream(bridge_lib):
+    """The chunked forward (all-reduces on their own stream, overlapping the next chunk's
+    GEMMs) gives the same losses as the one-stream forward."""
+    from rustane_b200 import nccl_unique_id
+    cfg = CONFIGS["600m-A"].replace(nlayers=3)
+    ctx = mp.get_context("spawn")
+    res = {}
+    for chunks in (1, 4):
+        out = ctx.Manager().dict()
+        nid = nccl_unique_id()
+        procs = [ctx.Process(target=_tp_rank_env, args=(r, 2, cfg, 4, 31, nid, chunks, out))
+                 for r in range(2)]
+        for q in procs:
+            q.start()
+        for q in procs:
+            q.join(600)
+            assert q.exitcode == 0
+        res[chunks] = out[0]
+    l1, p1, _, _ = res[1]
+    l4, p4, _, _ = res[4]
+    assert abs(l1 - l4) <= 1e-6 * l1
+    np.testing.assert_allclose(p4, p1, rtol=0, atol=1e-5)
