@@ -281,8 +281,11 @@ __global__ void __launch_bounds__(AB_THREADS)
 }
 
 // dQ = dq32 * scale with RoPE undone, into the q columns of dQKV (fp16).
-// One thread per (token, head, pair of dims).
-__global__ void attn_bwd_dq_kernel(const float* __restrict__ dq32, const float2* __restrict__ rope,
+// One thread per (token, head, pair of dims); rope_pm is the (cos, sin) table in
+// position-major order [seq][64], so the lanes of a warp (consecutive pairs) read it
+// contiguously.
+__global__ void attn_bwd_dq_kernel(const float* __restrict__ dq32,
+                                   const float2* __restrict__ rope_pm,
                                    __half* __restrict__ dqkv, int T, int seq, int heads,
                                    int n_qkv, float scale) {
   const int q_dim = heads * 128;
@@ -293,7 +296,10 @@ __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq32, const float2*
     const int c2 = (int)(i % (q_dim / 2));  // pair index across heads
     const float2 d = reinterpret_cast<const float2*>(dq32)[i];
     float a = d.x * scale, b = d.y * scale;
-    rope_back(a, b, rope, seq, c2 & 63, t % seq);
+    const float2 cs = rope_pm[(size_t)(t % seq) * 64 + (c2 & 63)];
+    const float ra = cs.x * a + cs.y * b, rb = -cs.y * a + cs.x * b;
+    a = ra;
+    b = rb;
     reinterpret_cast<uint32_t*>(dqkv + (size_t)t * n_qkv)[c2] = pack_half2(a, b);
   }
 }

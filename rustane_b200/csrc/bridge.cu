@@ -41,6 +41,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "attention_bwd.cuh"
+#include "attention_bwd_tc.cuh"
 #include "gemm_tc.cuh"
 #include "io.cuh"
 #include "ptx.cuh"
@@ -99,6 +100,37 @@ bool make_tmap_mn(CUtensorMap* map, const void* ptr, uint64_t mn, uint64_t k, ui
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// fp16 matrix [rows][cols] (row-major) tiled as 64 x box_rows boxes, 128B swizzle.
+bool make_tmap_rows(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows,
+                    uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// fp32 matrix [rows][cols] (row-major) tiled as box_cols x box_rows boxes, no swizzle
+// (the attention backward's dQ reduce-add target).
+bool make_tmap_f32_rows(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows,
+                        uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -232,6 +264,7 @@ void set_all_kernel_attrs() {
                        ATT_SMEM);
   cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
   cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_SMEM);
+  cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
 }
 
 struct DeviceInfo {
@@ -403,9 +436,10 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
 // accumulated in dq32, which this zeroes first), then dQ into dqkv.
 cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half* v,
                                  const __half* o, const __half* dout, const float* lse2,
-                                 float* dsum, float* dq32, const float2* rope, __half* dqkv,
-                                 int batch, int heads, int kv_heads, int seq, int sms,
-                                 cudaStream_t st) {
+                                 float* dsum, float* dq32, const float2* rope,
+                                 const float2* rope_pm, __half* dqkv, int batch, int heads,
+                                 int kv_heads, int seq, int sms, cudaStream_t st,
+                                 int* err = nullptr) {
   const int T = batch * seq;
   const int q_dim = heads * 128, n_qkv = q_dim + 2 * kv_heads * 128;
   const float scale = 1.0f / sqrtf(128.0f);
@@ -413,12 +447,27 @@ cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half*
   cudaError_t e = cudaMemsetAsync(dq32, 0, (size_t)T * q_dim * sizeof(float), st);
   if (e != cudaSuccess) return e;
   attn_bwd_dsum_kernel<<<(T * heads + 7) / 8, 256, 0, st>>>(o, dout, dsum, T, seq, heads);
-  dim3 grid(seq / AB_BK, kv_heads, batch);
-  attn_bwd_kernel<<<grid, AB_THREADS, AB_SMEM, st>>>(q, k, v, dout, lse2, dsum, rope, dq32, dqkv,
-                                                     seq, heads, kv_heads, scale_log2, scale);
+  CUtensorMap tq, tk, tv, tdo, tdq;
+  const bool tc = seq % AT_BK == 0 &&
+                  make_tmap_qkv(&tq, q, (uint64_t)batch * heads * seq, AT_BQ) &&
+                  make_tmap_qkv(&tk, k, (uint64_t)batch * kv_heads * seq, AT_BK) &&
+                  make_tmap_qkv(&tv, v, (uint64_t)batch * kv_heads * seq, AT_BK) &&
+                  make_tmap_rows(&tdo, dout, (uint64_t)q_dim, (uint64_t)T, AT_BQ) &&
+                  make_tmap_f32_rows(&tdq, dq32, (uint64_t)q_dim, (uint64_t)T, 128, AT_BQ);
+  if (tc) {  // tcgen05 path
+    dim3 grid(seq / AT_BK, kv_heads, batch);
+    attn_bwd_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, tdo, tdq, lse2, dsum, rope,
+                                                          dq32, dqkv, seq, heads, kv_heads,
+                                                          scale_log2, scale, err);
+  } else {
+    dim3 grid(seq / AB_BK, kv_heads, batch);
+    attn_bwd_kernel<<<grid, AB_THREADS, AB_SMEM, st>>>(q, k, v, dout, lse2, dsum, rope, dq32,
+                                                       dqkv, seq, heads, kv_heads, scale_log2,
+                                                       scale);
+  }
   const size_t pairs = (size_t)T * q_dim / 2;
   const int blocks = (int)std::min<size_t>((pairs + 255) / 256, (size_t)sms * 16);
-  attn_bwd_dq_kernel<<<blocks, 256, 0, st>>>(dq32, rope, dqkv, T, seq, heads, n_qkv, scale);
+  attn_bwd_dq_kernel<<<blocks, 256, 0, st>>>(dq32, rope_pm, dqkv, T, seq, heads, n_qkv, scale);
   return cudaGetLastError();
 }
 
@@ -519,6 +568,7 @@ struct cb_ctx {
   uint32_t* targets = nullptr; // [T]
   int64_t* eval_pos = nullptr; // [max_batch] window offsets into a cb_tokens array
   float2* rope = nullptr;      // [64, S] (cos, sin), pair-major
+  float2* rope_pm = nullptr;   // [S, 64] the same, position-major
   int* dev_err = nullptr;      // device error flag
   float* h_loss = nullptr;     // pinned
   int* h_err = nullptr;        // pinned
@@ -614,7 +664,7 @@ void free_ctx(cb_ctx* c) {
   for (auto ev : c->tp_ev)
     if (ev) cudaEventDestroy(ev);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
-  void* ptrs[] = {c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
+  void* ptrs[] = {c->rope_pm, c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
@@ -1190,6 +1240,7 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(dmalloc(&ctx->targets, T));
   CREATE_CUDA(dmalloc(&ctx->eval_pos, (size_t)ctx->max_batch));
   CREATE_CUDA(dmalloc(&ctx->rope, (size_t)S * 64));
+  CREATE_CUDA(dmalloc(&ctx->rope_pm, (size_t)S * 64));
   CREATE_CUDA(dmalloc(&ctx->dev_err, 1));
   CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_loss), sizeof(float)));
   CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_err), sizeof(int)));
@@ -1208,6 +1259,11 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
         tab[(size_t)i * S + p] = make_float2((float)std::cos(th), (float)std::sin(th));
       }
     CREATE_CUDA(cudaMemcpy(ctx->rope, tab.data(), tab.size() * sizeof(float2),
+                           cudaMemcpyHostToDevice));
+    std::vector<float2> pm(tab.size());
+    for (int p = 0; p < S; ++p)
+      for (int i = 0; i < 64; ++i) pm[(size_t)p * 64 + i] = tab[(size_t)i * S + p];
+    CREATE_CUDA(cudaMemcpy(ctx->rope_pm, pm.data(), pm.size() * sizeof(float2),
                            cudaMemcpyHostToDevice));
   }
 
@@ -2125,7 +2181,7 @@ cb_status cb_attention_bwd_f16(const void* q, const void* k, const void* v, cons
   if (e == cudaSuccess)
     e = launch_attention_bwd(static_cast<const __half*>(q), static_cast<const __half*>(k),
                              static_cast<const __half*>(v), static_cast<const __half*>(o),
-                             static_cast<const __half*>(dout), lse, dsum, dq32, rope,
+                             static_cast<const __half*>(dout), lse, dsum, dq32, rope, rope,
                              static_cast<__half*>(dqkv), batch, heads, kv_heads, seq,
                              device_info(dev).sms, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // the host table must outlive the copy

@@ -670,7 +670,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     TRY(grad_gemm(tg_dxh, mnmap(t->attn + lo * qd, qd, T), d, qd, t->g_wo + (size_t)l * d * qd));
     TRY(launch_attention_bwd(t->q + lo * qd, t->k + lo * c->kv_dim, t->v + lo * c->kv_dim,
                              t->attn + lo * qd, t->da, t->lse + lo * H, t->dsum, t->dq32, c->rope,
-                             t->dqkv, batch, H, Hk, S, di.sms, st));
+                             c->rope_pm, t->dqkv, batch, H, Hk, S, di.sms, st, c->dev_err));
     {
       EpiScaledF32 ep{t->dtmp, d, 1.0f};
       TRY(launch_gemm<EpiScaledF32, GEMM_B_MN>(m_o, ta_dqkv, tb_wqkv, tb_wqkv, T, d, nq, l, ep,
