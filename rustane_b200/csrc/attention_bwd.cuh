@@ -37,24 +37,32 @@ constexpr int AB_THREADS = 128;
 // K, V, Q, dO tiles (16 KB each) + dS^T (64 x 64 fp16, 8 KB)
 constexpr int AB_SMEM = 4 * 64 * 256 + 64 * 128;
 
-// D[b, h, q] = sum_d dO[t, h*128 + d] * O[t, h*128 + d]; one warp per (token, head).
+// D[b, h, q] = sum_d dO[t, h*128 + d] * O[t, h*128 + d]; 16 lanes per (token, head),
+// 16-byte loads.
 __global__ void attn_bwd_dsum_kernel(const __half* __restrict__ o, const __half* __restrict__ dout,
                                      float* __restrict__ dsum, int T, int seq, int heads) {
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (w >= T * heads) return;
-  const int t = w / heads, h = w % heads;
-  const size_t off = (size_t)t * heads * 128 + h * 128 + lane * 4;
-  const uint2 a = *reinterpret_cast<const uint2*>(o + off);
-  const uint2 g = *reinterpret_cast<const uint2*>(dout + off);
-  const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
-  const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
-  const float2 g0 = __half22float2(*reinterpret_cast<const __half2*>(&g.x));
-  const float2 g1 = __half22float2(*reinterpret_cast<const __half2*>(&g.y));
-  float v = a0.x * g0.x + a0.y * g0.y + a1.x * g1.x + a1.y * g1.y;
+  const int w = blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4);
+  const int sub = threadIdx.x & 15;
+  const bool ok = w < T * heads;
+  float v = 0.f;
+  int t = 0, h = 0;
+  if (ok) {
+    t = w / heads;
+    h = w % heads;
+    const size_t off = (size_t)t * heads * 128 + h * 128 + sub * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(o + off);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + off);
+    const __half2* ah = reinterpret_cast<const __half2*>(&a);
+    const __half2* gh = reinterpret_cast<const __half2*>(&g);
 #pragma unroll
-  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-  if (lane == 0) {
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = __half22float2(ah[k]), y = __half22float2(gh[k]);
+      v = fmaf(x.x, y.x, fmaf(x.y, y.y, v));
+    }
+  }
+#pragma unroll
+  for (int m = 8; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  if (ok && sub == 0) {
     const int b = t / seq, q = t % seq;
     dsum[((size_t)b * heads + h) * seq + q] = v;
   }
@@ -281,26 +289,35 @@ __global__ void __launch_bounds__(AB_THREADS)
 }
 
 // dQ = dq32 * scale with RoPE undone, into the q columns of dQKV (fp16).
-// One thread per (token, head, pair of dims); rope_pm is the (cos, sin) table in
-// position-major order [seq][64], so the lanes of a warp (consecutive pairs) read it
-// contiguously.
+// One thread per (token, 8 consecutive dims of one head): two 16-byte loads of dq32, two
+// of rope_pm (the (cos, sin) table in position-major order [seq][64]) and one 16-byte
+// store.
 __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq32,
                                    const float2* __restrict__ rope_pm,
                                    __half* __restrict__ dqkv, int T, int seq, int heads,
                                    int n_qkv, float scale) {
-  const int q_dim = heads * 128;
-  const size_t n = (size_t)T * q_dim / 2;
+  const int q8 = heads * 16;  // 8-dim groups per token
+  const size_t n = (size_t)T * q8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / (q_dim / 2));
-    const int c2 = (int)(i % (q_dim / 2));  // pair index across heads
-    const float2 d = reinterpret_cast<const float2*>(dq32)[i];
-    float a = d.x * scale, b = d.y * scale;
-    const float2 cs = rope_pm[(size_t)(t % seq) * 64 + (c2 & 63)];
-    const float ra = cs.x * a + cs.y * b, rb = -cs.y * a + cs.x * b;
-    a = ra;
-    b = rb;
-    reinterpret_cast<uint32_t*>(dqkv + (size_t)t * n_qkv)[c2] = pack_half2(a, b);
+    const int t = (int)(i / q8);
+    const int g = (int)(i - (size_t)t * q8);
+    const float4* src = reinterpret_cast<const float4*>(dq32) + 2 * i;
+    const float4 d0 = src[0], d1 = src[1];
+    const float4* rp =
+        reinterpret_cast<const float4*>(rope_pm + (size_t)(t % seq) * 64 + (g & 15) * 4);
+    const float4 r0 = rp[0], r1 = rp[1];  // (cos, sin) of pairs 4(g%16) .. +3
+    const float a[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    const float cs[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    uint32_t w[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float x = a[2 * p] * scale, y = a[2 * p + 1] * scale;
+      const float c = cs[2 * p], sn = cs[2 * p + 1];
+      w[p] = pack_half2(c * x + sn * y, -sn * x + c * y);
+    }
+    *reinterpret_cast<uint4*>(dqkv + (size_t)t * n_qkv + (size_t)g * 8) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 

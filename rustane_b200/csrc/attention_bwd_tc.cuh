@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int e = 0; e < 2; ++e) {
             const int jj = i * 2 + e;       // column within this half
             const int qi = half * 32 + jj;  // query index within the block
-            float p = exp2f(__uint_as_float(sv[half][jj]) * scale_log2 - lse_h[qi]);
+            float p = exp2_mufu(__uint_as_float(sv[half][jj]) * scale_log2 - lse_h[qi]);
             if (key > q0 + qi) p = 0.f;     // causal mask
             pp[e] = p;
             dd[e] = p * (__uint_as_float(dv[half][jj]) - d_h[qi]);

@@ -43,13 +43,6 @@ constexpr int FA_BAR_OFF = 98304;
 constexpr int FA_SMEM = FA_BAR_OFF + 256 + 1024;
 constexpr uint32_t FA_TMEM_COLS = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
 
-// 2^x on the special-function unit (MUFU); 2^-inf = +0.
-__device__ __forceinline__ float exp2_mufu(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // 2^x for x <= 0 on the FMA pipe, to share the softmax exponentials with the MUFU:
 // x = n + f with n = floor(x), f in [0, 1); 2^f by a degree-4 polynomial (a weighted
 // least-squares fit to 2^f on [0, 1), max relative error 2.6e-6, below the fp16

@@ -254,6 +254,7 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiCeBwd>();
   set_gemm_attrs_for<EpiScaledF32, GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwigluBwd, GEMM_B_MN>();
+  set_gemm_attrs_for<EpiStoreF16Dsum, GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32>();  // decode (decode.cuh)
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
@@ -432,21 +433,23 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
   return cudaGetLastError();
 }
 
-// Attention backward: D = rowsum(dO o O), the key-block kernel (dK, dV into dqkv; dQ
-// accumulated in dq32, which this zeroes first), then dQ into dqkv.
+// Attention backward: D = rowsum(dO o O) (unless the caller computed it: dsum_ready), the
+// key-block kernel (dK, dV into dqkv; dQ accumulated in dq32, which this zeroes first),
+// then dQ into dqkv.
 cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half* v,
                                  const __half* o, const __half* dout, const float* lse2,
                                  float* dsum, float* dq32, const float2* rope,
                                  const float2* rope_pm, __half* dqkv, int batch, int heads,
                                  int kv_heads, int seq, int sms, cudaStream_t st,
-                                 int* err = nullptr) {
+                                 int* err = nullptr, bool dsum_ready = false) {
   const int T = batch * seq;
   const int q_dim = heads * 128, n_qkv = q_dim + 2 * kv_heads * 128;
   const float scale = 1.0f / sqrtf(128.0f);
   const float scale_log2 = 1.4426950408889634f * scale;
   cudaError_t e = cudaMemsetAsync(dq32, 0, (size_t)T * q_dim * sizeof(float), st);
   if (e != cudaSuccess) return e;
-  attn_bwd_dsum_kernel<<<(T * heads + 7) / 8, 256, 0, st>>>(o, dout, dsum, T, seq, heads);
+  if (!dsum_ready)
+    attn_bwd_dsum_kernel<<<(T * heads + 15) / 16, 256, 0, st>>>(o, dout, dsum, T, seq, heads);
   CUtensorMap tq, tk, tv, tdo, tdq;
   const bool tc = seq % AT_BK == 0 &&
                   make_tmap_qkv(&tq, q, (uint64_t)batch * heads * seq, AT_BQ) &&
@@ -465,8 +468,8 @@ cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half*
                                                        dqkv, seq, heads, kv_heads, scale_log2,
                                                        scale);
   }
-  const size_t pairs = (size_t)T * q_dim / 2;
-  const int blocks = (int)std::min<size_t>((pairs + 255) / 256, (size_t)sms * 16);
+  const size_t groups = (size_t)T * q_dim / 8;
+  const int blocks = (int)std::min<size_t>((groups + 255) / 256, (size_t)sms * 16);
   attn_bwd_dq_kernel<<<blocks, 256, 0, st>>>(dq32, rope_pm, dqkv, T, seq, heads, n_qkv, scale);
   return cudaGetLastError();
 }

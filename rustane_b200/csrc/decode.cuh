@@ -233,7 +233,7 @@ __global__ void decode_swiglu_kernel(const float* __restrict__ part, int splits,
     const int b = i / hid, j = i % hid;
     const float h1 = sum_parts(part, splits, slice, (size_t)b * 2 * hid + 2 * j);
     const float h3 = sum_parts(part, splits, slice, (size_t)b * 2 * hid + 2 * j + 1);
-    g[i] = __float2half_rn(h1 / (1.0f + __expf(-h1)) * h3);
+    g[i] = __float2half_rn(__fdividef(h1, 1.0f + __expf(-h1)) * h3);
   }
 }
 

@@ -129,12 +129,13 @@ __device__ __forceinline__ void warp_store_rows(uint8_t* wbuf, const uint4 (&out
   __syncwarp();
 }
 
-// The inverse of warp_store_rows: lane L receives the NB-byte segment at src of row L
-// (src = nullptr: zeros) in in[0 .. NB/16); the warp's loads are coalesced over whole
-// row segments and transposed through the warp's shared buffer.
+// The inverse of warp_store_rows, in two halves so that one chunk's loads are in flight
+// while the previous chunk is processed. warp_issue_rows: the warp's loads, coalesced
+// over whole row segments, into registers (src = nullptr: zeros); warp_finish_rows:
+// those pieces transposed through the warp's shared buffer, so that lane L receives the
+// NB-byte segment of row L in in[0 .. NB/16).
 template <int NB>
-__device__ __forceinline__ void warp_load_rows(uint8_t* wbuf, const uint8_t* src,
-                                               uint4 (&in)[8]) {
+__device__ __forceinline__ void warp_issue_rows(const uint8_t* src, uint4 (&x)[NB / 16]) {
   constexpr int Q = NB / 16;
   constexpr int RPI = 32 / Q;
   const int lane = threadIdx.x & 31;
@@ -144,10 +145,23 @@ __device__ __forceinline__ void warp_load_rows(uint8_t* wbuf, const uint8_t* src
     const int r = k * RPI + lane / Q;
     const int j = lane % Q;
     const unsigned long long base = __shfl_sync(0xffffffffu, my, r);
-    uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (base) x = __ldg(reinterpret_cast<const uint4*>(base) + j);
+    x[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (base) x[k] = __ldg(reinterpret_cast<const uint4*>(base) + j);
+  }
+}
+
+template <int NB>
+__device__ __forceinline__ void warp_finish_rows(uint8_t* wbuf, const uint4 (&x)[NB / 16],
+                                                 uint4 (&in)[8]) {
+  constexpr int Q = NB / 16;
+  constexpr int RPI = 32 / Q;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < Q; ++k) {
+    const int r = k * RPI + lane / Q;
+    const int j = lane % Q;
     const int swr = (r / (8 / Q)) & (Q - 1);
-    *reinterpret_cast<uint4*>(wbuf + r * NB + ((j ^ swr) << 4)) = x;
+    *reinterpret_cast<uint4*>(wbuf + r * NB + ((j ^ swr) << 4)) = x[k];
   }
   __syncwarp();
   const int sw = (lane / (8 / Q)) & (Q - 1);
@@ -156,8 +170,9 @@ __device__ __forceinline__ void warp_load_rows(uint8_t* wbuf, const uint8_t* src
   __syncwarp();
 }
 
-// Epilogues with IN_BYTES > 0 read a row segment per chunk: the kernel loads it with
-// warp_load_rows (from in_src(row, col)) into the chunk's output array before chunk().
+// Epilogues with IN_BYTES > 0 read a row segment per chunk: the kernel loads it (from
+// in_src(row, col)) one chunk ahead with warp_issue_rows and hands it to chunk() in the
+// chunk's output array.
 template <class Epi, class = void>
 struct EpiInBytes { static constexpr int value = 0; };
 template <class Epi>
@@ -174,6 +189,52 @@ struct EpiStoreF16 {
                                         uint4 (&o)[8], uint8_t*& dst) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = pack8_f16(v + 8 * j);
+    dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// fp16 store of the attention-output gradient dA (token-major [T, heads*128]) that also
+// yields the attention backward's D[b, h, q] = sum_d dA[t, h*128+d] * O[t, h*128+d]
+// (t = b*seq + q): each thread owns one row, its four 32-column chunks of a head arrive
+// in order, and the dot product is taken over the fp16-rounded dA values the attention
+// kernel will read. O's row segment is the chunk input (IN_BYTES). Column tiles start on
+// head boundaries (BN = 256).
+struct EpiStoreF16Dsum {
+  using Pre = NoPre;
+  static constexpr int OUT_BYTES = 64;
+  static constexpr int IN_BYTES = 64;
+  __half* out;
+  int ldo;
+  const __half* o;  // attention output, same layout as out
+  float* dsum;      // [batch, heads, seq]
+  int seq, heads;
+  float acc;
+  __device__ __forceinline__ const uint8_t* in_src(int row, int col0) const {
+    return reinterpret_cast<const uint8_t*>(o + (size_t)row * ldo + col0);
+  }
+  __device__ __forceinline__ void begin_row(int, bool) { acc = 0.f; }
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
+                                        uint4 (&io)[8], uint8_t*& dst) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 ov = io[j];
+      const uint4 gv = pack8_f16(v + 8 * j);
+      const __half2* oh = reinterpret_cast<const __half2*>(&ov);
+      const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = __half22float2(oh[k]), g = __half22float2(gh[k]);
+        acc = fmaf(a.x, g.x, fmaf(a.y, g.y, acc));
+      }
+      io[j] = gv;
+    }
+    if ((col0 & 127) == 96) {  // last chunk of head col0 / 128
+      const int b = row / seq, q = row - b * seq;
+      dsum[((size_t)b * heads + (col0 >> 7)) * seq + q] = acc;
+      acc = 0.f;
+    }
     dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
@@ -346,7 +407,11 @@ struct EpiScaledF32Add {
 };
 
 // B rows interleave W1 and W3 columns: row 2j = W1[:, j], row 2j+1 = W3[:, j].
-// g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z).
+// g[row, j] = silu(h1_j) * h3_j, silu(z) = z / (1 + e^-z). The quotient uses the
+// approximate divide (reciprocal + multiply, 2 ulp; 0 once 1 + e^-z passes 2^126, the
+// limit of silu there) for a result rounded to fp16: with the IEEE divide the SwiGLU
+// epilogues kept the special-function (XU) pipe ~70 % busy (ncu) and the W1/W3 GEMM
+// ran 10 % slower.
 struct EpiSwiglu {
   using Pre = NoPre;
   static constexpr int OUT_BYTES = 32;
@@ -360,7 +425,7 @@ struct EpiSwiglu {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float h1 = v[2 * j], h3 = v[2 * j + 1];
-      r[j] = h1 / (1.0f + __expf(-h1)) * h3;
+      r[j] = __fdividef(h1, 1.0f + __expf(-h1)) * h3;
     }
     o[0] = pack8_f16(r);
     o[1] = pack8_f16(r + 8);
@@ -386,7 +451,7 @@ struct EpiSwigluSave {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float h1 = v[2 * j], h3 = v[2 * j + 1];
-      r[j] = h1 / (1.0f + __expf(-h1)) * h3;
+      r[j] = __fdividef(h1, 1.0f + __expf(-h1)) * h3;
     }
     uint4* hs = reinterpret_cast<uint4*>(h13 + (size_t)row * ldh + col0);
 #pragma unroll
@@ -426,7 +491,7 @@ struct EpiSwigluBwd {
       for (int k = 0; k < 4; ++k) {
         const float2 h = __half22float2(hh[k]);  // (h1, h3) of column 4i + k
         const float dg = v[4 * i + k];
-        const float sig = 1.0f / (1.0f + __expf(-h.x));
+        const float sig = __fdividef(1.0f, 1.0f + __expf(-h.x));
         const float dh3 = dg * h.x * sig;
         const float dh1 = dg * h.y * sig * (1.0f + h.x * (1.0f - sig));
         w[k] = pack_half2(dh1, dh3);
@@ -546,12 +611,12 @@ struct EpiCrossEntropy {
     }
     const float L2E = 1.4426950408889634f;
     if (cm > m) {
-      s *= exp2f((m - cm) * L2E);
+      s *= exp2_mufu((m - cm) * L2E);
       m = cm;
     }
     float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc += exp2f((z[i] - m) * L2E);
+    for (int i = 0; i < 32; ++i) acc += exp2_mufu((z[i] - m) * L2E);
     s += acc;
   }
   __device__ __forceinline__ void end_row(int row, int n_blk) {
@@ -788,6 +853,12 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(group * BN);
       typename Epi::Pre pa, pb;
       uint8_t* wbuf = epi_bufs + (warp - 2) * Cfg::EPI_BUF_BYTES;
+      constexpr int IN_NB = EpiInBytes<Epi>::value > 0 ? EpiInBytes<Epi>::value : 16;
+      uint4 in_next[IN_NB / 16];  // the next chunk's input pieces, loads in flight
+      auto issue_in = [&](int col) {
+        if constexpr (EpiInBytes<Epi>::value > 0)
+          warp_issue_rows<IN_NB>(row_ok && col < N ? e.in_src(row, col) : nullptr, in_next);
+      };
       // One chunk: TMEM -> registers, epilogue math, warp-cooperative store. Global
       // operands (Pre) are loaded one chunk ahead; the TMEM load latency is covered by
       // the other epilogue group. col < N is warp-uniform.
@@ -799,9 +870,10 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         tmem_ld_wait_regs(r);
         uint4 outv[8];
         uint8_t* dst = nullptr;
-        if constexpr (EpiInBytes<Epi>::value > 0)
-          warp_load_rows<(EpiInBytes<Epi>::value > 0 ? EpiInBytes<Epi>::value : 16)>(
-              wbuf, row_ok ? e.in_src(row, col) : nullptr, outv);
+        if constexpr (EpiInBytes<Epi>::value > 0) {
+          warp_finish_rows<IN_NB>(wbuf, in_next, outv);
+          if (c + 1 < NC) issue_in(col + 32);
+        }
         if (row_ok) {
           float v[32];
 #pragma unroll
@@ -814,6 +886,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       };
       const int col_base = n_blk * BN;
       if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
+      issue_in(col_base);
 #pragma unroll 1
       for (int c = 0; c < NC; c += 2) {
         const int col_b = col_base + (c + 1) * 32;

@@ -663,14 +663,15 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
                  t->dxh, g2));
     // attention: dA = (alpha dX2) Wo^T; dWo += s (alpha dX2)^T A
     {
-      EpiStoreF16 ep{t->da, qd};
-      TRY(launch_gemm<EpiStoreF16, GEMM_B_MN>(pick_mode(T, qd, di), ta_dxh, tb_wo, tb_wo, T, qd,
-                                              d, l, ep, c->dev_err, di, st));
+      EpiStoreF16Dsum ep{t->da, qd, t->attn + lo * qd, t->dsum, S, H, 0.f};
+      TRY(launch_gemm<EpiStoreF16Dsum, GEMM_B_MN>(pick_mode(T, qd, di), ta_dxh, tb_wo, tb_wo, T,
+                                                  qd, d, l, ep, c->dev_err, di, st));
     }
     TRY(grad_gemm(tg_dxh, mnmap(t->attn + lo * qd, qd, T), d, qd, t->g_wo + (size_t)l * d * qd));
     TRY(launch_attention_bwd(t->q + lo * qd, t->k + lo * c->kv_dim, t->v + lo * c->kv_dim,
                              t->attn + lo * qd, t->da, t->lse + lo * H, t->dsum, t->dq32, c->rope,
-                             c->rope_pm, t->dqkv, batch, H, Hk, S, di.sms, st, c->dev_err));
+                             c->rope_pm, t->dqkv, batch, H, Hk, S, di.sms, st, c->dev_err,
+                             /*dsum_ready=*/true));
     {
       EpiScaledF32 ep{t->dtmp, d, 1.0f};
       TRY(launch_gemm<EpiScaledF32, GEMM_B_MN>(m_o, ta_dqkv, tb_wqkv, tb_wqkv, T, d, nq, l, ep,
