@@ -119,10 +119,25 @@ bool make_tmap_rows(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t r
   return r == CUDA_SUCCESS;
 }
 
+// fp16 matrix [rows][cols] in 32 x 32 boxes, 64-byte swizzle (the fused residual
+// epilogue's fp16(x o gamma) store).
+bool make_tmap_h32(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // fp32 matrix [rows][cols] (row-major) tiled as box_cols x box_rows boxes, no swizzle
-// (the attention backward's dQ reduce-add target).
+// (the attention backward's dQ reduce-add target) or 128-byte swizzle.
 bool make_tmap_f32_rows(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows,
-                        uint32_t box_cols, uint32_t box_rows) {
+                        uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {cols, rows};
@@ -130,7 +145,8 @@ bool make_tmap_f32_rows(CUtensorMap* map, const void* ptr, uint64_t cols, uint64
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -224,7 +240,8 @@ constexpr int TP_COMM_SMS = 16;
 template <int BN, class Epi, int LAYOUT>
 void set_gemm_attr() {
   cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi, LAYOUT>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM_BYTES);
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       GemmCfg<BN, false, EpiTmaIn<Epi>::value>::SMEM_BYTES);
 }
 
 template <class Epi, int LAYOUT = 0>
@@ -232,7 +249,8 @@ void set_gemm_attrs_for() {
   set_gemm_attr<128, Epi, LAYOUT>();
   set_gemm_attr<256, Epi, LAYOUT>();
   cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi, LAYOUT>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<256, true>::SMEM_BYTES);
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       GemmCfg<256, true, EpiTmaIn<Epi>::value>::SMEM_BYTES);
 }
 
 void set_all_kernel_attrs() {
@@ -255,6 +273,11 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiScaledF32, GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwigluBwd, GEMM_B_MN>();
   set_gemm_attrs_for<EpiStoreF16Dsum, GEMM_B_MN>();
+  // fused residual + RMSNorm forward
+  set_gemm_attrs_for<EpiResidualNorm>();
+  set_gemm_attrs_for<RowScaled<EpiQkvRope>>();
+  set_gemm_attrs_for<RowScaled<EpiSwiglu>>();
+  set_gemm_attrs_for<RowScaled<EpiCrossEntropy>>();
   set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32>();  // decode (decode.cuh)
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
@@ -312,25 +335,35 @@ void ensure_attrs(int device) { (void)device_info(device); }
 
 int num_sms_of(int device) { return device_info(device).sms; }
 
+// The epilogue's input map (TMA_IN epilogues); the others get a zeroed map they never use.
+const CUtensorMap& tc_or_null(const CUtensorMap* tc) {
+  static const CUtensorMap zero{};
+  return tc ? *tc : zero;
+}
+
 template <int BN, class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                            int bz, const Epi& epi, int* err, int units, int splits,
-                           cudaStream_t st) {
+                           cudaStream_t st, const CUtensorMap* tc = nullptr,
+                           const CUtensorMap* td = nullptr) {
+  using Cfg = GemmCfg<BN, false, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
-  gemm_tn_kernel<BN, Epi, LAYOUT><<<grid, GEMM_THREADS, GemmCfg<BN>::SMEM_BYTES, st>>>(
-      ta, tb, M, N, K, bz, splits, epi, err);
+  gemm_tn_kernel<BN, Epi, LAYOUT><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(
+      ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
 
 template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
                              int K, int bz, const Epi& epi, int* err, int clusters, int splits,
-                             cudaStream_t st) {
+                             cudaStream_t st, const CUtensorMap* tc = nullptr,
+                             const CUtensorMap* td = nullptr) {
+  using Cfg = GemmCfg<256, true, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
-  gemm_tn_pair_kernel<Epi, LAYOUT><<<2 * pairs, GEMM_THREADS, GemmCfg<256, true>::SMEM_BYTES, st>>>(
-      ta, tb_half, M, N, K, bz, splits, epi, err);
+  gemm_tn_pair_kernel<Epi, LAYOUT><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(
+      ta, tb_half, tc_or_null(tc), tc_or_null(td), M, N, K, bz, splits, epi, err);
   return cudaGetLastError();
 }
 
@@ -370,13 +403,16 @@ int mode_block_n(int mode) { return mode == GM_SINGLE128 ? 128 : 256; }
 template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
-                        int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1) {
+                        int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1,
+                        const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr) {
   if (mode == GM_PAIR)
     return launch_gemm_pair<Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters,
-                                         splits, st);
+                                         splits, st, tc, td);
   if (mode == GM_SINGLE128)
-    return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st);
-  return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st);
+    return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st,
+                                            tc, td);
+  return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st,
+                                          tc, td);
 }
 
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
@@ -555,7 +591,10 @@ struct cb_ctx {
 
   // workspace
   float* x = nullptr;          // [T, dim] fp32 residual stream
-  __half* xn = nullptr;        // [T, dim] normalised activations (final: Xf)
+  __half* xn = nullptr;        // [T, dim] normalised activations (final: Xf), or fp16(x o gamma)
+                               // when the residual add + RMSNorm is fused (ss_part then holds
+                               // the rows' partial sums of x^2)
+  float* ss_part = nullptr;    // [T, dim/128]
   __half* q = nullptr;         // [B, H, S, 128]
   __half* k = nullptr;
   __half* v = nullptr;
@@ -578,6 +617,8 @@ struct cb_ctx {
 
   // tensor maps (A operands sized for max_batch; B per weight kind, both tile widths)
   CUtensorMap tm_xn, tm_attn, tm_g;
+  CUtensorMap tm_x;              // the fp32 residual in 32 x 32 boxes (fused residual epilogue)
+  CUtensorMap tm_xh;             // xn as fp16 32 x 32 boxes (its second output)
   CUtensorMap tm_q, tm_k, tm_v;  // attention operands ([B*H*S, 128] rows)
   CUtensorMap tm_wqkv[2], tm_wo[2], tm_w13[2], tm_w2[2], tm_embed[2];  // [0]=BN128 [1]=BN256
 
@@ -879,14 +920,43 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   const int m_13 = pick_mode(T, 2 * hid, di);
   const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
 
+  // Residual add + RMSNorm: fused into the projection's epilogue (EpiResidualNorm: x +=
+  // alpha * acc in place, xn = fp16(x o gamma), per-row partial sums of x^2; the next
+  // GEMM applies 1/rms per row, RowScaled) unless K is split or the model is tensor
+  // parallel; otherwise the projection writes delta and add_rmsnorm does the rest.
+  const bool fuse_norm = !tp && d % 128 == 0;
+  bool fused_last = false;  // the last projection used the fused epilogue
+  bool xn_scaled = false;   // xn holds fp16(x o gamma): consumers scale rows by 1/rms
+  auto consume = [&](int mode, const CUtensorMap& tb128, const CUtensorMap& tb256, int N,
+                     int layer, const auto& inner) -> cudaError_t {
+    using E = std::decay_t<decltype(inner)>;
+    if (xn_scaled) {
+      RowScaled<E> ep{inner, c->ss_part, d / 128, (float)d, RMS_EPS, 1.f};
+      return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di, st);
+    }
+    return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di, st);
+  };
+
   // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer. fp16
   // by default; fp32 when K is split in two (atomic adds into a zeroed buffer) or under
   // tensor parallelism, where the fp32 partials are summed across ranks (NCCL).
+  // gamma_next: the gain of the RMSNorm that follows (fused epilogue).
   bool delta_f32 = false;
   auto project = [&](int mode, int splits, const CUtensorMap& ta, const CUtensorMap& tb128,
-                     const CUtensorMap& tb256, int K, int layer, int cls) -> cudaError_t {
+                     const CUtensorMap& tb256, int K, int layer, int cls,
+                     const float* gamma_next) -> cudaError_t {
     cudaError_t r;
     delta_f32 = tp || splits > 1;
+    fused_last = fuse_norm && splits == 1;
+    if (fused_last) {
+      EpiResidualNorm ep{gamma_next, c->ss_part, d / 128, alpha, 0.f};
+      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, 1,
+                      &c->tm_x, &c->tm_xh);
+      if (r != cudaSuccess) return r;
+      mark(cls, 2.0 * Td * d * K,
+           Td * K * 2 + (double)d * K * 2 + Td * d * (4 + 4 + 2) + Td * (d / 128) * 4);
+      return cudaSuccess;
+    }
     if (splits > 1) {
       r = cudaMemsetAsync(c->delta32, 0, (size_t)T * d * sizeof(float), st);
       if (r != cudaSuccess) return r;
@@ -914,6 +984,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     return cudaSuccess;
   };
   auto add_norm = [&](const float* gamma) -> cudaError_t {
+    xn_scaled = fused_last;
+    if (fused_last) return cudaSuccess;  // done by the projection's epilogue
     cudaError_t r = delta_f32 ? launch_add_rmsnorm(c->x, c->x, c->delta32, gamma, c->xn, T, d, st)
                               : launch_add_rmsnorm(c->x, c->x, c->delta, gamma, c->xn, T, d, st);
     if (r == cudaSuccess) mark(K_RMSNORM, 0, Td * d * (4 + (delta_f32 ? 4 : 2) + 4 + 2));
@@ -921,15 +993,11 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   };
 
   for (int l = 0; l < L; ++l) {
-    if (l > 0) {  // residual add of the previous layer's down projection + RMSNorm(gamma1)
-      if ((e = add_norm(c->gamma + (size_t)l * 2 * d)) != cudaSuccess) return e;
-    }
     __half* kl = kv ? kv->k + (size_t)l * kv->layer_stride : c->k;
     __half* vl = kv ? kv->v + (size_t)l * kv->layer_stride : c->v;
     {
       EpiQkvRope ep{c->q, kl, vl, c->rope, S, c->heads_l, c->kv_heads_l};
-      e = launch_gemm(m_qkv, c->tm_xn, c->tm_wqkv[0], c->tm_wqkv[1], T, c->n_qkv, d, l, ep,
-                      c->dev_err, di, st);
+      e = consume(m_qkv, c->tm_wqkv[0], c->tm_wqkv[1], c->n_qkv, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
@@ -942,18 +1010,22 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
                          c->kv_heads_l, S, c->dev_err, st);
     if (e != cudaSuccess) return e;
     mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
-    e = project(m_o, s_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O);
+    e = project(m_o, s_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O,
+                c->gamma + (size_t)l * 2 * d + d);
     if (e != cudaSuccess) return e;
     if ((e = add_norm(c->gamma + (size_t)l * 2 * d + d)) != cudaSuccess) return e;
     {
       EpiSwiglu ep{c->g, hid};
-      e = launch_gemm(m_13, c->tm_xn, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep,
-                      c->dev_err, di, st);
+      e = consume(m_13, c->tm_w13[0], c->tm_w13[1], 2 * hid, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
-    e = project(m_2, s_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2);
+    const float* g_next = l + 1 < L ? c->gamma + (size_t)(l + 1) * 2 * d : c->gamma_final;
+    e = project(m_2, s_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2, g_next);
     if (e != cudaSuccess) return e;
+    if (l + 1 < L) {  // residual add + RMSNorm(gamma1) of the next layer
+      if ((e = add_norm(g_next)) != cudaSuccess) return e;
+    }
   }
   if ((e = add_norm(c->gamma_final)) != cudaSuccess) return e;
 
@@ -966,8 +1038,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     ep.targets = c->targets;
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
-    e = launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
-                    c->dev_err, di, st);
+    e = consume(m_head, c->tm_embed[0], c->tm_embed[1], V, 0, ep);
     if (e != cudaSuccess) return e;
     mark(K_GEMM_HEAD, 2.0 * Td * V * d, Td * d * 2 + (double)V * d * 2 + Td * nparts * 8 + Td * 8);
   }
@@ -1227,6 +1298,7 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(dmalloc(&ctx->gamma_final, (size_t)d));
   CREATE_CUDA(dmalloc(&ctx->x, T * d));
   CREATE_CUDA(dmalloc(&ctx->xn, T * d));
+  CREATE_CUDA(dmalloc(&ctx->ss_part, T * ((d + 127) / 128)));
   CREATE_CUDA(dmalloc(&ctx->q, T * ctx->q_dim));
   CREATE_CUDA(dmalloc(&ctx->k, T * ctx->kv_dim));
   CREATE_CUDA(dmalloc(&ctx->v, T * ctx->kv_dim));
@@ -1272,6 +1344,8 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
 
   bool ok = true;
   ok &= make_tmap(&ctx->tm_xn, ctx->xn, d, T, 1, 128);
+  ok &= make_tmap_f32_rows(&ctx->tm_x, ctx->x, d, T, 32, 32, /*swizzle128=*/true);
+  ok &= make_tmap_h32(&ctx->tm_xh, ctx->xn, d, T);
   ok &= make_tmap(&ctx->tm_attn, ctx->attn, ctx->q_dim, T, 1, 128);
   ok &= make_tmap(&ctx->tm_g, ctx->g, hid, T, 1, 128);
   ok &= make_tmap_qkv(&ctx->tm_q, ctx->q, T * ctx->heads_l, FA_BQ);

@@ -25,6 +25,11 @@
 //   EpiCrossEntropy  per-(row, N-tile) running max / sum-exp and target logit
 //                 of the tied LM head, so logits never reach HBM
 //                 (crates/engine/src/full_model.rs:436-471, cpu/cross_entropy.rs:58-96)
+//   EpiResidualNorm  x += alpha * acc in place (the fp32 residual, read by TMA two
+//                 chunks ahead), fp16(x * gamma) for the next GEMM and per-row partial
+//                 sums of x^2 (layer.rs:4471 vsma + the following rmsnorm)
+//   RowScaled<E>  E applied to acc * rinv[row], rinv from those partial sums: the
+//                 RMSNorm's 1/rms applied after the GEMM, where it commutes
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -41,7 +46,9 @@ constexpr int GEMM_EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
 // PAIR: a two-CTA cluster computes a 256 x BN tile (each CTA 128 rows, half of B).
-template <int BN, bool PAIR = false>
+// TMA_IN: the epilogue reads a 32 x 32 fp32 box of an input matrix per chunk (two 4 KB
+// slots per epilogue warp); the operand ring then has 4 stages.
+template <int BN, bool PAIR = false, bool TMA_IN = false>
 struct GemmCfg {
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
   static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
@@ -50,12 +57,14 @@ struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr int B_BYTES = B_ROWS * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (STAGE_BYTES <= 32768) ? 6 : 4;
+  static constexpr int STAGES = (STAGE_BYTES <= 32768 && !TMA_IN) ? 6 : 4;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int IN_SLOT_BYTES = 4096;  // 32 rows x 32 fp32, 128-byte swizzle
+  static constexpr int IN_BYTES = TMA_IN ? GEMM_EPI_WARPS * 2 * IN_SLOT_BYTES : 0;
+  static constexpr int BAR_BYTES = TMA_IN ? 512 : 256;
   static constexpr int EPI_BUF_BYTES = 4096;  // per epilogue warp (32 rows x 128 B)
   static constexpr int SMEM_BYTES =
-      STAGES * STAGE_BYTES + 1024 + BAR_BYTES + GEMM_EPI_WARPS * EPI_BUF_BYTES;
+      STAGES * STAGE_BYTES + IN_BYTES + 1024 + BAR_BYTES + GEMM_EPI_WARPS * EPI_BUF_BYTES;
 };
 
 // ------------------------------------------------------------------ epilogues
@@ -86,6 +95,20 @@ template <class Epi, class = void>
 struct EpiHasSplit { static constexpr bool value = false; };
 template <class Epi>
 struct EpiHasSplit<Epi, decltype(void(&Epi::set_split))> { static constexpr bool value = true; };
+
+// Epilogues with ROW_SCALE get the accumulator values multiplied by their member rs.
+template <class Epi, class = void>
+struct EpiRowScale { static constexpr bool value = false; };
+template <class Epi>
+struct EpiRowScale<Epi, decltype(void(Epi::ROW_SCALE))> { static constexpr bool value = Epi::ROW_SCALE; };
+
+// Epilogues with TMA_IN get, per chunk, the 32 fp32 values of their row from the
+// kernel's input tensor map (tmC) at the chunk's columns, and produce a second output
+// (OUT2_BYTES into out2 / dst2) besides the first.
+template <class Epi, class = void>
+struct EpiTmaIn { static constexpr bool value = false; };
+template <class Epi>
+struct EpiTmaIn<Epi, decltype(void(Epi::TMA_IN))> { static constexpr bool value = Epi::TMA_IN; };
 
 __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   uint4 w;
@@ -624,6 +647,105 @@ struct EpiCrossEntropy {
   }
 };
 
+// Residual update + the first half of the next RMSNorm, fused into the O and down
+// projections: x = x + alpha * acc (fp32, in place), xh = fp16(x * gamma) as the next
+// GEMM's A operand, and per row the sum of x^2 over each 128-column group into
+// ss_part[row][col / 128] (fixed-order partials: the consumer adds them in order, so the
+// loss stays bit-reproducible). The 1/rms factor is applied by the consumer GEMM
+// (RowScaled), since rmsnorm(x) W^T = rinv * ((x o gamma) W^T).
+// Data movement is all TMA (TMA_IN): the kernel loads each 32 x 32 box of the old x into
+// shared memory two chunks ahead (tmC), chunk_tma overwrites it in place with the new x
+// and writes fp16(x * gamma) into a 32 x 32 staging box, and the kernel stores both
+// boxes with TMA (tmC, tmD).
+struct EpiResidualNorm {
+  using Pre = NoPre;
+  static constexpr bool TMA_IN = true;
+  static constexpr int OUT_BYTES = 0;
+  const float* gamma;
+  float* ss_part;
+  int n_part;  // d / 128
+  float alpha;
+  float ss;
+  __device__ __forceinline__ void begin_row(int, bool) { ss = 0.f; }
+  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  // xrow: this row's 128 bytes of x in the 128-byte-swizzled box (16-byte piece k at
+  // xrow + ((k ^ sw128) << 4)); hrow: its 64 bytes in the 64-byte-swizzled fp16 box
+  // (piece k at hrow + ((k ^ sw64) << 4)).
+  __device__ __forceinline__ void chunk_tma(int row, int col0, const float (&v)[32],
+                                            uint8_t* xrow, int sw128, uint8_t* hrow,
+                                            int sw64) {
+    const float4* g4 = reinterpret_cast<const float4*>(gamma + col0);  // same for all lanes
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+    float4 a[8];  // loads of a half first: the in-place stores would otherwise order them
+#pragma unroll
+    for (int j = 4 * hh; j < 4 * hh + 4; ++j)
+      a[j] = *reinterpret_cast<const float4*>(xrow + ((j ^ sw128) << 4));
+#pragma unroll
+    for (int j = 4 * hh; j < 4 * hh + 4; ++j) {
+      const float4 g = __ldg(g4 + j);
+      float4 n;
+      n.x = fmaf(alpha, v[4 * j], a[j].x);
+      n.y = fmaf(alpha, v[4 * j + 1], a[j].y);
+      n.z = fmaf(alpha, v[4 * j + 2], a[j].z);
+      n.w = fmaf(alpha, v[4 * j + 3], a[j].w);
+      *reinterpret_cast<float4*>(xrow + ((j ^ sw128) << 4)) = n;
+      ss = fmaf(n.x, n.x, fmaf(n.y, n.y, fmaf(n.z, n.z, fmaf(n.w, n.w, ss))));
+      const uint2 h = make_uint2(pack_half2(n.x * g.x, n.y * g.y), pack_half2(n.z * g.z, n.w * g.w));
+      *reinterpret_cast<uint2*>(hrow + (((j >> 1) ^ sw64) << 4) + (j & 1) * 8) = h;
+    }
+    }
+    if ((col0 & 127) == 96) {  // last chunk of a 128-column group
+      ss_part[(size_t)row * n_part + (col0 >> 7)] = ss;
+      ss = 0.f;
+    }
+  }
+  __device__ __forceinline__ void end_row(int, int) {}
+};
+
+// The inner epilogue applied to acc * rinv[row], rinv = 1 / sqrt(sum(ss_part[row]) / d +
+// eps) from the partial sums EpiResidualNorm wrote (the RMSNorm of the row whose fp16
+// x * gamma is this GEMM's A operand).
+// (The kernel multiplies the accumulator values by rs as it reads them: ROW_SCALE.)
+template <class Inner>
+struct RowScaled {
+  using Pre = typename Inner::Pre;
+  static constexpr int OUT_BYTES = Inner::OUT_BYTES;
+  static constexpr bool ROW_SCALE = true;
+  Inner in;
+  const float* ss_part;
+  int n_part;
+  float dim;  // the row length d
+  float eps;
+  float rs;
+  __device__ __forceinline__ void begin_row(int row, bool valid) {
+    rs = 1.f;
+    if (valid) {
+      const float* p = ss_part + (size_t)row * n_part;
+      float t = 0.f;
+      if ((n_part & 3) == 0 && n_part <= 16) {  // up to 4 independent 16-byte loads, summed in order
+        float4 q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (4 * i < n_part) q[i] = __ldg(reinterpret_cast<const float4*>(p) + i);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (4 * i < n_part) t = (((t + q[i].x) + q[i].y) + q[i].z) + q[i].w;
+      } else {
+        for (int i = 0; i < n_part; ++i) t += p[i];
+      }
+      rs = 1.0f / sqrtf(t / dim + eps);
+    }
+    in.begin_row(row, valid);
+  }
+  __device__ __forceinline__ void prefetch(int row, int col0, Pre& p) { in.prefetch(row, col0, p); }
+  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre& p,
+                                        uint4 (&o)[8], uint8_t*& dst) {
+    in.chunk(row, col0, v, p, o, dst);  // v already scaled by rs
+  }
+  __device__ __forceinline__ void end_row(int row, int n_blk) { in.end_row(row, n_blk); }
+};
+
 // ------------------------------------------------------------------ kernel
 //
 // One body, two modes:
@@ -652,9 +774,11 @@ constexpr int MN_BOX_BYTES = 64 * 64 * 2;
 
 template <int BN, bool PAIR, class Epi, int LAYOUT = 0>
 __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
+                                             const CUtensorMap* tmC, const CUtensorMap* tmD,
                                              int M, int N, int K, int b_z, int splits,
                                              const Epi& epi, int* err) {
-  using Cfg = GemmCfg<BN, PAIR>;
+  constexpr bool TIN = EpiTmaIn<Epi>::value;
+  using Cfg = GemmCfg<BN, PAIR, TIN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int TILE_M = Cfg::TILE_M;
   constexpr int NC = BN / 32;  // TMEM chunks per row
@@ -663,13 +787,16 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* in_slots = smem + STAGES * Cfg::STAGE_BYTES;  // TMA_IN boxes (1024-aligned)
+  uint8_t* bar_base = in_slots + Cfg::IN_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  uint8_t* epi_bufs = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
+  uint64_t* in_bar = reinterpret_cast<uint64_t*>(bar_base + 256);  // TMA_IN: 2 per epilogue warp
+  uint8_t* epi_bufs = bar_base + Cfg::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -694,9 +821,16 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       mbar_init(&tempty[a], (PAIR ? 2 : 1) * 4);
     }
     mbar_init(drain, 1);
+    if constexpr (TIN) {
+      for (int i = 0; i < 2 * GEMM_EPI_WARPS; ++i) mbar_init(&in_bar[i], 1);
+    }
     fence_mbar_init();
     tma_prefetch_desc(tmA);
     tma_prefetch_desc(tmB);
+    if constexpr (TIN) {
+      tma_prefetch_desc(tmC);
+      tma_prefetch_desc(tmD);
+    }
   }
   if (warp == 1) {
     if (PAIR) {
@@ -837,14 +971,35 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         PAIR ? mapa_shared(smem_u32(&tempty[group]), 0) : smem_u32(&tempty[group]);
     uint32_t ph = 0;
     int it = 0;
+    // TMA_IN: this warp's two input slots; loads are issued two chunks ahead (the first
+    // two of a tile before its accumulator is ready) and consumed in order.
+    uint64_t* my_in_bar = in_bar + (warp - 2) * 2;
+    uint8_t* my_in = in_slots + (warp - 2) * 2 * Cfg::IN_SLOT_BYTES;
+    uint32_t in_issued = 0, in_used = 0;
     for (int u = unit; u < num_tiles; u += n_units, ++it) {
       if ((it & 1) != group) continue;
       const int tile = u / splits;
       const int m_blk = tile / n_tiles;
       const int n_blk = tile % n_tiles;
-      if (!mbar_wait(&tfull[group], ph, err)) break;
-      ph ^= 1u;
-      tc_fence_after();
+      const int row0w = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32;
+      auto in_issue = [&](int c) {
+        if constexpr (TIN) {
+          const int col = n_blk * BN + c * 32;
+          if (c < NC && col < N) {
+            const int slot = (int)(in_issued & 1u);
+            if (lane == 0) {
+              bulk_wait_read<0>();  // the slot's last store (chunk c - 2) has read it
+              mbar_arrive_expect_tx(&my_in_bar[slot], Cfg::IN_SLOT_BYTES);
+              tma_load_2d(my_in + slot * Cfg::IN_SLOT_BYTES, tmC, &my_in_bar[slot], col, row0w);
+            }
+            ++in_issued;
+          }
+        }
+      };
+      in_issue(0);
+      in_issue(1);
+      // Per-row setup and the first chunk's global loads go out before the accumulator
+      // is ready, so their latency hides behind the wait.
       const int row = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32 + lane;
       const bool row_ok = row < M;
       Epi e = epi;
@@ -870,23 +1025,54 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         tmem_ld_wait_regs(r);
         uint4 outv[8];
         uint8_t* dst = nullptr;
-        if constexpr (EpiInBytes<Epi>::value > 0) {
-          warp_finish_rows<IN_NB>(wbuf, in_next, outv);
-          if (c + 1 < NC) issue_in(col + 32);
-        }
-        if (row_ok) {
-          float v[32];
+        if constexpr (TIN) {
+          const int slot = (int)(in_used & 1u);
+          const bool in_ok = mbar_wait(&my_in_bar[slot], (in_used >> 1) & 1u, err);
+          ++in_used;
+          uint8_t* xbox = my_in + slot * Cfg::IN_SLOT_BYTES;
+          uint8_t* hbox = wbuf + slot * 2048;  // fp16 staging box, 32 rows x 64 B
+          if (lane == 0) bulk_wait_read<1>();  // chunk c - 2's store of hbox has read it
+          __syncwarp();
+          if (row_ok && in_ok) {
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          e.chunk(row, col, v, pre, outv, dst);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            e.chunk_tma(row, col, v, xbox + lane * 128, lane & 7, hbox + lane * 64,
+                        (lane >> 1) & 3);
+          }
+          fence_proxy_async_smem();  // generic writes -> visible to the TMA stores
+          __syncwarp();
+          if (lane == 0 && in_ok) {
+            tma_store_2d(tmC, xbox, col, row0w);  // rows past M are not written
+            tma_store_2d(tmD, hbox, col, row0w);
+            bulk_commit_group();
+          }
+          in_issue(c + 2);
+        } else {
+          if constexpr (EpiInBytes<Epi>::value > 0) {
+            warp_finish_rows<IN_NB>(wbuf, in_next, outv);
+            if (c + 1 < NC) issue_in(col + 32);
+          }
+          if (row_ok) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = __uint_as_float(r[i]);
+              if constexpr (EpiRowScale<Epi>::value) v[i] *= e.rs;
+            }
+            e.chunk(row, col, v, pre, outv, dst);
+          }
+          if constexpr (Epi::OUT_BYTES > 0)
+            warp_store_rows<(Epi::OUT_BYTES > 0 ? Epi::OUT_BYTES : 16), EpiAtomic<Epi>::value>(
+                wbuf, outv, dst, row_ok);
         }
-        if constexpr (Epi::OUT_BYTES > 0)
-          warp_store_rows<(Epi::OUT_BYTES > 0 ? Epi::OUT_BYTES : 16), EpiAtomic<Epi>::value>(
-              wbuf, outv, dst, row_ok);
       };
       const int col_base = n_blk * BN;
       if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
       issue_in(col_base);
+      if (!mbar_wait(&tfull[group], ph, err)) break;
+      ph ^= 1u;
+      tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < NC; c += 2) {
         const int col_b = col_base + (c + 1) * 32;
@@ -903,6 +1089,13 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         else mbar_arrive(&tempty[group]);
       }
     }
+    // Error exit: input loads still in flight complete before the CTA exits (bounded);
+    // the epilogue's TMA stores finish before the CTA's shared memory goes away.
+    for (; in_used < in_issued; ++in_used)
+      mbar_wait(&my_in_bar[in_used & 1u], (in_used >> 1) & 1u, err);
+    if constexpr (TIN) {
+      if (lane == 0) bulk_wait_all();
+    }
   }
 
   tc_fence_before();
@@ -916,19 +1109,23 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   }
 }
 
+// tmC, tmD: the TMA_IN epilogue's in/out matrix and its second output (unused otherwise).
 template <int BN, class Epi, int LAYOUT = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    int M, int N, int K, int b_z, int splits, Epi epi, int* err) {
-  gemm_tn_body<BN, false, Epi, LAYOUT>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
+  gemm_tn_body<BN, false, Epi, LAYOUT>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi, err);
 }
 
 template <class Epi, int LAYOUT = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int b_z,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC,
+                        const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int b_z,
                         int splits, Epi epi, int* err) {
-  gemm_tn_body<256, true, Epi, LAYOUT>(&tmA, &tmB, M, N, K, b_z, splits, epi, err);
+  gemm_tn_body<256, true, Epi, LAYOUT>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi, err);
 }
 
 }  // namespace cb

@@ -76,7 +76,11 @@ def test_training_step_matches_oracle(bridge_lib, kv_heads, softcap, loss_scale)
         g = k.grads()
         l_fwd = k.forward_loss(tok, tgt, softcap)
     assert abs(loss - l_ref) / l_ref <= 1e-3, (loss, l_ref)
-    assert abs(loss - l_fwd) <= 1e-5 * l_fwd
+    # The inference forward fuses the residual add + RMSNorm into the projections (fp32
+    # x += alpha * acc, 1/rms applied after the next GEMM); the training forward keeps
+    # the separate pass because it saves the normalised rows for the weight gradients.
+    # Same math, different fp16 rounding points: the losses agree to ~1e-5.
+    assert abs(loss - l_fwd) <= 1e-4 * l_fwd, (loss, l_fwd)
     _check_grads(g, g_ref)
 
 
