@@ -43,7 +43,7 @@ GEMM_CLASSES = ("gemm_qkv_rope", "gemm_o", "gemm_w13_swiglu", "gemm_w2", "gemm_l
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch, averaged
 # over the 81 GEMM launches of one forward, from one ncu capture of this bench's own
 # workload (profiles/gemm_tc_600m-A_b64_dram.md), keyed by (config, sequences per GPU).
-GEMM_TRAFFIC_PER_LAUNCH = {("600m-A", 64): 400.07e6}
+GEMM_TRAFFIC_PER_LAUNCH = {("600m-A", 64): 520.96e6}
 GEMM_TRAFFIC_SOURCE = "profiles/gemm_tc_600m-A_b64_dram.md"
 
 

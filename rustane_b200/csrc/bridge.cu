@@ -1052,8 +1052,11 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   return cudaSuccess;
 }
 
+// Upper bound on the profiled launches of one forward: 7 per layer with the separate
+// residual + norm pass (5 when it is fused into the projections), + 2 all-reduces per
+// layer under tensor parallelism.
 int launches_per_forward(const cb_ctx* c) {
-  return (c->tp_world > 1 ? 9 : 7) * c->cfg.nlayers + 4;  // + 2 all-reduces per layer
+  return (c->tp_world > 1 ? 9 : 7) * c->cfg.nlayers + 4;
 }
 
 // ---------------------------------------------------------- standalone LM head + CE
