@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_s0 = tmem, t_o = tmem + 128;
+  pdl_enter();  // lets the next GEMM (launched with PDL) schedule its CTAs early
 
   if (warp == 0) {
     if (lane == 0) {

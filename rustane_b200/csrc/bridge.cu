@@ -335,6 +335,27 @@ void ensure_attrs(int device) { (void)device_info(device); }
 
 int num_sms_of(int device) { return device_info(device).sms; }
 
+// Kernel launch, optionally with programmatic dependent launch (PDL): the kernel's CTAs
+// may be scheduled while the previous kernel on the stream finishes, run their setup,
+// and wait in pdl_enter() before touching memory. Every kernel launched with pdl = true
+// calls pdl_enter() before its first global access. Captured into a CUDA graph the
+// attribute becomes a programmatic dependency edge.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // The epilogue's input map (TMA_IN epilogues); the others get a zeroed map they never use.
 const CUtensorMap& tc_or_null(const CUtensorMap* tc) {
   static const CUtensorMap zero{};
@@ -345,26 +366,26 @@ template <int BN, class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                            int bz, const Epi& epi, int* err, int units, int splits,
                            cudaStream_t st, const CUtensorMap* tc = nullptr,
-                           const CUtensorMap* td = nullptr) {
+                           const CUtensorMap* td = nullptr, bool pdl = false) {
   using Cfg = GemmCfg<BN, false, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
-  gemm_tn_kernel<BN, Epi, LAYOUT><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(
-      ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K, bz, splits, epi, err);
-  return cudaGetLastError();
+  return launch_k(gemm_tn_kernel<BN, Epi, LAYOUT>, dim3(grid), dim3(GEMM_THREADS),
+                  Cfg::SMEM_BYTES, st, pdl, ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K, bz,
+                  splits, epi, err);
 }
 
 template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
                              int K, int bz, const Epi& epi, int* err, int clusters, int splits,
                              cudaStream_t st, const CUtensorMap* tc = nullptr,
-                             const CUtensorMap* td = nullptr) {
+                             const CUtensorMap* td = nullptr, bool pdl = false) {
   using Cfg = GemmCfg<256, true, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
-  gemm_tn_pair_kernel<Epi, LAYOUT><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(
-      ta, tb_half, tc_or_null(tc), tc_or_null(td), M, N, K, bz, splits, epi, err);
-  return cudaGetLastError();
+  return launch_k(gemm_tn_pair_kernel<Epi, LAYOUT>, dim3(2 * pairs), dim3(GEMM_THREADS),
+                  Cfg::SMEM_BYTES, st, pdl, ta, tb_half, tc_or_null(tc), tc_or_null(td), M, N, K,
+                  bz, splits, epi, err);
 }
 
 // Tile mode for an M x N GEMM: the best of (last-wave fill) x (per-tile operand
@@ -404,15 +425,16 @@ template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb128,
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
                         int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1,
-                        const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr) {
+                        const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr,
+                        bool pdl = false) {
   if (mode == GM_PAIR)
     return launch_gemm_pair<Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters,
-                                         splits, st, tc, td);
+                                         splits, st, tc, td, pdl);
   if (mode == GM_SINGLE128)
     return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st,
-                                            tc, td);
+                                            tc, td, pdl);
   return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st,
-                                          tc, td);
+                                          tc, td, pdl);
 }
 
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
@@ -925,6 +947,9 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   // GEMM applies 1/rms per row, RowScaled) unless K is split or the model is tensor
   // parallel; otherwise the projection writes delta and add_rmsnorm does the rest.
   const bool fuse_norm = !tp && d % 128 == 0;
+  // GEMMs use programmatic dependent launch (setup overlaps the previous kernel's tail)
+  // outside tensor parallelism and eager profiling.
+  const bool pdl = !tp && !prof;
   bool fused_last = false;  // the last projection used the fused epilogue
   bool xn_scaled = false;   // xn holds fp16(x o gamma): consumers scale rows by 1/rms
   auto consume = [&](int mode, const CUtensorMap& tb128, const CUtensorMap& tb256, int N,
@@ -932,9 +957,11 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     using E = std::decay_t<decltype(inner)>;
     if (xn_scaled) {
       RowScaled<E> ep{inner, c->ss_part, d / 128, (float)d, RMS_EPS, 1.f};
-      return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di, st);
+      return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di, st, 1,
+                         nullptr, nullptr, pdl);
     }
-    return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di, st);
+    return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di, st, 1,
+                       nullptr, nullptr, pdl);
   };
 
   // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer. fp16
@@ -951,7 +978,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if (fused_last) {
       EpiResidualNorm ep{gamma_next, c->ss_part, d / 128, alpha, 0.f};
       r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, 1,
-                      &c->tm_x, &c->tm_xh);
+                      &c->tm_x, &c->tm_xh, pdl);
       if (r != cudaSuccess) return r;
       mark(cls, 2.0 * Td * d * K,
            Td * K * 2 + (double)d * K * 2 + Td * d * (4 + 4 + 2) + Td * (d / 128) * 4);

@@ -846,6 +846,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_enter();  // the setup above overlaps the previous kernel under PDL
 
   if (warp == 0) {
     if (lane == 0) {

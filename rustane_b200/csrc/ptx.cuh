@@ -89,6 +89,17 @@ __device__ __forceinline__ float exp2_mufu(float x) {
   return y;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the previous
+// kernel on the stream is still running: pdl_enter waits (griddepcontrol.wait) until that
+// kernel has completed and its memory is visible, then lets the next kernel start its own
+// launch. Everything before pdl_enter must not touch memory other kernels write or read.
+// Without the launch attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -16,6 +16,8 @@
 #include <math_constants.h>
 #include <stdint.h>
 
+#include "ptx.cuh"
+
 namespace cb {
 
 constexpr float RMS_EPS = 1e-5f;
@@ -56,6 +58,7 @@ __global__ void embed_rmsnorm_kernel(const uint32_t* __restrict__ tokens,
                                      const float* __restrict__ gamma, float* __restrict__ x,
                                      __half* __restrict__ xn, int T, int dim, int vocab,
                                      int* err, float* __restrict__ rinv_out = nullptr) {
+  pdl_enter();
   const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
