@@ -15,8 +15,7 @@
 //                                      overwrites S_j, V MN-major from its TMA tile)
 //   warps 2..5    : softmax, one thread per query row (TMEM lane): reads its 64 scores,
 //                   applies the causal mask on the diagonal tiles, updates the running
-//                   max / sum in base 2 (exponentials split between the MUFU and an FMA
-//                   polynomial), rescales its O row in TMEM only when the max grows past
+//                   max / sum in base 2 (exponentials on the MUFU), rescales its O row in TMEM only when the max grows past
 //                   the reference max by 2^8, writes P (fp16, packed in pairs) over its
 //                   S row in TMEM, and at the end divides O by the row sum and stores
 //                   the output row.
@@ -43,23 +42,6 @@ constexpr int FA_BAR_OFF = 98304;
 constexpr int FA_SMEM = FA_BAR_OFF + 256 + 1024;
 constexpr uint32_t FA_TMEM_COLS = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
 
-// 2^x for x <= 0 on the FMA pipe, to share the softmax exponentials with the MUFU:
-// x = n + f with n = floor(x), f in [0, 1); 2^f by a degree-4 polynomial (a weighted
-// least-squares fit to 2^f on [0, 1), max relative error 2.6e-6, below the fp16
-// rounding of P); 2^n added to the exponent bits. Returns 0 below -126 (masked keys).
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float n = floorf(xc);
-  const float f = xc - n;
-  float p = 0.013534540310502052f;
-  p = fmaf(p, f, 0.05201074853539467f);
-  p = fmaf(p, f, 0.24144317209720612f);
-  p = fmaf(p, f, 0.69300377368927f);
-  p = fmaf(p, f, 1.0000026226043701f);
-  const float r = __int_as_float(__float_as_int(p) + ((int)n << 23));
-  return x < -126.0f ? 0.0f : r;
-}
-
 // The O accumulator and row sum keep a stale reference max until the running max
 // exceeds it by this much (base-2 log): P values stay <= 2^8, and most tiles skip
 // the TMEM read-scale-write of O.
@@ -68,9 +50,9 @@ constexpr float FA_RESCALE_THRESHOLD = 8.0f;
 __global__ void __launch_bounds__(FA_THREADS, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, __half* __restrict__ out, int seq,
-                       int heads, int kv_heads, float scale_log2, float* __restrict__ lse,
-                       int* err) {
+                       const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmO, int seq, int heads,
+                       int kv_heads, float scale_log2, float* __restrict__ lse, int* err) {
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -115,6 +97,7 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, FA_TMEM_COLS);
@@ -249,9 +232,12 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       const float neg_m = -m_run;
       float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
+      // All exponentials on the MUFU (ex2.approx): measured faster than sending half of
+      // them to an FMA-pipe polynomial (3.45-3.50 against 3.73 ms of attention per
+      // 600m-A forward), the MUFU not being the limit here.
       for (int i = 0; i < 64; i += 2) {
         s[i] = exp2_mufu(fmaf(s[i], scale_log2, neg_m));
-        s[i + 1] = exp2_fma(fmaf(s[i + 1], scale_log2, neg_m));
+        s[i + 1] = exp2_mufu(fmaf(s[i + 1], scale_log2, neg_m));
         l8[(i >> 1) & 7] += s[i] + s[i + 1];
       }
       const float sum = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
@@ -285,19 +271,22 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(pv_done, (n_kv - 1) & 1, err)) {
+    const bool fin = ok && mbar_wait(pv_done, (n_kv - 1) & 1, err);
+    if (fin) {
       tc_fence_after();
       const float inv = 1.0f / l_run;
       // Log-sum-exp of the scaled scores in base 2 (lse2 = log2 sum_k 2^(s_k c)), kept
       // for the backward pass: P = 2^(s c - lse2).
       if (lse) lse[q_row0 + r] = m_run + log2f(l_run);
-      __half* dst = out + ((size_t)b * seq + q_idx) * ((size_t)heads * 128) + h * 128;
+      // O / l in fp16 into the Q tile's shared memory (free: every MMA has completed),
+      // in the 128-byte-swizzled layout of the output tensor map (two 64-column halves
+      // of [128 rows][128 B]), then one TMA store of the 128 x 128 tile.
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(t_o + lane_off + c * 32, o);
         tmem_ld_wait_regs(o);
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+        uint8_t* half_tile = smem + FA_Q_OFF + (c >> 1) * 16384 + r * 128;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           uint4 w;
@@ -305,9 +294,19 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
           w.y = pack_half2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
           w.z = pack_half2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
           w.w = pack_half2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
-          d4[k] = w;
+          const int chunk = (c & 1) * 4 + k;  // 16-byte chunk within the 128-byte row
+          *reinterpret_cast<uint4*>(half_tile + ((chunk ^ (r & 7)) << 4)) = w;
         }
       }
+    }
+    fence_proxy_async_smem();
+    named_barrier_sync(1, 128);  // the four softmax warps
+    if (threadIdx.x == 64 && fin) {
+      const int o_row = b * seq + qt * FA_BQ;
+      tma_store_2d(&tmO, smem + FA_Q_OFF, h * 128, o_row);
+      tma_store_2d(&tmO, smem + FA_Q_OFF + 16384, h * 128 + 64, o_row);
+      bulk_commit_group();
+      bulk_wait_read<0>();  // shared memory stays valid until the store has read it
     }
   }
 

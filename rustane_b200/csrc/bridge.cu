@@ -479,9 +479,11 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
                              int batch, int heads, int kv_heads, int seq, int* err,
                              cudaStream_t st, float* lse = nullptr) {
   const float scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
-  if (tq && seq % FA_BQ == 0) {
+  CUtensorMap to;  // the output [batch*seq, heads*128] in 128-query x 64-column boxes
+  if (tq && seq % FA_BQ == 0 &&
+      make_tmap_rows(&to, out, (uint64_t)heads * 128, (uint64_t)batch * seq, FA_BQ)) {
     dim3 grid(seq / FA_BQ, heads, batch);
-    attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, out, seq, heads,
+    attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, to, seq, heads,
                                                           kv_heads, scale_log2, lse, err);
   } else {
     dim3 grid(seq / ATT_BQ, heads, batch);
