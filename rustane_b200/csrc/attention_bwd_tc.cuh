@@ -19,6 +19,8 @@
 //   dQ warps (thread = dim): dQ^T from TMEM into a [64 queries][128 dims] fp32 tile in
 //   shared memory, added into dq32 by one TMA reduce-add.
 // The block's log-sum-exp and D values (64 floats each) arrive with Q and dO by bulk copy.
+// At the end the softmax warps write dK (scaled, RoPE undone) and dV into the K / V tiles'
+// shared memory and store them to dQKV with TMA.
 // 320 threads: warp 0 TMA producer (K, V once; Q and dO double-buffered), warp 1 TMEM
 // owner + MMA issuer, warps 2-5 softmax, warps 6-9 dQ. Every mbarrier wait is bounded.
 #pragma once
@@ -54,9 +56,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                        const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmDQ,
+                       const __grid_constant__ CUtensorMap tmDKV,
                        const float* __restrict__ lse2, const float* __restrict__ dsum,
                        const float2* __restrict__ rope, float* __restrict__ dq32,
-                       __half* __restrict__ dqkv, int seq, int heads, int kv_heads,
+                       int seq, int heads, int kv_heads,
                        float scale_log2, float scale, int* err) {
   extern __shared__ uint8_t at_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int kt = blockIdx.x;  // key block: early blocks see the most queries, launched first
   const int hk = blockIdx.y, b = blockIdx.z;
   const int group = heads / kv_heads;
-  const int q_dim = heads * 128, n_qkv = q_dim + 2 * kv_heads * 128;
+  const int q_dim = heads * 128;
   const int k0 = kt * AT_BK;
   const int qb0 = k0 / AT_BQ, n_qb = seq / AT_BQ - qb0;  // query blocks at or after the keys
   const int n_steps = group * n_qb;
@@ -103,6 +106,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmDQ);
+    tma_prefetch_desc(&tmDKV);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, AT_TMEM_COLS);
@@ -270,11 +274,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // ---------------- dK (scaled, RoPE undone) and dV rows of this key into dQKV
-    if (ok && mbar_wait(done, 0, err)) {
+    // ---------------- dK (scaled, RoPE undone) and dV of this CTA's keys into dQKV: each
+    // thread writes its key row into the K / V tiles' shared memory (free once every MMA
+    // is done), 128-byte swizzled like the tensor map tmDKV, then two TMA stores per tile.
+    const bool fin = ok && mbar_wait(done, 0, err);
+    if (fin) {
       tc_fence_after();
-      __half* rk = dqkv + ((size_t)b * seq + key) * n_qkv + q_dim + (size_t)hk * 128;
-      __half* rv = rk + (size_t)kv_heads * 128;
+      uint8_t* krow = smem + AT_K_OFF + r * 128;
+      uint8_t* vrow = smem + AT_V_OFF + r * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t kw[32], vw[32];
@@ -282,8 +289,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tmem_ld_32x32b_x32(t_dv + lane_off + c * 32, vw);
         tmem_ld_wait_regs(kw);
         tmem_ld_wait_regs(vw);
-        uint4* ko = reinterpret_cast<uint4*>(rk + c * 32);
-        uint4* vo = reinterpret_cast<uint4*>(rv + c * 32);
+        const int hoff = (c >> 1) * 16384;  // dims 0-63 | 64-127
 #pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) {
           uint32_t kp[4], vp[4];
@@ -295,10 +301,24 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             kp[i] = pack_half2(a0, a1);
             vp[i] = pack_half2(__uint_as_float(vw[col]), __uint_as_float(vw[col + 1]));
           }
-          ko[g4] = make_uint4(kp[0], kp[1], kp[2], kp[3]);
-          vo[g4] = make_uint4(vp[0], vp[1], vp[2], vp[3]);
+          const int chunk = (c & 1) * 4 + g4;  // 16-byte chunk within the 128-byte row
+          const int off = hoff + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(krow + off) = make_uint4(kp[0], kp[1], kp[2], kp[3]);
+          *reinterpret_cast<uint4*>(vrow + off) = make_uint4(vp[0], vp[1], vp[2], vp[3]);
         }
       }
+    }
+    fence_proxy_async_smem();
+    named_barrier_sync(2, 128);  // the four softmax warps
+    if (threadIdx.x == 2 * 32 && fin) {
+      const int row = b * seq + k0;
+      const int ck = q_dim + hk * 128, cv = q_dim + kv_heads * 128 + hk * 128;
+      tma_store_2d(&tmDKV, smem + AT_K_OFF, ck, row);
+      tma_store_2d(&tmDKV, smem + AT_K_OFF + 16384, ck + 64, row);
+      tma_store_2d(&tmDKV, smem + AT_V_OFF, cv, row);
+      tma_store_2d(&tmDKV, smem + AT_V_OFF + 16384, cv + 64, row);
+      bulk_commit_group();
+      bulk_wait_read<0>();  // shared memory stays valid until the stores have read it
     }
   } else {
     // ---------------- dQ warps: thread = head dim (TMEM lane), adds dQ^T into dq32

@@ -510,8 +510,9 @@ cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half*
   if (e != cudaSuccess) return e;
   if (!dsum_ready)
     attn_bwd_dsum_kernel<<<(T * heads + 15) / 16, 256, 0, st>>>(o, dout, dsum, T, seq, heads);
-  CUtensorMap tq, tk, tv, tdo, tdq;
+  CUtensorMap tq, tk, tv, tdo, tdq, tdkv;
   const bool tc = seq % AT_BK == 0 &&
+                  make_tmap_rows(&tdkv, dqkv, (uint64_t)n_qkv, (uint64_t)T, AT_BK) &&
                   make_tmap_qkv(&tq, q, (uint64_t)batch * heads * seq, AT_BQ) &&
                   make_tmap_qkv(&tk, k, (uint64_t)batch * kv_heads * seq, AT_BK) &&
                   make_tmap_qkv(&tv, v, (uint64_t)batch * kv_heads * seq, AT_BK) &&
@@ -519,8 +520,8 @@ cudaError_t launch_attention_bwd(const __half* q, const __half* k, const __half*
                   make_tmap_f32_rows(&tdq, dq32, (uint64_t)q_dim, (uint64_t)T, 128, AT_BQ);
   if (tc) {  // tcgen05 path
     dim3 grid(seq / AT_BK, kv_heads, batch);
-    attn_bwd_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, tdo, tdq, lse2, dsum, rope,
-                                                          dq32, dqkv, seq, heads, kv_heads,
+    attn_bwd_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, tdo, tdq, tdkv, lse2, dsum,
+                                                          rope, dq32, seq, heads, kv_heads,
                                                           scale_log2, scale, err);
   } else {
     dim3 grid(seq / AB_BK, kv_heads, batch);
