@@ -440,7 +440,11 @@ cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb12
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
 // accumulate: split-K = 2 doubles the work units when the tiles alone leave the last
 // wave mostly empty (few tokens per GPU). CB_GEMM_SPLIT=1|2 forces the split.
-void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* splits) {
+// max_split = 1 when the projection can carry the fused residual + norm epilogue (which
+// needs whole sums): the separate norm pass a split would bring back costs about half of
+// the down projection's GEMM time, more than a split's fill ever gains.
+void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* splits,
+                     int max_split = 2) {
   static const int forced_split = [] {
     const char* e = getenv("CB_GEMM_SPLIT");
     return e ? atoi(e) : 0;
@@ -452,7 +456,8 @@ void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* 
   const bool n256 = (N % 256) == 0;
   const long kb = (K + GEMM_BK - 1) / GEMM_BK;
   double best = -1.0;
-  for (int sp = 1; sp <= 2; ++sp) {
+  const int sp_max = forced_split ? forced_split : max_split;  // CB_GEMM_SPLIT overrides
+  for (int sp = 1; sp <= sp_max; ++sp) {
     if (forced_split && sp != forced_split) continue;
     // The zeroing and the fp32 atomics cost about as much as a 16-k-block half saves:
     // only long reductions (the down projection) split.
@@ -940,8 +945,9 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   const DeviceInfo& di = device_info(c->device);
   const int m_qkv = pick_mode(T, c->n_qkv, di);
   int m_o, s_o, m_2, s_2;
-  pick_projection(T, d, c->q_dim, di, &m_o, &s_o);
-  pick_projection(T, d, hid, di, &m_2, &s_2);
+  const int max_split = (!tp && d % 128 == 0) ? 1 : 2;  // see pick_projection
+  pick_projection(T, d, c->q_dim, di, &m_o, &s_o, max_split);
+  pick_projection(T, d, hid, di, &m_2, &s_2, max_split);
   const int m_13 = pick_mode(T, 2 * hid, di);
   const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
 
