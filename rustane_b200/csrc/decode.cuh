@@ -20,11 +20,21 @@
 
 namespace cb {
 
-// Sum of the split-K partials of element (row b, column c): part[s][b][n].
+// Sum of the split-K partials of element (row b, column c): part[s][b][n], added in split
+// order. All loads go out before the first add (predicated up to DEC_MAX_SPLITS): the
+// partials were just written and sit in L2, and one dependent load per split made these
+// kernels latency-bound.
+constexpr int DEC_MAX_SPLITS = 16;
 __device__ __forceinline__ float sum_parts(const float* __restrict__ part, int splits,
                                            size_t slice, size_t idx) {
+  float a[DEC_MAX_SPLITS];
+#pragma unroll
+  for (int s = 0; s < DEC_MAX_SPLITS; ++s)
+    a[s] = s < splits ? __ldg(part + (size_t)s * slice + idx) : 0.f;
   float acc = 0.f;
-  for (int s = 0; s < splits; ++s) acc += part[(size_t)s * slice + idx];
+#pragma unroll
+  for (int s = 0; s < DEC_MAX_SPLITS; ++s)
+    if (s < splits) acc += a[s];
   return acc;
 }
 
@@ -378,7 +388,7 @@ static cb_status alloc_decode(cb_ctx* c) {
 // unit per SM, every split non-empty.
 static int decode_splits(int N, int K, const DeviceInfo& di) {
   const int tiles = (N + 127) / 128, kb = (K + GEMM_BK - 1) / GEMM_BK;
-  int s = std::max(1, std::min(16, (di.sms + tiles / 2) / tiles));
+  int s = std::max(1, std::min(DEC_MAX_SPLITS, (di.sms + tiles / 2) / tiles));
   s = std::min(s, kb);
   const int per = (kb + s - 1) / s;
   return (kb + per - 1) / per;
