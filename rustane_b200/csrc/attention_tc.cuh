@@ -15,12 +15,14 @@
 //                                      overwrites S_j, V MN-major from its TMA tile)
 //   warps 2..5    : softmax, one thread per query row (TMEM lane): reads its 64 scores,
 //                   applies the causal mask on the diagonal tiles, updates the running
-//                   max / sum in base 2 (exponentials on the MUFU), rescales its O row in TMEM only when the max grows past
-//                   the reference max by 2^8, writes P (fp16, packed in pairs) over its
-//                   S row in TMEM, and at the end divides O by the row sum and stores
-//                   the output row.
+//                   max / sum in base 2 (exponentials on the MUFU), rescales its O row in
+//                   TMEM only when the max grows past the reference max by 2^8, writes P
+//                   (fp16, packed in pairs) over its S row in TMEM, and at the end divides
+//                   O by the row sum into the Q tile's shared memory, from where one TMA
+//                   store writes the 128 x 128 output tile.
 // Layout: q, k, v are [batch, heads, seq, 128] fp16 (rows of a [batch*heads*seq, 128]
-// matrix for the tensor maps); out is [batch*seq, heads*128] fp16. seq % 128 == 0.
+// matrix for the tensor maps); the output (tensor map tmO) is [batch*seq, heads*128]
+// fp16. seq % 128 == 0.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
