@@ -738,7 +738,7 @@ void free_ctx(cb_ctx* c) {
   for (auto ev : c->tp_ev)
     if (ev) cudaEventDestroy(ev);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
-  void* ptrs[] = {c->rope_pm, c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
+  void* ptrs[] = {c->ss_part, c->rope_pm, c->eval_pos, c->delta32, c->delta, c->embed, c->wqkv, c->wo, c->w13, c->w2, c->gamma,
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
