@@ -487,7 +487,7 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
   CUtensorMap to;  // the output [batch*seq, heads*128] in 128-query x 64-column boxes
   if (tq && seq % FA_BQ == 0 &&
       make_tmap_rows(&to, out, (uint64_t)heads * 128, (uint64_t)batch * seq, FA_BQ)) {
-    dim3 grid(seq / FA_BQ, heads, batch);
+    dim3 grid((seq / FA_BQ + 1) / 2, heads, batch);  // two query tiles per CTA
     attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, to, seq, heads,
                                                           kv_heads, scale_log2, lse, err);
   } else {
