@@ -498,7 +498,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
       EpiQkvRope ep{q, k, v, c->rope, S, H, Hk};
       const CUtensorMap ta = kmap(xn, d, T);
       TRY(launch_gemm(m_qkv, ta, c->tm_wqkv[0], c->tm_wqkv[1], T, nq, d, l, ep, c->dev_err, di,
-                      st));
+                      st, 1, nullptr, nullptr, true));
     }
     {
       CUtensorMap tq, tk, tv;
@@ -511,7 +511,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     {
       EpiScaledF16 ep{c->delta, d, alpha};
       const CUtensorMap ta = kmap(attn, qd, T);
-      TRY(launch_gemm(m_o, ta, c->tm_wo[0], c->tm_wo[1], T, d, qd, l, ep, c->dev_err, di, st));
+      TRY(launch_gemm(m_o, ta, c->tm_wo[0], c->tm_wo[1], T, d, qd, l, ep, c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     float* x2 = t->x2 + lo * d;
     __half* x2n = t->x2n + lo * d;
@@ -522,12 +522,12 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
       EpiSwigluSave ep{g, hid, t->h13 + lo * 2 * hid, 2 * hid};
       const CUtensorMap ta = kmap(x2n, d, T);
       TRY(launch_gemm(m_13, ta, c->tm_w13[0], c->tm_w13[1], T, 2 * hid, d, l, ep, c->dev_err,
-                      di, st));
+                      di, st, 1, nullptr, nullptr, true));
     }
     {
       EpiScaledF16 ep{c->delta, d, alpha};
       const CUtensorMap ta = kmap(g, hid, T);
-      TRY(launch_gemm(m_2, ta, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err, di, st));
+      TRY(launch_gemm(m_2, ta, c->tm_w2[0], c->tm_w2[1], T, d, hid, l, ep, c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     const bool last = l + 1 == L;
     TRY(launch_add_rmsnorm(x2, last ? t->x_last : t->x_in + (lo + Ts) * d, c->delta,
@@ -546,7 +546,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
     TRY(launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
-                    c->dev_err, di, st));
+                    c->dev_err, di, st, 1, nullptr, nullptr, true));
   }
   ce_finalize_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->ce_part, nparts, c->tgt_logit,
                                                             c->tok_loss, c->block_sums, T);
@@ -563,12 +563,12 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     if (splits == 1) {
       EpiScaledF32Add ep{grad, N, s_w};  // one add per element: order-independent
       return launch_gemm<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>(mode, ta, tb, tb, M, N, T, 0,
-                                                                 ep, c->dev_err, di, st);
+                                                                 ep, c->dev_err, di, st, 1, nullptr, nullptr, true);
     }
     if ((size_t)splits * M * N > t->gpart_elems) return cudaErrorInvalidValue;
     EpiPartialF32 ep{t->gpart, N, s_w, (size_t)M * N};
     cudaError_t r = launch_gemm<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>(
-        mode, ta, tb, tb, M, N, T, 0, ep, c->dev_err, di, st, splits);
+        mode, ta, tb, tb, M, N, T, 0, ep, c->dev_err, di, st, splits, nullptr, nullptr, true);
     if (r != cudaSuccess) return r;
     const size_t n = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((n / 4 + 255) / 256, (size_t)di.sms * 16);
@@ -582,6 +582,8 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     return cudaGetLastError();
   };
   // RMSNorm backward + residual, with the gain gradient (+= s_w sum_t dy x_hat) into dgam_out
+  // Every GEMM of the step is launched with programmatic dependent launch (its CTAs set
+  // up while the kernel before drains and wait in pdl_enter() before touching memory).
   auto norm_bwd = [&](const float* dy, const float* x, const float* gamma, const float* rinv,
                       const float* dres, float* dx, __half* dxh, float* dgam_out) {
     const int nb = (T + RB_ROWS - 1) / RB_ROWS, th = ROW_WARPS * 32;
@@ -621,13 +623,13 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
     TRY(launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
-                    c->dev_err, di, st));
+                    c->dev_err, di, st, 1, nullptr, nullptr, true));
   }
   {
     EpiScaledF32 ep{t->dtmp, d, 1.0f};
     const CUtensorMap ta = kmap(t->dl, V, T), tb = mnmap(c->embed, d, V);
     TRY(launch_gemm<EpiScaledF32, GEMM_B_MN>(pick_mode(T, d, di), ta, tb, tb, T, d, V, 0, ep,
-                                             c->dev_err, di, st));
+                                             c->dev_err, di, st, 1, nullptr, nullptr, true));
     TRY(grad_gemm(mnmap(t->dl, V, T), mnmap(c->xn, d, T), V, d, t->g_embed));
   }
   float* dX = t->dxa;
@@ -647,14 +649,14 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     {
       EpiSwigluBwd ep{t->dh13, t->h13 + lo * 2 * hid, 2 * hid};
       TRY(launch_gemm<EpiSwigluBwd, GEMM_B_MN>(pick_mode(T, hid, di), ta_dxh, tb_w2, tb_w2, T,
-                                               hid, d, l, ep, c->dev_err, di, st));
+                                               hid, d, l, ep, c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     TRY(grad_gemm(tg_dxh, mnmap(t->g + lo * hid, hid, T), d, hid,
                   t->g_w2 + (size_t)l * d * hid));
     {
       EpiScaledF32 ep{t->dtmp, d, 1.0f};
       TRY(launch_gemm<EpiScaledF32, GEMM_B_MN>(m_2, ta_dh13, tb_w13, tb_w13, T, d, 2 * hid, l,
-                                               ep, c->dev_err, di, st));
+                                               ep, c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     TRY(grad_gemm(tg_dh13, mnmap(t->x2n + lo * d, d, T), 2 * hid, d,
                   t->g_w13 + (size_t)l * 2 * hid * d));
@@ -665,7 +667,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     {
       EpiStoreF16Dsum ep{t->da, qd, t->attn + lo * qd, t->dsum, S, H, 0.f};
       TRY(launch_gemm<EpiStoreF16Dsum, GEMM_B_MN>(pick_mode(T, qd, di), ta_dxh, tb_wo, tb_wo, T,
-                                                  qd, d, l, ep, c->dev_err, di, st));
+                                                  qd, d, l, ep, c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     TRY(grad_gemm(tg_dxh, mnmap(t->attn + lo * qd, qd, T), d, qd, t->g_wo + (size_t)l * d * qd));
     TRY(launch_attention_bwd(t->q + lo * qd, t->k + lo * c->kv_dim, t->v + lo * c->kv_dim,
@@ -675,7 +677,7 @@ static cudaError_t enqueue_train_step(cb_ctx* c, int batch, float softcap, float
     {
       EpiScaledF32 ep{t->dtmp, d, 1.0f};
       TRY(launch_gemm<EpiScaledF32, GEMM_B_MN>(m_o, ta_dqkv, tb_wqkv, tb_wqkv, T, d, nq, l, ep,
-                                               c->dev_err, di, st));
+                                               c->dev_err, di, st, 1, nullptr, nullptr, true));
     }
     TRY(grad_gemm(tg_dqkv, mnmap(t->xn + lo * d, d, T), nq, d,
                   t->g_wqkv + (size_t)l * nq * d));
