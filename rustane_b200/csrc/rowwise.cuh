@@ -5,7 +5,6 @@
 //                          RMSNorm output Xn = X * rinv * gamma in fp16
 //                          (crates/engine/src/cpu/embedding.rs:8-17,
 //                           cpu/rmsnorm.rs:149-183, EPS = 1e-5 at :10)
-//   rmsnorm_kernel       : Xn = X * rinv * gamma (fp32 in, fp16 out)
 //   add_rmsnorm_kernel   : X += delta (the scaled O / down projection), then the norm
 //   ce_finalize_kernel   : per-token loss from the LM-head epilogue partials,
 //                          loss_t = log(sum_v e^{z_v - m}) + m - z_tgt
@@ -90,33 +89,6 @@ __global__ void embed_rmsnorm_kernel(const uint32_t* __restrict__ tokens,
     const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) f[i] = f[i] * rinv * gg[i];
-    *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
-  }
-}
-
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                               __half* __restrict__ xn, int T, int dim) {
-  const int row = blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= T) return;
-  const float* xr = x + (size_t)row * dim;
-  float ss = 0.f;
-  for (int c = lane * 8; c < dim; c += 256) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + c);
-    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
-    ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z +
-          b.w * b.w;
-  }
-  ss = warp_sum(ss);
-  const float rinv = 1.0f / sqrtf(ss / (float)dim + RMS_EPS);
-  __half* o = xn + (size_t)row * dim;
-  for (int c = lane * 8; c < dim; c += 256) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + c);
-    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
-    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
-    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
-    float f[8] = {a.x * rinv * g0.x, a.y * rinv * g0.y, a.z * rinv * g0.z, a.w * rinv * g0.w,
-                  b.x * rinv * g1.x, b.y * rinv * g1.y, b.z * rinv * g1.z, b.w * rinv * g1.w};
     *reinterpret_cast<uint4*>(o + c) = f8_to_h8(f);
   }
 }
@@ -295,19 +267,6 @@ __global__ void gather_norm_rows_kernel(const float* __restrict__ x,
   const float rinv = 1.0f / sqrtf(tot / (float)dim + RMS_EPS);
   for (int c = threadIdx.x; c < dim; c += blockDim.x)
     out[c] = __float2half_rn(xr[c] * rinv * gamma[c]);
-}
-
-__global__ void gather_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ rows,
-                                   int n, int n_pad, int dim, __half* __restrict__ dst) {
-  const int r = blockIdx.x;
-  if (r >= n_pad) return;
-  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)r * dim);
-  if (r < n) {
-    const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)rows[r] * dim);
-    for (int c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = s[c];
-  } else {
-    for (int c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = make_uint4(0, 0, 0, 0);
-  }
 }
 
 }  // namespace cb
