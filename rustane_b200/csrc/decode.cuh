@@ -212,6 +212,7 @@ __global__ void decode_attn_combine_kernel(const DecAttnPart* __restrict__ acc, 
 // x[b] += alpha * (sum of the partials of row b); xn[b] = RMSNorm(x[b]) * gamma. One
 // block per row (the partial sums are many short independent loads: spread them).
 constexpr int DEC_NORM_THREADS = 512;
+constexpr int DEC_NORM_PER_THREAD = 16;  // rows up to 8192 wide
 
 __global__ void __launch_bounds__(DEC_NORM_THREADS)
     decode_residual_norm_kernel(const float* __restrict__ part, int splits, int B, int dim,
@@ -222,11 +223,22 @@ __global__ void __launch_bounds__(DEC_NORM_THREADS)
   const int b = blockIdx.x;
   const size_t slice = (size_t)B * dim;
   float* xr = x + (size_t)b * dim;
+  // The row stays in registers (dim <= DEC_NORM_THREADS * DEC_NORM_PER_THREAD), and gamma
+  // is loaded with the residual, so the kernel makes one round trip to memory before the
+  // reduction instead of three.
+  float v[DEC_NORM_PER_THREAD], gm[DEC_NORM_PER_THREAD];
   float ss = 0.f;
-  for (int c = threadIdx.x; c < dim; c += DEC_NORM_THREADS) {
-    const float v = xr[c] + alpha * sum_parts(part, splits, slice, (size_t)b * dim + c);
-    xr[c] = v;
-    ss += v * v;
+#pragma unroll
+  for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
+    const int c = threadIdx.x + i * DEC_NORM_THREADS;
+    v[i] = 0.f;
+    gm[i] = 0.f;
+    if (c < dim) {
+      gm[i] = __ldg(gamma + c);
+      v[i] = xr[c] + alpha * sum_parts(part, splits, slice, (size_t)b * dim + c);
+      xr[c] = v[i];
+      ss += v[i] * v[i];
+    }
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -235,8 +247,11 @@ __global__ void __launch_bounds__(DEC_NORM_THREADS)
 #pragma unroll
   for (int w = 0; w < DEC_NORM_THREADS / 32; ++w) tot += red[w];
   const float rinv = 1.0f / sqrtf(tot / (float)dim + RMS_EPS);
-  for (int c = threadIdx.x; c < dim; c += DEC_NORM_THREADS)
-    xn[(size_t)b * dim + c] = __float2half_rn(xr[c] * rinv * gamma[c]);
+#pragma unroll
+  for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
+    const int c = threadIdx.x + i * DEC_NORM_THREADS;
+    if (c < dim) xn[(size_t)b * dim + c] = __float2half_rn(v[i] * rinv * gm[i]);
+  }
 }
 
 // g[b][j] = silu(h1) * h3 from the interleaved W1/W3 partial sums.
@@ -343,6 +358,9 @@ void free_decode_state(DecodeState* s) {
 static cb_status alloc_decode(cb_ctx* c) {
   if (c->decode) return CB_OK;
   const cb_model_config& cfg = c->cfg;
+  if (cfg.dim > DEC_NORM_THREADS * DEC_NORM_PER_THREAD)
+    return fail(c, CB_ERR_UNSUPPORTED, "decode supports dim <= " +
+                                           std::to_string(DEC_NORM_THREADS * DEC_NORM_PER_THREAD));
   const size_t B = c->max_batch, S = cfg.seq, L = cfg.nlayers, d = cfg.dim, V = cfg.vocab;
   const size_t h = c->hidden_l, qd = c->q_dim, nq = c->n_qkv;
   DecodeState* s = new DecodeState;
