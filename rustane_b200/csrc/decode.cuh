@@ -24,22 +24,26 @@ namespace cb {
 // order. All loads go out before the first add (predicated up to DEC_MAX_SPLITS): the
 // partials were just written and sit in L2, and one dependent load per split made these
 // kernels latency-bound.
+// MAXS (>= splits) bounds the predicated loads: the element-wise kernels are instantiated
+// for up to 4 splits (QKV, W1/W3, LM head) and up to DEC_MAX_SPLITS (O, down).
 constexpr int DEC_MAX_SPLITS = 16;
+template <int MAXS = DEC_MAX_SPLITS>
 __device__ __forceinline__ float sum_parts(const float* __restrict__ part, int splits,
                                            size_t slice, size_t idx) {
-  float a[DEC_MAX_SPLITS];
+  float a[MAXS];
 #pragma unroll
-  for (int s = 0; s < DEC_MAX_SPLITS; ++s)
+  for (int s = 0; s < MAXS; ++s)
     a[s] = s < splits ? __ldg(part + (size_t)s * slice + idx) : 0.f;
   float acc = 0.f;
 #pragma unroll
-  for (int s = 0; s < DEC_MAX_SPLITS; ++s)
+  for (int s = 0; s < MAXS; ++s)
     if (s < splits) acc += a[s];
   return acc;
 }
 
 // QKV of the new token: RoPE at `pos` on Q and K (sdpa_fwd.rs:53-60), Q to qbuf [B][qd],
 // K and V into cache slot `pos` ([B][kv_heads][seq][128] of this layer).
+template <int MAXS>
 __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, int B, int n_qkv,
                                   int heads, int kv_heads, const int* __restrict__ pos_ptr,
                                   const float2* __restrict__ rope, int seq,
@@ -52,8 +56,8 @@ __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, in
   const int pairs = n_qkv / 2;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * pairs; i += gridDim.x * blockDim.x) {
     const int b = i / pairs, col = 2 * (i % pairs);
-    float a0 = sum_parts(part, splits, slice, (size_t)b * n_qkv + col);
-    float a1 = sum_parts(part, splits, slice, (size_t)b * n_qkv + col + 1);
+    float a0 = sum_parts<MAXS>(part, splits, slice, (size_t)b * n_qkv + col);
+    float a1 = sum_parts<MAXS>(part, splits, slice, (size_t)b * n_qkv + col + 1);
     if (col < qd + kvd) {  // rotate Q and K
       const float2 cs = rope[(size_t)((col & 127) >> 1) * seq + pos];
       const float r0 = a0 * cs.x - a1 * cs.y, r1 = a1 * cs.x + a0 * cs.y;
@@ -255,20 +259,22 @@ __global__ void __launch_bounds__(DEC_NORM_THREADS)
 }
 
 // g[b][j] = silu(h1) * h3 from the interleaved W1/W3 partial sums.
+template <int MAXS>
 __global__ void decode_swiglu_kernel(const float* __restrict__ part, int splits, int B, int hid,
                                      __half* __restrict__ g) {
   pdl_enter();
   const size_t slice = (size_t)B * 2 * hid;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * hid; i += gridDim.x * blockDim.x) {
     const int b = i / hid, j = i % hid;
-    const float h1 = sum_parts(part, splits, slice, (size_t)b * 2 * hid + 2 * j);
-    const float h3 = sum_parts(part, splits, slice, (size_t)b * 2 * hid + 2 * j + 1);
+    const float h1 = sum_parts<MAXS>(part, splits, slice, (size_t)b * 2 * hid + 2 * j);
+    const float h3 = sum_parts<MAXS>(part, splits, slice, (size_t)b * 2 * hid + 2 * j + 1);
     g[i] = __float2half_rn(__fdividef(h1, 1.0f + __expf(-h1)) * h3);
   }
 }
 
 // Logits of row b (softcapped when softcap > 0, full_model.rs:456-461) and the greedy
 // next token (largest logit, lowest id on ties). One block per row.
+template <int MAXS>
 __global__ void decode_logits_kernel(const float* __restrict__ part, int splits, int B, int V,
                                      float softcap, float* __restrict__ logits,
                                      uint32_t* __restrict__ next) {
@@ -280,7 +286,7 @@ __global__ void decode_logits_kernel(const float* __restrict__ part, int splits,
   float best = -CUDART_INF_F;
   int bi = 0x7fffffff;
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    float z = sum_parts(part, splits, slice, (size_t)b * V + v);
+    float z = sum_parts<MAXS>(part, splits, slice, (size_t)b * V + v);
     if (softcap > 0.f) z = softcap * tanhf(z / softcap);
     logits[(size_t)b * V + v] = z;
     if (z > best) {  // v increases along the loop: ties keep the lower id
@@ -453,7 +459,8 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
     if ((e = gemm(s->tm_xn, c->tm_wqkv[0], nq, d, l, 1.0f, &sp)) != cudaSuccess) return e;
     const float* part = s->part;
     const int* dpos = s->d_pos;
-    if ((e = launch_k(decode_qkv_kernel, dim3((B * nq / 2 + 255) / 256), dim3(256), 0, st, false,
+    if ((e = launch_k(sp <= 4 ? decode_qkv_kernel<4> : decode_qkv_kernel<DEC_MAX_SPLITS>,
+                      dim3((B * nq / 2 + 255) / 256), dim3(256), 0, st, false,
                       part, sp, B, nq, H, Hk, dpos, (const float2*)c->rope, S, s->q, kc, vc)) !=
         cudaSuccess)
       return e;
@@ -471,7 +478,8 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
                       s->xn)) != cudaSuccess)
       return e;
     if ((e = gemm(s->tm_xn, c->tm_w13[0], 2 * hid, d, l, 1.0f, &sp)) != cudaSuccess) return e;
-    if ((e = launch_k(decode_swiglu_kernel, dim3((B * hid + 255) / 256), dim3(256), 0, st, false,
+    if ((e = launch_k(sp <= 4 ? decode_swiglu_kernel<4> : decode_swiglu_kernel<DEC_MAX_SPLITS>,
+                      dim3((B * hid + 255) / 256), dim3(256), 0, st, false,
                       part, sp, B, hid, s->g)) != cudaSuccess)
       return e;
     if ((e = gemm(s->tm_g, c->tm_w2[0], d, hid, l, alpha, &sp)) != cudaSuccess) return e;
@@ -481,7 +489,8 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
       return e;
   }
   if ((e = gemm(s->tm_xn, c->tm_embed[0], V, d, 0, 1.0f, &sp)) != cudaSuccess) return e;
-  if ((e = launch_k(decode_logits_kernel, dim3(B), dim3(256), 0, st, false, (const float*)s->part,
+  if ((e = launch_k(sp <= 4 ? decode_logits_kernel<4> : decode_logits_kernel<DEC_MAX_SPLITS>,
+                    dim3(B), dim3(1024), 0, st, false, (const float*)s->part,
                     sp, B, V, softcap, s->logits, s->next)) != cudaSuccess)
     return e;
   return launch_k(decode_advance_kernel, dim3(1), dim3(1), 0, st, false, s->d_pos);
