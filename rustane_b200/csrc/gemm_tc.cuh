@@ -119,6 +119,21 @@ __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   return w;
 }
 
+// softcap * tanh(z / softcap) over a 32-value chunk (der: 1 - tanh^2, nullable), out of
+// line: tanhf inlined 32 times into the unrolled epilogues made the LM-head GEMM's code
+// large enough to stall its warps on instruction fetch (ncu: "no instruction" stalls 5.8
+// per issue against 0.2 in the W1/W3 GEMM, tensor pipe 45 % against 75 % active), for a
+// path that is off by default. The callers copy through a local array only when softcap
+// > 0, so the default path keeps its values in registers.
+__device__ __noinline__ void softcap_chunk(float* z, float softcap, float* der) {
+  const float inv = 1.0f / softcap;
+  for (int i = 0; i < 32; ++i) {
+    const float t = tanhf(z[i] * inv);
+    z[i] = softcap * t;
+    if (der) der[i] = 1.0f - t * t;
+  }
+}
+
 // Warp-cooperative transposed store of 32 row segments of NB bytes (32, 64 or 128):
 // lane L owns row L's segment (out[0 .. NB/16)) and its address; `wbuf` is this warp's
 // 32*NB-byte shared buffer. Pieces are XOR-swizzled so both phases are conflict-free.
@@ -273,18 +288,21 @@ struct EpiStoreF32 {
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
   __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
                                         uint4 (&o)[8], uint8_t*& dst) {
+    float z[32];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      if (softcap > 0.f) {
-        const float inv = 1.0f / softcap;
-        w.x = softcap * tanhf(w.x * inv);
-        w.y = softcap * tanhf(w.y * inv);
-        w.z = softcap * tanhf(w.z * inv);
-        w.w = softcap * tanhf(w.w * inv);
-      }
-      o[j] = *reinterpret_cast<const uint4*>(&w);
+    for (int i = 0; i < 32; ++i) z[i] = v[i];
+    if (softcap > 0.f) {
+      float t[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] = z[i];
+      softcap_chunk(t, softcap, nullptr);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) z[i] = t[i];
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      o[j] = make_uint4(__float_as_uint(z[4 * j]), __float_as_uint(z[4 * j + 1]),
+                        __float_as_uint(z[4 * j + 2]), __float_as_uint(z[4 * j + 3]));
     dst = reinterpret_cast<uint8_t*>(out + (size_t)row * ldo + col0);
   }
   __device__ __forceinline__ void end_row(int, int) {}
@@ -549,18 +567,29 @@ struct EpiCeBwd {
   __device__ __forceinline__ void prefetch(int, int, Pre&) {}
   __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
                                         uint4 (&o)[8], uint8_t*& dst) {
+    float z[32], der[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      z[i] = v[i];
+      der[i] = 1.0f;
+    }
+    if (softcap > 0.f) {
+      float t[32], dt[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] = z[i];
+      softcap_chunk(t, softcap, dt);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        z[i] = t[i];
+        der[i] = dt[i];
+      }
+    }
     float r[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      float z = v[i], der = 1.0f;
-      if (softcap > 0.f) {
-        const float t = tanhf(z / softcap);
-        z = softcap * t;
-        der = 1.0f - t * t;
-      }
-      float g = __expf(z - lse);
+      float g = __expf(z[i] - lse);
       if (col0 + i == tgt) g -= 1.0f;
-      r[i] = g * der;
+      r[i] = g * der[i];
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = pack8_f16(r + 8 * j);
@@ -617,14 +646,19 @@ struct EpiCrossEntropy {
   __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
                                         uint4 (&)[8], uint8_t*&) {
     float z[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) z[i] = v[i];
+    if (softcap > 0.f) {
+      float t[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] = z[i];
+      softcap_chunk(t, softcap, nullptr);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) z[i] = t[i];
+    }
     float cm = -CUDART_INF_F;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float t = v[i];
-      if (softcap > 0.f) t = softcap * tanhf(t / softcap);
-      z[i] = t;
-      cm = fmaxf(cm, t);
-    }
+    for (int i = 0; i < 32; ++i) cm = fmaxf(cm, z[i]);
     const unsigned rel = (unsigned)(tgt - col0);
     if (rel < 32u) {
       float zt = z[0];
