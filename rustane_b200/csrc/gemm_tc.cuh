@@ -692,7 +692,9 @@ struct EpiCrossEntropy {
 // and writes fp16(x * gamma) into a 32 x 32 staging box, and the kernel stores both
 // boxes with TMA (tmC, tmD).
 struct EpiResidualNorm {
-  using Pre = NoPre;
+  struct Pre {
+    float4 g[8];  // gamma of the chunk's 32 columns, loaded one chunk ahead
+  };
   static constexpr bool TMA_IN = true;
   static constexpr int OUT_BYTES = 0;
   const float* gamma;
@@ -701,14 +703,17 @@ struct EpiResidualNorm {
   float alpha;
   float ss;
   __device__ __forceinline__ void begin_row(int, bool) { ss = 0.f; }
-  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
+  __device__ __forceinline__ void prefetch(int, int col0, Pre& p) {
+    const float4* g4 = reinterpret_cast<const float4*>(gamma + col0);  // same for all lanes
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p.g[j] = __ldg(g4 + j);
+  }
   // xrow: this row's 128 bytes of x in the 128-byte-swizzled box (16-byte piece k at
   // xrow + ((k ^ sw128) << 4)); hrow: its 64 bytes in the 64-byte-swizzled fp16 box
   // (piece k at hrow + ((k ^ sw64) << 4)).
   __device__ __forceinline__ void chunk_tma(int row, int col0, const float (&v)[32],
-                                            uint8_t* xrow, int sw128, uint8_t* hrow,
-                                            int sw64) {
-    const float4* g4 = reinterpret_cast<const float4*>(gamma + col0);  // same for all lanes
+                                            const Pre& p, uint8_t* xrow, int sw128,
+                                            uint8_t* hrow, int sw64) {
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
     float4 a[8];  // loads of a half first: the in-place stores would otherwise order them
@@ -717,7 +722,7 @@ struct EpiResidualNorm {
       a[j] = *reinterpret_cast<const float4*>(xrow + ((j ^ sw128) << 4));
 #pragma unroll
     for (int j = 4 * hh; j < 4 * hh + 4; ++j) {
-      const float4 g = __ldg(g4 + j);
+      const float4 g = p.g[j];
       float4 n;
       n.x = fmaf(alpha, v[4 * j], a[j].x);
       n.y = fmaf(alpha, v[4 * j + 1], a[j].y);
@@ -1072,7 +1077,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            e.chunk_tma(row, col, v, xbox + lane * 128, lane & 7, hbox + lane * 64,
+            e.chunk_tma(row, col, v, pre, xbox + lane * 128, lane & 7, hbox + lane * 64,
                         (lane >> 1) & 3);
           }
           fence_proxy_async_smem();  // generic writes -> visible to the TMA stores
