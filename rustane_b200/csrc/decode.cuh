@@ -46,7 +46,7 @@ __device__ __forceinline__ float sum_parts(const float* __restrict__ part, int s
 template <int MAXS>
 __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, int B, int n_qkv,
                                   int heads, int kv_heads, const int* __restrict__ pos_ptr,
-                                  const float2* __restrict__ rope, int seq,
+                                  const float2* __restrict__ cs_pos, int seq,
                                   __half* __restrict__ qbuf, __half* __restrict__ kc,
                                   __half* __restrict__ vc) {
   pdl_enter();
@@ -59,7 +59,7 @@ __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, in
     float a0 = sum_parts<MAXS>(part, splits, slice, (size_t)b * n_qkv + col);
     float a1 = sum_parts<MAXS>(part, splits, slice, (size_t)b * n_qkv + col + 1);
     if (col < qd + kvd) {  // rotate Q and K
-      const float2 cs = rope[(size_t)((col & 127) >> 1) * seq + pos];
+      const float2 cs = cs_pos[(col & 127) >> 1];  // no dependency on pos: one round trip
       const float r0 = a0 * cs.x - a1 * cs.y, r1 = a1 * cs.x + a0 * cs.y;
       a0 = r0;
       a1 = r1;
@@ -319,9 +319,19 @@ __global__ void decode_logits_kernel(const float* __restrict__ part, int splits,
   }
 }
 
-__global__ void decode_advance_kernel(int* pos) {
+// Position bookkeeping of the decode graph, one block of 64 threads: with advance the
+// position moves to pos + 1 (end of a step), otherwise it stays; either way cs_pos
+// receives the (cos, sin) of every frequency pair at the new position (pair-major table
+// [64][seq]), so the next step's QKV kernel loads its rotation without first reading
+// the position.
+__global__ void decode_set_pos_kernel(int* pos_ptr, int advance, const float2* __restrict__ rope,
+                                      int seq, float2* __restrict__ cs_pos) {
   pdl_enter();
-  *pos += 1;
+  const int pos = *pos_ptr + advance;
+  __syncthreads();  // every thread has read the old position
+  if (threadIdx.x == 0) *pos_ptr = pos;
+  const int p = pos < seq ? pos : seq - 1;  // a full sequence takes no further step
+  if (threadIdx.x < 64) cs_pos[threadIdx.x] = rope[(size_t)threadIdx.x * seq + p];
 }
 
 }  // namespace cb
@@ -346,6 +356,7 @@ struct DecodeState {
   uint32_t* next = nullptr;   // [max_batch]
   uint32_t* tok = nullptr;    // [max_batch]
   int* d_pos = nullptr;
+  float2* d_cs = nullptr;     // [64] (cos, sin) of each RoPE pair at d_pos
   int pos = 0;                // host copy: position of the next token
   int batch = 0;              // sequences of the last prefill
   float softcap = 0.f;
@@ -396,6 +407,7 @@ static cb_status alloc_decode(cb_ctx* c) {
   get(&s->next, B);
   get(&s->tok, B);
   get(&s->d_pos, 1);
+  get(&s->d_cs, 64);
   if (ok) {
     ok = make_tmap(&s->tm_xn, s->xn, d, B, 1, 128) && make_tmap(&s->tm_o, s->o, qd, B, 1, 128) &&
          make_tmap(&s->tm_g, s->g, h, B, 1, 128);
@@ -461,7 +473,7 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
     const int* dpos = s->d_pos;
     if ((e = launch_k(sp <= 4 ? decode_qkv_kernel<4> : decode_qkv_kernel<DEC_MAX_SPLITS>,
                       dim3((B * nq / 2 + 255) / 256), dim3(256), 0, st, false,
-                      part, sp, B, nq, H, Hk, dpos, (const float2*)c->rope, S, s->q, kc, vc)) !=
+                      part, sp, B, nq, H, Hk, dpos, (const float2*)s->d_cs, S, s->q, kc, vc)) !=
         cudaSuccess)
       return e;
     if ((e = launch_k(decode_attn_kernel, dim3(H, B, kv_splits), dim3(128), 0, st, false,
@@ -493,7 +505,8 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
                     dim3(B), dim3(1024), 0, st, false, (const float*)s->part,
                     sp, B, V, softcap, s->logits, s->next)) != cudaSuccess)
     return e;
-  return launch_k(decode_advance_kernel, dim3(1), dim3(1), 0, st, false, s->d_pos);
+  return launch_k(decode_set_pos_kernel, dim3(1), dim3(64), 0, st, false, s->d_pos, 1,
+                  (const float2*)c->rope, S, s->d_cs);
 }
 
 extern "C" {
@@ -528,6 +541,8 @@ cb_status cb_prefill(cb_ctx* ctx, const uint32_t* tokens, int32_t batch, int32_t
   s->batch = batch;
   s->softcap = softcap;
   CB_CUDA(cudaMemcpyAsync(s->d_pos, &s->pos, sizeof(int), cudaMemcpyHostToDevice, st));
+  decode_set_pos_kernel<<<1, 64, 0, st>>>(s->d_pos, 0, ctx->rope, S, s->d_cs);
+  CB_CUDA(cudaGetLastError());
   rc = read_device_error(ctx);
   if (rc != CB_OK) return rc;
   ctx->last_batch = batch;
