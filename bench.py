@@ -155,7 +155,66 @@ def cpu_oracle_sample(cfg, seed, tok, tgt, budget_s):
         elapsed += time.perf_counter() - t0
         losses.append(loss)
         n_done += 1
-    return dict(seqs=n_done, seconds=elapsed, threads=threads, losses=losses)
+    torch_s = torch_cpu_seconds(model, tok[:n_done * cfg.seq], tgt[:n_done * cfg.seq])
+    return dict(seqs=n_done, seconds=elapsed, threads=threads, losses=losses,
+                torch_seconds=torch_s)
+
+
+def torch_cpu_seconds(model, tok, tgt):
+    """Seconds for torch's own CPU kernels (float32, fused causal attention; the
+    optional second CPU figure) to run the same sequences one call each, as the
+    reference's forward takes one sequence per call, after one untimed call."""
+    import torch
+    from oracle import torch_ref
+    torch.set_num_threads(host_threads())
+    seq = model.cfg.seq
+    with torch.inference_mode():
+        torch_ref.forward(model, tok[:seq], tgt[:seq], dtype=torch.float32,
+                          fused_attention=True)
+        t0 = time.perf_counter()
+        for i in range(tok.size // seq):
+            s = slice(i * seq, (i + 1) * seq)
+            torch_ref.forward(model, tok[s], tgt[s], dtype=torch.float32, fused_attention=True)
+        return time.perf_counter() - t0
+
+
+def cpu_oracle_extrapolated(cfg, seed, tok, tgt):
+    """For models too deep to push a whole sequence through the CPU oracle inside the
+    bench's time box: time one sequence through 1-layer and 2-layer variants of the
+    same width (weights from the same generator), the faster of two passes each after
+    an untimed one, and extrapolate linearly in depth, t(L) = t(1) + (L - 1) * (t(2) - t(1)). The
+    embedding, final norm, head and CE are in t(1) once; every layer costs the same."""
+    from oracle import oracle
+    oracle.set_threads(host_threads())
+    s = slice(0, cfg.seq)
+    models = {nl: oracle.OracleModel(cfg.replace(nlayers=nl), seed=seed,
+                                     scheme=oracle.SCHEME_NORMAL, sigma=0.02) for nl in (1, 2)}
+    for m in models.values():
+        m.forward(tok[s], tgt[s])
+    t = {nl: float("inf") for nl in models}
+    for _ in range(2):  # the faster of two passes: the difference of two times is noisy
+        for nl, m in models.items():
+            t0 = time.perf_counter()
+            m.forward(tok[s], tgt[s])
+            t[nl] = min(t[nl], time.perf_counter() - t0)
+    tt = {nl: min(torch_cpu_seconds(m, tok[s], tgt[s]) for _ in range(2))
+          for nl, m in models.items()}
+    del models
+
+    def depth(t):
+        return t[1] + (cfg.nlayers - 1) * max(t[2] - t[1], 0.0)
+
+    return dict(seqs=1, seconds=depth(t), threads=oracle.max_threads(), t1=t[1], t2=t[2],
+                torch_seconds=depth(tt))
+
+
+def torch_cpu_figure(cfg, r, extrapolated):
+    import torch
+    return {"value": r["seqs"] * cfg.seq / r["torch_seconds"], "unit": "tokens/s",
+            "threads": torch.get_num_threads(),
+            "sample": ("same sequences, torch float32 on the host cores (fused causal "
+                       "attention), one sequence per call"
+                       + (", extrapolated in depth like the oracle" if extrapolated else ""))}
 
 
 def cpu_model_name():
@@ -617,7 +676,16 @@ def main():
 
     # ---- 4. CPU baseline on the host cores (rank 0 at N = 1)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.dim <= 2048:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.dim > 2048:
+        r = cpu_oracle_extrapolated(cfg, args.seed, tok_np, tgt_np)
+        cpu = {"value": cfg.seq / r["seconds"], "unit": "tokens/s", "cores": r["threads"],
+               "kind": "port",
+               "sample": (f"extrapolated: one {cfg.seq}-token sequence through 1- and 2-layer "
+                          f"variants of {args.config} ({r['t1']:.2f} s, {r['t2']:.2f} s), "
+                          f"linear in depth to {cfg.nlayers} layers; fp32 CPU oracle, "
+                          f"{r['threads']} threads, {cpu_model_name()}"),
+               "torch_cpu": torch_cpu_figure(cfg, r, extrapolated=True)}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_oracle_sample(cfg, args.seed, tok_np, tgt_np, args.cpu_budget_s)
         cpu_val = r["seqs"] * cfg.seq / r["seconds"]
         gpu_seq_losses = kern.forward_loss(tok_np[:r["seqs"] * cfg.seq],
@@ -628,7 +696,8 @@ def main():
                           f"{cpu_model_name()}"),
                "parity": {"loss_cpu": float(np.mean(r["losses"])), "loss_gpu": gpu_seq_losses,
                           "rel": abs(gpu_seq_losses - float(np.mean(r["losses"])))
-                          / float(np.mean(r["losses"]))}}
+                          / float(np.mean(r["losses"]))},
+               "torch_cpu": torch_cpu_figure(cfg, r, extrapolated=False)}
 
     if rank == 0:
         line = {

@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import torch_ref
 from oracle.oracle import (OracleModel, SCHEME_NORMAL, SCHEME_REFERENCE, lib, reference_tokens)
 from rustane_b200.model import custom_config
 
@@ -94,55 +95,21 @@ def test_normal_init_statistics(oracle_lib):
 
 def _torch_forward64(m: OracleModel, tokens, targets, softcap=0.0):
     """Independent float64 restatement (torch) of the same forward."""
-    cfg = m.cfg
-    S, d = cfg.seq, cfg.dim
-    f = lambda a: torch.from_numpy(np.asarray(a, np.float64))
-    E = f(m.embed)
-    tok = torch.from_numpy(np.asarray(tokens, np.int64)).view(-1, S)
-    x = E[tok]  # [B, S, d]
-    alpha = 1.0 / np.sqrt(2.0 * cfg.nlayers)
-    p = torch.arange(S, dtype=torch.float64)[:, None]
-    i = torch.arange(64, dtype=torch.float64)[None, :]
-    th = p * torch.pow(torch.tensor(10000.0, dtype=torch.float64), -2.0 * i / 128.0)
-    cos, sin = torch.cos(th), torch.sin(th)
+    return torch_ref.forward(m, tokens, targets, softcap, dtype=torch.float64)
 
-    def norm(v, g):
-        return v / torch.sqrt((v * v).mean(-1, keepdim=True) + 1e-5) * f(g)
 
-    def rope(v):  # [B, S, n*128]
-        B_ = v.shape[0]
-        v = v.view(B_, S, -1, 64, 2)
-        a, b = v[..., 0], v[..., 1]
-        c, s = cos[None, :, None, :], sin[None, :, None, :]
-        return torch.stack([a * c - b * s, b * c + a * s], -1).view(B_, S, -1)
-
-    for lw in m.layers:
-        xn = norm(x, lw["gamma1"])
-        q, k, v = rope(xn @ f(lw["wq"])), rope(xn @ f(lw["wk"])), xn @ f(lw["wv"])
-        B_ = q.shape[0]
-        q = q.view(B_, S, cfg.heads, 128).transpose(1, 2)
-        k = k.view(B_, S, cfg.kv_heads, 128).transpose(1, 2)
-        v = v.view(B_, S, cfg.kv_heads, 128).transpose(1, 2)
-        k = k.repeat_interleave(cfg.gqa_ratio, dim=1)
-        v = v.repeat_interleave(cfg.gqa_ratio, dim=1)
-        sc = q @ k.transpose(-1, -2) / np.sqrt(128.0)
-        mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
-        sc = sc.masked_fill(mask, float("-inf"))
-        a = torch.softmax(sc, -1) @ v
-        a = a.transpose(1, 2).reshape(B_, S, -1)
-        x = x + alpha * (a @ f(lw["wo"]))
-        xn = norm(x, lw["gamma2"])
-        h1, h3 = xn @ f(lw["w1"]), xn @ f(lw["w3"])
-        g = h1 * torch.sigmoid(h1) * h3
-        x = x + alpha * (g @ f(lw["w2"]).T)
-    xf = norm(x, m.gamma_final)
-    z = xf @ E.T
-    if softcap > 0:
-        z = softcap * torch.tanh(z / softcap)
-    tgt = torch.from_numpy(np.asarray(targets, np.int64)).view(-1, S)
-    lse = torch.logsumexp(z, -1)
-    ptl = lse - torch.gather(z, -1, tgt[..., None])[..., 0]
-    return ptl.mean().item(), ptl.reshape(-1).numpy(), z.reshape(-1, cfg.vocab).numpy()
+def test_torch_fp32_fused_attention_matches_float64(oracle_lib):
+    """The bench's torch-CPU figure (float32, fused causal attention) computes the
+    same forward."""
+    cfg = custom_config(256, 512, 2, 2, 64, 512)
+    m = OracleModel(cfg, seed=5, scheme=SCHEME_NORMAL, sigma=0.05)
+    rng = np.random.default_rng(3)
+    tok = rng.integers(0, cfg.vocab, cfg.seq).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, cfg.seq).astype(np.uint32)
+    l64, p64, _ = _torch_forward64(m, tok, tgt)
+    l32, p32, _ = torch_ref.forward(m, tok, tgt, dtype=torch.float32, fused_attention=True)
+    assert abs(l32 - l64) / l64 < 1e-5
+    np.testing.assert_allclose(p32, p64, rtol=1e-4, atol=1e-4)
 
 
 @pytest.mark.parametrize("softcap", [0.0, 15.0])
