@@ -35,6 +35,10 @@
 //                      RMSNorm1 backward + dx2; weight gradients as accumulate_dw
 //   RMSNorm backward   cpu/rmsnorm.rs:190-238
 //
+// The single ops (embedding, RMSNorm, SwiGLU gate, CE, SGEMM) are also exported as
+// orc_op_* so that ports of the reference's CPU-op unit tests run against the very
+// functions the forward and backward use.
+//
 // Weights come from rustane_b200/csrc/weight_init.h, the generator the CUDA
 // bridge also uses, so both sides see bit-identical fp16-valued weights.
 // Accumulations that the reference does in f32 (norm sums, CE log-sum-exp) are
@@ -222,6 +226,69 @@ void transpose(const float* in, int rows, int cols, float* out) {
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r)
     for (int c = 0; c < cols; ++c) out[(size_t)c * rows + r] = in[(size_t)r * cols + c];
+}
+
+// ------------------------------------------------------------ embedding, SwiGLU, CE
+// out[t, :] = table[ids[t], :] (cpu/embedding.rs:8-17).
+void embedding_forward(const float* table, int d, const uint32_t* ids, int n, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < n; ++t)
+    memcpy(out + (size_t)t * d, table + (size_t)ids[t] * d, (size_t)d * 4);
+}
+
+// dtable[ids[t], :] += dout[t, :], in position order (cpu/embedding.rs:20-44).
+void embedding_backward(const float* dout, int d, const uint32_t* ids, int n, float* dtable) {
+  for (int t = 0; t < n; ++t) {
+    float* dst = dtable + (size_t)ids[t] * d;
+    const float* src = dout + (size_t)t * d;
+    for (int i = 0; i < d; ++i) dst[i] += src[i];
+  }
+}
+
+// g = silu(h1) * h3 with silu(z) = z / (1 + e^-z) (cpu/silu.rs:8-46,
+// kernels/ffn_fused.rs:105-107).
+inline float silu_gate1(float h1, float h3) { return h1 / (1.0f + expf(-h1)) * h3; }
+
+// Backward of g = silu(h1) * h3: dh3 = dg silu(h1), dh1 = dg h3 silu'(h1) with
+// silu'(z) = s (1 + z (1 - s)), s = sigmoid(z) (cpu/silu.rs:23-34).
+inline void silu_gate_backward1(float dg, float h1, float h3, float* dh1, float* dh3) {
+  const float sig = 1.0f / (1.0f + expf(-h1));
+  const float silu = h1 * sig;
+  const float dsil = sig * (1.0f + h1 * (1.0f - sig));
+  *dh3 = dg * silu;
+  *dh1 = dg * h3 * dsil;
+}
+
+// Cross-entropy of one row of logits z [V] (cpu/cross_entropy.rs:13-41, 58-96):
+// loss = log sum_v exp(z_v - m) + m - z_tgt, m = max_v z_v; the sum in double. With
+// dl != nullptr also dl_v = (softmax_v - [v == tgt]) * scale (cross_entropy.rs:43-56,
+// scaled as forward_backward_batch scales by inv_seq), times the softcap derivative
+// 1 - (z_v / softcap)^2 when softcap > 0 (z holds the capped logits, so
+// z / softcap = tanh(raw / softcap)). dl may alias z.
+double ce_row(const float* z, int V, int tgt, float softcap, double scale, float* dl) {
+  float mx = -INFINITY;
+  for (int i = 0; i < V; ++i) mx = std::max(mx, z[i]);
+  double se = 0.0;
+  for (int i = 0; i < V; ++i) se += exp((double)z[i] - mx);
+  const double loss = log(se) + mx - z[tgt];
+  if (dl) {
+    for (int i = 0; i < V; ++i) {
+      const double pr = exp((double)z[i] - mx) / se;
+      double g = (pr - (i == tgt ? 1.0 : 0.0)) * scale;
+      if (softcap > 0.f) {
+        const double th = z[i] / softcap;
+        g *= 1.0 - th * th;
+      }
+      dl[i] = (float)g;
+    }
+  }
+  return loss;
+}
+
+// z = softcap * tanh(z / softcap) when softcap > 0 (full_model.rs:456-461).
+inline void softcap_row(float* z, int V, float softcap) {
+  if (softcap > 0.f)
+    for (int i = 0; i < V; ++i) z[i] = softcap * tanhf(z[i] / softcap);
 }
 
 // dW[R, N] += X^T dY for X [T, R], dY [T, N] (accumulate_dw of the reference).
@@ -438,6 +505,81 @@ float orc_f16_bits_to_f32(uint16_t h) { return cb_f16_bits_to_f32(h); }
 uint64_t orc_lcg_jump(uint64_t s0, uint64_t k) { return cb_lcg_jump(s0, k); }
 float orc_lcg_value(uint64_t s, float scale) { return cb_lcg_value(s, scale); }
 
+// ---- the oracle's row and element ops, exposed one by one so that the reference's
+// CPU-op unit tests (cpu/{embedding,rmsnorm,silu,cross_entropy,vdsp}.rs test modules)
+// run against the same functions the oracle forward and backward use. Rows are
+// token-major [n, d]. Return 1 on a null or bad argument, 3 on an id >= vocab.
+
+int orc_op_embedding(const float* table, int vocab, int d, const uint32_t* ids, int n,
+                     float* out) {
+  if (!table || !ids || !out || vocab <= 0 || d <= 0 || n < 0) return 1;
+  for (int t = 0; t < n; ++t)
+    if (ids[t] >= (uint32_t)vocab) return 3;
+  embedding_forward(table, d, ids, n, out);
+  return 0;
+}
+
+int orc_op_embedding_backward(const float* dout, int vocab, int d, const uint32_t* ids, int n,
+                              float* dtable) {
+  if (!dout || !ids || !dtable || vocab <= 0 || d <= 0 || n < 0) return 1;
+  for (int t = 0; t < n; ++t)
+    if (ids[t] >= (uint32_t)vocab) return 3;
+  embedding_backward(dout, d, ids, n, dtable);
+  return 0;
+}
+
+int orc_op_rmsnorm(const float* x, const float* gamma, float* out, float* rinv, int n, int d) {
+  if (!x || !gamma || !out || !rinv || n < 0 || d <= 0) return 1;
+  rmsnorm_save(x, gamma, out, rinv, n, d);
+  return 0;
+}
+
+// dx is written; dgamma accumulates over the rows.
+int orc_op_rmsnorm_backward(const float* dy, const float* x, const float* gamma,
+                            const float* rinv, float* dx, float* dgamma, int n, int d) {
+  if (!dy || !x || !gamma || !rinv || !dx || !dgamma || n < 0 || d <= 0) return 1;
+  rmsnorm_backward(dy, x, gamma, rinv, dx, false, dgamma, n, d);
+  return 0;
+}
+
+int orc_op_silu_gate(const float* gate, const float* up, float* out, int64_t n) {
+  if (!gate || !up || !out || n < 0) return 1;
+  for (int64_t i = 0; i < n; ++i) out[i] = silu_gate1(gate[i], up[i]);
+  return 0;
+}
+
+int orc_op_silu_gate_backward(const float* dout, const float* gate, const float* up,
+                              float* dgate, float* dup, int64_t n) {
+  if (!dout || !gate || !up || !dgate || !dup || n < 0) return 1;
+  for (int64_t i = 0; i < n; ++i) silu_gate_backward1(dout[i], gate[i], up[i], &dgate[i], &dup[i]);
+  return 0;
+}
+
+// Per-row CE of raw logits [n, V] (softcapped first when softcap > 0): losses [n];
+// dlogits [n, V] (nullable) = d(loss_row * scale) / d(raw logits).
+int orc_op_cross_entropy(const float* logits, const uint32_t* targets, int n, int V,
+                         float softcap, float scale, float* losses, float* dlogits) {
+  if (!logits || !targets || !losses || n < 0 || V <= 0) return 1;
+  for (int t = 0; t < n; ++t)
+    if (targets[t] >= (uint32_t)V) return 3;
+  std::vector<float> z((size_t)V);
+  for (int t = 0; t < n; ++t) {
+    memcpy(z.data(), logits + (size_t)t * V, (size_t)V * 4);
+    softcap_row(z.data(), V, softcap);
+    losses[t] = (float)ce_row(z.data(), V, (int)targets[t], softcap, scale,
+                              dlogits ? dlogits + (size_t)t * V : nullptr);
+  }
+  return 0;
+}
+
+// C[M, N] = A[M, K] op(B): op(B) = B [K, N], or B [N, K] transposed when b_trans
+// (the LM head's x_final embed^T, cpu/vdsp.rs:354-376 sgemm_at, is the b_trans form).
+int orc_op_sgemm(int M, int N, int K, const float* A, const float* B, int b_trans, float* C) {
+  if (!A || !B || !C || M < 0 || N < 0 || K <= 0) return 1;
+  sgemm(M, N, K, A, B, b_trans != 0, C);
+  return 0;
+}
+
 // Full forward + loss for `batch` sequences back to back.
 //   loss:            mean CE over batch*seq positions
 //   per_token_loss:  nullable [batch*seq]
@@ -461,9 +603,7 @@ int orc_forward(const orc_config* cfg, const float* embed, const float* gamma_fi
       Vb((size_t)T * kvd), A((size_t)T * qd), O((size_t)T * d), H1((size_t)T * hid),
       H3((size_t)T * hid);
 
-  // embedding (cpu/embedding.rs:8-17)
-#pragma omp parallel for schedule(static)
-  for (int t = 0; t < T; ++t) memcpy(&X[(size_t)t * d], embed + (size_t)tokens[t] * d, d * 4);
+  embedding_forward(embed, d, tokens, T, X.data());
 
   for (int l = 0; l < L; ++l) {
     const orc_layer& w = layers[l];
@@ -481,10 +621,7 @@ int orc_forward(const orc_config* cfg, const float* embed, const float* gamma_fi
     sgemm(T, hid, d, Xn.data(), w.w1, false, H1.data());
     sgemm(T, hid, d, Xn.data(), w.w3, false, H3.data());
 #pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < (int64_t)T * hid; ++i) {
-      const float h1 = H1[i];
-      H1[i] = h1 / (1.0f + expf(-h1)) * H3[i];  // silu(h1) * h3 (cpu/silu.rs:37-46)
-    }
+    for (int64_t i = 0; i < (int64_t)T * hid; ++i) H1[i] = silu_gate1(H1[i], H3[i]);
     sgemm(T, d, hid, H1.data(), w.w2, true, O.data());  // gate @ W2^T
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)T * d; ++i) X[i] = X[i] + alpha * O[i];
@@ -506,18 +643,11 @@ int orc_forward(const orc_config* cfg, const float* embed, const float* gamma_fi
   for (int t0 = 0; t0 < T; t0 += CH) {
     const int n = std::min(CH, T - t0);
     sgemm(n, V, d, Xn.data() + (size_t)t0 * d, embed, true, Z.data());
-    if (softcap > 0.f) {
-#pragma omp parallel for schedule(static)
-      for (int64_t i = 0; i < (int64_t)n * V; ++i) Z[i] = softcap * tanhf(Z[i] / softcap);
-    }
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < n; ++r) {
-      const float* z = Z.data() + (size_t)r * V;
-      float mx = -INFINITY;
-      for (int i = 0; i < V; ++i) mx = std::max(mx, z[i]);
-      double se = 0.0;
-      for (int i = 0; i < V; ++i) se += exp((double)z[i] - mx);
-      tok_loss[t0 + r] = log(se) + mx - z[targets[t0 + r]];
+      float* z = Z.data() + (size_t)r * V;
+      softcap_row(z, V, softcap);
+      tok_loss[t0 + r] = ce_row(z, V, (int)targets[t0 + r], softcap, 0.0, nullptr);
     }
     if (sampled_logits && sample_rows) {
       for (int i = 0; i < n_sample; ++i) {
@@ -564,8 +694,7 @@ int orc_forward_backward(const orc_config* cfg, const float* embed, const float*
   };
   std::vector<Cache> cache(L);
   std::vector<float> X(Td), O(Td);
-#pragma omp parallel for schedule(static)
-  for (int t = 0; t < T; ++t) memcpy(&X[(size_t)t * d], embed + (size_t)tokens[t] * d, d * 4);
+  embedding_forward(embed, d, tokens, T, X.data());
   for (int l = 0; l < L; ++l) {
     const orc_layer& w = layers[l];
     Cache& c = cache[l];
@@ -597,10 +726,7 @@ int orc_forward_backward(const orc_config* cfg, const float* embed, const float*
     sgemm(T, hid, d, c.x2n.data(), w.w1, false, c.h1.data());
     sgemm(T, hid, d, c.x2n.data(), w.w3, false, c.h3.data());
 #pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < (int64_t)T * hid; ++i) {
-      const float h1 = c.h1[i];
-      c.g[i] = h1 / (1.0f + expf(-h1)) * c.h3[i];
-    }
+    for (int64_t i = 0; i < (int64_t)T * hid; ++i) c.g[i] = silu_gate1(c.h1[i], c.h3[i]);
     sgemm(T, d, hid, c.g.data(), w.w2, true, O.data());
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)Td; ++i) X[i] = X[i] + alpha * O[i];
@@ -621,23 +747,8 @@ int orc_forward_backward(const orc_config* cfg, const float* embed, const float*
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < n; ++r) {
       float* z = Z.data() + (size_t)r * V;
-      if (softcap > 0.f)
-        for (int i = 0; i < V; ++i) z[i] = softcap * tanhf(z[i] / softcap);
-      float mx = -INFINITY;
-      for (int i = 0; i < V; ++i) mx = std::max(mx, z[i]);
-      double se = 0.0;
-      for (int i = 0; i < V; ++i) se += exp((double)z[i] - mx);
-      const int tgt = (int)targets[t0 + r];
-      part[r] = log(se) + mx - z[tgt];
-      for (int i = 0; i < V; ++i) {
-        double pr = exp((double)z[i] - mx) / se;
-        double g = (pr - (i == tgt ? 1.0 : 0.0)) * inv_seq;
-        if (softcap > 0.f) {
-          const double th = z[i] / softcap;  // tanh(raw / softcap)
-          g *= 1.0 - th * th;
-        }
-        z[i] = (float)g;  // z now holds dl
-      }
+      softcap_row(z, V, softcap);
+      part[r] = ce_row(z, V, (int)targets[t0 + r], softcap, inv_seq, z);  // z now holds dl
     }
     for (int r = 0; r < n; ++r) loss_sum += part[r];
     sgemm(n, d, V, Z.data(), embed, false, dXf.data() + (size_t)t0 * d);
@@ -662,14 +773,8 @@ int orc_forward_backward(const orc_config* cfg, const float* embed, const float*
     for (int64_t i = 0; i < (int64_t)Td; ++i) dffn[i] = alpha * dY[i];
     sgemm(T, hid, d, dffn.data(), w.w2, false, dsilu.data());  // dffn @ W2
 #pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < (int64_t)T * hid; ++i) {
-      const float h1 = c.h1[i];
-      const float sig = 1.0f / (1.0f + expf(-h1));
-      const float silu = h1 * sig;
-      const float dsil = sig * (1.0f + h1 * (1.0f - sig));
-      dh3[i] = dsilu[i] * silu;
-      dh1[i] = dsilu[i] * c.h3[i] * dsil;
-    }
+    for (int64_t i = 0; i < (int64_t)T * hid; ++i)
+      silu_gate_backward1(dsilu[i], c.h1[i], c.h3[i], &dh1[i], &dh3[i]);
     sgemm(T, d, hid, dh1.data(), w.w1, true, dxa.data());  // dh1 @ W1^T
     {
       std::vector<float> t3(Td);
@@ -711,12 +816,7 @@ int orc_forward_backward(const orc_config* cfg, const float* embed, const float*
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)Td; ++i) dY[i] += dx2[i];
   }
-  // embedding backward (embedding.rs:34-44): dembed[tok] += dy, in position order
-  for (int t = 0; t < T; ++t) {
-    float* dst = d_embed + (size_t)tokens[t] * d;
-    const float* src = dY.data() + (size_t)t * d;
-    for (int i = 0; i < d; ++i) dst[i] += src[i];
-  }
+  embedding_backward(dY.data(), d, tokens, T, d_embed);
   return 0;
 }
 

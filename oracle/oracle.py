@@ -70,8 +70,119 @@ def lib() -> C.CDLL:
         L.orc_lcg_jump.argtypes = [C.c_uint64, C.c_uint64]
         L.orc_lcg_value.restype = C.c_float
         L.orc_lcg_value.argtypes = [C.c_uint64, C.c_float]
+        pu = C.POINTER(C.c_uint32)
+        for name, args in (
+                ("orc_op_embedding", [pf, C.c_int, C.c_int, pu, C.c_int, pf]),
+                ("orc_op_embedding_backward", [pf, C.c_int, C.c_int, pu, C.c_int, pf]),
+                ("orc_op_rmsnorm", [pf, pf, pf, pf, C.c_int, C.c_int]),
+                ("orc_op_rmsnorm_backward", [pf, pf, pf, pf, pf, pf, C.c_int, C.c_int]),
+                ("orc_op_silu_gate", [pf, pf, pf, C.c_int64]),
+                ("orc_op_silu_gate_backward", [pf, pf, pf, pf, pf, C.c_int64]),
+                ("orc_op_cross_entropy", [pf, pu, C.c_int, C.c_int, C.c_float, C.c_float, pf,
+                                          pf]),
+                ("orc_op_sgemm", [C.c_int, C.c_int, C.c_int, pf, pf, C.c_int, pf])):
+            getattr(L, name).restype = C.c_int
+            getattr(L, name).argtypes = args
         _lib = L
     return _lib
+
+
+# ---- the oracle's single ops (the functions its forward and backward use), for the
+# ports of the reference's CPU-op unit tests. Float arrays are float32, rows token-major.
+
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def _u32p(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def _check(rc, name):
+    if rc != 0:
+        raise ValueError(f"{name} failed: {rc}")
+
+
+def op_embedding(table, ids):
+    """out[t] = table[ids[t]] (cpu/embedding.rs:8-17); table [V, d]."""
+    table = _f32(table)
+    ids = np.ascontiguousarray(ids, np.uint32).reshape(-1)
+    out = np.empty((ids.size, table.shape[1]), np.float32)
+    _check(lib().orc_op_embedding(_fp(table), table.shape[0], table.shape[1], _u32p(ids),
+                                  ids.size, _fp(out)), "orc_op_embedding")
+    return out
+
+
+def op_embedding_backward(dout, ids, vocab):
+    """dtable [vocab, d] with dtable[ids[t]] += dout[t] (cpu/embedding.rs:20-44)."""
+    dout = _f32(dout)
+    ids = np.ascontiguousarray(ids, np.uint32).reshape(-1)
+    dtable = np.zeros((vocab, dout.shape[1]), np.float32)
+    _check(lib().orc_op_embedding_backward(_fp(dout), vocab, dout.shape[1], _u32p(ids),
+                                           ids.size, _fp(dtable)),
+           "orc_op_embedding_backward")
+    return dtable
+
+
+def op_rmsnorm(x, gamma):
+    """(out, rinv) per row of x [n, d] (cpu/rmsnorm.rs:15-42, 83-107)."""
+    x, gamma = _f32(np.atleast_2d(x)), _f32(gamma)
+    out = np.empty_like(x)
+    rinv = np.empty(x.shape[0], np.float32)
+    _check(lib().orc_op_rmsnorm(_fp(x), _fp(gamma), _fp(out), _fp(rinv), x.shape[0],
+                                x.shape[1]), "orc_op_rmsnorm")
+    return out, rinv
+
+
+def op_rmsnorm_backward(dy, x, gamma, rinv):
+    """(dx, dgamma) (cpu/rmsnorm.rs:44-81, 109-147); dgamma sums over the rows."""
+    dy, x, gamma, rinv = _f32(np.atleast_2d(dy)), _f32(np.atleast_2d(x)), _f32(gamma), _f32(rinv)
+    dx = np.empty_like(x)
+    dgamma = np.zeros(x.shape[1], np.float32)
+    _check(lib().orc_op_rmsnorm_backward(_fp(dy), _fp(x), _fp(gamma), _fp(rinv), _fp(dx),
+                                         _fp(dgamma), x.shape[0], x.shape[1]),
+           "orc_op_rmsnorm_backward")
+    return dx, dgamma
+
+
+def op_silu_gate(gate, up):
+    """silu(gate) * up (cpu/silu.rs:37-46)."""
+    gate, up = _f32(gate), _f32(up)
+    out = np.empty_like(gate)
+    _check(lib().orc_op_silu_gate(_fp(gate), _fp(up), _fp(out), gate.size), "orc_op_silu_gate")
+    return out
+
+
+def op_silu_gate_backward(dout, gate, up):
+    """(dgate, dup) of out = silu(gate) * up (cpu/silu.rs:23-34)."""
+    dout, gate, up = _f32(dout), _f32(gate), _f32(up)
+    dgate, dup = np.empty_like(gate), np.empty_like(up)
+    _check(lib().orc_op_silu_gate_backward(_fp(dout), _fp(gate), _fp(up), _fp(dgate), _fp(dup),
+                                           gate.size), "orc_op_silu_gate_backward")
+    return dgate, dup
+
+
+def op_cross_entropy(logits, targets, softcap=0.0, scale=1.0, grad=True):
+    """(losses [n], dlogits [n, V] or None) of raw logits [n, V]
+    (cpu/cross_entropy.rs:13-96; softcap full_model.rs:456-461)."""
+    z = _f32(np.atleast_2d(logits))
+    t = np.ascontiguousarray(targets, np.uint32).reshape(-1)
+    losses = np.empty(z.shape[0], np.float32)
+    dl = np.empty_like(z) if grad else None
+    _check(lib().orc_op_cross_entropy(_fp(z), _u32p(t), z.shape[0], z.shape[1], softcap, scale,
+                                      _fp(losses), _fp(dl) if grad else None),
+           "orc_op_cross_entropy")
+    return losses, dl
+
+
+def op_sgemm(a, b, b_trans=False):
+    """a [M, K] @ b [K, N], or a @ b.T for b [N, K] when b_trans (the oracle's GEMM)."""
+    a, b = _f32(a), _f32(b)
+    M, K = a.shape
+    N = b.shape[0] if b_trans else b.shape[1]
+    c = np.empty((M, N), np.float32)
+    _check(lib().orc_op_sgemm(M, N, K, _fp(a), _fp(b), int(b_trans), _fp(c)), "orc_op_sgemm")
+    return c
 
 
 def _fp(a):
