@@ -182,6 +182,22 @@ def test_deterministic_and_batch_consistent(bridge_lib):
         assert abs(float(np.mean(p1)) - l1) < 1e-5
 
 
+def test_stability_loop_is_bit_exact(bridge_lib):
+    """1000 forwards through the public host API give bit-identical per-token losses
+    (the reference's all_forward_kernels_1000_iters stability loop,
+    tests/phase3_kernels.rs:315, and its workspace-reuse bit-exactness checks,
+    test_combined_forward_correctness.rs:212-213)."""
+    cfg = custom_config(256, 512, 2, 2, 128)
+    tok, tgt = _tokens(cfg, 2, 21)
+    with CompiledKernels(cfg, 0, 2) as k:
+        k.init_weights(11, CB_INIT_NORMAL, 0.05)
+        l0, p0 = k.forward_loss(tok, tgt, per_token=True)
+        assert np.isfinite(l0)
+        for _ in range(999):
+            l1, p1 = k.forward_loss(tok, tgt, per_token=True)
+            assert l1 == l0 and np.array_equal(p1, p0)
+
+
 def test_forward_api_variants(bridge_lib):
     cfg = custom_config(256, 512, 2, 2, 128, 1024)
     tok, tgt = _tokens(cfg, 1, 13)
