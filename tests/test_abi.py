@@ -80,6 +80,27 @@ def test_null_context_calls_are_rejected(bridge_lib):
     assert bridge_lib.cb_last_error(None) == b"null context"
 
 
+_NULL_OK = {"cb_destroy", "cb_tokens_close"}          # releasing nothing is fine
+_STRINGS = {"cb_version", "cb_create_error", "cb_last_error"}
+
+
+@pytest.mark.parametrize("name", sorted(B.EXPORTED))
+def test_every_entry_point_rejects_null_arguments(bridge_lib, name):
+    """Every call returns a status (never aborts, as the boundary promises): with null
+    pointers and zero sizes each one answers CB_ERR_INVALID_ARG, without touching a
+    device."""
+    fn = getattr(bridge_lib, name)
+    args = [0 if a in (C.c_int32, C.c_int64, C.c_uint64) else 0.0 if a is C.c_float else None
+            for a in fn.argtypes]
+    r = fn(*args)
+    if name in _STRINGS:
+        assert isinstance(r, bytes)
+    elif name in _NULL_OK:
+        assert r == B.CB_OK
+    else:
+        assert r == B.CB_ERR_INVALID_ARG, (name, r)
+
+
 def test_python_api_raises_without_gpu(bridge_lib):
     n = C.c_int32()
     bridge_lib.cb_device_count(C.byref(n))
