@@ -126,6 +126,13 @@ cb_status cb_nccl_unique_id(void* out);
  *            first head, first kv head, first hidden column} of a context. */
 cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info);
 
+/* The same info[8] for rank tp_rank of a tp_world split of `cfg`, without a context
+ * or a GPU (the split cb_create_tp uses; host-side sharding code and tests share it).
+ * CB_ERR_INVALID_ARG for an invalid config, rank or world (world above the kv heads
+ * or the 64-column hidden blocks). */
+cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
+                          int32_t* info);
+
 /* Frees every device resource of the context. NULL is accepted. */
 cb_status cb_destroy(cb_ctx* ctx);
 

@@ -1209,6 +1209,36 @@ cb_status validate_cfg(const cb_model_config* cfg, std::string* why) {
   return CB_OK;
 }
 
+// Megatron split of one model over tp_world ranks: kv heads (with their query heads)
+// and 64-column hidden blocks are divided as evenly as possible, e.g. 52 heads over 8
+// ranks = 7,7,7,7,6,6,6,6. info[8] = {tp_rank, tp_world, local heads, local kv heads,
+// local hidden, first head, first kv head, first hidden column}.
+cb_status tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
+                       int32_t* info, std::string* why) {
+  if (validate_cfg(cfg, why) != CB_OK) return CB_ERR_INVALID_ARG;
+  if (tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) {
+    *why = "bad tensor-parallel rank/world";
+    return CB_ERR_INVALID_ARG;
+  }
+  if (tp_world > cfg->kv_heads || tp_world > cfg->hidden / 64) {
+    *why = "tensor-parallel world larger than the kv heads or hidden blocks";
+    return CB_ERR_INVALID_ARG;
+  }
+  const int grp = cfg->heads / cfg->kv_heads;
+  int kv0, nkv, b0, nb;
+  split_even(cfg->kv_heads, tp_world, tp_rank, &kv0, &nkv);
+  split_even(cfg->hidden / 64, tp_world, tp_rank, &b0, &nb);
+  info[0] = tp_rank;
+  info[1] = tp_world;
+  info[2] = nkv * grp;
+  info[3] = nkv;
+  info[4] = nb * 64;
+  info[5] = kv0 * grp;
+  info[6] = kv0;
+  info[7] = b0 * 64;
+  return CB_OK;
+}
+
 }  // namespace
 
 // ============================================================== C ABI
@@ -1271,12 +1301,9 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
     return CB_ERR_UNSUPPORTED;
   }
 
-  if (tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) {
-    g_create_error = "bad tensor-parallel rank/world";
-    return CB_ERR_INVALID_ARG;
-  }
-  if (tp_world > cfg->kv_heads || tp_world > cfg->hidden / 64) {
-    g_create_error = "tensor-parallel world larger than the kv heads or hidden blocks";
+  int32_t part[8];
+  if (tp_partition(cfg, tp_world, tp_rank, part, &why) != CB_OK) {
+    g_create_error = why;
     return CB_ERR_INVALID_ARG;
   }
   if (tp_world > 1 && !nccl_api().ok()) {
@@ -1290,20 +1317,12 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   ctx->max_batch = max_batch;
   ctx->tp_rank = tp_rank;
   ctx->tp_world = tp_world;
-  {
-    // Megatron split: kv heads (with their query heads) and 64-column hidden blocks
-    // are divided as evenly as possible, e.g. 52 heads over 8 ranks = 7,7,7,7,6,6,6,6.
-    const int grp = cfg->heads / cfg->kv_heads;
-    int kv0, nkv, b0, nb;
-    split_even(cfg->kv_heads, tp_world, tp_rank, &kv0, &nkv);
-    split_even(cfg->hidden / 64, tp_world, tp_rank, &b0, &nb);
-    ctx->kv_heads_l = nkv;
-    ctx->heads_l = nkv * grp;
-    ctx->hidden_l = nb * 64;
-    ctx->kv_off = kv0 * 128;
-    ctx->q_off = kv0 * grp * 128;
-    ctx->hid_off = b0 * 64;
-  }
+  ctx->heads_l = part[2];
+  ctx->kv_heads_l = part[3];
+  ctx->hidden_l = part[4];
+  ctx->q_off = part[5] * 128;
+  ctx->kv_off = part[6] * 128;
+  ctx->hid_off = part[7];
   ctx->q_dim = ctx->heads_l * 128;
   ctx->kv_dim = ctx->kv_heads_l * 128;
   ctx->n_qkv = ctx->q_dim + 2 * ctx->kv_dim;
@@ -1479,6 +1498,13 @@ cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info) {
   info[6] = ctx->kv_off / 128;
   info[7] = ctx->hid_off;
   return CB_OK;
+}
+
+cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
+                          int32_t* info) {
+  if (!info) return CB_ERR_INVALID_ARG;
+  std::string why;
+  return tp_partition(cfg, tp_world, tp_rank, info, &why);
 }
 
 cb_status cb_destroy(cb_ctx* ctx) {

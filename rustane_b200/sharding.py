@@ -11,6 +11,8 @@ Two pieces, both host logic:
   the global batch of independent sequences is split into equal contiguous
   slices, one per rank; ranks never exchange activations. Only the scalar
   results (time, loss) are combined, on the host side of the job.
+* The tensor-parallel split (`tp_partition`), answered by the bridge library
+  itself (cb_tp_partition), so host code sees exactly the split cb_create_tp uses.
 """
 from __future__ import annotations
 
@@ -119,6 +121,37 @@ def rank_shard(tokens: np.ndarray, targets: np.ndarray, seq: int, rank: int,
     if b > tokens.size:
         raise ValueError("rank slice beyond the global batch")
     return tokens[a:b], targets[a:b]
+
+
+@dataclass(frozen=True)
+class TpPartition:
+    """Rank `rank` of a `world`-way Megatron split: query heads [head0, head0 + heads),
+    kv heads [kv_head0, kv_head0 + kv_heads) and hidden columns [hidden0, hidden0 +
+    hidden) (layer.rs:972-1003, 1906-2053: head-sharded attention, hidden-sharded FFN)."""
+    rank: int
+    world: int
+    heads: int
+    kv_heads: int
+    hidden: int
+    head0: int
+    kv_head0: int
+    hidden0: int
+
+
+def tp_partition(cfg, world: int, rank: int) -> TpPartition:
+    """The split cb_create_tp uses (no GPU needed); raises ValueError when the config,
+    rank or world is invalid for tensor parallelism."""
+    import ctypes as C
+
+    from . import bridge as B
+    lib = B.load_library()
+    c = B.cb_model_config(cfg.dim, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.hd, cfg.seq,
+                          cfg.nlayers, cfg.vocab)
+    info = (C.c_int32 * 8)()
+    rc = lib.cb_tp_partition(C.byref(c), world, rank, info)
+    if rc != B.CB_OK:
+        raise ValueError(f"no {world}-way tensor-parallel split of this config (rank {rank})")
+    return TpPartition(*list(info))
 
 
 def reduce_max(value: float, device=None) -> float:

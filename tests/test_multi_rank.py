@@ -1,5 +1,6 @@
 """CPU tests of the multi-rank host logic (gloo, world size 2) and of the
-shard-count policy ported from crates/engine/src/sharding.rs.
+shard-count policy ported from crates/engine/src/sharding.rs; the tensor-parallel
+split of cb_create_tp is checked by emulating its ranks on the CPU.
 
 The data-parallel forward shards whole sequences over ranks with no data-path
 collective; only scalars (times, losses) are reduced. Here each rank runs the
@@ -93,3 +94,128 @@ def test_resolve_modes_fail_fast_and_auto_adjust():
     assert [a.axis for a in adj.adjustments] == ["ATTN_FWD_SHARDS", "FFN_FWD_SHARDS"]
     none = resolve_modes(cfg, None, None)
     assert (none.attn_shards, none.ffn_shards) == (1, 1)
+
+
+# ---- tensor parallelism: the Megatron split cb_create_tp uses, checked on CPU ranks
+
+TP_CASES = {
+    # 3 heads over 2 ranks (2 + 1), hidden 320 = 5 blocks of 64 (3 + 2)
+    "uneven": custom_config(256, 320, 3, 2, 64),
+    # grouped-query: 4 query heads on 2 kv heads, one kv head (two query heads) per rank
+    "gqa": custom_config(256, 384, 4, 2, 64).replace(kv_heads=2),
+}
+
+
+def _tp_forward64(m, part, tokens, targets, all_reduce):
+    """One rank's Megatron forward in float64: Wq/Wk/Wv and W1/W3 column slices of its
+    heads and hidden columns, Wo and W2 row slices, the partial O and down outputs summed
+    over the ranks (where the GPU contexts call an NCCL all-reduce), everything else
+    replicated (layer.rs:1906-2053, 4943-5139)."""
+    import torch
+    cfg = m.cfg
+    S, hd = cfg.seq, cfg.hd
+    f = lambda a: torch.from_numpy(np.asarray(a, np.float64))  # noqa: E731
+    q0, q1 = part.head0 * hd, (part.head0 + part.heads) * hd
+    k0, k1 = part.kv_head0 * hd, (part.kv_head0 + part.kv_heads) * hd
+    c0, c1 = part.hidden0, part.hidden0 + part.hidden
+    E = f(m.embed)
+    x = E[torch.from_numpy(np.asarray(tokens, np.int64)).view(-1, S)]
+    alpha = 1.0 / np.sqrt(2.0 * cfg.nlayers)
+    p = torch.arange(S, dtype=torch.float64)[:, None]
+    i = torch.arange(hd // 2, dtype=torch.float64)[None, :]
+    th = p * torch.pow(torch.tensor(10000.0, dtype=torch.float64), -2.0 * i / hd)
+    cos, sin = torch.cos(th)[None, :, None, :], torch.sin(th)[None, :, None, :]
+
+    def norm(v, g):
+        return v / torch.sqrt((v * v).mean(-1, keepdim=True) + 1e-5) * f(g)
+
+    def rope(v):
+        w = v.view(v.shape[0], S, -1, hd // 2, 2)
+        a, b = w[..., 0], w[..., 1]
+        return torch.stack([a * cos - b * sin, b * cos + a * sin], -1).view(v.shape)
+
+    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+    for lw in m.layers:
+        xn = norm(x, lw["gamma1"])
+        q = rope(xn @ f(lw["wq"])[:, q0:q1])
+        k = rope(xn @ f(lw["wk"])[:, k0:k1])
+        v = xn @ f(lw["wv"])[:, k0:k1]
+        B_ = q.shape[0]
+        q = q.view(B_, S, part.heads, hd).transpose(1, 2)
+        k = k.view(B_, S, part.kv_heads, hd).transpose(1, 2)
+        v = v.view(B_, S, part.kv_heads, hd).transpose(1, 2)
+        grp = part.heads // part.kv_heads
+        k, v = k.repeat_interleave(grp, dim=1), v.repeat_interleave(grp, dim=1)
+        sc = (q @ k.transpose(-1, -2) / np.sqrt(float(hd))).masked_fill(mask, float("-inf"))
+        a = (torch.softmax(sc, -1) @ v).transpose(1, 2).reshape(B_, S, -1)
+        x = x + alpha * all_reduce(a @ f(lw["wo"])[q0:q1, :])
+        xn = norm(x, lw["gamma2"])
+        h1, h3 = xn @ f(lw["w1"])[:, c0:c1], xn @ f(lw["w3"])[:, c0:c1]
+        x = x + alpha * all_reduce((h1 * torch.sigmoid(h1) * h3) @ f(lw["w2"])[:, c0:c1].T)
+    z = norm(x, m.gamma_final) @ E.T
+    tgt = torch.from_numpy(np.asarray(targets, np.int64)).view(-1, S)
+    ptl = torch.logsumexp(z, -1) - torch.gather(z, -1, tgt[..., None])[..., 0]
+    return ptl.reshape(-1).numpy()
+
+
+def _tp_rank_main(rank, world, port, case, out):
+    import torch.distributed as dist
+    from oracle.oracle import OracleModel
+    from rustane_b200.sharding import tp_partition
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = TP_CASES[case]
+        m = OracleModel(cfg, seed=5, sigma=0.05)
+        tok, tgt = global_tokens(cfg.vocab, cfg.seq, 2, SEED)
+
+        def all_reduce(t):
+            t = t.contiguous()
+            dist.all_reduce(t)
+            return t
+
+        part = tp_partition(cfg, world, rank)
+        out[rank] = (part, _tp_forward64(m, part, tok, tgt, all_reduce))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", sorted(TP_CASES))
+def test_tensor_parallel_split_equals_single_process(oracle_lib, bridge_lib, case):
+    """Two gloo ranks, each holding only its cb_tp_partition share of the heads and
+    hidden columns, reproduce the single-process forward (float64, so the only
+    difference is summation order)."""
+    from oracle import torch_ref
+    from oracle.oracle import OracleModel
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_tp_rank_main, args=(world, _free_port(), case, out), nprocs=world,
+                       join=True, start_method="spawn")
+    cfg = TP_CASES[case]
+    parts = [out[r][0] for r in range(world)]
+    # the shares tile the heads, kv heads and hidden columns exactly once
+    assert sum(p.heads for p in parts) == cfg.heads
+    assert sum(p.kv_heads for p in parts) == cfg.kv_heads
+    assert sum(p.hidden for p in parts) == cfg.hidden
+    assert [p.head0 for p in parts] == [0, parts[0].heads]
+    assert [p.hidden0 for p in parts] == [0, parts[0].hidden]
+    tok, tgt = global_tokens(cfg.vocab, cfg.seq, 2, SEED)
+    _, want, _ = torch_ref.forward(OracleModel(cfg, seed=5, sigma=0.05), tok, tgt)
+    for r in range(world):
+        np.testing.assert_allclose(out[r][1], want, rtol=0, atol=1e-10)
+
+
+def test_tp_partition_matches_the_split_rule(bridge_lib):
+    """52 heads over 8 ranks = 7,7,7,7,6,6,6,6; 17920 hidden = 280 blocks = 35 each."""
+    from rustane_b200.model import CONFIGS
+    from rustane_b200.sharding import tp_partition
+    parts = [tp_partition(CONFIGS["32B"], 8, r) for r in range(8)]
+    assert [p.heads for p in parts] == [7, 7, 7, 7, 6, 6, 6, 6]
+    assert [p.head0 for p in parts] == [0, 7, 14, 21, 28, 34, 40, 46]
+    assert all(p.hidden == 2240 for p in parts)
+    with pytest.raises(ValueError):
+        tp_partition(CONFIGS["600m-A"], 13, 0)  # more ranks than kv heads
+    with pytest.raises(ValueError):
+        tp_partition(CONFIGS["600m-A"], 2, 2)  # rank out of range
