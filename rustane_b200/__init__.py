@@ -11,6 +11,8 @@ from .engine import (CompiledKernels, ForwardResult, ForwardScheduler, LayerGrad
                      forward_backward, forward_losses, forward_only_ws, forward_ws,
                      nccl_unique_id)
 from .checkpoint import load_checkpoint, save_checkpoint
+from .parallel_bench import (ParallelBenchError, ParallelBenchRequest, ParallelBenchRunner,
+                             ResolvedParallelBenchConfig)
 from .data import (DeviceTokens, TokenBytes, TokenData, compute_bpb, random_position,
                    validate)
 
@@ -21,4 +23,6 @@ __all__ = [
     "forward_only_ws", "forward_ws", "nccl_unique_id", "LayerGrads", "ModelGrads",
     "forward_backward", "load_checkpoint", "save_checkpoint",
     "DeviceTokens", "TokenBytes", "TokenData", "compute_bpb", "random_position", "validate",
+    "ParallelBenchError", "ParallelBenchRequest", "ParallelBenchRunner",
+    "ResolvedParallelBenchConfig",
 ]
