@@ -25,6 +25,28 @@ def test_library_exports_every_declared_symbol(bridge_lib):
         assert hasattr(bridge_lib, name), name
 
 
+def _header_arity():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(cb_\w+)\s*\(([^)]*)\)\s*;", text):
+        params = [p for p in (x.strip() for x in m.group(2).split(",")) if p and p != "void"]
+        out[m.group(1)] = len(params)
+    return out
+
+
+def test_python_and_rust_bindings_match_header_arity(bridge_lib):
+    """The ctypes table (rustane_b200/bridge.py) and the Rust extern block in
+    INTEGRATION.md declare every entry point with the header's parameter count."""
+    arity = _header_arity()
+    assert sorted(arity) == header_functions()
+    for name, n in arity.items():
+        assert len(getattr(bridge_lib, name).argtypes) == n, name
+    rust = HEADER.parents[1].joinpath("INTEGRATION.md").read_text()
+    bound = {m.group(1): len([p for p in m.group(2).split(",") if p.strip()])
+             for m in re.finditer(r"pub fn (cb_\w+)\(([^)]*)\)", rust)}
+    assert bound == arity
+
+
 def test_version(bridge_lib):
     assert b"sm_100a" in bridge_lib.cb_version()
 
