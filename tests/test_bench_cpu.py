@@ -57,3 +57,11 @@ def test_cpu_baseline_helpers(oracle_lib):
     e["torch_seconds"] = "torch CPU forward failed: test"
     assert bench.torch_cpu_figure(cfg, e, extrapolated=True) == {
         "unavailable": "torch CPU forward failed: test"}
+
+
+def test_bench_rejects_short_warmup():
+    """The timing rules need at least 3 warm-up steps; the bench refuses fewer before
+    it touches a device."""
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--warmup", "2"], cwd=ROOT,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode != 0 and "--warmup must be >= 3" in out.stderr
