@@ -159,3 +159,25 @@ def test_bench_gemm_classes_exist_in_bridge():
     table = src[src.index("kclass_name"):src.index("kclass_name") + 800]
     for c in bench.GEMM_CLASSES:
         assert f'"{c}"' in table, c
+
+
+def test_plain_c_client_compiles_links_and_runs(bridge_lib, tmp_path):
+    """include/cuda_bridge.h is strict C99 (a Rust, cgo or C caller needs no C++), and a
+    C program linked against the library gets status codes and messages back from the
+    host-only calls (tests/c_abi_client.c)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    root = HEADER.parents[1]
+    lib_dir = root / "rustane_b200"
+    exe = tmp_path / "c_abi_client"
+    cc = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                         f"-I{root / 'include'}", str(root / "tests" / "c_abi_client.c"),
+                         f"-L{lib_dir}", "-lcudabridge", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "c client: ok" in run.stdout
