@@ -219,3 +219,30 @@ def test_tp_partition_matches_the_split_rule(bridge_lib):
         tp_partition(CONFIGS["600m-A"], 13, 0)  # more ranks than kv heads
     with pytest.raises(ValueError):
         tp_partition(CONFIGS["600m-A"], 2, 2)  # rank out of range
+
+
+def test_tp_partition_properties(bridge_lib):
+    """For every valid split the ranks' shares tile the kv heads (with their query heads)
+    and the 64-column hidden blocks exactly once, in rank order, each share within one
+    unit of the others."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+    from rustane_b200.sharding import tp_partition
+
+    @settings(max_examples=200, deadline=None)
+    @given(kv=st.integers(1, 64), grp=st.sampled_from([1, 2, 4, 8]),
+           blocks=st.integers(1, 400), data=st.data())
+    def check(kv, grp, blocks, data):
+        cfg = ModelConfig(256, 64 * blocks, kv * grp, kv, 128, 64, 1, 1024)
+        world = data.draw(st.integers(1, min(kv, blocks)))
+        parts = [tp_partition(cfg, world, r) for r in range(world)]
+        head0 = kv0 = col0 = 0
+        for p in parts:
+            assert (p.head0, p.kv_head0, p.hidden0) == (head0, kv0, col0)
+            assert p.heads == p.kv_heads * grp and p.kv_heads >= 1 and p.hidden >= 64
+            head0, kv0, col0 = head0 + p.heads, kv0 + p.kv_heads, col0 + p.hidden
+        assert (head0, kv0, col0) == (cfg.heads, cfg.kv_heads, cfg.hidden)
+        assert max(p.kv_heads for p in parts) - min(p.kv_heads for p in parts) <= 1
+        assert max(p.hidden for p in parts) - min(p.hidden for p in parts) <= 64
+
+    check()
