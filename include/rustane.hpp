@@ -1,0 +1,305 @@
+// rustane.hpp — C++17 host API over the C ABI of cuda_bridge.h, for callers in
+// compiled code. It keeps the reference engine's model-config and forward/loss API
+// (whiskeypolitik/rustane, crates/engine) with the same names, argument meaning and
+// error behaviour:
+//   ModelConfig                 crates/engine/src/model.rs:5-17 (presets :21-151,
+//                               param_count :109-114)
+//   LayerWeights, ModelWeights  layer.rs:52-63, full_model.rs:19-23 (random :132-141)
+//   CompiledKernels             layer.rs:909,967 (compile, compile_forward_only)
+//   ModelForwardWorkspace       full_model.rs:206-264 (new, new_lean)
+//   forward_only_ws, forward_ws full_model.rs:378,494
+//   forward, ForwardResult      full_model.rs:915, :121-129
+//   forward_losses              full_model.rs:1603
+//   ForwardScheduler            multistream.rs:54-161 (one worker per device and
+//                               host thread, whole sequences, results in order)
+// The reference panics when an ANE evaluation fails (layer.rs:1678); here every failed
+// call throws CudaBridgeError carrying the cb_status and the library's message.
+// Header-only: link -lcudabridge.
+#ifndef RUSTANE_HPP
+#define RUSTANE_HPP
+
+#include <atomic>
+#include <cstdint>
+#include <exception>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <utility>
+#include <vector>
+
+#include "cuda_bridge.h"
+
+namespace rustane {
+
+class CudaBridgeError : public std::runtime_error {
+ public:
+  CudaBridgeError(cb_status status, const std::string& what)
+      : std::runtime_error(what + " (status " + std::to_string(status) + ")"), status_(status) {}
+  cb_status status() const { return status_; }
+
+ private:
+  cb_status status_;
+};
+
+struct ModelConfig {
+  int32_t dim, hidden, heads, kv_heads, hd, seq, nlayers, vocab;
+
+  int32_t q_dim() const { return heads * hd; }
+  int32_t kv_dim() const { return kv_heads * hd; }
+  int32_t gqa_ratio() const { return heads / kv_heads; }
+  // Same estimate as ModelConfig::param_count (model.rs:109-114).
+  int64_t param_count() const {
+    const int64_t per_layer = 4LL * dim * dim + 3LL * dim * hidden;
+    return nlayers * per_layer + (int64_t)vocab * dim + (int64_t)dim * (2 * nlayers + 1);
+  }
+  cb_model_config c() const { return {dim, hidden, heads, kv_heads, hd, seq, nlayers, vocab}; }
+  bool operator==(const ModelConfig& o) const {
+    return dim == o.dim && hidden == o.hidden && heads == o.heads && kv_heads == o.kv_heads &&
+           hd == o.hd && seq == o.seq && nlayers == o.nlayers && vocab == o.vocab;
+  }
+  bool operator!=(const ModelConfig& o) const { return !(*this == o); }
+
+  // Reference presets (model.rs).
+  static ModelConfig gpt_karpathy() { return {768, 2048, 6, 6, 128, 512, 6, 8192}; }
+  static ModelConfig gpt_1024() { return {1024, 2816, 8, 8, 128, 512, 8, 8192}; }
+  static ModelConfig target_600m() { return {1536, 4096, 12, 12, 128, 512, 20, 8192}; }
+  static ModelConfig target_800m() { return {1792, 4864, 14, 14, 128, 512, 24, 8192}; }
+  static ModelConfig target_1b() { return {2048, 5632, 16, 16, 128, 512, 28, 8192}; }
+  static ModelConfig target_1_5b() { return {2304, 6144, 18, 18, 128, 512, 32, 8192}; }
+  static ModelConfig mha_28l() { return {1024, 3072, 8, 8, 128, 256, 28, 8192}; }
+};
+
+// MHA config with hd = 128 (custom_config, tests/bench_fwd_only_scale.rs:24-44).
+inline ModelConfig custom_config(int32_t dim, int32_t hidden, int32_t heads, int32_t nlayers,
+                                 int32_t seq, int32_t vocab = 8192) {
+  return {dim, hidden, heads, heads, 128, seq, nlayers, vocab};
+}
+
+// Host f32 layer weights in the reference orientation (x @ W): wq [dim, q_dim],
+// wk/wv [dim, kv_dim], wo [q_dim, dim], w1/w3/w2 [dim, hidden], gamma1/gamma2 [dim].
+struct LayerWeights {
+  std::vector<float> wq, wk, wv, wo, w1, w3, w2, gamma1, gamma2;
+};
+
+// Either host arrays or a device-side generator spec (no host copy of the model).
+struct ModelWeights {
+  std::vector<float> embed;        // [vocab, dim]
+  std::vector<LayerWeights> layers;
+  std::vector<float> gamma_final;  // [dim]
+  bool generated = false;
+  int32_t scheme = CB_INIT_NORMAL;
+  uint64_t seed = 0;
+  float sigma = 0.02f;
+  uint64_t generation = next_generation();
+
+  // The reference's own init (ModelWeights::random, full_model.rs:132-141).
+  static ModelWeights random(const ModelConfig&) {
+    ModelWeights w;
+    w.generated = true;
+    w.scheme = CB_INIT_REFERENCE;
+    return w;
+  }
+  // All matrices ~N(0, sigma), gains 1.0 (the benchmark init).
+  static ModelWeights normal(const ModelConfig&, uint64_t seed = 0, float sigma = 0.02f) {
+    ModelWeights w;
+    w.generated = true;
+    w.scheme = CB_INIT_NORMAL;
+    w.seed = seed;
+    w.sigma = sigma;
+    return w;
+  }
+
+ private:
+  static uint64_t next_generation() {
+    static std::atomic<uint64_t> counter{0};
+    return ++counter;
+  }
+};
+
+// The reference's forward workspace; device buffers live in the context here, so it
+// carries no state.
+struct ModelForwardWorkspace {
+  static ModelForwardWorkspace new_(const ModelConfig&) { return {}; }
+  static ModelForwardWorkspace new_lean(const ModelConfig&) { return {}; }
+};
+
+struct ForwardResult {
+  float loss = 0.f;
+  std::vector<float> per_token_loss;
+};
+
+inline void check(cb_status s, const cb_ctx* ctx, const char* call) {
+  if (s == CB_OK) return;
+  const char* msg = ctx ? cb_last_error(ctx) : cb_create_error();
+  throw CudaBridgeError(s, std::string(call) + ": " + (msg && *msg ? msg : "failed"));
+}
+
+// One cb_ctx: device weights, workspace and captured forward graphs for up to
+// max_batch sequences on one GPU. Not thread-safe (one per host thread).
+class CompiledKernels {
+ public:
+  CompiledKernels(const ModelConfig& cfg, int32_t device = 0, int32_t max_batch = 1)
+      : cfg_(cfg), device_(device), max_batch_(max_batch) {
+    const cb_model_config c = cfg.c();
+    cb_ctx* h = nullptr;
+    check(cb_create(&c, device, max_batch, &h), nullptr, "cb_create");
+    ctx_.reset(h);
+  }
+  static CompiledKernels compile_forward_only(const ModelConfig& cfg, int32_t device = 0,
+                                              int32_t max_batch = 1) {
+    return CompiledKernels(cfg, device, max_batch);
+  }
+  static CompiledKernels compile(const ModelConfig& cfg, int32_t device = 0,
+                                 int32_t max_batch = 1) {
+    return CompiledKernels(cfg, device, max_batch);
+  }
+
+  const ModelConfig& cfg() const { return cfg_; }
+  int32_t device() const { return device_; }
+  int32_t max_batch() const { return max_batch_; }
+  cb_ctx* handle() const { return ctx_.get(); }
+
+  void init_weights(uint64_t seed, int32_t scheme = CB_INIT_NORMAL, float sigma = 0.02f) {
+    check(cb_init_weights(ctx_.get(), seed, scheme, sigma), ctx_.get(), "cb_init_weights");
+    loaded_generation_ = 0;
+  }
+
+  // Uploads (or generates) `w` unless this context already holds it.
+  void load_weights(const ModelWeights& w) {
+    if (loaded_generation_ == w.generation) return;
+    if (w.generated) {
+      init_weights(w.seed, w.scheme, w.sigma);
+    } else {
+      if ((int32_t)w.layers.size() != cfg_.nlayers)
+        throw std::invalid_argument("layer count does not match the config");
+      std::vector<cb_layer_weights_f32> arr(w.layers.size());
+      for (size_t i = 0; i < w.layers.size(); ++i) {
+        const LayerWeights& l = w.layers[i];
+        arr[i] = {l.wq.data(), l.wk.data(), l.wv.data(), l.wo.data(), l.w1.data(),
+                  l.w3.data(), l.w2.data(), l.gamma1.data(), l.gamma2.data()};
+      }
+      check(cb_load_weights_f32(ctx_.get(), w.embed.data(), w.gamma_final.data(), arr.data()),
+            ctx_.get(), "cb_load_weights_f32");
+    }
+    loaded_generation_ = w.generation;
+  }
+
+  // Mean next-token loss of whole sequences held back to back in tokens/targets;
+  // per_token (nullable) receives every position's loss.
+  float forward_loss(const std::vector<uint32_t>& tokens, const std::vector<uint32_t>& targets,
+                     float softcap = 0.f, std::vector<float>* per_token = nullptr) {
+    if (tokens.size() != targets.size() || tokens.empty() || tokens.size() % cfg_.seq != 0)
+      throw std::invalid_argument("tokens/targets must hold whole sequences of cfg.seq");
+    const int32_t batch = (int32_t)(tokens.size() / cfg_.seq);
+    float loss = 0.f;
+    if (per_token) per_token->assign(tokens.size(), 0.f);
+    check(cb_forward_loss(ctx_.get(), tokens.data(), targets.data(), batch, softcap, &loss,
+                          per_token ? per_token->data() : nullptr),
+          ctx_.get(), "cb_forward_loss");
+    return loss;
+  }
+
+  // Logits of rows (b * seq + s) of the last forward, [rows.size() * vocab].
+  std::vector<float> sampled_logits(const std::vector<int32_t>& rows) {
+    std::vector<float> out(rows.size() * (size_t)cfg_.vocab);
+    check(cb_sampled_logits(ctx_.get(), rows.data(), (int32_t)rows.size(), out.data()),
+          ctx_.get(), "cb_sampled_logits");
+    return out;
+  }
+
+ private:
+  struct Destroy {
+    void operator()(cb_ctx* c) const { cb_destroy(c); }
+  };
+  ModelConfig cfg_;
+  int32_t device_, max_batch_;
+  std::unique_ptr<cb_ctx, Destroy> ctx_;
+  uint64_t loaded_generation_ = 0;
+};
+
+// full_model.rs:378 / :494: mean next-token cross-entropy.
+inline float forward_only_ws(const ModelConfig& cfg, CompiledKernels& kernels,
+                             const ModelWeights& weights, const std::vector<uint32_t>& tokens,
+                             const std::vector<uint32_t>& targets, float softcap,
+                             ModelForwardWorkspace&) {
+  if (kernels.cfg() != cfg) throw std::invalid_argument("kernels were compiled for another config");
+  kernels.load_weights(weights);
+  return kernels.forward_loss(tokens, targets, softcap);
+}
+
+inline float forward_ws(const ModelConfig& cfg, CompiledKernels& kernels,
+                        const ModelWeights& weights, const std::vector<uint32_t>& tokens,
+                        const std::vector<uint32_t>& targets, float softcap,
+                        ModelForwardWorkspace& ws) {
+  return forward_only_ws(cfg, kernels, weights, tokens, targets, softcap, ws);
+}
+
+// full_model.rs:915: loss and the per-position losses.
+inline ForwardResult forward(const ModelConfig& cfg, CompiledKernels& kernels,
+                             const ModelWeights& weights, const std::vector<uint32_t>& tokens,
+                             const std::vector<uint32_t>& targets, float softcap = 0.f) {
+  if (kernels.cfg() != cfg) throw std::invalid_argument("kernels were compiled for another config");
+  kernels.load_weights(weights);
+  ForwardResult r;
+  r.loss = kernels.forward_loss(tokens, targets, softcap, &r.per_token_loss);
+  return r;
+}
+
+// full_model.rs:1603: per-position losses.
+inline std::vector<float> forward_losses(const ModelConfig& cfg, CompiledKernels& kernels,
+                                         const ModelWeights& weights,
+                                         const std::vector<uint32_t>& tokens,
+                                         const std::vector<uint32_t>& targets,
+                                         float softcap = 0.f) {
+  return forward(cfg, kernels, weights, tokens, targets, softcap).per_token_loss;
+}
+
+// Sequence-parallel forward workers (multistream.rs:54-161): one CompiledKernels per
+// entry of `devices`, each driven by its own host thread, pulling whole sequences;
+// losses come back in request order. No communication between workers.
+class ForwardScheduler {
+ public:
+  using Request = std::pair<std::vector<uint32_t>, std::vector<uint32_t>>;
+
+  ForwardScheduler(const ModelConfig& cfg, const ModelWeights& weights,
+                   const std::vector<int32_t>& devices, int32_t max_batch = 1) {
+    for (int32_t d : devices) {
+      workers_.emplace_back(new CompiledKernels(cfg, d, max_batch));
+      workers_.back()->load_weights(weights);
+    }
+  }
+
+  std::vector<float> run_batch(const std::vector<Request>& requests, float softcap = 0.f) {
+    std::vector<float> out(requests.size(), 0.f);
+    std::atomic<size_t> next{0};
+    std::mutex err_mu;
+    std::exception_ptr err;
+    auto work = [&](CompiledKernels* k) {
+      for (;;) {
+        const size_t i = next.fetch_add(1);
+        if (i >= requests.size()) return;
+        try {
+          out[i] = k->forward_loss(requests[i].first, requests[i].second, softcap);
+        } catch (...) {
+          std::lock_guard<std::mutex> lk(err_mu);
+          if (!err) err = std::current_exception();
+          return;
+        }
+      }
+    };
+    std::vector<std::thread> threads;
+    for (auto& w : workers_) threads.emplace_back(work, w.get());
+    for (auto& t : threads) t.join();
+    if (err) std::rethrow_exception(err);
+    return out;
+  }
+
+ private:
+  std::vector<std::unique_ptr<CompiledKernels>> workers_;
+};
+
+}  // namespace rustane
+
+#endif  // RUSTANE_HPP

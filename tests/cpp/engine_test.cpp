@@ -1,0 +1,167 @@
+// C++ tests of the host API in include/rustane.hpp, written like the reference engine's
+// own Rust tests of the same calls. Built and run by tests/test_cpp_host.py:
+//   engine_test cpu   host-only checks (configs, errors), no device needed
+//   engine_test gpu   forward through CompiledKernels / forward_only_ws / forward /
+//                     forward_losses / ForwardScheduler on device 0, checked against
+//                     the CPU oracle (oracle/liboracle.so, test infrastructure) with
+//                     the tolerances of the Python parity tests
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "rustane.hpp"
+
+// The CPU oracle's C interface (oracle/forward_ref.cpp).
+extern "C" {
+struct orc_config {
+  int32_t dim, hidden, heads, kv_heads, hd, seq, nlayers, vocab;
+};
+struct orc_layer {
+  float *wq, *wk, *wv, *wo, *w1, *w3, *w2, *gamma1, *gamma2;
+};
+int orc_gen_weights(const orc_config* cfg, uint64_t seed, int scheme, float sigma, float* embed,
+                    float* gamma_final, const orc_layer* layers);
+int orc_forward(const orc_config* cfg, const float* embed, const float* gamma_final,
+                const orc_layer* layers, const uint32_t* tokens, const uint32_t* targets,
+                int batch, float softcap, float* loss, float* per_token_loss,
+                const int32_t* sample_rows, int n_sample, float* sampled_logits);
+}
+
+using namespace rustane;
+
+static int failures = 0;
+#define EXPECT(cond)                                              \
+  do {                                                            \
+    if (!(cond)) {                                                \
+      std::fprintf(stderr, "FAILED line %d: %s\n", __LINE__, #cond); \
+      ++failures;                                                 \
+    }                                                             \
+  } while (0)
+
+template <class F>
+static bool throws_status(F f, cb_status want, const char* text) {
+  try {
+    f();
+  } catch (const CudaBridgeError& e) {
+    return e.status() == want && std::strstr(e.what(), text) != nullptr;
+  }
+  return false;
+}
+
+static void cpu_tests() {
+  // model.rs doc comment: 600M preset ~579M parameters
+  EXPECT(std::fabs(ModelConfig::target_600m().param_count() / 1e6 - 579.0) < 1.0);
+  const ModelConfig c = custom_config(1536, 4096, 12, 20, 512);
+  EXPECT(c == ModelConfig::target_600m() && c.q_dim() == 1536 && c.gqa_ratio() == 1);
+  ModelConfig bad = c;
+  bad.hd = 64;
+  EXPECT(throws_status([&] { CompiledKernels k(bad); }, CB_ERR_INVALID_ARG, "hd must be 128"));
+  int32_t n = 0;
+  EXPECT(cb_device_count(&n) == CB_OK);
+  if (n == 0)
+    EXPECT(throws_status([&] { CompiledKernels::compile_forward_only(c); }, CB_ERR_UNSUPPORTED,
+                         "no CUDA device"));
+}
+
+struct Oracle {
+  orc_config c;
+  std::vector<float> embed, gamma_final;
+  std::vector<LayerWeights> layers;
+  std::vector<orc_layer> ptrs;
+  Oracle(const ModelConfig& m, uint64_t seed, float sigma)
+      : c{m.dim, m.hidden, m.heads, m.kv_heads, m.hd, m.seq, m.nlayers, m.vocab} {
+    const size_t d = m.dim, h = m.hidden, qd = m.q_dim(), kvd = m.kv_dim();
+    embed.resize((size_t)m.vocab * d);
+    gamma_final.resize(d);
+    layers.resize(m.nlayers);
+    for (auto& l : layers) {
+      l.wq.resize(d * qd), l.wk.resize(d * kvd), l.wv.resize(d * kvd), l.wo.resize(qd * d);
+      l.w1.resize(d * h), l.w3.resize(d * h), l.w2.resize(d * h);
+      l.gamma1.resize(d), l.gamma2.resize(d);
+      ptrs.push_back({l.wq.data(), l.wk.data(), l.wv.data(), l.wo.data(), l.w1.data(),
+                      l.w3.data(), l.w2.data(), l.gamma1.data(), l.gamma2.data()});
+    }
+    orc_gen_weights(&c, seed, CB_INIT_NORMAL, sigma, embed.data(), gamma_final.data(),
+                    ptrs.data());
+  }
+  float loss(const std::vector<uint32_t>& t, const std::vector<uint32_t>& g) const {
+    float l = 0.f;
+    orc_forward(&c, embed.data(), gamma_final.data(), ptrs.data(), t.data(), g.data(),
+                (int)(t.size() / c.seq), 0.f, &l, nullptr, nullptr, 0, nullptr);
+    return l;
+  }
+};
+
+static std::vector<uint32_t> random_tokens(size_t n, uint32_t vocab, uint32_t seed) {
+  std::mt19937 rng(seed);
+  std::vector<uint32_t> v(n);
+  for (auto& x : v) x = rng() % vocab;
+  return v;
+}
+
+static void gpu_tests() {
+  const ModelConfig cfg = custom_config(256, 512, 2, 2, 128, 1024);
+  const ModelWeights w = ModelWeights::normal(cfg, 1, 0.05f);
+  const auto tok = random_tokens(2 * cfg.seq, cfg.vocab, 5);
+  const auto tgt = random_tokens(2 * cfg.seq, cfg.vocab, 6);
+  const Oracle ora(cfg, 1, 0.05f);
+  const float want = ora.loss(tok, tgt);
+
+  CompiledKernels k = CompiledKernels::compile_forward_only(cfg, 0, 2);
+  ModelForwardWorkspace ws = ModelForwardWorkspace::new_lean(cfg);
+  const float loss = forward_only_ws(cfg, k, w, tok, tgt, 0.f, ws);
+  EXPECT(std::fabs(loss - want) / want <= 1e-3f);  // the parity tests' loss tolerance
+
+  const ForwardResult r = forward(cfg, k, w, tok, tgt);
+  double mean = 0;
+  for (float x : r.per_token_loss) mean += x;
+  mean /= r.per_token_loss.size();
+  EXPECT(r.loss == loss && std::fabs(mean - loss) < 1e-5);
+  EXPECT(forward_losses(cfg, k, w, tok, tgt) == r.per_token_loss);
+
+  // host arrays in the reference orientation give the device generator's bits
+  ModelWeights host;
+  host.embed = ora.embed;
+  host.layers = ora.layers;
+  host.gamma_final = ora.gamma_final;
+  EXPECT(forward_only_ws(cfg, k, host, tok, tgt, 0.f, ws) == loss);
+
+  bool rejected = false;
+  try {
+    k.forward_loss(std::vector<uint32_t>(cfg.seq + 1), std::vector<uint32_t>(cfg.seq + 1));
+  } catch (const std::invalid_argument&) {
+    rejected = true;
+  }
+  EXPECT(rejected);
+
+  // two workers (both on device 0 here) return every loss in request order
+  std::vector<ForwardScheduler::Request> reqs;
+  std::vector<float> single;
+  for (uint32_t i = 0; i < 4; ++i) {
+    reqs.push_back({random_tokens(cfg.seq, cfg.vocab, 20 + i),
+                    random_tokens(cfg.seq, cfg.vocab, 30 + i)});
+  }
+  CompiledKernels one(cfg, 0, 1);
+  for (const auto& q : reqs) single.push_back(forward_only_ws(cfg, one, w, q.first, q.second, 0.f, ws));
+  ForwardScheduler sched(cfg, w, {0, 0});
+  const std::vector<float> got = sched.run_batch(reqs);
+  for (size_t i = 0; i < reqs.size(); ++i) EXPECT(std::fabs(got[i] - single[i]) <= 1e-6f);
+  std::printf("gpu: loss %.6f oracle %.6f\n", loss, want);
+}
+
+int main(int argc, char** argv) {
+  const std::string mode = argc > 1 ? argv[1] : "cpu";
+  try {
+    if (mode == "cpu") cpu_tests();
+    else gpu_tests();
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "exception: %s\n", e.what());
+    ++failures;
+  }
+  std::printf(failures ? "engine_test %s: %d failure(s)\n" : "engine_test %s: ok\n",
+              mode.c_str(), failures);
+  return failures ? 1 : 0;
+}
