@@ -84,6 +84,8 @@ struct LayerWeights {
 };
 
 // Either host arrays or a device-side generator spec (no host copy of the model).
+// A context uploads a ModelWeights once and skips later loads of the same generation;
+// after changing the arrays in place, call touch() so the next load uploads them.
 struct ModelWeights {
   std::vector<float> embed;        // [vocab, dim]
   std::vector<LayerWeights> layers;
@@ -110,6 +112,8 @@ struct ModelWeights {
     w.sigma = sigma;
     return w;
   }
+  // A new generation: the next load_weights uploads these arrays again.
+  void touch() { generation = next_generation(); }
 
  private:
   static uint64_t next_generation() {

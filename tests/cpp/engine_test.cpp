@@ -61,6 +61,10 @@ static void cpu_tests() {
   EXPECT(throws_status([&] { CompiledKernels k(bad); }, CB_ERR_INVALID_ARG, "hd must be 128"));
   int32_t n = 0;
   EXPECT(cb_device_count(&n) == CB_OK);
+  ModelWeights a = ModelWeights::normal(c, 1), b = a;
+  EXPECT(a.generation == b.generation);
+  b.touch();
+  EXPECT(b.generation != a.generation);
   if (n == 0)
     EXPECT(throws_status([&] { CompiledKernels::compile_forward_only(c); }, CB_ERR_UNSUPPORTED,
                          "no CUDA device"));
@@ -128,6 +132,11 @@ static void gpu_tests() {
   host.layers = ora.layers;
   host.gamma_final = ora.gamma_final;
   EXPECT(forward_only_ws(cfg, k, host, tok, tgt, 0.f, ws) == loss);
+  // changed in place: the same generation is not uploaded again until touch()
+  for (float& x : host.embed) x *= 2.f;
+  EXPECT(forward_only_ws(cfg, k, host, tok, tgt, 0.f, ws) == loss);
+  host.touch();
+  EXPECT(forward_only_ws(cfg, k, host, tok, tgt, 0.f, ws) != loss);
 
   bool rejected = false;
   try {
