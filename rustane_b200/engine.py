@@ -79,6 +79,11 @@ class ModelWeights:
         """All matrices ~N(0, sigma), gains 1.0 (the benchmark init)."""
         return cls(scheme=B.CB_INIT_NORMAL, seed=seed, sigma=sigma)
 
+    def touch(self) -> None:
+        """A new generation: a context uploads a ModelWeights once and skips later loads
+        of the same generation, so call this after changing the arrays in place."""
+        self.generation = ModelWeights._next_gen()
+
     @classmethod
     def from_arrays(cls, embed, layers: Sequence[LayerWeights], gamma_final) -> "ModelWeights":
         return cls(embed=np.ascontiguousarray(embed, np.float32), layers=list(layers),

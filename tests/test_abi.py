@@ -181,3 +181,11 @@ def test_plain_c_client_compiles_links_and_runs(bridge_lib, tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "c client: ok" in run.stdout
+
+
+def test_model_weights_touch_gives_a_new_generation():
+    from rustane_b200 import ModelWeights
+    w = ModelWeights.normal(CONFIGS["600m-A"], seed=1)
+    g = w.generation
+    w.touch()
+    assert w.generation != g
