@@ -12,17 +12,25 @@
 //   forward_losses              full_model.rs:1603
 //   ForwardScheduler            multistream.rs:54-161 (one worker per device and
 //                               host thread, whole sequences, results in order)
+//   ParallelBenchRunner         parallel_bench.rs:24-364 (shard requests from the
+//                               environment, resolution as sharding.rs:162-307,
+//                               mode labels, forward_loss :239)
 // The reference panics when an ANE evaluation fails (layer.rs:1678); here every failed
 // call throws CudaBridgeError carrying the cb_status and the library's message.
 // Header-only: link -lcudabridge.
 #ifndef RUSTANE_HPP
 #define RUSTANE_HPP
 
+#include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdint>
+#include <cstdlib>
 #include <exception>
 #include <memory>
 #include <mutex>
+#include <numeric>
+#include <optional>
 #include <stdexcept>
 #include <string>
 #include <thread>
@@ -302,6 +310,172 @@ class ForwardScheduler {
 
  private:
   std::vector<std::unique_ptr<CompiledKernels>> workers_;
+};
+
+// ---------------------------------------------------------------- ParallelBenchRunner
+
+class ParallelBenchError : public std::invalid_argument {
+ public:
+  using std::invalid_argument::invalid_argument;
+};
+
+enum class ShardPolicy { FailFast, AutoAdjustNearest };
+
+// Sorted divisors (sharding.rs:286-300).
+inline std::vector<int32_t> divisors(int32_t value) {
+  std::vector<int32_t> out;
+  for (int32_t i = 1; (int64_t)i * i <= value; ++i)
+    if (value % i == 0) {
+      out.push_back(i);
+      if (i != value / i) out.push_back(value / i);
+    }
+  std::sort(out.begin(), out.end());
+  return out;
+}
+
+// The divisor closest to `requested`; the smaller one on a tie (sharding.rs:302-307).
+inline int32_t nearest_divisor(const std::vector<int32_t>& divs, int32_t requested) {
+  return *std::min_element(divs.begin(), divs.end(), [&](int32_t a, int32_t b) {
+    const int64_t da = std::llabs((int64_t)requested - a), db = std::llabs((int64_t)requested - b);
+    return da != db ? da < db : a < b;
+  });
+}
+
+inline std::string join(const std::vector<int32_t>& v) {
+  std::string s;
+  for (size_t i = 0; i < v.size(); ++i) s += (i ? ", " : "") + std::to_string(v[i]);
+  return s;
+}
+
+// One forward axis (sharding.rs:227-260): unset -> 1 shard; a divisor -> itself;
+// otherwise FailFast throws and AutoAdjustNearest takes the nearest divisor.
+inline int32_t resolve_axis(const std::string& axis, const std::string& shape_name,
+                            int32_t shape_value, std::optional<int32_t> requested,
+                            ShardPolicy policy, std::vector<std::string>* notes) {
+  if (!requested) return 1;
+  if (*requested <= 0) throw ParallelBenchError(axis + " must be positive");
+  const std::vector<int32_t> valid = divisors(shape_value);
+  if (std::find(valid.begin(), valid.end(), *requested) != valid.end()) return *requested;
+  const std::string where = shape_name + "=" + std::to_string(shape_value);
+  if (policy == ShardPolicy::FailFast)
+    throw ParallelBenchError(axis + "=" + std::to_string(*requested) + " is invalid for " +
+                             where + "; valid divisors: " + join(valid));
+  const int32_t applied = nearest_divisor(valid, *requested);
+  notes->push_back("requested " + axis + "=" + std::to_string(*requested) + ", applied " +
+                   std::to_string(applied) + " (nearest valid divisor for " + where + ")");
+  return applied;
+}
+
+inline std::optional<int32_t> env_count(const char* var) {
+  const char* raw = std::getenv(var);
+  if (!raw) return std::nullopt;
+  char* end = nullptr;
+  const long v = std::strtol(raw, &end, 10);
+  if (end == raw || *end != '\0')
+    throw ParallelBenchError(std::string(var) + " must be an integer, got '" + raw + "'");
+  if (v <= 0) throw ParallelBenchError(std::string(var) + " must be positive");
+  return (int32_t)v;
+}
+
+// Requested forward shard counts (parallel_bench.rs:24-39).
+struct ParallelBenchRequest {
+  std::optional<int32_t> attn_request, ffn_request;
+  ShardPolicy policy = ShardPolicy::FailFast;
+
+  // ATTN_FWD_SHARDS / FFN_FWD_SHARDS, or the ATTN_SHARDS / FFN_SHARDS shorthand (not
+  // both for one axis), as ShardRequest::from_env (sharding.rs:64-100) reads them.
+  static ParallelBenchRequest from_env(ShardPolicy policy = ShardPolicy::FailFast) {
+    ParallelBenchRequest r;
+    r.policy = policy;
+    const char* names[2][4] = {{"ATTN_SHARDS", "ATTN_FWD_SHARDS", "ATTN_BWD_SHARDS", "attention"},
+                               {"FFN_SHARDS", "FFN_FWD_SHARDS", "FFN_BWD_SHARDS", "FFN"}};
+    for (int a = 0; a < 2; ++a) {
+      const auto shorthand = env_count(names[a][0]);
+      const auto fwd = env_count(names[a][1]);
+      const auto bwd = env_count(names[a][2]);
+      if (shorthand && (fwd || bwd))
+        throw ParallelBenchError(std::string(names[a][0]) + "=" + std::to_string(*shorthand) +
+                                 " conflicts with per-direction " + names[a][3] +
+                                 " shard vars; use per-direction vars or the shorthand, "
+                                 "not both");
+      (a == 0 ? r.attn_request : r.ffn_request) = shorthand ? shorthand : fwd;
+    }
+    return r;
+  }
+};
+
+// What a request resolved to (parallel_bench.rs:57-88).
+struct ResolvedParallelBenchConfig {
+  std::optional<int32_t> requested_attn, requested_ffn;
+  int32_t applied_attn = 1, applied_ffn = 1;
+  std::vector<std::string> notes;
+
+  std::string mode_label() const {
+    const bool a = applied_attn > 1, f = applied_ffn > 1;
+    if (a && f) return "attn" + std::to_string(applied_attn) + "_ffn" + std::to_string(applied_ffn);
+    if (a) return "attn" + std::to_string(applied_attn);
+    if (f) return "ffn" + std::to_string(applied_ffn);
+    return "baseline";
+  }
+  std::string benchmark_suffix() const {
+    const std::string l = mode_label();
+    return l == "baseline" ? "" : "_" + l;
+  }
+};
+
+// resolve_parallel_bench_config (parallel_bench.rs:316-364): attention splits into
+// groups of kv heads (gcd(heads, kv_heads) of them), the FFN along the hidden width.
+inline ResolvedParallelBenchConfig resolve_parallel_bench_config(
+    const ModelConfig& cfg, const ParallelBenchRequest& req) {
+  ResolvedParallelBenchConfig r;
+  r.requested_attn = req.attn_request;
+  r.requested_ffn = req.ffn_request;
+  r.applied_attn = resolve_axis("ATTN_FWD_SHARDS", "attention group count",
+                                std::gcd(cfg.heads, cfg.kv_heads), req.attn_request, req.policy,
+                                &r.notes);
+  r.applied_ffn = resolve_axis("FFN_FWD_SHARDS", "hidden width", cfg.hidden, req.ffn_request,
+                               req.policy, &r.notes);
+  return r;
+}
+
+// ParallelBenchRunner (parallel_bench.rs:110-290) on one B200: every resolved mode runs
+// the same single-context forward, since each kernel already covers all heads and hidden
+// columns of a layer that the reference splits into side-by-side ANE programs.
+class ParallelBenchRunner {
+ public:
+  // (runner, compile seconds); an invalid request throws ParallelBenchError before
+  // anything is compiled (parallel_bench.rs:165-233).
+  static std::pair<ParallelBenchRunner, float> compile(const ModelConfig& cfg,
+                                                       const ParallelBenchRequest& request = {},
+                                                       bool use_lean_workspace = true,
+                                                       int32_t device = 0,
+                                                       int32_t max_batch = 1) {
+    ResolvedParallelBenchConfig resolved = resolve_parallel_bench_config(cfg, request);
+    const auto t0 = std::chrono::steady_clock::now();
+    CompiledKernels k(cfg, device, max_batch);
+    const float s = std::chrono::duration<float>(std::chrono::steady_clock::now() - t0).count();
+    return {ParallelBenchRunner(cfg, std::move(resolved), std::move(k), use_lean_workspace), s};
+  }
+
+  const ResolvedParallelBenchConfig& resolved() const { return resolved_; }
+  CompiledKernels& kernels() { return kernels_; }
+  bool use_lean_workspace() const { return lean_; }
+
+  // Mean next-token loss of the sequences in tokens/targets (parallel_bench.rs:239-289).
+  float forward_loss(const ModelWeights& weights, const std::vector<uint32_t>& tokens,
+                     const std::vector<uint32_t>& targets, float softcap,
+                     ModelForwardWorkspace& ws) {
+    return forward_only_ws(cfg_, kernels_, weights, tokens, targets, softcap, ws);
+  }
+
+ private:
+  ParallelBenchRunner(const ModelConfig& cfg, ResolvedParallelBenchConfig resolved,
+                      CompiledKernels kernels, bool lean)
+      : cfg_(cfg), resolved_(std::move(resolved)), kernels_(std::move(kernels)), lean_(lean) {}
+  ModelConfig cfg_;
+  ResolvedParallelBenchConfig resolved_;
+  CompiledKernels kernels_;
+  bool lean_;
 };
 
 }  // namespace rustane

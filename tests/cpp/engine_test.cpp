@@ -7,6 +7,7 @@
 //                     the tolerances of the Python parity tests
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <random>
 #include <string>
@@ -51,7 +52,65 @@ static bool throws_status(F f, cb_status want, const char* text) {
   return false;
 }
 
+template <class F>
+static bool throws_bench_error(F f, const char* text) {
+  try {
+    f();
+  } catch (const ParallelBenchError& e) {
+    return std::strstr(e.what(), text) != nullptr;
+  }
+  return false;
+}
+
+// parallel_bench.rs / sharding.rs host logic (request parsing, resolution, labels).
+static void bench_runner_tests() {
+  // sharding.rs:326-368: divisors sorted; the smaller divisor wins a tie
+  EXPECT(divisors(12) == std::vector<int32_t>({1, 2, 3, 4, 6, 12}));
+  EXPECT(divisors(52) == std::vector<int32_t>({1, 2, 4, 13, 26, 52}));
+  EXPECT(nearest_divisor(divisors(12), 5) == 4 && nearest_divisor(divisors(52), 8) == 4);
+
+  const char* vars[] = {"ATTN_SHARDS", "FFN_SHARDS", "ATTN_FWD_SHARDS", "FFN_FWD_SHARDS",
+                        "ATTN_BWD_SHARDS", "FFN_BWD_SHARDS"};
+  for (const char* v : vars) unsetenv(v);
+  ParallelBenchRequest r = ParallelBenchRequest::from_env();
+  EXPECT(!r.attn_request && !r.ffn_request);
+  setenv("ATTN_FWD_SHARDS", "4", 1);
+  setenv("FFN_SHARDS", "8", 1);
+  r = ParallelBenchRequest::from_env(ShardPolicy::AutoAdjustNearest);
+  EXPECT(r.attn_request == 4 && r.ffn_request == 8 && r.policy == ShardPolicy::AutoAdjustNearest);
+  setenv("ATTN_FWD_SHARDS", "x", 1);
+  EXPECT(throws_bench_error([] { ParallelBenchRequest::from_env(); }, "must be an integer"));
+  setenv("ATTN_FWD_SHARDS", "0", 1);
+  EXPECT(throws_bench_error([] { ParallelBenchRequest::from_env(); }, "must be positive"));
+  unsetenv("ATTN_FWD_SHARDS");
+  setenv("FFN_BWD_SHARDS", "2", 1);
+  EXPECT(throws_bench_error([] { ParallelBenchRequest::from_env(); }, "conflicts"));
+  for (const char* v : vars) unsetenv(v);
+
+  const ModelConfig cfg = ModelConfig::target_600m();  // 12 heads, hidden 4096
+  ParallelBenchRequest q;
+  EXPECT(resolve_parallel_bench_config(cfg, q).mode_label() == "baseline");
+  EXPECT(resolve_parallel_bench_config(cfg, q).benchmark_suffix().empty());
+  q.attn_request = 4;
+  q.ffn_request = 8;
+  EXPECT(resolve_parallel_bench_config(cfg, q).benchmark_suffix() == "_attn4_ffn8");
+  q.ffn_request.reset();
+  q.attn_request = 5;
+  EXPECT(throws_bench_error([&] { resolve_parallel_bench_config(cfg, q); }, "valid divisors"));
+  EXPECT(throws_bench_error([&] { ParallelBenchRunner::compile(cfg, q); }, "valid divisors"));
+  q.policy = ShardPolicy::AutoAdjustNearest;
+  const ResolvedParallelBenchConfig adj = resolve_parallel_bench_config(cfg, q);
+  EXPECT(adj.applied_attn == 4 && adj.requested_attn == 5 && adj.mode_label() == "attn4");
+  EXPECT(adj.notes.size() == 1 && adj.notes[0].find("applied 4") != std::string::npos);
+  int32_t n = 0;
+  cb_device_count(&n);
+  if (n == 0)
+    EXPECT(throws_status([&] { ParallelBenchRunner::compile(cfg, q); }, CB_ERR_UNSUPPORTED,
+                         "no CUDA device"));
+}
+
 static void cpu_tests() {
+  bench_runner_tests();
   // model.rs doc comment: 600M preset ~579M parameters
   EXPECT(std::fabs(ModelConfig::target_600m().param_count() / 1e6 - 579.0) < 1.0);
   const ModelConfig c = custom_config(1536, 4096, 12, 20, 512);
