@@ -1,5 +1,5 @@
 // C++ tests of the host API in include/rustane.hpp, written like the reference engine's
-// own Rust tests of the same calls. Built and run by tests/test_cpp_host.py:
+// own Rust tests of the same calls. Built and run by tests/test_host_cpp.py:
 //   engine_test cpu   host-only checks (configs, errors), no device needed
 //   engine_test gpu   forward through CompiledKernels / forward_only_ws / forward /
 //                     forward_losses / ForwardScheduler on device 0, checked against
