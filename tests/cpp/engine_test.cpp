@@ -102,6 +102,12 @@ static void bench_runner_tests() {
   const ResolvedParallelBenchConfig adj = resolve_parallel_bench_config(cfg, q);
   EXPECT(adj.applied_attn == 4 && adj.requested_attn == 5 && adj.mode_label() == "attn4");
   EXPECT(adj.notes.size() == 1 && adj.notes[0].find("applied 4") != std::string::npos);
+  // test_combined_forward_correctness.rs:245-268: one attention group, 8 requested -> baseline
+  const ModelConfig odd = {256, 768, 1, 1, 128, 16, 2, 256};
+  ParallelBenchRequest o;
+  o.attn_request = 8;
+  o.policy = ShardPolicy::AutoAdjustNearest;
+  EXPECT(resolve_parallel_bench_config(odd, o).mode_label() == "baseline");
   int32_t n = 0;
   cb_device_count(&n);
   if (n == 0)

@@ -248,3 +248,17 @@ def test_oracle_backward_accumulates(oracle_lib):
     np.testing.assert_allclose(g2["embed"], ga["embed"] + gb["embed"], rtol=1e-4, atol=1e-7)
     np.testing.assert_allclose(g2["layers"][0]["w1"], ga["layers"][0]["w1"] + gb["layers"][0]["w1"],
                                rtol=1e-4, atol=1e-7)
+
+
+def test_oracle_odd_config_matches_float64_torch(oracle_lib):
+    """The reference's odd test shape (test_combined_forward_correctness.rs:245-257: one
+    head, hidden 768, seq 16, vocab 256, 2 layers) through the oracle and torch float64."""
+    cfg = custom_config(256, 768, 1, 2, 16, 256)
+    m = OracleModel(cfg, seed=8, scheme=SCHEME_NORMAL, sigma=0.05)
+    rng = np.random.default_rng(8)
+    tok = rng.integers(0, cfg.vocab, 3 * cfg.seq).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, 3 * cfg.seq).astype(np.uint32)
+    loss, ptl, _ = m.forward(tok, tgt)
+    l64, p64, _ = _torch_forward64(m, tok, tgt)
+    assert abs(loss - l64) / l64 < 1e-5
+    np.testing.assert_allclose(ptl, p64, rtol=1e-4, atol=1e-4)

@@ -81,3 +81,14 @@ def test_runner_forward_loss_is_the_engine_forward(bridge_lib):
         loss = runner.forward_loss(w, tok, tgt)
         assert loss == runner.kernels.forward_loss(tok, tgt)
         assert 0 < loss < 20  # the reference's sanity bound (phase4_training.rs:106-124)
+
+
+ODD = ModelConfig(256, 768, 1, 1, 128, 16, 2, 256)  # test_combined_forward_correctness.rs:245-257
+
+
+def test_odd_config_single_head_falls_back_to_baseline():
+    """One attention group: a request for 8 attention shards adjusts to 1, i.e. the
+    baseline mode (test_combined_forward_correctness.rs:245-268)."""
+    r = resolve_parallel_bench_config(ODD, ParallelBenchRequest(8, None,
+                                                                ShardPolicy.AUTO_ADJUST_NEAREST))
+    assert (r.applied_attn, r.mode_label()) == (1, "baseline")
