@@ -12,6 +12,11 @@
 //   forward_losses              full_model.rs:1603
 //   ForwardScheduler            multistream.rs:54-161 (one worker per device and
 //                               host thread, whole sequences, results in order)
+//   load_checkpoint             bin/train.rs:238-346 (RSTK files, cb_load_rstk)
+//   DeviceTokens, eval_windows  data.rs:11-91, bin/train.rs:197-236 (uint16 token
+//                               files in HBM, validation sums for val_loss/val_bpb)
+//   forward_backward, ModelGrads full_model.rs:592-702, :26-30, :143-160 (training step)
+//   prefill, decode_step        single-token decode with a KV cache
 //   ParallelBenchRunner         parallel_bench.rs:24-364 (shard requests from the
 //                               environment, resolution as sharding.rs:162-307,
 //                               mode labels, forward_loss :239)
@@ -142,11 +147,75 @@ struct ForwardResult {
   std::vector<float> per_token_loss;
 };
 
+// Gradients in the reference orientation, laid out like the weights (ModelGrads,
+// full_model.rs:26-30, :143-160).
+struct ModelGrads {
+  std::vector<float> embed, gamma_final;
+  std::vector<LayerWeights> layers;
+
+  static ModelGrads zeros(const ModelConfig& c) {
+    const size_t d = c.dim, h = c.hidden, qd = c.q_dim(), kvd = c.kv_dim();
+    ModelGrads g;
+    g.embed.assign((size_t)c.vocab * d, 0.f);
+    g.gamma_final.assign(d, 0.f);
+    g.layers.resize(c.nlayers);
+    for (LayerWeights& l : g.layers) {
+      l.wq.assign(d * qd, 0.f), l.wk.assign(d * kvd, 0.f), l.wv.assign(d * kvd, 0.f);
+      l.wo.assign(qd * d, 0.f), l.w1.assign(d * h, 0.f), l.w3.assign(d * h, 0.f);
+      l.w2.assign(d * h, 0.f), l.gamma1.assign(d, 0.f), l.gamma2.assign(d, 0.f);
+    }
+    return g;
+  }
+};
+
+// Sums of an evaluation pass; val_loss and val_bpb as validate forms them
+// (train.rs:197-236, compute_bpb data.rs:75-91).
+struct EvalTotals {
+  double loss_sum = 0, nats = 0;
+  int64_t bytes = 0, tokens = 0;
+  double val_loss() const { return tokens ? loss_sum / tokens : 0.0; }
+  double val_bpb() const { return bytes ? nats / (0.6931471805599453 * bytes) : 0.0; }
+  EvalTotals& operator+=(const EvalTotals& o) {
+    loss_sum += o.loss_sum, nats += o.nats, bytes += o.bytes, tokens += o.tokens;
+    return *this;
+  }
+};
+
 inline void check(cb_status s, const cb_ctx* ctx, const char* call) {
   if (s == CB_OK) return;
   const char* msg = ctx ? cb_last_error(ctx) : cb_create_error();
   throw CudaBridgeError(s, std::string(call) + ": " + (msg && *msg ? msg : "failed"));
 }
+
+// A uint16 token array resident in one device's HBM (TokenData, data.rs:11-44, which
+// memory-maps the file; 1e9 tokens take 2 GB).
+class DeviceTokens {
+ public:
+  static DeviceTokens open(const std::string& path, int32_t device = 0) {
+    cb_tokens* t = nullptr;
+    check(cb_tokens_open(path.c_str(), device, &t), nullptr, "cb_tokens_open");
+    return DeviceTokens(t);
+  }
+  static DeviceTokens from_host(const std::vector<uint16_t>& tokens, int32_t device = 0) {
+    cb_tokens* t = nullptr;
+    check(cb_tokens_from_host(tokens.data(), (int64_t)tokens.size(), device, &t), nullptr,
+          "cb_tokens_from_host");
+    return DeviceTokens(t);
+  }
+  int64_t len() const {
+    int64_t n = 0;
+    check(cb_tokens_len(t_.get(), &n), nullptr, "cb_tokens_len");
+    return n;
+  }
+  const cb_tokens* handle() const { return t_.get(); }
+
+ private:
+  struct Close {
+    void operator()(cb_tokens* t) const { cb_tokens_close(t); }
+  };
+  explicit DeviceTokens(cb_tokens* t) : t_(t) {}
+  std::unique_ptr<cb_tokens, Close> t_;
+};
 
 // One cb_ctx: device weights, workspace and captured forward graphs for up to
 // max_batch sequences on one GPU. Not thread-safe (one per host thread).
@@ -211,6 +280,101 @@ class CompiledKernels {
                           per_token ? per_token->data() : nullptr),
           ctx_.get(), "cb_forward_loss");
     return loss;
+  }
+
+  // RSTK checkpoint straight into the device weights; returns the header's step.
+  uint32_t load_checkpoint(const std::string& path) {
+    uint32_t step = 0;
+    check(cb_load_rstk(ctx_.get(), path.c_str(), &step), ctx_.get(), "cb_load_rstk");
+    loaded_generation_ = 0;
+    return step;
+  }
+
+  // One forward over windows of a device token array: sequence b reads tokens
+  // data[positions[b] .. + seq) and targets one position later (train.rs:556-558).
+  float forward_loss_windows(const DeviceTokens& data, const std::vector<int64_t>& positions,
+                             float softcap = 0.f, std::vector<float>* per_token = nullptr) {
+    float loss = 0.f;
+    if (per_token) per_token->assign(positions.size() * (size_t)cfg_.seq, 0.f);
+    check(cb_forward_loss_windows(ctx_.get(), data.handle(), positions.data(),
+                                  (int32_t)positions.size(), softcap, &loss,
+                                  per_token ? per_token->data() : nullptr),
+          ctx_.get(), "cb_forward_loss_windows");
+    return loss;
+  }
+
+  // Device sums of validation steps [step_begin, step_end); token_bytes (nullable) are
+  // the byte lengths of the token ids (TokenBytes, data.rs:47-73).
+  EvalTotals eval_windows(const DeviceTokens& data, const std::vector<int32_t>* token_bytes,
+                          int64_t step_begin, int64_t step_end, float softcap = 0.f) {
+    cb_eval_totals t{};
+    check(cb_eval_windows(ctx_.get(), data.handle(), token_bytes ? token_bytes->data() : nullptr,
+                          token_bytes ? (int32_t)token_bytes->size() : 0, step_begin, step_end,
+                          softcap, &t),
+          ctx_.get(), "cb_eval_windows");
+    EvalTotals r;
+    r.loss_sum = t.loss_sum, r.nats = t.nats, r.bytes = t.bytes, r.tokens = t.tokens;
+    return r;
+  }
+
+  // ---- training step (full_model.rs:592-702): gradients accumulate on the device
+  void enable_training() {
+    check(cb_enable_training(ctx_.get()), ctx_.get(), "cb_enable_training");
+  }
+  void zero_grads() { check(cb_zero_grads(ctx_.get()), ctx_.get(), "cb_zero_grads"); }
+  float forward_backward(const std::vector<uint32_t>& tokens,
+                         const std::vector<uint32_t>& targets, float softcap = 0.f,
+                         float loss_scale = 1.f) {
+    if (tokens.size() != targets.size() || tokens.empty() || tokens.size() % cfg_.seq != 0)
+      throw std::invalid_argument("tokens/targets must hold whole sequences of cfg.seq");
+    float loss = 0.f;
+    check(cb_forward_backward(ctx_.get(), tokens.data(), targets.data(),
+                              (int32_t)(tokens.size() / cfg_.seq), softcap, loss_scale, &loss),
+          ctx_.get(), "cb_forward_backward");
+    return loss;
+  }
+  // Host copy of the accumulated gradients.
+  ModelGrads grads() {
+    ModelGrads g = ModelGrads::zeros(cfg_);
+    std::vector<cb_layer_grads_f32> arr(g.layers.size());
+    for (size_t i = 0; i < g.layers.size(); ++i) {
+      LayerWeights& l = g.layers[i];
+      arr[i] = {l.wq.data(), l.wk.data(), l.wv.data(), l.wo.data(), l.w1.data(),
+                l.w3.data(), l.w2.data(), l.gamma1.data(), l.gamma2.data()};
+    }
+    check(cb_get_grads_f32(ctx_.get(), g.embed.data(), g.gamma_final.data(), arr.data()),
+          ctx_.get(), "cb_get_grads_f32");
+    return g;
+  }
+
+  // ---- single-token decode with a KV cache
+  // Prefills `batch` prompts of equal length held back to back; returns each prompt's
+  // last-position logits [batch * vocab].
+  std::vector<float> prefill(const std::vector<uint32_t>& prompts, int32_t batch,
+                             float softcap = 0.f) {
+    if (batch <= 0 || prompts.empty() || prompts.size() % (size_t)batch != 0)
+      throw std::invalid_argument("prompts must hold batch prompts of equal length");
+    std::vector<float> logits((size_t)batch * cfg_.vocab);
+    check(cb_prefill(ctx_.get(), prompts.data(), batch, (int32_t)(prompts.size() / batch),
+                     softcap, logits.data()),
+          ctx_.get(), "cb_prefill");
+    return logits;
+  }
+  // Advances every sequence by one token; returns the greedy next tokens, and the
+  // next-token logits [batch * vocab] into `logits` when given.
+  std::vector<uint32_t> decode_step(const std::vector<uint32_t>& tokens,
+                                    std::vector<float>* logits = nullptr) {
+    std::vector<uint32_t> next(tokens.size());
+    if (logits) logits->assign(tokens.size() * (size_t)cfg_.vocab, 0.f);
+    check(cb_decode_step(ctx_.get(), tokens.data(), (int32_t)tokens.size(),
+                         logits ? logits->data() : nullptr, next.data()),
+          ctx_.get(), "cb_decode_step");
+    return next;
+  }
+  int32_t decode_position() const {
+    int32_t pos = 0;
+    check(cb_decode_position(ctx_.get(), &pos), ctx_.get(), "cb_decode_position");
+    return pos;
   }
 
   // Logits of rows (b * seq + s) of the last forward, [rows.size() * vocab].

@@ -115,8 +115,28 @@ static void bench_runner_tests() {
                          "no CUDA device"));
 }
 
+static void host_type_tests() {
+  const ModelConfig c = custom_config(256, 512, 2, 2, 128, 1024);
+  const ModelGrads g = ModelGrads::zeros(c);
+  EXPECT(g.embed.size() == 1024u * 256 && g.layers.size() == 2);
+  EXPECT(g.layers[1].wq.size() == 256u * 256 && g.layers[1].w2.size() == 256u * 512);
+  EvalTotals t;
+  t.loss_sum = 20.0, t.tokens = 10, t.nats = 6.931471805599453, t.bytes = 5;
+  EvalTotals u = t;
+  u += t;
+  EXPECT(std::fabs(t.val_loss() - 2.0) < 1e-12 && std::fabs(u.val_bpb() - 2.0) < 1e-12);
+  bool threw = false;
+  try {
+    DeviceTokens::open("/nonexistent/tokens.bin", 0);
+  } catch (const CudaBridgeError& e) {
+    threw = e.status() != CB_OK;
+  }
+  EXPECT(threw);
+}
+
 static void cpu_tests() {
   bench_runner_tests();
+  host_type_tests();
   // model.rs doc comment: 600M preset ~579M parameters
   EXPECT(std::fabs(ModelConfig::target_600m().param_count() / 1e6 - 579.0) < 1.0);
   const ModelConfig c = custom_config(1536, 4096, 12, 20, 512);
