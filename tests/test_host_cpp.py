@@ -18,7 +18,7 @@ def _build(tmp_path):
     oracle.build()
     exe = tmp_path / "engine_test"
     libs = f"{ROOT / 'rustane_b200'}:{ROOT / 'oracle'}"
-    cc = subprocess.run([gxx, "-std=c++17", "-O1", "-Wall", "-Wextra", "-Werror",
+    cc = subprocess.run([gxx, "-std=c++17", "-O1", "-Wall", "-Wextra", "-Wpedantic", "-Wshadow", "-Werror",
                          f"-I{ROOT / 'include'}", str(ROOT / "tests" / "cpp" / "engine_test.cpp"),
                          f"-L{ROOT / 'rustane_b200'}", "-lcudabridge", f"-L{ROOT / 'oracle'}",
                          "-loracle", f"-Wl,-rpath,{libs}", "-pthread", "-o", str(exe)],
