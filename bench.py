@@ -719,6 +719,15 @@ def main():
                           / float(np.mean(r["losses"]))},
                "torch_cpu": torch_cpu_figure(cfg, r, extrapolated=False)}
 
+    # GPU over CPU, end to end (host copies included), against both CPU figures: the
+    # oracle (the reference arm's code) and torch's float32 CPU kernels, the faster one
+    speedup = None
+    if cpu and "value" in cpu and e2e:
+        speedup = {"e2e_vs_cpu_oracle": round(e2e["value"] / cpu["value"], 1)}
+        tc = cpu.get("torch_cpu") or {}
+        if "value" in tc:
+            speedup["e2e_vs_torch_cpu"] = round(e2e["value"] / tc["value"], 1)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -743,6 +752,7 @@ def main():
             "roofline": roofline,
             "kernels": kernels,
             "cpu_baseline": cpu,
+            "speedup_over_cpu": speedup,
             "e2e": e2e,
             "gpu_launches": int(sum(v["launches"] for v in times.values())),
             "clocks": clk,

@@ -171,6 +171,16 @@ cb_status cb_forward_loss_async(cb_ctx* ctx, const uint32_t* d_tokens, const uin
  * error flag raised by earlier asynchronous forwards. */
 cb_status cb_check_device_error(cb_ctx* ctx);
 
+/* Self-test of the bounded device waits that every pipeline kernel uses: runs, on
+ * the context's stream, a one-block kernel whose consumer waits for a barrier that
+ * nothing arrives on, with a limit of limit_us microseconds (1 .. 2e6; the kernels
+ * of the forward use 2 s). The wait expires, the kernel frees its TMEM and returns,
+ * and this call returns CB_ERR_DEVICE_TIMEOUT through the same device error flag
+ * the forward reports with (then cleared), leaving the context usable. Any other
+ * status means the timeout path is broken. No counterpart in the reference (its
+ * supervisor timeouts are host-side, tests/theory_runner_supervisor.rs:14-74). */
+cb_status cb_selftest_wait_timeout(cb_ctx* ctx, uint32_t limit_us);
+
 /* Logits of selected positions of the LAST forward (row = b*seq + s), the
  * sampled-row dump used for parity checks (the full [T, vocab] logits never
  * reach device memory otherwise). logits_out: host [n_rows * vocab] f32, with
@@ -379,7 +389,9 @@ cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* t
  * Limits: T <= 8192 and vocab <= 16384; larger sizes return CB_ERR_INVALID_ARG (split
  * the tokens into chunks of at most 8192).
  * The first call on a device looks up the array's device address with that device
- * current; make that first call before any stream capture on the device.
+ * current; make that first call before any stream capture on the device. After a
+ * cudaDeviceReset the next call sees the new context and looks the address up again
+ * (the array's contents do not survive a reset; nothing carries over between calls).
  * All calls share the one array and it keeps the last call's contents: calls that
  * overlap on the GPU (other streams or threads on the same device) race, so the
  * caller must serialise them.

@@ -243,8 +243,8 @@ class CompiledKernels {
   cb_ctx* handle() const { return ctx_.get(); }
 
   void init_weights(uint64_t seed, int32_t scheme = CB_INIT_NORMAL, float sigma = 0.02f) {
-    check(cb_init_weights(ctx_.get(), seed, scheme, sigma), ctx_.get(), "cb_init_weights");
     loaded_generation_ = 0;
+    check(cb_init_weights(ctx_.get(), seed, scheme, sigma), ctx_.get(), "cb_init_weights");
   }
 
   // Uploads (or generates) `w` unless this context already holds it.
@@ -255,6 +255,27 @@ class CompiledKernels {
     } else {
       if ((int32_t)w.layers.size() != cfg_.nlayers)
         throw std::invalid_argument("layer count does not match the config");
+      // cb_load_weights_f32 reads a fixed number of floats from every pointer: a short
+      // vector would be read past its end, so each size is checked against the config.
+      const size_t d = cfg_.dim, h = cfg_.hidden, qd = cfg_.q_dim(), kvd = cfg_.kv_dim();
+      auto need = [](const std::vector<float>& v, size_t n, const std::string& what) {
+        if (v.size() != n)
+          throw std::invalid_argument(what + " holds " + std::to_string(v.size()) +
+                                      " floats, the config needs " + std::to_string(n));
+      };
+      need(w.embed, (size_t)cfg_.vocab * d, "embed");
+      need(w.gamma_final, d, "gamma_final");
+      for (size_t i = 0; i < w.layers.size(); ++i) {
+        const LayerWeights& l = w.layers[i];
+        const std::string p = "layer " + std::to_string(i) + " ";
+        need(l.wq, d * qd, p + "wq"), need(l.wk, d * kvd, p + "wk"), need(l.wv, d * kvd, p + "wv");
+        need(l.wo, qd * d, p + "wo"), need(l.w1, d * h, p + "w1"), need(l.w3, d * h, p + "w3");
+        need(l.w2, d * h, p + "w2"), need(l.gamma1, d, p + "gamma1");
+        need(l.gamma2, d, p + "gamma2");
+      }
+      // A failed upload leaves the device weights half written: forget the old generation
+      // first, so a retry with the same ModelWeights uploads again.
+      loaded_generation_ = 0;
       std::vector<cb_layer_weights_f32> arr(w.layers.size());
       for (size_t i = 0; i < w.layers.size(); ++i) {
         const LayerWeights& l = w.layers[i];

@@ -1,8 +1,8 @@
 """ctypes binding of include/cuda_bridge.h (libcudabridge.so).
 
-This is the Python-side view of the C ABI; a Rust engine binds the same
-symbols through `extern "C"`. There is no CPU fallback: if the
-library is missing or a call fails, an exception is raised.
+This is the Python-side view of the C ABI; the Rust engine binds the same
+symbols through the cuda-bridge crate (crates/cuda-bridge/src/lib.rs). There is no
+CPU fallback: if the library is missing or a call fails, an exception is raised.
 """
 from __future__ import annotations
 
@@ -39,7 +39,8 @@ EXPORTED = [
     "cb_version", "cb_device_count", "cb_create", "cb_create_tp", "cb_nccl_unique_id",
     "cb_tp_info", "cb_tp_partition", "cb_destroy", "cb_init_weights",
     "cb_load_weights_f32", "cb_forward_loss", "cb_forward_loss_async",
-    "cb_check_device_error", "cb_sampled_logits", "cb_set_profiling", "cb_kernel_times",
+    "cb_check_device_error", "cb_selftest_wait_timeout", "cb_sampled_logits",
+    "cb_set_profiling", "cb_kernel_times",
     "cb_reset_kernel_times", "cb_get_stream", "cb_last_error", "cb_create_error",
     "cb_gemm_f16", "cb_gemm_f16_layout", "cb_attention_f16", "cb_attention_fwd_lse_f16",
     "cb_attention_bwd_f16", "cb_lm_head_ce_f16",
@@ -111,6 +112,7 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_forward_loss": (i32, [vp, pu32, pu32, i32, f32, pf, pf]),
         "cb_forward_loss_async": (i32, [vp, vp, vp, i32, f32, vp, vp, vp]),
         "cb_check_device_error": (i32, [vp]),
+        "cb_selftest_wait_timeout": (i32, [vp, C.c_uint32]),
         "cb_sampled_logits": (i32, [vp, pi32, i32, pf]),
         "cb_set_profiling": (i32, [vp, i32]),
         "cb_kernel_times": (i32, [vp, C.POINTER(cb_kernel_time), i32, pi32]),

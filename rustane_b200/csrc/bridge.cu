@@ -1522,6 +1522,8 @@ cb_status cb_init_weights(cb_ctx* ctx, uint64_t seed, int32_t scheme, float sigm
   if (scheme == CB_INIT_NORMAL && !(sigma > 0.f))
     return fail(ctx, CB_ERR_INVALID_ARG, "sigma must be positive");
   CB_CUDA(cudaSetDevice(ctx->device));
+  // A failure part-way leaves the weights half overwritten: no forward may run on them.
+  ctx->weights_ready = false;
   const cb_model_config& cfg = ctx->cfg;
   InitParams p;
   p.seed = seed;
@@ -1626,6 +1628,7 @@ cb_status cb_load_weights_f32(cb_ctx* ctx, const float* embed, const float* gamm
     }
   }
   CB_CUDA(cudaSetDevice(ctx->device));
+  ctx->weights_ready = false;  // as for cb_init_weights: a failed upload leaves none ready
   size_t next = 0;
   auto fetch = [&](float* dst, size_t n) -> bool {
     if (cudaMemcpyAsync(dst, src[next++], n * sizeof(float), cudaMemcpyHostToDevice,
@@ -2073,6 +2076,64 @@ cb_status cb_check_device_error(cb_ctx* ctx) {
   return CB_OK;
 }
 
+// Self-test of the bounded device waits: a miniature of the pipeline kernels whose
+// producer never produces. Warp 1 owns a TMEM allocation (as the GEMM and attention
+// kernels do) and lane 0 of it waits for a "full" barrier nothing arrives on; warps
+// 2-3 wait for the barrier that consumer would release. The consumer's wait expires
+// after limit_ns and records DEV_ERR_WAIT_TIMEOUT in *err; the other warps see the
+// flag and stop waiting too (their own limit is far longer); warp 1 frees its TMEM
+// and the kernel returns, leaving the context usable.
+__global__ void __launch_bounds__(128) wait_selftest_kernel(uint64_t limit_ns, int* err) {
+  __shared__ uint64_t bar_full, bar_done;
+  __shared__ uint32_t tmem_slot;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_full, 1);
+    mbar_init(&bar_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1 && lane == 0) {
+    if (mbar_wait_for(&bar_full, 0, err, limit_ns)) mbar_arrive(&bar_done);
+  } else if (warp >= 2) {
+    mbar_wait_for(&bar_done, 0, err, 64 * limit_ns);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_slot, 32);
+  }
+}
+
+cb_status cb_selftest_wait_timeout(cb_ctx* ctx, uint32_t limit_us) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (limit_us < 1 || limit_us > 2000000)
+    return fail(ctx, CB_ERR_INVALID_ARG, "limit_us must be in [1, 2000000]");
+  CB_CUDA(cudaSetDevice(ctx->device));
+  CB_CUDA(cudaStreamSynchronize(ctx->stream));
+  wait_selftest_kernel<<<1, 128, 0, ctx->stream>>>((uint64_t)limit_us * 1000ull, ctx->dev_err);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost,
+                          ctx->stream));
+  CB_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (*ctx->h_err != 0) {
+    const int code = *ctx->h_err;
+    CB_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream));
+    CB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
+                "self-test: a device wait expired after " + std::to_string(limit_us) +
+                    " us (device error flag " + std::to_string(code) + ")");
+  }
+  return CB_OK;
+}
+
 cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, float* logits_out) {
   if (!ctx) return CB_ERR_INVALID_ARG;
   if (ctx->last_batch <= 0) return fail(ctx, CB_ERR_NOT_READY, "no forward has run");
@@ -2364,7 +2425,10 @@ cb_status cb_lm_head_ce_f16(const void* xf, const void* embed, const uint32_t* t
 // every GPU that loads this library holds it until the process exits. Host code
 // may not pass the array's name to a kernel (on the host it is only a stand-in
 // symbol), so the first call on each device looks up its device address with
-// cudaGetSymbolAddress, with that device current, and caches it.
+// cudaGetSymbolAddress, with that device current, and caches it together with the
+// device's current CUDA context. A caller that resets the device (cudaDeviceReset)
+// gets a new primary context in which the array has a new address: the next call
+// sees the context change and looks the address up again.
 namespace {
 
 constexpr int NOALLOC_MAX_TOKENS = 8192;
@@ -2377,19 +2441,48 @@ static __device__ __align__(256) unsigned char g_lm_ce_scratch[NOALLOC_SCRATCH_B
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[64] = {};
+unsigned long long g_noalloc_ctx_id[64] = {};
 
-// Device address of g_lm_ce_scratch on the current device (looked up once per device).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// A driver entry point resolved once through the runtime (no -lcuda link).
+template <class Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<Fn>(p);
+  return nullptr;
+}
+
+// Device address of g_lm_ce_scratch on the current device: looked up once per device
+// and again whenever the device's current context is not the one it was looked up in
+// (context ids are unique for the life of the process, unlike context handles).
 cudaError_t noalloc_scratch(void** out) {
+  static const CtxGetCurrentFn get_ctx = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  // cudaSetDevice makes the device's primary context current on this thread (creating
+  // it if needed), so the context read below is the one this call's kernels run in.
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return e;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_ctx || !get_id || get_ctx(&ctx) != CUDA_SUCCESS || !ctx ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return cudaErrorContextIsDestroyed;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  if (!g_noalloc_addr[dev] || g_noalloc_ctx_id[dev] != id) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_lm_ce_scratch);
     if (e != cudaSuccess) return e;
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx_id[dev] = id;
   }
   *out = g_noalloc_addr[dev];
   return cudaSuccess;

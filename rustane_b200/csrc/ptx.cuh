@@ -64,14 +64,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with parity `parity` to complete. Returns false
-// (and records DEV_ERR_WAIT_TIMEOUT in *err) when the time limit is reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// (and records DEV_ERR_WAIT_TIMEOUT in *err) when `limit_ns` of global time have
+// passed, or as soon as another thread has recorded an error in *err.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0u) {
-      if (global_timer_ns() - t0 > CB_WAIT_LIMIT_NS) {
+      if (global_timer_ns() - t0 > limit_ns) {
         if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
         return false;
       }
@@ -80,6 +82,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
   }
   return true;
+}
+
+// The wait every pipeline kernel uses: bounded by CB_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, CB_WAIT_LIMIT_NS);
 }
 
 // 2^x on the special-function unit (MUFU); 2^-inf = +0.

@@ -212,8 +212,8 @@ class CompiledKernels:
     # ---- weights
     def init_weights(self, seed: int = 0, scheme: int = B.CB_INIT_NORMAL,
                      sigma: float = 0.02) -> None:
-        self._check(self.lib.cb_init_weights(self.handle, seed, scheme, sigma))
         self._loaded_generation = None
+        self._check(self.lib.cb_init_weights(self.handle, seed, scheme, sigma))
 
     def load_weights(self, w: ModelWeights) -> None:
         if self._loaded_generation == w.generation:
@@ -222,19 +222,35 @@ class CompiledKernels:
             self.init_weights(w.seed, w.scheme, w.sigma)
         else:
             cfg = self.cfg
-            if len(w.layers) != cfg.nlayers:
+            if w.layers is None or len(w.layers) != cfg.nlayers:
                 raise ValueError("layer count does not match the config")
-            keep = []
+            d, h = cfg.dim, cfg.hidden
+            qd, kvd = cfg.heads * cfg.hd, cfg.kv_heads * cfg.hd
+            sizes = dict(wq=d * qd, wk=d * kvd, wv=d * kvd, wo=qd * d, w1=d * h, w3=d * h,
+                         w2=d * h, gamma1=d, gamma2=d)
+
+            def f32(a, n, what):
+                # the C call reads exactly n floats from each pointer
+                a = np.ascontiguousarray(a, np.float32)
+                if a.size != n:
+                    raise ValueError(f"{what} holds {a.size} values, the config needs {n}")
+                return a
+
+            keep = [f32(w.embed, cfg.vocab * d, "embed"),
+                    f32(w.gamma_final, d, "gamma_final")]
             arr = (B.cb_layer_weights_f32 * cfg.nlayers)()
             for i, lw in enumerate(w.layers):
                 fields = {}
-                for name in ("wq", "wk", "wv", "wo", "w1", "w3", "w2", "gamma1", "gamma2"):
-                    a = np.ascontiguousarray(getattr(lw, name), np.float32)
+                for name, n in sizes.items():
+                    a = f32(getattr(lw, name), n, f"layer {i} {name}")
                     keep.append(a)
                     fields[name] = _fptr(a)
                 arr[i] = B.cb_layer_weights_f32(**fields)
-            self._check(self.lib.cb_load_weights_f32(self.handle, _fptr(w.embed),
-                                                     _fptr(w.gamma_final), arr))
+            # a failed upload leaves the device weights half written: forget the old
+            # generation first, so a retry with the same ModelWeights uploads again
+            self._loaded_generation = None
+            self._check(self.lib.cb_load_weights_f32(self.handle, _fptr(keep[0]),
+                                                     _fptr(keep[1]), arr))
         self._loaded_generation = w.generation
 
     # ---- training (backward pass)
@@ -371,6 +387,12 @@ class CompiledKernels:
 
     def check_device_error(self) -> None:
         self._check(self.lib.cb_check_device_error(self.handle))
+
+    def selftest_wait_timeout(self, limit_us: int = 1000) -> int:
+        """Runs the bounded-wait self-test kernel (a wait nothing ever completes, with a
+        limit of limit_us) and returns its status without raising: CB_ERR_DEVICE_TIMEOUT
+        when the expiry path works. The context stays usable afterwards."""
+        return int(self.lib.cb_selftest_wait_timeout(self.handle, int(limit_us)))
 
     def sampled_logits(self, rows) -> np.ndarray:
         r = np.ascontiguousarray(np.asarray(rows, dtype=np.int32).reshape(-1))

@@ -5,6 +5,7 @@
 //                     forward_losses / ForwardScheduler on device 0, checked against
 //                     the CPU oracle (oracle/liboracle.so, test infrastructure) with
 //                     the tolerances of the Python parity tests
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -12,6 +13,8 @@
 #include <random>
 #include <string>
 #include <vector>
+
+#include <unistd.h>
 
 #include "rustane.hpp"
 
@@ -191,6 +194,129 @@ static std::vector<uint32_t> random_tokens(size_t n, uint32_t vocab, uint32_t se
   return v;
 }
 
+// RSTK file (bin/train.rs:238-273): "RSTK", u32 version 1, step, dim, nlayers, vocab,
+// seq, then the f32 tensors in checkpoint order.
+static std::string write_rstk(const ModelConfig& c, const Oracle& o, uint32_t step) {
+  char tmpl[] = "/tmp/engine_test_XXXXXX";
+  const int fd = mkstemp(tmpl);
+  if (fd < 0) throw std::runtime_error("mkstemp failed");
+  FILE* f = fdopen(fd, "wb");
+  const uint32_t h[6] = {1u, step, (uint32_t)c.dim, (uint32_t)c.nlayers, (uint32_t)c.vocab,
+                         (uint32_t)c.seq};
+  std::fwrite("RSTK", 1, 4, f);
+  std::fwrite(h, 4, 6, f);
+  auto put = [&](const std::vector<float>& v) { std::fwrite(v.data(), 4, v.size(), f); };
+  put(o.embed);
+  put(o.gamma_final);
+  for (const LayerWeights& l : o.layers) {
+    put(l.wq), put(l.wk), put(l.wv), put(l.wo), put(l.w1), put(l.w3), put(l.w2);
+    put(l.gamma1), put(l.gamma2);
+  }
+  std::fclose(f);
+  return tmpl;
+}
+
+// The wrappers of the later rows on a GPU: weight-size checks, checkpoint load, device
+// token windows and evaluation sums, the training step with its gradients, prefill and
+// decode. Each is compared with the forward the earlier checks pinned to the oracle.
+static void later_row_tests(const ModelConfig& cfg, const Oracle& ora, const ModelWeights& w,
+                            const std::vector<uint32_t>& tok, const std::vector<uint32_t>& tgt,
+                            float loss) {
+  CompiledKernels k(cfg, 0, 2);
+  ModelForwardWorkspace ws = ModelForwardWorkspace::new_lean(cfg);
+  EXPECT(forward_only_ws(cfg, k, w, tok, tgt, 0.f, ws) == loss);
+
+  // a short weight vector is refused before any copy; the loaded weights stay usable
+  ModelWeights bad;
+  bad.embed = ora.embed;
+  bad.layers = ora.layers;
+  bad.gamma_final = ora.gamma_final;
+  bad.layers[1].wq.resize(bad.layers[1].wq.size() - 1);
+  bool refused = false;
+  try {
+    k.load_weights(bad);
+  } catch (const std::invalid_argument& e) {
+    refused = std::strstr(e.what(), "layer 1 wq") != nullptr;
+  }
+  EXPECT(refused);
+  EXPECT(k.forward_loss(tok, tgt) == loss);
+
+  // checkpoint: the file of the oracle's arrays loads to the same bits as the device init
+  const std::string path = write_rstk(cfg, ora, 1234);
+  EXPECT(k.load_checkpoint(path) == 1234u);
+  EXPECT(k.forward_loss(tok, tgt) == loss);
+  std::remove(path.c_str());
+
+  // token windows from a device-resident array equal the host-token forward
+  std::vector<uint16_t> stream(3 * cfg.seq + 1);
+  for (size_t i = 0; i < stream.size(); ++i) stream[i] = (uint16_t)((i * 7919u + 13u) % cfg.vocab);
+  const DeviceTokens data = DeviceTokens::from_host(stream, 0);
+  EXPECT(data.len() == (int64_t)stream.size());
+  const std::vector<int64_t> pos = {0, (int64_t)cfg.seq + 5};
+  std::vector<uint32_t> wt, wg;
+  for (int64_t p0 : pos)
+    for (int32_t i = 0; i < cfg.seq; ++i) {
+      wt.push_back(stream[p0 + i]);
+      wg.push_back(stream[p0 + i + 1]);
+    }
+  std::vector<float> ptl_win, ptl_host;
+  const float l_win = k.forward_loss_windows(data, pos, 0.f, &ptl_win);
+  const float l_host = k.forward_loss(wt, wg, 0.f, &ptl_host);
+  EXPECT(l_win == l_host && ptl_win == ptl_host);
+  // validation steps 0 and 1 evaluate the windows at (vs * seq) % (n - seq - 1) = 0 and
+  // seq: their sums equal the per-token losses of those windows (train.rs:197-236)
+  const EvalTotals tot = k.eval_windows(data, nullptr, 0, 2);
+  std::vector<float> ptl_val;
+  k.forward_loss_windows(data, {0, (int64_t)cfg.seq}, 0.f, &ptl_val);
+  double want_sum = 0;
+  for (float x : ptl_val) want_sum += x;
+  EXPECT(tot.tokens == 2 * (int64_t)cfg.seq);
+  EXPECT(std::fabs(tot.loss_sum - want_sum) <= 1e-6 * want_sum);
+
+  // training step: the loss equals the forward's, gradients accumulate and zero
+  k.enable_training();
+  k.zero_grads();
+  const float l_train = k.forward_backward(tok, tgt);
+  EXPECT(std::fabs(l_train - loss) <= 1e-4f * loss);
+  ModelGrads g1 = k.grads();
+  double n1 = 0;
+  for (float x : g1.layers[0].wq) n1 += (double)x * x;
+  EXPECT(n1 > 0 && std::isfinite(n1));
+  k.forward_backward(tok, tgt);
+  ModelGrads g2 = k.grads();
+  double d2 = 0;
+  for (size_t i = 0; i < g1.layers[0].wq.size(); ++i) {
+    const double e = g2.layers[0].wq[i] - 2.0 * g1.layers[0].wq[i];
+    d2 += e * e;
+  }
+  EXPECT(d2 <= 1e-8 * 4 * n1);
+  k.zero_grads();
+  ModelGrads g0 = k.grads();
+  EXPECT(std::all_of(g0.embed.begin(), g0.embed.end(), [](float x) { return x == 0.f; }));
+
+  // prefill + one decode step against the forward's logits at the same positions
+  const int32_t plen = 40;
+  std::vector<uint32_t> prompt(tok.begin(), tok.begin() + plen);
+  const std::vector<float> last = k.prefill(prompt, 1);
+  std::vector<float> step_logits;
+  const std::vector<uint32_t> nxt = k.decode_step({tok[plen]}, &step_logits);
+  EXPECT(k.decode_position() == plen + 1 && nxt.size() == 1);
+  const std::vector<uint32_t> one_tok(tok.begin(), tok.begin() + cfg.seq);
+  const std::vector<uint32_t> one_tgt(tgt.begin(), tgt.begin() + cfg.seq);
+  k.forward_loss(one_tok, one_tgt);
+  const std::vector<float> z = k.sampled_logits({plen - 1, plen});
+  float dz = 0.f;
+  for (int32_t v = 0; v < cfg.vocab; ++v) {
+    dz = std::max(dz, std::fabs(last[v] - z[v]));
+    dz = std::max(dz, std::fabs(step_logits[v] - z[cfg.vocab + v]));
+  }
+  EXPECT(dz <= 2e-2f);  // the parity tests' logit tolerance
+  const uint32_t argmax = (uint32_t)(std::max_element(step_logits.begin(), step_logits.end()) -
+                                     step_logits.begin());
+  EXPECT(nxt[0] == argmax);
+  std::printf("gpu: later rows ok (decode logits max|d| %.2e)\n", dz);
+}
+
 static void gpu_tests() {
   const ModelConfig cfg = custom_config(256, 512, 2, 2, 128, 1024);
   const ModelWeights w = ModelWeights::normal(cfg, 1, 0.05f);
@@ -244,6 +370,7 @@ static void gpu_tests() {
   const std::vector<float> got = sched.run_batch(reqs);
   for (size_t i = 0; i < reqs.size(); ++i) EXPECT(std::fabs(got[i] - single[i]) <= 1e-6f);
   std::printf("gpu: loss %.6f oracle %.6f\n", loss, want);
+  later_row_tests(cfg, ora, w, tok, tgt, loss);
 }
 
 int main(int argc, char** argv) {

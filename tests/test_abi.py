@@ -34,17 +34,34 @@ def _header_arity():
     return out
 
 
+RUST_FFI = HEADER.parents[1] / "crates" / "cuda-bridge" / "src" / "lib.rs"
+
+
 def test_python_and_rust_bindings_match_header_arity(bridge_lib):
-    """The ctypes table (rustane_b200/bridge.py) and the Rust extern block in
-    INTEGRATION.md declare every entry point with the header's parameter count."""
+    """The ctypes table (rustane_b200/bridge.py) and the extern block of the Rust
+    cuda-bridge crate (crates/cuda-bridge/src/lib.rs) declare every entry point with
+    the header's parameter count."""
     arity = _header_arity()
     assert sorted(arity) == header_functions()
     for name, n in arity.items():
         assert len(getattr(bridge_lib, name).argtypes) == n, name
-    rust = HEADER.parents[1].joinpath("INTEGRATION.md").read_text()
+    rust = RUST_FFI.read_text()
+    block = rust[rust.index('unsafe extern "C" {'):]
+    block = block[:block.index("\n    }\n")]
     bound = {m.group(1): len([p for p in m.group(2).split(",") if p.strip()])
-             for m in re.finditer(r"pub fn (cb_\w+)\(([^)]*)\)", rust)}
+             for m in re.finditer(r"pub fn (cb_\w+)\(([^)]*)\)", block)}
     assert bound == arity
+
+
+def test_rust_crate_layout():
+    """The crate that replaces crates/ane-bridge: a manifest with the workspace's
+    package values, a build script that runs nvcc for sm_100a, and the library."""
+    crate = RUST_FFI.parents[1]
+    manifest = (crate / "Cargo.toml").read_text()
+    assert 'name = "cuda-bridge"' in manifest and 'edition = "2024"' in manifest
+    build = (crate / "build.rs").read_text()
+    assert "arch=compute_100a,code=sm_100a" in build and "bridge.cu" in build
+    assert "cargo:rustc-link-lib=dylib=cudabridge" in build
 
 
 def test_version(bridge_lib):
@@ -112,7 +129,7 @@ def test_every_entry_point_rejects_null_arguments(bridge_lib, name):
     pointers and zero sizes each one answers CB_ERR_INVALID_ARG, without touching a
     device."""
     fn = getattr(bridge_lib, name)
-    args = [0 if a in (C.c_int32, C.c_int64, C.c_uint64) else 0.0 if a is C.c_float else None
+    args = [0 if a in (C.c_int32, C.c_int64, C.c_uint32, C.c_uint64) else 0.0 if a is C.c_float else None
             for a in fn.argtypes]
     r = fn(*args)
     if name in _STRINGS:
