@@ -244,6 +244,13 @@ void set_gemm_attr() {
                        GemmCfg<BN, false, EpiTmaIn<Epi>::value>::SMEM_BYTES);
 }
 
+template <int BN, class Epi, int LAYOUT, bool FIX>
+void set_gemm_attr_fix() {
+  cudaFuncSetAttribute(gemm_tn_kernel<BN, Epi, LAYOUT, FIX>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       GemmCfg<BN, false, EpiTmaIn<Epi>::value>::SMEM_BYTES);
+}
+
 template <class Epi, int LAYOUT = 0>
 void set_gemm_attrs_for() {
   set_gemm_attr<128, Epi, LAYOUT>();
@@ -251,6 +258,13 @@ void set_gemm_attrs_for() {
   cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi, LAYOUT>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                        GemmCfg<256, true, EpiTmaIn<Epi>::value>::SMEM_BYTES);
+  if constexpr (EpiCanFix<Epi>::value && LAYOUT == 0) {  // the split-K (SplitFix) variants
+    set_gemm_attr_fix<128, Epi, LAYOUT, true>();
+    set_gemm_attr_fix<256, Epi, LAYOUT, true>();
+    cudaFuncSetAttribute(gemm_tn_pair_kernel<Epi, LAYOUT, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemmCfg<256, true, EpiTmaIn<Epi>::value>::SMEM_BYTES);
+  }
 }
 
 void set_all_kernel_attrs() {
@@ -366,26 +380,40 @@ template <int BN, class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                            int bz, const Epi& epi, int* err, int units, int splits,
                            cudaStream_t st, const CUtensorMap* tc = nullptr,
-                           const CUtensorMap* td = nullptr, bool pdl = false) {
+                           const CUtensorMap* td = nullptr, bool pdl = false,
+                           SplitFix fix = SplitFix{}) {
   using Cfg = GemmCfg<BN, false, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
+  if constexpr (EpiCanFix<Epi>::value && LAYOUT == 0) {
+    if (fix.ws && splits > 1)
+      return launch_k(gemm_tn_kernel<BN, Epi, LAYOUT, true>, dim3(grid), dim3(GEMM_THREADS),
+                      Cfg::SMEM_BYTES, st, pdl, ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K,
+                      bz, splits, epi, fix, err);
+  }
   return launch_k(gemm_tn_kernel<BN, Epi, LAYOUT>, dim3(grid), dim3(GEMM_THREADS),
                   Cfg::SMEM_BYTES, st, pdl, ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K, bz,
-                  splits, epi, err);
+                  splits, epi, SplitFix{}, err);
 }
 
 template <class Epi, int LAYOUT = 0>
 cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, int M, int N,
                              int K, int bz, const Epi& epi, int* err, int clusters, int splits,
                              cudaStream_t st, const CUtensorMap* tc = nullptr,
-                             const CUtensorMap* td = nullptr, bool pdl = false) {
+                             const CUtensorMap* td = nullptr, bool pdl = false,
+                             SplitFix fix = SplitFix{}) {
   using Cfg = GemmCfg<256, true, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
+  if constexpr (EpiCanFix<Epi>::value && LAYOUT == 0) {
+    if (fix.ws && splits > 1)
+      return launch_k(gemm_tn_pair_kernel<Epi, LAYOUT, true>, dim3(2 * pairs),
+                      dim3(GEMM_THREADS), Cfg::SMEM_BYTES, st, pdl, ta, tb_half, tc_or_null(tc),
+                      tc_or_null(td), M, N, K, bz, splits, epi, fix, err);
+  }
   return launch_k(gemm_tn_pair_kernel<Epi, LAYOUT>, dim3(2 * pairs), dim3(GEMM_THREADS),
                   Cfg::SMEM_BYTES, st, pdl, ta, tb_half, tc_or_null(tc), tc_or_null(td), M, N, K,
-                  bz, splits, epi, err);
+                  bz, splits, epi, SplitFix{}, err);
 }
 
 // Tile mode for an M x N GEMM: the best of (last-wave fill) x (per-tile operand
@@ -426,15 +454,17 @@ cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb12
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
                         int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1,
                         const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr,
-                        bool pdl = false) {
+                        bool pdl = false, SplitFix fix = SplitFix{}) {
   if (mode == GM_PAIR)
     return launch_gemm_pair<Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters,
-                                         splits, st, tc, td, pdl);
+                                         splits, st, tc, td, pdl, fix);
   if (mode == GM_SINGLE128)
     return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st,
-                                            tc, td, pdl);
+                                            tc, td, pdl, fix);
+  if (EpiTmaIn<Epi>::value)  // 128 x 256 tiles leave no shared memory for the input boxes
+    return cudaErrorInvalidConfiguration;
   return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st,
-                                          tc, td, pdl);
+                                          tc, td, pdl, fix);
 }
 
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
@@ -475,6 +505,123 @@ void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* 
         *splits = sp;
       }
   }
+}
+
+// ------------------------------------------------------- split-K plans (SplitFix)
+// Workspace of the last-arrival split-K reduction: fp32 partial slabs (kept small enough
+// to stay in L2 between the write and the read) and one arrival counter per tile half.
+constexpr size_t FIX_WS_BYTES = 32u << 20;
+constexpr int FIX_COUNTERS = 16384;
+
+struct GemmPlan {
+  int mode = GM_PAIR;
+  int splits = 1;
+};
+
+int plan_bm(int mode) { return mode == GM_PAIR ? 256 : 128; }
+int plan_bn(int mode) { return mode == GM_SINGLE128 ? 128 : 256; }
+
+// Whether (mode, splits) fits the reduction's workspace: one 128 x BN fp32 slab per unit
+// (per CTA of a pair) and one counter per tile half.
+bool plan_fits(int mode, int splits, int M, int N) {
+  if (splits <= 1) return true;
+  const long tiles = (long)((M + plan_bm(mode) - 1) / plan_bm(mode)) *
+                     ((N + plan_bn(mode) - 1) / plan_bn(mode));
+  const long halves = tiles * (mode == GM_PAIR ? 2 : 1);
+  return halves <= FIX_COUNTERS &&
+         (size_t)halves * splits * GEMM_BM * plan_bn(mode) * sizeof(float) <= FIX_WS_BYTES;
+}
+
+// Estimated duration of an M x N x K GEMM of the fused forward under (mode, splits), in
+// units of one SM's time for one 128 x 256 x 64 block of MMAs. A persistent grid runs
+// ceil(units / slots) waves of units; a unit costs its k-blocks (128-wide tiles move
+// more operand bytes per FLOP; a pair moves the fewest) plus a fixed start-up, and the
+// last unit's epilogue is exposed. A split unit also writes its fp32 partial, and the
+// tile's last unit reads the other splits' partials before its epilogue.
+double plan_cost(int mode, int splits, int M, int N, int K, const DeviceInfo& di, bool tin) {
+  const int bm = plan_bm(mode), bn = plan_bn(mode);
+  const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+  const long units = tiles * splits;
+  const long slots = mode == GM_PAIR ? di.pair_clusters : di.sms;
+  const long waves = (units + slots - 1) / slots;
+  const int kb = (K + GEMM_BK - 1) / GEMM_BK;
+  const int kbu = (kb + splits - 1) / splits;
+  const double t_kb = mode == GM_PAIR ? 1.0 : (mode == GM_SINGLE256 ? 1.18 : 0.64);
+  const double nc = bn / 32.0;
+  const double t_start = 3.0;
+  const double t_epi = nc * (tin ? 1.0 : 0.6);
+  double t_unit = t_start + kbu * t_kb;
+  double t_tail = t_epi;
+  if (splits > 1) {
+    t_unit += nc * 0.4;                    // the partial written to L2
+    t_tail += nc * 0.5 * (splits - 1);     // the last unit's reads of the others
+  }
+  return waves * t_unit + t_tail;
+}
+
+// Tuning override for tests and sweeps: CB_GEMM_PLAN="qkv=128x2,o=pairx1,w13=...,down=...,
+// head=..." (mode pair|256|128, x splits). Read on every plan, so a process can switch
+// plans between eager (profiled) forwards; captured graphs keep the plan they were built
+// with.
+bool plan_override(const char* cls, GemmPlan* out) {
+  const char* e = getenv("CB_GEMM_PLAN");
+  if (!e) return false;
+  std::string spec(e), key = std::string(cls) + "=";
+  size_t pos = 0;
+  while (pos < spec.size()) {
+    size_t end = spec.find(',', pos);
+    if (end == std::string::npos) end = spec.size();
+    const std::string item = spec.substr(pos, end - pos);
+    pos = end + 1;
+    if (item.compare(0, key.size(), key) != 0) continue;
+    const std::string v = item.substr(key.size());
+    const size_t x = v.find('x');
+    const std::string m = v.substr(0, x);
+    GemmPlan p;
+    if (m == "pair") p.mode = GM_PAIR;
+    else if (m == "256") p.mode = GM_SINGLE256;
+    else if (m == "128") p.mode = GM_SINGLE128;
+    else return false;
+    p.splits = x == std::string::npos ? 1 : std::max(1, atoi(v.c_str() + x + 1));
+    *out = p;
+    return true;
+  }
+  return false;
+}
+
+// Plan of one GEMM of the fused forward (QKV, O, W1/W3, down, LM head): the cheapest
+// (mode, splits) by plan_cost among the tile shapes N allows (a pair and 128 x 256 tiles
+// need N % 256 == 0; 128 x 256 tiles have no room for the TMA_IN epilogue's boxes) and
+// splits that leave each unit at least 8 k-blocks and fit the reduction's workspace.
+// Deterministic: the same shapes always give the same plan, so the summation order and
+// the loss bits do not change from call to call.
+GemmPlan plan_gemm(const char* cls, int M, int N, int K, const DeviceInfo& di, bool tin,
+                   bool can_split) {
+  GemmPlan best;
+  if (plan_override(cls, &best)) {
+    if (best.mode != GM_SINGLE128 && N % 256 != 0) best.mode = GM_SINGLE128;
+    if (tin && best.mode == GM_SINGLE256) best.mode = GM_SINGLE128;
+    if (!can_split || !plan_fits(best.mode, best.splits, M, N)) best.splits = 1;
+    return best;
+  }
+  const int kb = (K + GEMM_BK - 1) / GEMM_BK;
+  double best_cost = 1e300;
+  const int modes[3] = {GM_PAIR, GM_SINGLE256, GM_SINGLE128};
+  for (int mode : modes) {
+    if (mode != GM_SINGLE128 && N % 256 != 0) continue;
+    if (tin && mode == GM_SINGLE256) continue;
+    for (int sp = 1; sp <= (can_split ? 8 : 1); ++sp) {
+      if (sp > 1 && (kb + sp - 1) / sp < 8) break;
+      if (!plan_fits(mode, sp, M, N)) continue;
+      const double c = plan_cost(mode, sp, M, N, K, di, tin);
+      if (c < best_cost * 0.97) {  // a split must win clearly
+        best_cost = c;
+        best.mode = mode;
+        best.splits = sp;
+      }
+    }
+  }
+  return best;
 }
 
 // Causal attention: tcgen05 kernel when seq is a multiple of 128 (tensor maps given),
@@ -642,6 +789,8 @@ struct cb_ctx {
   float2* rope = nullptr;      // [64, S] (cos, sin), pair-major
   float2* rope_pm = nullptr;   // [S, 64] the same, position-major
   int* dev_err = nullptr;      // device error flag
+  float4* fix_ws = nullptr;    // split-K partial slabs (FIX_WS_BYTES; single-GPU contexts)
+  int* fix_cnt = nullptr;      // split-K arrival counters [FIX_COUNTERS], zero between launches
   float* h_loss = nullptr;     // pinned
   int* h_err = nullptr;        // pinned
 
@@ -688,6 +837,12 @@ thread_local std::string g_create_error;
 cb_status fail(cb_ctx* c, cb_status code, const std::string& msg) {
   if (c) c->err = msg;
   return code;
+}
+
+// After a kernel stopped early (an expired wait), split-K arrival counters may be left
+// part-way: zero them with the error flag, so the next launch counts from zero.
+void reset_split_counters(cb_ctx* c, cudaStream_t st) {
+  if (c->fix_cnt) cudaMemsetAsync(c->fix_cnt, 0, FIX_COUNTERS * sizeof(int), st);
 }
 
 #define CB_CUDA(call)                                                                  \
@@ -742,7 +897,7 @@ void free_ctx(cb_ctx* c) {
                   c->gamma_final, c->x,  c->xn,    c->q,        c->k,        c->v,
                   c->attn,  c->g,     c->ce_part,  c->tgt_logit, c->tok_loss, c->block_sums,
                   c->loss,  c->tokens, c->targets, c->rope,     c->dev_err,  c->samp_a,
-                  c->samp_out};
+                  c->samp_out, c->fix_ws, c->fix_cnt};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->h_loss) cudaFreeHost(c->h_loss);
@@ -943,34 +1098,45 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   mark(K_EMBED_NORM, 0, Td * 4 + Td * d * (2 + 4 + 2));
 
   const DeviceInfo& di = device_info(c->device);
-  const int m_qkv = pick_mode(T, c->n_qkv, di);
-  int m_o, s_o, m_2, s_2;
-  const int max_split = (!tp && d % 128 == 0) ? 1 : 2;  // see pick_projection
-  pick_projection(T, d, c->q_dim, di, &m_o, &s_o, max_split);
-  pick_projection(T, d, hid, di, &m_2, &s_2, max_split);
-  const int m_13 = pick_mode(T, 2 * hid, di);
-  const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
-
   // Residual add + RMSNorm: fused into the projection's epilogue (EpiResidualNorm: x +=
   // alpha * acc in place, xn = fp16(x o gamma), per-row partial sums of x^2; the next
-  // GEMM applies 1/rms per row, RowScaled) unless K is split or the model is tensor
-  // parallel; otherwise the projection writes delta and add_rmsnorm does the rest.
+  // GEMM applies 1/rms per row, RowScaled) unless the model is tensor parallel (the
+  // partials are all-reduced first) or d % 128 != 0; otherwise the projection writes
+  // delta and add_rmsnorm does the rest.
   const bool fuse_norm = !tp && d % 128 == 0;
+  // Single-GPU GEMMs with too few tiles split K, reduced by the tile's last split
+  // (SplitFix), so every fused epilogue still sees whole sums.
+  const bool can_fix = !tp && c->fix_ws != nullptr;
+  const SplitFix fix{c->fix_ws, c->fix_cnt};
+  const GemmPlan p_qkv = plan_gemm("qkv", T, c->n_qkv, d, di, false, can_fix);
+  int m_o, s_o, m_2, s_2;
+  if (fuse_norm) {
+    const GemmPlan po = plan_gemm("o", T, d, c->q_dim, di, true, can_fix);
+    const GemmPlan p2 = plan_gemm("down", T, d, hid, di, true, can_fix);
+    m_o = po.mode, s_o = po.splits, m_2 = p2.mode, s_2 = p2.splits;
+  } else {
+    pick_projection(T, d, c->q_dim, di, &m_o, &s_o, 2);
+    pick_projection(T, d, hid, di, &m_2, &s_2, 2);
+  }
+  const GemmPlan p_13 = plan_gemm("w13", T, 2 * hid, d, di, false, can_fix);
+  const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
+
   // GEMMs use programmatic dependent launch (setup overlaps the previous kernel's tail)
   // outside tensor parallelism and eager profiling.
   const bool pdl = !tp && !prof;
   bool fused_last = false;  // the last projection used the fused epilogue
   bool xn_scaled = false;   // xn holds fp16(x o gamma): consumers scale rows by 1/rms
-  auto consume = [&](int mode, const CUtensorMap& tb128, const CUtensorMap& tb256, int N,
-                     int layer, const auto& inner) -> cudaError_t {
+  auto consume = [&](const GemmPlan& plan, const CUtensorMap& tb128, const CUtensorMap& tb256,
+                     int N, int layer, const auto& inner) -> cudaError_t {
     using E = std::decay_t<decltype(inner)>;
+    const SplitFix f = plan.splits > 1 ? fix : SplitFix{};
     if (xn_scaled) {
       RowScaled<E> ep{inner, c->ss_part, d / 128, (float)d, RMS_EPS, 1.f};
-      return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di, st, 1,
-                         nullptr, nullptr, pdl);
+      return launch_gemm(plan.mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di,
+                         st, plan.splits, nullptr, nullptr, pdl, f);
     }
-    return launch_gemm(mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di, st, 1,
-                       nullptr, nullptr, pdl);
+    return launch_gemm(plan.mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di,
+                       st, plan.splits, nullptr, nullptr, pdl, f);
   };
 
   // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer. fp16
@@ -982,12 +1148,12 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
                      const CUtensorMap& tb256, int K, int layer, int cls,
                      const float* gamma_next) -> cudaError_t {
     cudaError_t r;
-    delta_f32 = tp || splits > 1;
-    fused_last = fuse_norm && splits == 1;
+    fused_last = fuse_norm && (splits == 1 || can_fix);
+    delta_f32 = !fused_last && (tp || splits > 1);
     if (fused_last) {
       EpiResidualNorm ep{gamma_next, c->ss_part, d / 128, alpha, 0.f};
-      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, 1,
-                      &c->tm_x, &c->tm_xh, pdl);
+      r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, splits,
+                      &c->tm_x, &c->tm_xh, pdl, splits > 1 ? fix : SplitFix{});
       if (r != cudaSuccess) return r;
       mark(cls, 2.0 * Td * d * K,
            Td * K * 2 + (double)d * K * 2 + Td * d * (4 + 4 + 2) + Td * (d / 128) * 4);
@@ -1033,7 +1199,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     __half* vl = kv ? kv->v + (size_t)l * kv->layer_stride : c->v;
     {
       EpiQkvRope ep{c->q, kl, vl, c->rope, S, c->heads_l, c->kv_heads_l};
-      e = consume(m_qkv, c->tm_wqkv[0], c->tm_wqkv[1], c->n_qkv, l, ep);
+      e = consume(p_qkv, c->tm_wqkv[0], c->tm_wqkv[1], c->n_qkv, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
@@ -1052,7 +1218,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if ((e = add_norm(c->gamma + (size_t)l * 2 * d + d)) != cudaSuccess) return e;
     {
       EpiSwiglu ep{c->g, hid};
-      e = consume(m_13, c->tm_w13[0], c->tm_w13[1], 2 * hid, l, ep);
+      e = consume(p_13, c->tm_w13[0], c->tm_w13[1], 2 * hid, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
@@ -1065,8 +1231,8 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   }
   if ((e = add_norm(c->gamma_final)) != cudaSuccess) return e;
 
-  const int m_head = pick_mode(T, V, di);
-  const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
+  const GemmPlan p_head = plan_gemm("head", T, V, d, di, false, can_fix);
+  const int nparts = (V + mode_block_n(p_head.mode) - 1) / mode_block_n(p_head.mode);
   {
     EpiCrossEntropy ep{};
     ep.part = c->ce_part;
@@ -1074,7 +1240,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     ep.targets = c->targets;
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
-    e = consume(m_head, c->tm_embed[0], c->tm_embed[1], V, 0, ep);
+    e = consume(p_head, c->tm_embed[0], c->tm_embed[1], V, 0, ep);
     if (e != cudaSuccess) return e;
     mark(K_GEMM_HEAD, 2.0 * Td * V * d, Td * d * 2 + (double)V * d * 2 + Td * nparts * 8 + Td * 8);
   }
@@ -1375,6 +1541,11 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
   CREATE_CUDA(dmalloc(&ctx->rope, (size_t)S * 64));
   CREATE_CUDA(dmalloc(&ctx->rope_pm, (size_t)S * 64));
   CREATE_CUDA(dmalloc(&ctx->dev_err, 1));
+  if (ctx->tp_world == 1) {  // split-K reduction of the fused single-GPU forward
+    CREATE_CUDA(dmalloc(&ctx->fix_ws, FIX_WS_BYTES / sizeof(float4)));
+    CREATE_CUDA(dmalloc(&ctx->fix_cnt, (size_t)FIX_COUNTERS));
+    CREATE_CUDA(cudaMemset(ctx->fix_cnt, 0, FIX_COUNTERS * sizeof(int)));
+  }
   CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_loss), sizeof(float)));
   CREATE_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ctx->h_err), sizeof(int)));
   CREATE_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int)));
@@ -1834,6 +2005,7 @@ static cb_status read_device_error(cb_ctx* ctx) {
   if (*ctx->h_err != 0) {
     const int code = *ctx->h_err;
     cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream);
+    reset_split_counters(ctx, ctx->stream);
     cudaStreamSynchronize(ctx->stream);
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 code == DEV_ERR_BAD_TOKEN ? "token id out of range in the token data"
@@ -2031,6 +2203,7 @@ cb_status cb_forward_loss(cb_ctx* ctx, const uint32_t* tokens, const uint32_t* t
   if (*ctx->h_err != 0) {
     int code = *ctx->h_err;
     cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), st);
+    reset_split_counters(ctx, st);
     cudaStreamSynchronize(st);
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 "device error flag " + std::to_string(code));
@@ -2070,6 +2243,7 @@ cb_status cb_check_device_error(cb_ctx* ctx) {
   if (*ctx->h_err != 0) {
     int code = *ctx->h_err;
     cudaMemset(ctx->dev_err, 0, sizeof(int));
+    reset_split_counters(ctx, nullptr);
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 "device error flag " + std::to_string(code));
   }
@@ -2126,6 +2300,7 @@ cb_status cb_selftest_wait_timeout(cb_ctx* ctx, uint32_t limit_us) {
   if (*ctx->h_err != 0) {
     const int code = *ctx->h_err;
     CB_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream));
+    reset_split_counters(ctx, ctx->stream);
     CB_CUDA(cudaStreamSynchronize(ctx->stream));
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 "self-test: a device wait expired after " + std::to_string(limit_us) +

@@ -785,6 +785,98 @@ struct RowScaled {
   __device__ __forceinline__ void end_row(int row, int n_blk) { in.end_row(row, n_blk); }
 };
 
+// Split-K with a last-arrival reduction, for the fused epilogues that need whole sums
+// (residual + norm, RoPE, SwiGLU, cross-entropy) when a GEMM has too few tiles to fill
+// the GPU. Work unit = (tile, K split). Every unit writes its fp32 partial accumulator to
+// `ws` (slab [tile][rank][split], laid out [chunk][float4 column group][row] so that each
+// warp store and load covers 512 contiguous bytes), then adds 1 to the tile's counter in
+// `cnt`. The unit that brings the counter to `splits` adds the partials in split order
+// (0, 1, ..., its own taken from TMEM) and runs the epilogue; it also resets the counter
+// for the next launch. No unit ever waits for another, and the summation order is fixed,
+// so results are bit-reproducible. ws = nullptr: plain (unsplit or accumulating) units.
+struct SplitFix {
+  float4* ws;
+  int* cnt;
+};
+
+// Split-K helpers (only the FIX instantiations of the kernel contain them).
+// splitfix_write: the thread's row of the first n_chunks 32-column chunks of the TMEM
+// accumulator at t_row into its slab (dst = slab + row; float4 group j of chunk c at
+// dst[(c * 8 + j) * 128]).
+__device__ __forceinline__ void splitfix_write(uint32_t t_row, int n_chunks, float4* dst) {
+#pragma unroll 1
+  for (int c = 0; c < n_chunks; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    tmem_ld_wait_regs(r);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcg(dst + ((size_t)c * 8 + j) * 128,
+             make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+  }
+}
+
+// splitfix_reduce: the accumulator's first n_chunks chunks replaced by the sum of all
+// splits' partials in split order (slab s at slab0 + s * slab_f4 float4s; this unit's own,
+// my_split, read from TMEM), in 16-column halves; the next split's loads are issued
+// before the current one's adds.
+__device__ __forceinline__ void splitfix_reduce(uint32_t t_row, int n_chunks, const float4* slab0,
+                                             int slab_f4, int splits, int my_split, int rr) {
+#pragma unroll 1
+  for (int h = 0; h < 2 * n_chunks; ++h) {
+    const int c = h >> 1;
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(t_row + h * 16, r);
+    float4 nxt[4];
+    auto load = [&](int sp) {
+      const float4* src = slab0 + (size_t)sp * slab_f4 + ((size_t)c * 8 + (h & 1) * 4) * 128 + rr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) nxt[j] = __ldcg(src + j * 128);
+    };
+    int loaded = -1;  // the split whose half is in (or on its way to) nxt
+    if (my_split != 0) {
+      load(0);
+      loaded = 0;
+    }
+    tmem_ld_wait_regs16(r);
+    float acc[16];
+#pragma unroll 1
+    for (int sp = 0; sp < splits; ++sp) {
+      float t[16];
+      if (sp == my_split) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = __uint_as_float(r[i]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[4 * j] = nxt[j].x;
+          t[4 * j + 1] = nxt[j].y;
+          t[4 * j + 2] = nxt[j].z;
+          t[4 * j + 3] = nxt[j].w;
+        }
+      }
+      int o = sp + 1;  // the next split read from memory
+      if (o == my_split) ++o;
+      if (o < splits && o != loaded) {
+        load(o);
+        loaded = o;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = (sp == 0) ? t[i] : acc[i] + t[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(acc[i]);
+    tmem_st_32x32b_x16(t_row + h * 16, r);
+  }
+}
+
+template <class Epi>
+struct EpiCanFix {
+  static constexpr bool value =
+      !EpiAtomic<Epi>::value && !EpiHasSplit<Epi>::value && EpiInBytes<Epi>::value == 0;
+};
+
 // ------------------------------------------------------------------ kernel
 //
 // One body, two modes:
@@ -811,11 +903,11 @@ constexpr int GEMM_A_MN = 1;
 constexpr int GEMM_B_MN = 2;
 constexpr int MN_BOX_BYTES = 64 * 64 * 2;
 
-template <int BN, bool PAIR, class Epi, int LAYOUT = 0>
+template <int BN, bool PAIR, class Epi, int LAYOUT = 0, bool FIX = false>
 __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
                                              const CUtensorMap* tmC, const CUtensorMap* tmD,
                                              int M, int N, int K, int b_z, int splits,
-                                             const Epi& epi, int* err) {
+                                             const Epi& epi, SplitFix fix, int* err) {
   constexpr bool TIN = EpiTmaIn<Epi>::value;
   using Cfg = GemmCfg<BN, PAIR, TIN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -834,6 +926,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  static_assert((2 * STAGES + 5) * 8 + 4 <= 160, "barriers overlap the split-K flags");
   uint64_t* in_bar = reinterpret_cast<uint64_t*>(bar_base + 256);  // TMA_IN: 2 per epilogue warp
   uint8_t* epi_bufs = bar_base + Cfg::BAR_BYTES;
 
@@ -860,6 +953,13 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
       mbar_init(&tempty[a], (PAIR ? 2 : 1) * 4);
     }
     mbar_init(drain, 1);
+    if constexpr (FIX) {  // split-K hand-offs of the two epilogue groups
+      uint64_t* fb = reinterpret_cast<uint64_t*>(bar_base + 176);
+      mbar_init(&fb[0], 4);
+      mbar_init(&fb[1], 4);
+      mbar_init(&fb[2], 1);
+      mbar_init(&fb[3], 1);
+    }
     if constexpr (TIN) {
       for (int i = 0; i < 2 * GEMM_EPI_WARPS; ++i) mbar_init(&in_bar[i], 1);
     }
@@ -1016,12 +1116,30 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
     uint64_t* my_in_bar = in_bar + (warp - 2) * 2;
     uint8_t* my_in = in_slots + (warp - 2) * 2 * Cfg::IN_SLOT_BYTES;
     uint32_t in_issued = 0, in_used = 0;
+    // Split-K reduction (SplitFix), in the barrier area after the barriers and the TMEM
+    // slot (which end below byte 160): each group's "this unit arrived last" flag, and
+    // its two hand-off barriers (four warps' partials written -> flag decided).
+    volatile int* fix_last = reinterpret_cast<volatile int*>(bar_base + 160);
+    uint64_t* fix_written = reinterpret_cast<uint64_t*>(bar_base + 176) + group;
+    uint64_t* fix_decided = reinterpret_cast<uint64_t*>(bar_base + 192) + group;
+    uint32_t fix_ph = 0;
+    // FIX: the instantiation for split units with the last-arrival reduction; the
+    // others are compiled without it (no register cost on the unsplit paths).
+    constexpr bool CAN_FIX = FIX && EpiCanFix<Epi>::value;
+    const bool fixing = CAN_FIX && fix.ws != nullptr && splits > 1;
+    const int rr = quad * 32 + lane;  // the row this thread owns within the CTA's 128
     for (int u = unit; u < num_tiles; u += n_units, ++it) {
       if ((it & 1) != group) continue;
       const int tile = u / splits;
+      const int my_split = u % splits;
       const int m_blk = tile / n_tiles;
       const int n_blk = tile % n_tiles;
       const int row0w = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32;
+      const int slab_tile = tile * (PAIR ? 2 : 1) + (int)rank;
+      // slab s of this tile: 128 rows x BN fp32 as [chunk][8 float4 groups][128 rows]
+      auto slab = [&](int s) -> float4* {
+        return fix.ws + ((size_t)slab_tile * splits + s) * (size_t)(GEMM_BM * BN / 4);
+      };
       auto in_issue = [&](int c) {
         if constexpr (TIN) {
           const int col = n_blk * BN + c * 32;
@@ -1036,8 +1154,10 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
           }
         }
       };
-      in_issue(0);
-      in_issue(1);
+      if (!fixing) {  // a split unit learns only after its accumulator whether it reduces
+        in_issue(0);
+        in_issue(1);
+      }
       // Per-row setup and the first chunk's global loads go out before the accumulator
       // is ready, so their latency hides behind the wait.
       const int row = m_blk * TILE_M + (int)rank * GEMM_BM + quad * 32 + lane;
@@ -1108,11 +1228,59 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
         }
       };
       const int col_base = n_blk * BN;
-      if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
+      if (!fixing && row_ok && col_base < N) e.prefetch(row, col_base, pa);
       issue_in(col_base);
       if (!mbar_wait(&tfull[group], ph, err)) break;
       ph ^= 1u;
       tc_fence_after();
+      if constexpr (CAN_FIX) {
+        if (fixing) {
+          // this unit's partial out to its slab (raw accumulator: the row scale and the
+          // epilogue apply to the sum)
+          const int n_chunks = min(NC, (N - col_base + 31) / 32);
+          splitfix_write(t_row, n_chunks, slab(my_split) + rr);
+          __threadfence();  // the partial is visible device-wide before the arrival
+          // The group's four warps hand over through mbarriers with bounded waits (a warp
+          // that gives up on an error never leaves the others waiting without a limit).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(fix_written);
+          if (quad == 0 && lane == 0) {
+            int last = -1;  // -1: the hand-off failed (an expired wait)
+            if (mbar_wait(fix_written, fix_ph, err)) {
+              const int old = atomicAdd(&fix.cnt[slab_tile], 1);
+              last = old == splits - 1;
+              if (last) fix.cnt[slab_tile] = 0;  // all splits arrived: zero for the next launch
+            }
+            fix_last[group] = last;
+            mbar_arrive(fix_decided);
+          }
+          const bool decided = mbar_wait(fix_decided, fix_ph, err);
+          fix_ph ^= 1u;
+          const int last_flag = decided ? fix_last[group] : -1;
+          if (last_flag < 0) break;
+          if (!last_flag) {  // another split reduces this tile: hand the TMEM back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (PAIR) mbar_arrive_cluster(tempty_addr);
+              else mbar_arrive(&tempty[group]);
+            }
+            continue;
+          }
+          __threadfence();  // the other splits' partials, published before their arrivals
+          // Sum of all splits' partials in split order, this unit's own taken from TMEM,
+          // written back over the accumulator: the epilogue below then runs unchanged.
+          // The next split's loads are issued before the current one's adds.
+          splitfix_reduce(t_row, n_chunks, slab(0), GEMM_BM * BN / 4, splits, my_split, rr);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          tc_fence_after();
+          in_issue(0);
+          in_issue(1);
+          if (row_ok && col_base < N) e.prefetch(row, col_base, pa);
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < NC; c += 2) {
         const int col_b = col_base + (c + 1) * 32;
@@ -1150,22 +1318,24 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
 }
 
 // tmC, tmD: the TMA_IN epilogue's in/out matrix and its second output (unused otherwise).
-template <int BN, class Epi, int LAYOUT = 0>
+template <int BN, class Epi, int LAYOUT = 0, bool FIX = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
-                   int M, int N, int K, int b_z, int splits, Epi epi, int* err) {
-  gemm_tn_body<BN, false, Epi, LAYOUT>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi, err);
+                   int M, int N, int K, int b_z, int splits, Epi epi, SplitFix fix, int* err) {
+  gemm_tn_body<BN, false, Epi, LAYOUT, FIX>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi,
+                                            fix, err);
 }
 
-template <class Epi, int LAYOUT = 0>
+template <class Epi, int LAYOUT = 0, bool FIX = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC,
                         const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int b_z,
-                        int splits, Epi epi, int* err) {
-  gemm_tn_body<256, true, Epi, LAYOUT>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi, err);
+                        int splits, Epi epi, SplitFix fix, int* err) {
+  gemm_tn_body<256, true, Epi, LAYOUT, FIX>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi,
+                                            fix, err);
 }
 
 }  // namespace cb
