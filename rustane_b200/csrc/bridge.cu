@@ -595,12 +595,23 @@ bool plan_override(const char* cls, GemmPlan* out) {
 // splits that leave each unit at least 8 k-blocks and fit the reduction's workspace.
 // Deterministic: the same shapes always give the same plan, so the summation order and
 // the loss bits do not change from call to call.
+// The split count the kernel actually runs: with kb_per = ceil(kb / splits) k-blocks per
+// unit, ceil(kb / kb_per) units cover K, and every one of them gets at least one k-block
+// (a unit with none would hand over an accumulator it never wrote).
+int effective_splits(int K, int splits) {
+  const int kb = (K + GEMM_BK - 1) / GEMM_BK;
+  if (splits <= 1 || kb <= 1) return 1;
+  const int kb_per = (kb + splits - 1) / splits;
+  return (kb + kb_per - 1) / kb_per;
+}
+
 GemmPlan plan_gemm(const char* cls, int M, int N, int K, const DeviceInfo& di, bool tin,
                    bool can_split) {
   GemmPlan best;
   if (plan_override(cls, &best)) {
     if (best.mode != GM_SINGLE128 && N % 256 != 0) best.mode = GM_SINGLE128;
     if (tin && best.mode == GM_SINGLE256) best.mode = GM_SINGLE128;
+    best.splits = effective_splits(K, best.splits);
     if (!can_split || !plan_fits(best.mode, best.splits, M, N)) best.splits = 1;
     return best;
   }
@@ -612,6 +623,7 @@ GemmPlan plan_gemm(const char* cls, int M, int N, int K, const DeviceInfo& di, b
     if (tin && mode == GM_SINGLE256) continue;
     for (int sp = 1; sp <= (can_split ? 8 : 1); ++sp) {
       if (sp > 1 && (kb + sp - 1) / sp < 8) break;
+      if (effective_splits(K, sp) != sp) continue;
       if (!plan_fits(mode, sp, M, N)) continue;
       const double c = plan_cost(mode, sp, M, N, K, di, tin);
       if (c < best_cost * 0.97) {  // a split must win clearly

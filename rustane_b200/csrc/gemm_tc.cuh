@@ -938,7 +938,8 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   const int m_tiles = (M + TILE_M - 1) / TILE_M;
   const int n_tiles = (N + BN - 1) / BN;
   // Work unit = (tile, K split): unit u covers tile u / splits and k-blocks
-  // [split * kb_per, ...) of it. splits > 1 only with an accumulating epilogue.
+  // [split * kb_per, ...) of it. splits > 1 only with an accumulating, partial-buffer or
+  // SplitFix epilogue; the host keeps splits <= ceil(kb / kb_per), so no unit is empty.
   const int num_tiles = m_tiles * n_tiles * splits;
   const int kb_total = (K + GEMM_BK - 1) / GEMM_BK;
   const int kb_per = (kb_total + splits - 1) / splits;
