@@ -381,7 +381,7 @@ cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, 
                            int bz, const Epi& epi, int* err, int units, int splits,
                            cudaStream_t st, const CUtensorMap* tc = nullptr,
                            const CUtensorMap* td = nullptr, bool pdl = false,
-                           SplitFix fix = SplitFix{}, L2Next pf = L2Next{}) {
+                           SplitFix fix = SplitFix{}) {
   using Cfg = GemmCfg<BN, false, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   const int grid = tiles < units ? tiles : units;
@@ -389,11 +389,11 @@ cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, int M, 
     if (fix.ws && splits > 1)
       return launch_k(gemm_tn_kernel<BN, Epi, LAYOUT, true>, dim3(grid), dim3(GEMM_THREADS),
                       Cfg::SMEM_BYTES, st, pdl, ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K,
-                      bz, splits, epi, fix, pf, err);
+                      bz, splits, epi, fix, err);
   }
   return launch_k(gemm_tn_kernel<BN, Epi, LAYOUT>, dim3(grid), dim3(GEMM_THREADS),
                   Cfg::SMEM_BYTES, st, pdl, ta, tb, tc_or_null(tc), tc_or_null(td), M, N, K, bz,
-                  splits, epi, SplitFix{}, pf, err);
+                  splits, epi, SplitFix{}, err);
 }
 
 template <class Epi, int LAYOUT = 0>
@@ -401,7 +401,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, 
                              int K, int bz, const Epi& epi, int* err, int clusters, int splits,
                              cudaStream_t st, const CUtensorMap* tc = nullptr,
                              const CUtensorMap* td = nullptr, bool pdl = false,
-                             SplitFix fix = SplitFix{}, L2Next pf = L2Next{}) {
+                             SplitFix fix = SplitFix{}) {
   using Cfg = GemmCfg<256, true, EpiTmaIn<Epi>::value>;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256) * splits;
   const int pairs = tiles < clusters ? tiles : clusters;
@@ -409,11 +409,11 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, 
     if (fix.ws && splits > 1)
       return launch_k(gemm_tn_pair_kernel<Epi, LAYOUT, true>, dim3(2 * pairs),
                       dim3(GEMM_THREADS), Cfg::SMEM_BYTES, st, pdl, ta, tb_half, tc_or_null(tc),
-                      tc_or_null(td), M, N, K, bz, splits, epi, fix, pf, err);
+                      tc_or_null(td), M, N, K, bz, splits, epi, fix, err);
   }
   return launch_k(gemm_tn_pair_kernel<Epi, LAYOUT>, dim3(2 * pairs), dim3(GEMM_THREADS),
                   Cfg::SMEM_BYTES, st, pdl, ta, tb_half, tc_or_null(tc), tc_or_null(td), M, N, K,
-                  bz, splits, epi, SplitFix{}, pf, err);
+                  bz, splits, epi, SplitFix{}, err);
 }
 
 // Tile mode for an M x N GEMM: the best of (last-wave fill) x (per-tile operand
@@ -454,17 +454,17 @@ cudaError_t launch_gemm(int mode, const CUtensorMap& ta, const CUtensorMap& tb12
                         const CUtensorMap& tb256, int M, int N, int K, int bz, const Epi& epi,
                         int* err, const DeviceInfo& di, cudaStream_t st, int splits = 1,
                         const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr,
-                        bool pdl = false, SplitFix fix = SplitFix{}, L2Next pf = L2Next{}) {
+                        bool pdl = false, SplitFix fix = SplitFix{}) {
   if (mode == GM_PAIR)
     return launch_gemm_pair<Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.pair_clusters,
-                                         splits, st, tc, td, pdl, fix, pf);
+                                         splits, st, tc, td, pdl, fix);
   if (mode == GM_SINGLE128)
     return launch_gemm_bn<128, Epi, LAYOUT>(ta, tb128, M, N, K, bz, epi, err, di.sms, splits, st,
-                                            tc, td, pdl, fix, pf);
+                                            tc, td, pdl, fix);
   if (EpiTmaIn<Epi>::value)  // 128 x 256 tiles leave no shared memory for the input boxes
     return cudaErrorInvalidConfiguration;
   return launch_gemm_bn<256, Epi, LAYOUT>(ta, tb256, M, N, K, bz, epi, err, di.sms, splits, st,
-                                          tc, td, pdl, fix, pf);
+                                          tc, td, pdl, fix);
 }
 
 // Tile mode and K split for a row-parallel projection (O or down) whose epilogue can
@@ -510,7 +510,7 @@ void pick_projection(int M, int N, int K, const DeviceInfo& di, int* mode, int* 
 // ------------------------------------------------------- split-K plans (SplitFix)
 // Workspace of the last-arrival split-K reduction: fp32 partial slabs (kept small enough
 // to stay in L2 between the write and the read) and one arrival counter per tile half.
-constexpr size_t FIX_WS_BYTES = 128u << 20;
+constexpr size_t FIX_WS_BYTES = 64u << 20;
 constexpr int FIX_COUNTERS = 16384;
 
 struct GemmPlan {
@@ -557,17 +557,6 @@ double plan_cost(int mode, int splits, int M, int N, int K, const DeviceInfo& di
     t_tail += nc * 1.0 * (splits - 1);     // the last unit's reads of the others
   }
   return waves * t_unit + t_tail;
-}
-
-// Next-weights L2 prefetch (L2Next in gemm_tc.cuh) for forwards of at most this many
-// tokens: their GEMMs wait on the latency of DRAM loads, not on the tensor pipe.
-// CB_L2_PREFETCH=0|1 overrides (read whenever a forward is planned).
-constexpr int L2PF_MAX_TOKENS = 8192;
-
-bool want_l2_prefetch(int T) {
-  const char* e = getenv("CB_L2_PREFETCH");
-  if (e) return atoi(e) != 0;
-  return T <= L2PF_MAX_TOKENS;
 }
 
 // Tuning override for tests and sweeps: CB_GEMM_PLAN="qkv=128x2,o=pairx1,w13=...,down=...,
@@ -1142,12 +1131,6 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     pick_projection(T, d, hid, di, &m_2, &s_2, 2);
   }
   const GemmPlan p_13 = plan_gemm("w13", T, 2 * hid, d, di, false, can_fix);
-  // each GEMM prefetches the weight slab of the GEMM after it (few tokens only)
-  const bool l2pf = !tp && want_l2_prefetch(T);
-  auto next_w = [&](const __half* w, size_t elems) -> L2Next {
-    if (!l2pf) return L2Next{};
-    return L2Next{reinterpret_cast<const uint8_t*>(w), (uint64_t)elems * sizeof(__half)};
-  };
   const double attn_flops = 2.0 * 2.0 * (double)batch * c->heads_l * 128.0 * S * (S + 1) / 2.0;
 
   // GEMMs use programmatic dependent launch (setup overlaps the previous kernel's tail)
@@ -1156,16 +1139,16 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   bool fused_last = false;  // the last projection used the fused epilogue
   bool xn_scaled = false;   // xn holds fp16(x o gamma): consumers scale rows by 1/rms
   auto consume = [&](const GemmPlan& plan, const CUtensorMap& tb128, const CUtensorMap& tb256,
-                     int N, int layer, const auto& inner, L2Next pf) -> cudaError_t {
+                     int N, int layer, const auto& inner) -> cudaError_t {
     using E = std::decay_t<decltype(inner)>;
     const SplitFix f = plan.splits > 1 ? fix : SplitFix{};
     if (xn_scaled) {
       RowScaled<E> ep{inner, c->ss_part, d / 128, (float)d, RMS_EPS, 1.f};
       return launch_gemm(plan.mode, c->tm_xn, tb128, tb256, T, N, d, layer, ep, c->dev_err, di,
-                         st, plan.splits, nullptr, nullptr, pdl, f, pf);
+                         st, plan.splits, nullptr, nullptr, pdl, f);
     }
     return launch_gemm(plan.mode, c->tm_xn, tb128, tb256, T, N, d, layer, inner, c->dev_err, di,
-                       st, plan.splits, nullptr, nullptr, pdl, f, pf);
+                       st, plan.splits, nullptr, nullptr, pdl, f);
   };
 
   // Row-parallel projection (O or down): alpha * A * B^T into the delta buffer. fp16
@@ -1175,14 +1158,14 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
   bool delta_f32 = false;
   auto project = [&](int mode, int splits, const CUtensorMap& ta, const CUtensorMap& tb128,
                      const CUtensorMap& tb256, int K, int layer, int cls,
-                     const float* gamma_next, L2Next pf) -> cudaError_t {
+                     const float* gamma_next) -> cudaError_t {
     cudaError_t r;
     fused_last = fuse_norm && (splits == 1 || can_fix);
     delta_f32 = !fused_last && (tp || splits > 1);
     if (fused_last) {
       EpiResidualNorm ep{gamma_next, c->ss_part, d / 128, alpha, 0.f};
       r = launch_gemm(mode, ta, tb128, tb256, T, d, K, layer, ep, c->dev_err, di, st, splits,
-                      &c->tm_x, &c->tm_xh, pdl, splits > 1 ? fix : SplitFix{}, pf);
+                      &c->tm_x, &c->tm_xh, pdl, splits > 1 ? fix : SplitFix{});
       if (r != cudaSuccess) return r;
       mark(cls, 2.0 * Td * d * K,
            Td * K * 2 + (double)d * K * 2 + Td * d * (4 + 4 + 2) + Td * (d / 128) * 4);
@@ -1228,8 +1211,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     __half* vl = kv ? kv->v + (size_t)l * kv->layer_stride : c->v;
     {
       EpiQkvRope ep{c->q, kl, vl, c->rope, S, c->heads_l, c->kv_heads_l};
-      e = consume(p_qkv, c->tm_wqkv[0], c->tm_wqkv[1], c->n_qkv, l, ep,
-                  next_w(c->wo + l * wo_layer_elems(c), wo_layer_elems(c)));
+      e = consume(p_qkv, c->tm_wqkv[0], c->tm_wqkv[1], c->n_qkv, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_QKV, 2.0 * Td * c->n_qkv * d,
            Td * d * 2 + (double)c->n_qkv * d * 2 + Td * c->n_qkv * 2);
@@ -1243,21 +1225,17 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if (e != cudaSuccess) return e;
     mark(K_ATTN, attn_flops, Td * (c->q_dim + 2 * c->kv_dim) * 2 + Td * c->q_dim * 2);
     e = project(m_o, s_o, c->tm_attn, c->tm_wo[0], c->tm_wo[1], c->q_dim, l, K_GEMM_O,
-                c->gamma + (size_t)l * 2 * d + d,
-                next_w(c->w13 + l * w13_layer_elems(c), w13_layer_elems(c)));
+                c->gamma + (size_t)l * 2 * d + d);
     if (e != cudaSuccess) return e;
     if ((e = add_norm(c->gamma + (size_t)l * 2 * d + d)) != cudaSuccess) return e;
     {
       EpiSwiglu ep{c->g, hid};
-      e = consume(p_13, c->tm_w13[0], c->tm_w13[1], 2 * hid, l, ep,
-                  next_w(c->w2 + l * w2_layer_elems(c), w2_layer_elems(c)));
+      e = consume(p_13, c->tm_w13[0], c->tm_w13[1], 2 * hid, l, ep);
       if (e != cudaSuccess) return e;
       mark(K_GEMM_W13, 2.0 * Td * 2 * hid * d, Td * d * 2 + 2.0 * hid * d * 2 + Td * hid * 2);
     }
     const float* g_next = l + 1 < L ? c->gamma + (size_t)(l + 1) * 2 * d : c->gamma_final;
-    e = project(m_2, s_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2, g_next,
-                l + 1 < L ? next_w(c->wqkv + (l + 1) * wqkv_layer_elems(c), wqkv_layer_elems(c))
-                          : next_w(c->embed, (size_t)V * d));
+    e = project(m_2, s_2, c->tm_g, c->tm_w2[0], c->tm_w2[1], hid, l, K_GEMM_W2, g_next);
     if (e != cudaSuccess) return e;
     if (l + 1 < L) {  // residual add + RMSNorm(gamma1) of the next layer
       if ((e = add_norm(g_next)) != cudaSuccess) return e;
@@ -1274,7 +1252,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     ep.targets = c->targets;
     ep.tgt_logit = c->tgt_logit;
     ep.softcap = softcap;
-    e = consume(p_head, c->tm_embed[0], c->tm_embed[1], V, 0, ep, L2Next{});
+    e = consume(p_head, c->tm_embed[0], c->tm_embed[1], V, 0, ep);
     if (e != cudaSuccess) return e;
     mark(K_GEMM_HEAD, 2.0 * Td * V * d, Td * d * 2 + (double)V * d * 2 + Td * nparts * 8 + Td * 8);
   }

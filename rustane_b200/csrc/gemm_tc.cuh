@@ -871,26 +871,6 @@ __device__ __forceinline__ void splitfix_reduce(uint32_t t_row, int n_chunks, co
   }
 }
 
-// L2 prefetch of the weights the NEXT kernel will read (forward GEMMs with few tokens):
-// such a GEMM is bound by the latency of its TMA loads from DRAM, and with the next
-// weight slab already in L2 the next kernel's loads come back several times sooner.
-// Weights are written by no kernel of the forward, so the prefetch may run before the
-// previous kernel has finished. Each CTA prefetches its 1/gridDim share.
-struct L2Next {
-  const uint8_t* ptr;   // 16-byte aligned
-  uint64_t bytes;       // multiple of 16
-};
-
-__device__ __forceinline__ void prefetch_share(const L2Next& pf) {
-  if (!pf.ptr || pf.bytes == 0) return;
-  const uint64_t share = ((pf.bytes + gridDim.x - 1) / gridDim.x + 15) & ~uint64_t(15);
-  const uint64_t b0 = share * blockIdx.x;
-  const uint64_t b1 = min(pf.bytes, b0 + share);
-  constexpr uint64_t CHUNK = 64 * 1024;
-  for (uint64_t o = b0; o < b1; o += CHUNK)
-    prefetch_l2_bulk(pf.ptr + o, (uint32_t)min(CHUNK, b1 - o));
-}
-
 template <class Epi>
 struct EpiCanFix {
   static constexpr bool value =
@@ -927,8 +907,7 @@ template <int BN, bool PAIR, class Epi, int LAYOUT = 0, bool FIX = false>
 __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
                                              const CUtensorMap* tmC, const CUtensorMap* tmD,
                                              int M, int N, int K, int b_z, int splits,
-                                             const Epi& epi, SplitFix fix, L2Next pf,
-                                             int* err) {
+                                             const Epi& epi, SplitFix fix, int* err) {
   constexpr bool TIN = EpiTmaIn<Epi>::value;
   using Cfg = GemmCfg<BN, PAIR, TIN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -1007,7 +986,6 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap* tmA, const CUten
   if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (warp == 2 && lane == 0) prefetch_share(pf);  // weights only: safe before pdl_enter
   pdl_enter();  // the setup above overlaps the previous kernel under PDL
 
   if (warp == 0) {
@@ -1345,10 +1323,9 @@ template <int BN, class Epi, int LAYOUT = 0, bool FIX = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
-                   int M, int N, int K, int b_z, int splits, Epi epi, SplitFix fix, L2Next pf,
-                   int* err) {
+                   int M, int N, int K, int b_z, int splits, Epi epi, SplitFix fix, int* err) {
   gemm_tn_body<BN, false, Epi, LAYOUT, FIX>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi,
-                                            fix, pf, err);
+                                            fix, err);
 }
 
 template <class Epi, int LAYOUT = 0, bool FIX = false>
@@ -1357,9 +1334,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC,
                         const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int b_z,
-                        int splits, Epi epi, SplitFix fix, L2Next pf, int* err) {
+                        int splits, Epi epi, SplitFix fix, int* err) {
   gemm_tn_body<256, true, Epi, LAYOUT, FIX>(&tmA, &tmB, &tmC, &tmD, M, N, K, b_z, splits, epi,
-                                            fix, pf, err);
+                                            fix, err);
 }
 
 }  // namespace cb

@@ -108,14 +108,6 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 // -------------------------------------------------------------------- TMA
-// Bulk prefetch of global memory into L2 (no completion to wait for): p 16-byte
-// aligned, bytes a multiple of 16.
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
-               "r"(bytes)
-               : "memory");
-}
-
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
