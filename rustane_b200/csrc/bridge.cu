@@ -646,9 +646,10 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
   CUtensorMap to;  // the output [batch*seq, heads*128] in 128-query x 64-column boxes
   if (tq && seq % FA_BQ == 0 &&
       make_tmap_rows(&to, out, (uint64_t)heads * 128, (uint64_t)batch * seq, FA_BQ)) {
-    dim3 grid((seq / FA_BQ + 1) / 2, heads, batch);  // two query tiles per CTA
+    // one CTA per block of 256 query rows (two tiles), heaviest blocks first
+    const int grid = fa_blocks(seq) * heads * batch;
     attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, to, seq, heads,
-                                                          kv_heads, scale_log2, lse, err);
+                                                          kv_heads, batch, scale_log2, lse, err);
   } else {
     dim3 grid(seq / ATT_BQ, heads, batch);
     attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(q, k, v, out, seq, heads,

@@ -105,8 +105,8 @@ def test_gemm_rejects_bad_shapes(bridge_lib):
         B.CB_ERR_INVALID_ARG
 
 
-# seq 384 and 640 give an odd number of 128-query tiles: the tcgen05 kernel pairs tiles
-# (n-1-p, p) per CTA and runs the middle one alone.
+# The tcgen05 kernel gives each CTA a block of two 128-query tiles (2m, 2m+1); seq 128,
+# 384 and 640 end in a block with one tile.
 @pytest.mark.parametrize("batch,heads,seq", [(1, 1, 64), (2, 3, 128), (1, 2, 384), (1, 12, 512),
                                              (2, 3, 640), (2, 4, 2048)])
 def test_attention_matches_torch(bridge_lib, batch, heads, seq):
@@ -189,6 +189,31 @@ def test_lm_head_ce_bad_target_is_nan(bridge_lib):
     assert torch.isnan(ptl[5]) and torch.isfinite(ptl[:5]).all()
     assert bridge_lib.cb_lm_head_ce_f16(_ptr(xf), _ptr(emb), _ptr(tgt), T, 100, V, 0.0, _ptr(ptl),
                                         None, _stream()) == B.CB_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("batch,heads,kv_heads,seq", [(1, 8, 2, 640), (2, 6, 3, 2048),
+                                                      (3, 2, 1, 128)])
+def test_attention_gqa_forward_and_lse_match_torch(bridge_lib, batch, heads, kv_heads, seq):
+    """Grouped-query attention forward with the base-2 log-sum-exp it keeps for the
+    backward pass, against float32 torch."""
+    g = torch.Generator(device="cuda").manual_seed(seq + 7 * heads + kv_heads)
+    q = torch.randn(batch, heads, seq, 128, device="cuda", generator=g).half()
+    k = torch.randn(batch, kv_heads, seq, 128, device="cuda", generator=g).half()
+    v = torch.randn(batch, kv_heads, seq, 128, device="cuda", generator=g).half()
+    out = torch.empty(batch * seq, heads * 128, device="cuda", dtype=torch.float16)
+    lse = torch.empty(batch, heads, seq, device="cuda", dtype=torch.float32)
+    assert bridge_lib.cb_attention_fwd_lse_f16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse),
+                                               batch, heads, kv_heads, seq, _stream()) == 0
+    grp = heads // kv_heads
+    kk, vv = k.float().repeat_interleave(grp, 1), v.float().repeat_interleave(grp, 1)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), kk, vv, is_causal=True)
+    ref = ref.transpose(1, 2).reshape(batch * seq, heads * 128)
+    s = (q.float() @ kk.transpose(-1, -2)) / 128 ** 0.5
+    mask = torch.ones(seq, seq, device="cuda", dtype=torch.bool).triu(1)
+    lse_ref = torch.logsumexp(s.masked_fill(mask, float("-inf")), dim=-1) / math.log(2)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=3e-3)
+    torch.testing.assert_close(lse, lse_ref, rtol=0, atol=2e-3)
 
 
 def _attn_ref(q, k, v, group):
