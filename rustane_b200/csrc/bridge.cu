@@ -646,8 +646,11 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
   CUtensorMap to;  // the output [batch*seq, heads*128] in 128-query x 64-column boxes
   if (tq && seq % FA_BQ == 0 &&
       make_tmap_rows(&to, out, (uint64_t)heads * 128, (uint64_t)batch * seq, FA_BQ)) {
-    // one CTA per block of 256 query rows (two tiles), heaviest blocks first
-    const int grid = fa_blocks(seq) * heads * batch;
+    // persistent: one CTA per SM over the blocks of 256 query rows, heaviest first
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int items = fa_blocks(seq) * heads * batch;
+    const int grid = std::min(items, num_sms_of(dev));
     attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, to, seq, heads,
                                                           kv_heads, batch, scale_log2, lse, err);
   } else {
