@@ -114,7 +114,14 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
  * shard outputs on the CPU (layer.rs:5121, 2018). Embedding, norms, residual and
  * the LM head + loss are replicated. Every rank passes the same 128-byte NCCL
  * unique id (from cb_nccl_unique_id on one rank) and must run the same sequence
- * of calls. NCCL is loaded at run time ($CB_NCCL_LIB or libnccl.so.2). */
+ * of calls. NCCL is loaded at run time ($CB_NCCL_LIB or libnccl.so.2).
+ *
+ * Failure handling: the communicator is non-blocking. Its set-up and every wait of a
+ * forward poll the stream and ncclCommGetAsyncError against a host deadline
+ * ($CB_NCCL_TIMEOUT_MS, default 120000). When a peer has left (its collective never
+ * completes) or NCCL reports an error, the communicator is aborted (ncclCommAbort makes
+ * its kernels return) and the call returns CB_ERR_NCCL; every later call on the context
+ * returns CB_ERR_NCCL at once, and the context should be destroyed. */
 cb_status cb_create_tp(const cb_model_config* cfg, int32_t device, int32_t max_batch,
                        int32_t tp_rank, int32_t tp_world, const void* nccl_unique_id,
                        cb_ctx** out);

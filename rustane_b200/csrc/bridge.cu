@@ -28,10 +28,12 @@
 #include <cmath>
 #include <cstdio>
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <type_traits>
 #include <utility>
@@ -766,6 +768,8 @@ struct cb_ctx {
   int q_off = 0, kv_off = 0, hid_off = 0;  // offsets of the share in the full model
   int tp_rank = 0, tp_world = 1;
   ncclComm_t comm = nullptr;
+  bool nccl_failed = false;  // the communicator was aborted: no further collectives
+  std::string nccl_why;      // why it was aborted
   cudaStream_t comm_stream = nullptr;           // tensor parallel: the all-reduces' stream
   cudaEvent_t tp_ev[4 * 8] = {};                // chunk hand-offs between the two streams
   float* delta32 = nullptr;  // [T, dim] fp32 partial projections, all-reduced across ranks
@@ -853,6 +857,105 @@ thread_local std::string g_create_error;
 cb_status fail(cb_ctx* c, cb_status code, const std::string& msg) {
   if (c) c->err = msg;
   return code;
+}
+
+// ---------------------------------------------- NCCL failure handling (tensor parallel)
+// A rank whose peer has left would otherwise wait in an all-reduce for good. The
+// communicator is non-blocking: every NCCL call is settled by polling
+// ncclCommGetAsyncError, and every wait for a tensor-parallel forward polls the stream
+// and the communicator's asynchronous error. On an error, or when nothing completes
+// within the deadline ($CB_NCCL_TIMEOUT_MS, default 120 s), the communicator is aborted
+// (ncclCommAbort makes its kernels return) and the call returns CB_ERR_NCCL; the
+// context then refuses further forwards with CB_ERR_NCCL. (The reference supervises its
+// workers the same way from the host: a child process with a timeout, aborted on panic,
+// crates/engine/src/bin/theory_runner.rs:9-15.)
+int nccl_timeout_ms() {
+  const char* e = getenv("CB_NCCL_TIMEOUT_MS");
+  const int v = e ? atoi(e) : 0;
+  return v > 0 ? v : 120000;
+}
+
+void nccl_abort(cb_ctx* c, const std::string& why) {
+  if (c->comm && nccl_api().abort) nccl_api().abort(c->comm);
+  c->comm = nullptr;
+  c->nccl_failed = true;
+  c->nccl_why = why;
+  c->err = why;
+}
+
+// Waits until the communicator has no operation in progress (the enqueue of a
+// non-blocking call, or the set-up of a new communicator); r is the call's own result.
+// On an error or after the deadline the communicator is aborted. Returns ncclSuccess
+// or the failure.
+ncclResult_t nccl_settle(cb_ctx* c, ncclResult_t r, const char* what) {
+  if (r != ncclSuccess && r != ncclInProgress) {
+    nccl_abort(c, std::string(what) + ": " + nccl_api().error_string(r));
+    return r;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  const auto limit = std::chrono::milliseconds(nccl_timeout_ms());
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    const ncclResult_t q = nccl_api().async_error(c->comm, &state);
+    if (q != ncclSuccess) state = q;
+    if (state == ncclSuccess) return ncclSuccess;
+    if (state != ncclInProgress) {
+      nccl_abort(c, std::string(what) + ": " + nccl_api().error_string(state));
+      return state;
+    }
+    if (std::chrono::steady_clock::now() - t0 > limit) {
+      nccl_abort(c, std::string(what) + ": no progress within " +
+                        std::to_string(nccl_timeout_ms()) + " ms");
+      return ncclInternalError;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// cudaStreamSynchronize for a context: a tensor-parallel one polls the stream and the
+// communicator instead, so that a collective whose peer has left ends in CB_ERR_NCCL.
+cb_status sync_ctx_stream(cb_ctx* c, cudaStream_t st) {
+  if (c->nccl_failed) {  // aborted earlier: never wait for good on what it left behind
+    const auto t1 = std::chrono::steady_clock::now();
+    while (cudaStreamQuery(st) == cudaErrorNotReady &&
+           std::chrono::steady_clock::now() - t1 < std::chrono::seconds(1))
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
+    return fail(c, CB_ERR_NCCL, "the tensor-parallel communicator was aborted: " + c->nccl_why);
+  }
+  if (c->tp_world == 1 || !c->comm) {
+    const cudaError_t e = cudaStreamSynchronize(st);
+    return e == cudaSuccess
+               ? CB_OK
+               : fail(c, CB_ERR_CUDA, std::string("cudaStreamSynchronize: ") + cudaGetErrorString(e));
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  const auto limit = std::chrono::milliseconds(nccl_timeout_ms());
+  std::string why;
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return CB_OK;
+    if (q != cudaErrorNotReady)
+      return fail(c, CB_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(q));
+    ncclResult_t state = ncclSuccess;
+    if (nccl_api().async_error(c->comm, &state) == ncclSuccess && state != ncclSuccess &&
+        state != ncclInProgress) {
+      why = std::string("NCCL asynchronous error: ") + nccl_api().error_string(state);
+      break;
+    }
+    if (std::chrono::steady_clock::now() - t0 > limit) {
+      why = "tensor-parallel forward made no progress within " +
+            std::to_string(nccl_timeout_ms()) + " ms (a peer rank may have left)";
+      break;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  nccl_abort(c, why);
+  // the aborted collectives return; give the stream a bounded time to drain
+  const auto t1 = std::chrono::steady_clock::now();
+  while (cudaStreamQuery(st) == cudaErrorNotReady &&
+         std::chrono::steady_clock::now() - t1 < std::chrono::seconds(10))
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  return fail(c, CB_ERR_NCCL, why);
 }
 
 // After a kernel stopped early (an expired wait), split-K arrival counters may be left
@@ -947,10 +1050,7 @@ cudaError_t enqueue_forward_tp_chunked(cb_ctx* c, int batch, int chunks, float s
   } while (0)
   auto nccl_sum = [&](float* buf, size_t n) -> cudaError_t {
     ncclResult_t nr = nccl_api().all_reduce(buf, buf, n, ncclFloat32, ncclSum, c->comm, cs);
-    if (nr != ncclSuccess) {
-      c->err = std::string("ncclAllReduce: ") + nccl_api().error_string(nr);
-      return cudaErrorUnknown;
-    }
+    if (nccl_settle(c, nr, "ncclAllReduce") != ncclSuccess) return cudaErrorUnknown;
     return cudaSuccess;
   };
   cudaEvent_t* ev_proj = c->tp_ev;               // projection of chunk j written
@@ -1193,10 +1293,7 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
     if (tp) {
       ncclResult_t nr = nccl_api().all_reduce(c->delta32, c->delta32, (size_t)T * d, ncclFloat32,
                                               ncclSum, c->comm, st);
-      if (nr != ncclSuccess) {
-        c->err = std::string("ncclAllReduce: ") + nccl_api().error_string(nr);
-        return cudaErrorUnknown;
-      }
+      if (nccl_settle(c, nr, "ncclAllReduce") != ncclSuccess) return cudaErrorUnknown;
       mark(K_ALLREDUCE, 0, Td * d * 4);
     }
     return cudaSuccess;
@@ -1611,11 +1708,14 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
     std::memcpy(&id, nccl_id, sizeof(id));
     // NCCL's all-reduces run beside the GEMMs (tp_chunked_forward): cap them at
     // TP_COMM_SMS CTAs, the SMs the GEMMs leave free while they overlap.
+    // Non-blocking: the set-up (which waits for every rank) is polled with a deadline.
     ncclResult_t nr;
     if (nccl_api().init_rank_config) {
       ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
       conf.maxCTAs = TP_COMM_SMS;
+      conf.blocking = 0;
       nr = nccl_api().init_rank_config(&ctx->comm, tp_world, id, tp_rank, &conf);
+      if (ctx->comm) nr = nccl_settle(ctx, nr, "ncclCommInitRankConfig");
     } else {
       nr = nccl_api().init_rank(&ctx->comm, tp_world, id, tp_rank);
     }
@@ -1625,15 +1725,15 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
       CREATE_CUDA(cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking));
     }
     if (nr != ncclSuccess) {
+      const std::string why = ctx->nccl_failed ? ctx->err : nccl_api().error_string(nr);
       ctx->comm = nullptr;
-      return bail(CB_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl_api().error_string(nr));
+      return bail(CB_ERR_NCCL, "ncclCommInitRank: " + why);
     }
     // One eager all-reduce so NCCL sets up its connections before any graph capture.
     nr = nccl_api().all_reduce(ctx->delta32, ctx->delta32, 1, ncclFloat32, ncclSum, ctx->comm,
                                ctx->stream);
-    if (nr != ncclSuccess)
-      return bail(CB_ERR_NCCL, std::string("ncclAllReduce: ") + nccl_api().error_string(nr));
-    CREATE_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (nccl_settle(ctx, nr, "ncclAllReduce") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
+    if (sync_ctx_stream(ctx, ctx->stream) != CB_OK) return bail(CB_ERR_NCCL, ctx->err);
   }
 
   const int nev = launches_per_forward(ctx) + 1;
@@ -1697,7 +1797,7 @@ cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t 
 cb_status cb_destroy(cb_ctx* ctx) {
   if (!ctx) return CB_OK;
   cudaSetDevice(ctx->device);
-  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->stream) sync_ctx_stream(ctx, ctx->stream);  // bounded for tensor-parallel contexts
   free_ctx(ctx);
   return CB_OK;
 }
@@ -2017,12 +2117,12 @@ static cb_status windows_forward(cb_ctx* ctx, const cb_tokens* data, size_t firs
 static cb_status read_device_error(cb_ctx* ctx) {
   CB_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost,
                           ctx->stream));
-  CB_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (const cb_status rc = sync_ctx_stream(ctx, ctx->stream); rc != CB_OK) return rc;
   if (*ctx->h_err != 0) {
     const int code = *ctx->h_err;
     cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream);
     reset_split_counters(ctx, ctx->stream);
-    cudaStreamSynchronize(ctx->stream);
+    sync_ctx_stream(ctx, ctx->stream);
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 code == DEV_ERR_BAD_TOKEN ? "token id out of range in the token data"
                                           : "device error flag " + std::to_string(code));
@@ -2135,7 +2235,7 @@ cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* tok
     if (e != cudaSuccess) rc = fail(ctx, CB_ERR_CUDA, "evaluation read-back");
   }
   if (rc == CB_OK) rc = read_device_error(ctx);
-  cudaStreamSynchronize(st);
+  sync_ctx_stream(ctx, st);
   cleanup();
   if (rc != CB_OK) return rc;
   out->loss_sum = h.loss_sum;
@@ -2146,9 +2246,12 @@ cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* tok
 }
 
 static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStream_t st) {
+  if (ctx->nccl_failed)
+    return fail(ctx, CB_ERR_NCCL, "the tensor-parallel communicator was aborted: " + ctx->nccl_why);
   if (ctx->profiling) {
     harvest(ctx);
     cudaError_t e = enqueue_forward(ctx, batch, softcap, st, true);
+    if (e != cudaSuccess && ctx->nccl_failed) return fail(ctx, CB_ERR_NCCL, ctx->err);
     if (e != cudaSuccess) return fail(ctx, CB_ERR_CUDA, std::string("forward: ") + cudaGetErrorString(e));
     ctx->pending_harvest = true;
   } else {
@@ -2164,6 +2267,7 @@ static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStre
       cudaError_t e2 = cudaStreamEndCapture(ctx->stream, &graph);
       if (e != cudaSuccess || e2 != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
+        if (ctx->nccl_failed) return fail(ctx, CB_ERR_NCCL, ctx->err);
         return fail(ctx, CB_ERR_CUDA,
                     std::string("graph capture: ") +
                         cudaGetErrorString(e != cudaSuccess ? e : e2));
@@ -2215,12 +2319,12 @@ cb_status cb_forward_loss(cb_ctx* ctx, const uint32_t* tokens, const uint32_t* t
   if (per_token_loss)
     CB_CUDA(cudaMemcpyAsync(per_token_loss, ctx->tok_loss, T * sizeof(float),
                             cudaMemcpyDeviceToHost, st));
-  CB_CUDA(cudaStreamSynchronize(st));
+  if ((rc = sync_ctx_stream(ctx, st)) != CB_OK) return rc;
   if (*ctx->h_err != 0) {
     int code = *ctx->h_err;
     cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), st);
     reset_split_counters(ctx, st);
-    cudaStreamSynchronize(st);
+    sync_ctx_stream(ctx, st);
     return fail(ctx, code == DEV_ERR_WAIT_TIMEOUT ? CB_ERR_DEVICE_TIMEOUT : CB_ERR_INVALID_ARG,
                 "device error flag " + std::to_string(code));
   }
@@ -2254,6 +2358,7 @@ cb_status cb_forward_loss_async(cb_ctx* ctx, const uint32_t* d_tokens, const uin
 cb_status cb_check_device_error(cb_ctx* ctx) {
   if (!ctx) return CB_ERR_INVALID_ARG;
   CB_CUDA(cudaSetDevice(ctx->device));
+  if (const cb_status rc = sync_ctx_stream(ctx, ctx->stream); rc != CB_OK) return rc;
   CB_CUDA(cudaDeviceSynchronize());
   CB_CUDA(cudaMemcpy(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (*ctx->h_err != 0) {
@@ -2307,7 +2412,7 @@ cb_status cb_selftest_wait_timeout(cb_ctx* ctx, uint32_t limit_us) {
   if (limit_us < 1 || limit_us > 2000000)
     return fail(ctx, CB_ERR_INVALID_ARG, "limit_us must be in [1, 2000000]");
   CB_CUDA(cudaSetDevice(ctx->device));
-  CB_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (const cb_status rc = sync_ctx_stream(ctx, ctx->stream); rc != CB_OK) return rc;
   wait_selftest_kernel<<<1, 128, 0, ctx->stream>>>((uint64_t)limit_us * 1000ull, ctx->dev_err);
   CB_CUDA(cudaGetLastError());
   CB_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost,
@@ -2338,7 +2443,7 @@ cb_status cb_sampled_logits(cb_ctx* ctx, const int32_t* rows, int32_t n_rows, fl
   const int d = ctx->cfg.dim, V = ctx->cfg.vocab;
   const int n_pad = (n_rows + 127) / 128 * 128;
   cudaStream_t st = ctx->stream;
-  CB_CUDA(cudaStreamSynchronize(st));
+  if (const cb_status rc = sync_ctx_stream(ctx, st); rc != CB_OK) return rc;
   if (n_pad > ctx->samp_cap) {
     if (ctx->samp_a) cudaFree(ctx->samp_a);
     if (ctx->samp_out) cudaFree(ctx->samp_out);

@@ -127,3 +127,64 @@ def test_tp2_two_stream_chunks_equal_one_stream(bridge_lib):
     l4, p4, _, _ = res[4]
     assert abs(l1 - l4) <= 1e-6 * l1
     np.testing.assert_allclose(p4, p1, rtol=0, atol=1e-5)
+
+
+def _tp_rank_leaves(rank, nccl_id, left, out):
+    """Rank 1 runs one forward and exits between steps (nothing of it in flight); rank 0
+    then runs its next forward, whose all-reduce has no peer."""
+    import os
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"     # no multicast objects bound to a leaving rank
+    os.environ["CB_NCCL_TIMEOUT_MS"] = "5000"
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels, CudaBridgeError
+    from rustane_b200 import bridge as B
+    cfg = custom_config(512, 1024, 4, 2, 256, 2048)
+    tok, tgt = _tokens(cfg, 2, 41)
+    k = CompiledKernels(cfg, rank, 2, tp_rank=rank, tp_world=2, nccl_id=nccl_id)
+    k.init_weights(41, CB_INIT_NORMAL, 0.02)
+    out[f"loss{rank}"] = k.forward_loss(tok, tgt)
+    if rank == 1:
+        left.set()
+        os._exit(0)  # leaves without any clean-up, like a worker that died between steps
+    left.wait(60)
+    time.sleep(2.0)  # the peer process is gone
+    t0 = time.perf_counter()
+    try:
+        k.forward_loss(tok, tgt)
+        out["status"] = B.CB_OK
+    except CudaBridgeError as e:
+        out["status"] = e.status
+        out["message"] = str(e)
+    out["seconds"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    try:
+        k.forward_loss(tok, tgt)
+        out["again"] = B.CB_OK
+    except CudaBridgeError as e:
+        out["again"] = e.status
+    out["again_seconds"] = time.perf_counter() - t0
+    k.close()
+
+
+@needs2
+def test_tp2_peer_leaving_gives_nccl_error_within_deadline(bridge_lib):
+    """A tensor-parallel rank whose peer has left gets CB_ERR_NCCL from its next forward
+    within the NCCL deadline (5 s here): the bridge polls the stream and the
+    communicator's asynchronous error and aborts the communicator, instead of waiting in
+    the all-reduce for good; the context then refuses further forwards at once."""
+    from rustane_b200 import bridge as B
+    from rustane_b200 import nccl_unique_id
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    left = ctx.Event()
+    nid = nccl_unique_id()
+    procs = [ctx.Process(target=_tp_rank_leaves, args=(r, nid, left, out)) for r in range(2)]
+    for q in procs:
+        q.start()
+    for q in procs:
+        q.join(180)
+        assert q.exitcode == 0, q.exitcode
+    assert abs(out["loss0"] - out["loss1"]) <= 1e-6 * out["loss0"]
+    assert out["status"] == B.CB_ERR_NCCL, out.get("message")
+    assert out["seconds"] < 5.0 + 15.0, out["seconds"]
+    assert out["again"] == B.CB_ERR_NCCL and out["again_seconds"] < 1.0
