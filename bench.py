@@ -66,13 +66,18 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--decode-batch", type=int, default=64,
                    help="sequences decoded together (--workload decode)")
-    p.add_argument("--workload", choices=("forward", "train", "decode", "validate", "rstk-load"),
+    p.add_argument("--attn-shape", default=None,
+                   help="batch,heads,seq for --workload attention (default: the config's "
+                        "heads and seq at --global-batch sequences)")
+    p.add_argument("--workload", choices=("forward", "train", "decode", "validate", "rstk-load",
+                                          "attention"),
                    default="forward",
                    help="forward: the headline forward+loss step; train: one training step "
                         "(forward + backward into fp32 gradients); validate: the evaluation "
                         "loop over an HBM-resident uint16 token file (val_loss + val_bpb); "
                         "rstk-load: RSTK checkpoint file -> fp16 device weights (1 GPU); "
-                        "decode: single-token steps with a KV cache after a prefill (1 GPU)")
+                        "decode: single-token steps with a KV cache after a prefill (1 GPU); "
+                        "attention: the causal attention kernel alone (cb_attention_f16, 1 GPU)")
     return p.parse_args()
 
 
@@ -442,6 +447,94 @@ def run_decode_workload(args):
     print(json.dumps(line), flush=True)
 
 
+def run_attention_workload(args):
+    """The causal attention kernel alone through the public cb_attention_f16: K launches
+    on device-resident q, k, v ([batch, heads, seq, 128] fp16, N(0, 1)), the L2 flushed
+    (a 256 MB write) before each launch, CUDA events around each launch on the launching
+    stream, the median reported. Throughput counts the causal FLOPs only,
+    4 * 128 * seq * (seq + 1) / 2 per (batch, head); peak = the measured burst bf16 GEMM
+    rate (the kernel runs alone). torch's fused SDPA (a library kernel) is timed the same
+    way on the same tensors for comparison."""
+    import ctypes as C
+    import torch
+    from rustane_b200 import bridge as B
+    from rustane_b200.model import CONFIGS
+
+    if args.gpus != 1:
+        raise SystemExit("--workload attention runs on one GPU")
+    torch.cuda.set_device(0)
+    if args.attn_shape:
+        batch, heads, seq = (int(x) for x in args.attn_shape.split(","))
+    else:
+        cfg = CONFIGS[args.config]
+        batch, heads, seq = args.global_batch, cfg.heads, cfg.seq
+    lib = B.load_library()
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    q, k, v = (torch.randn(batch, heads, seq, 128, device="cuda", generator=g).half()
+               for _ in range(3))
+    out = torch.empty(batch * seq, heads * 128, device="cuda", dtype=torch.float16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    flops = 4.0 * batch * heads * 128 * seq * (seq + 1) / 2
+
+    def ours():
+        rc = lib.cb_attention_f16(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                  C.c_void_p(v.data_ptr()), C.c_void_p(out.data_ptr()),
+                                  batch, heads, seq, C.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"cb_attention_f16 returned {rc}")
+
+    def sdpa():
+        torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+    def timed(fn, n):
+        ts = []
+        for _ in range(n):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    for _ in range(args.warmup):
+        ours()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms = timed(ours, args.steps)
+    clk = clocks.stop()
+    for _ in range(args.warmup):
+        sdpa()
+    ms_sdpa = timed(sdpa, args.steps)
+    ref = torch.nn.functional.scaled_dot_product_attention(q[:1], k[:1], v[:1], is_causal=True)
+    got = out[:seq].view(seq, heads, 128).permute(1, 0, 2)
+    err = float((got.float() - ref[0].float()).abs().max())
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tf = flops / (ms / 1e3) / 1e12
+    line = {
+        "metric": "causal attention TFLOP/s (cb_attention_f16, head dim 128)",
+        "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "fp16", "data": "synthetic (N(0,1) q, k, v)",
+        "config": {"workload": f"attention batch {batch} x heads {heads} x seq {seq} x 128",
+                   "batch": batch, "heads": heads, "seq_len": seq,
+                   "l2": "flushed (256 MB write) before every launch"},
+        "roofline": {"kernel": "attn_fwd_tc_kernel", "bound": "tensor", "achieved": round(tf, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                     "peak_source": f"bf16_tflops burst ({peak_kind})",
+                     "flops_per_launch": flops, "traffic": None},
+        "torch_sdpa": {"ms": ms_sdpa, "tflops": round(flops / (ms_sdpa / 1e3) / 1e12, 1)},
+        "max_abs_err_vs_torch_sdpa_seq0": err,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_train_workload(args):
     """Training step throughput (forward + backward, gradients accumulated on the
     device), sequence-sharded over the GPUs like the forward (data parallel: each rank
@@ -542,6 +635,9 @@ def main():
         return
     if args.workload == "decode":
         run_decode_workload(args)
+        return
+    if args.workload == "attention":
+        run_attention_workload(args)
         return
     if args.workload != "forward":
         run_io_workload(args)

@@ -129,6 +129,7 @@ pub mod ffi {
         pub fn cb_gemm_f16(a: *const c_void, b: *const c_void, c: *mut c_void, m: i32, n: i32, k: i32, out_f32: i32, block_n: i32, stream: *mut c_void) -> cb_status;
         pub fn cb_gemm_f16_layout(a: *const c_void, b: *const c_void, c: *mut c_void, m: i32, n: i32, k: i32, layout: i32, out_f32: i32, block_n: i32, stream: *mut c_void) -> cb_status;
         pub fn cb_attention_f16(q: *const c_void, k: *const c_void, v: *const c_void, out: *mut c_void, batch: i32, heads: i32, seq: i32, stream: *mut c_void) -> cb_status;
+        pub fn cb_attention_schedule(batch: i32, heads: i32, kv_heads: i32, seq: i32, sms: i32, table: *mut i32, cap: usize, grid: *mut i32, len: *mut usize) -> cb_status;
         pub fn cb_attention_fwd_lse_f16(q: *const c_void, k: *const c_void, v: *const c_void, out: *mut c_void, lse: *mut f32, batch: i32, heads: i32, kv_heads: i32, seq: i32, stream: *mut c_void) -> cb_status;
         pub fn cb_attention_bwd_f16(q: *const c_void, k: *const c_void, v: *const c_void, o: *const c_void, dout: *const c_void, lse: *const f32, dqkv: *mut c_void, batch: i32, heads: i32, kv_heads: i32, seq: i32, stream: *mut c_void) -> cb_status;
         pub fn cb_lm_head_ce_f16(xf: *const c_void, embed: *const c_void, targets: *const u32, t: i32, dim: i32, vocab: i32, softcap: f32, per_token_loss: *mut f32, loss: *mut f32, stream: *mut c_void) -> cb_status;

@@ -28,6 +28,7 @@
 #ifndef RUSTANE_CUDA_BRIDGE_H
 #define RUSTANE_CUDA_BRIDGE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -358,6 +359,20 @@ cb_status cb_gemm_f16_layout(const void* A, const void* B, void* C, int32_t M, i
  * heads*128] fp16, scale 1/sqrt(128). seq % 64 == 0. */
 cb_status cb_attention_f16(const void* q, const void* k, const void* v, void* out,
                            int32_t batch, int32_t heads, int32_t seq, void* stream);
+
+/* The work split of the attention kernel (seq % 128 == 0) on a GPU with `sms` SMs,
+ * without a GPU: its persistent CTAs (two per SM) take 128-query tiles from this table,
+ * made once per shape. Of two splits, the one whose last CTA ends first by a cost model
+ * (a tile costs its 64-key steps + 1) is used: head-major (the tiles of one head after
+ * another, latest first, dealt in rounds of alternating direction) or chunked greedy
+ * (heads in chunks whose K and V take at most 8 MB, the latest query tiles of a chunk
+ * first, each to the CTA with the least work so far). Writes into table[cap] (ints): [grid + 1]
+ * offsets, then the items ((b * heads + h) * (seq / 128) + query tile) of CTA 0, 1, ...;
+ * *grid = the CTA count, *len = the table's length. CB_ERR_INVALID_ARG for an invalid
+ * shape or a table longer than cap (*len is set either way). */
+cb_status cb_attention_schedule(int32_t batch, int32_t heads, int32_t kv_heads, int32_t seq,
+                                int32_t sms, int32_t* table, size_t cap, int32_t* grid,
+                                size_t* len);
 
 /* cb_attention_f16 that also writes lse [batch, heads, seq] (f32): the base-2
  * log-sum-exp of each query's scaled scores, lse = log2 sum_k 2^(s_k log2(e)/sqrt(128)),

@@ -42,7 +42,8 @@ EXPORTED = [
     "cb_check_device_error", "cb_selftest_wait_timeout", "cb_sampled_logits",
     "cb_set_profiling", "cb_kernel_times",
     "cb_reset_kernel_times", "cb_get_stream", "cb_last_error", "cb_create_error",
-    "cb_gemm_f16", "cb_gemm_f16_layout", "cb_attention_f16", "cb_attention_fwd_lse_f16",
+    "cb_gemm_f16", "cb_gemm_f16_layout", "cb_attention_f16", "cb_attention_schedule",
+    "cb_attention_fwd_lse_f16",
     "cb_attention_bwd_f16", "cb_lm_head_ce_f16",
     "cb_lm_head_ce_f16_noalloc", "cb_load_rstk", "cb_tokens_open", "cb_tokens_from_host",
     "cb_tokens_len", "cb_tokens_close", "cb_forward_loss_windows", "cb_eval_windows",
@@ -123,6 +124,7 @@ def load_library(path: Path | None = None) -> C.CDLL:
         "cb_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp]),
         "cb_gemm_f16_layout": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
         "cb_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+        "cb_attention_schedule": (i32, [i32, i32, i32, i32, i32, vp, C.c_size_t, vp, vp]),
         "cb_attention_fwd_lse_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "cb_attention_bwd_f16": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "cb_lm_head_ce_f16": (i32, [vp, vp, vp, i32, i32, i32, f32, vp, vp, vp]),

@@ -3,147 +3,159 @@
 // graph, crates/engine/src/kernels/sdpa_fwd.rs:223-258: scores * 1/sqrt(hd), causal
 // mask, softmax, P*V); masked keys are skipped, not added as -65504.
 //
-// Work item = one block of 256 query rows of one (batch, head): two 128-row query tiles
-// Q0, Q1 (tiles 2m and 2m+1), worked on at the same time by two softmax warpgroups and
-// fed by one stream of 128-key blocks K_j, V_j shared by both (a block of seq % 256 ==
-// 128 rows at the end of a sequence has tile 0 only). Tile t needs key blocks 0..qt_t;
-// the last block of each tile is its diagonal. The MMAs of the two tiles interleave so
-// that one tile's softmax always runs while the tensor cores work on the other tile:
-//   S0_0, S1_0, [P0_0] PV0_0, S0_1, [P1_0] PV1_0, S1_1, [P0_1] PV0_1, S0_2, ...
-// (S_t(j+1) reuses the TMEM columns of P_t(j); tcgen05 MMAs of one thread run in
-// order, so it is issued right after PV_t(j), which reads them.)
-//
-// Persistent: one CTA per SM takes items i, i + grid, i + 2 grid, ... (heaviest items,
-// the latest query rows, first). TMEM and the barriers are set up once; the next item's
-// Q tile is loaded as soon as the current item's last S of that tile has completed, and
-// its K/V blocks stream through the same rings, so one item's tail overlaps the next
-// item's start. (A CTA per item spent longer in set-up, cold loads and drain than in its
-// few key blocks at seq 512.)
-//
-// 384 threads (three warpgroups), one CTA per SM (224 KB of shared memory, all 512 TMEM
-// columns):
-//   warps 0..3    : softmax of tile 0, warps 4..7 : softmax of tile 1 (224 registers a
-//                   thread, setmaxnreg); one thread per query row (TMEM lane). Per key
-//                   block: all 128 scores of the row loaded from TMEM at once, the row
-//                   max, P = 2^(s c - m) in base 2 on the MUFU, the row sum, and P (fp16
-//                   pairs) written over the scores. Only the diagonal block takes the
-//                   causal mask (a uniform branch). The O row in TMEM is rescaled only
-//                   when the running max passes the reference max by 2^8 (lazy
-//                   rescaling); by the time S_t(j) is complete, PV_t(j-1) is too (it was
-//                   issued before), so O is stable when it is rescaled. At the end of a
-//                   tile, O / l in fp16 goes through the warpgroup's 16 KB staging buffer
-//                   in two 64-column halves, each written by one TMA store.
-//   warp 8 lane 0 : TMA producer: per item Q0, Q1, then per key block j: K_j and V_j into
-//                   two-deep rings, 128-byte swizzle.
-//   warp 9        : TMEM owner; lane 0 issues the UMMAs:
-//                     S_t = Q_t K_j^T   (M=128, N=128 keys, K=128; A and B K-major)
-//                     O_t += P_t V_j    (M=128, N=128, K=128 keys; P from TMEM where it
-//                                        overwrote S_t, V MN-major from its TMA tile)
-//   warps 8..11 run with 56 registers a thread (warps 10 and 11 have no role).
-// Every role walks the same item sequence and counts its own barrier phases.
+// Persistent: the work items are single 128-query tiles of one (batch, head). The host
+// gives every CTA a list of tiles (a schedule table, see attn_schedule in bridge.cu):
+// tiles are taken in chunks of heads whose K and V fit in L2 together, the latest (most
+// key steps) tiles of a chunk first, each assigned to the CTA with the least work so far,
+// so the CTAs finish within about one small tile of each other and the tiles that run at
+// the same time share their K and V through L2 (a CTA per pair of tiles left up to a
+// third of the SMs idle in the last wave at 8-64 sequences of 512; heaviest-first over
+// all heads at once re-read K and V from HBM for every tile). One tile's output is
+// written while the next tile's first Q K^T runs: the next Q is loaded as soon as the
+// tile's last S is done, the output is staged in the V buffers (the next tile's first V
+// waits for the store to have read them). 96 KB of shared memory and 256 TMEM columns,
+// so two CTAs share an SM (grid = min(tiles, 2 x SMs)).
+// 192 threads:
+//   warp 0 lane 0 : TMA producer. Per tile its Q (128 x 128), then per 64-key step j:
+//                   K_j one step ahead of V_j (both double-buffered), 128-byte swizzle.
+//   warp 1        : TMEM owner; lane 0 issues the UMMAs:
+//                     S_j = Q K_j^T   (M=128, N=64, K=128; A and B K-major) into one of
+//                                      two TMEM S buffers, S_{j+1} issued before P_j is
+//                                      ready so it overlaps the softmax of step j (at a
+//                                      tile boundary the tile's last PV goes first: the
+//                                      next tile's S needs its Q, loaded only then)
+//                     O  += P_j V_j   (M=128, N=128, K=64; P read from TMEM, where it
+//                                      overwrites S_j, V MN-major from its TMA tile)
+//   warps 2..5    : softmax, one thread per query row (TMEM lane): reads its 64 scores,
+//                   applies the causal mask on the diagonal steps, updates the running
+//                   max / sum in base 2 (exponentials on the MUFU), rescales its O row in
+//                   TMEM only when the max grows past the reference max by 2^8, writes P
+//                   (fp16, packed in pairs) over its S row in TMEM, and at the end of a
+//                   tile divides O by the row sum into the V buffers' shared memory, from
+//                   where one TMA store per 64 columns writes the 128 x 128 output tile.
 // Layout: q, k, v are [batch, heads, seq, 128] fp16 (rows of a [batch*heads*seq, 128]
-// matrix for the tensor maps, K and V in 128-row boxes); the output (tensor map tmO,
-// 64-column x 128-row boxes) is [batch*seq, heads*128] fp16. seq % 128 == 0.
+// matrix for the tensor maps); the output (tensor map tmO) is [batch*seq, heads*128]
+// fp16. seq % 128 == 0.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <math_constants.h>
 #include <stdint.h>
 
-#include <type_traits>
-
 #include "ptx.cuh"
 
 namespace cb {
 
-constexpr int FA_BQ = 128;   // query rows per tile
-constexpr int FA_BKV = 128;  // keys per block (rows of the K and V tensor-map boxes)
-constexpr int FA_THREADS = 384;
-// setmaxnreg budget: 2 x 128 x 224 + 128 x 56 = 64512 = 384 x 168 registers at launch
-constexpr int FA_SOFTMAX_REGS = 224;
-constexpr int FA_CONTROL_REGS = 56;
+constexpr int FA_BQ = 128;
+constexpr int FA_BKV = 64;
+constexpr int FA_THREADS = 192;
 // shared memory map (bytes from the 1024-aligned base)
-constexpr int FA_Q_OFF = 0;        // 2 tiles x 32 KB: head dims 0-63 | 64-127, [128 rows][128 B]
-constexpr int FA_K_OFF = 65536;    // 2 slots x 32 KB: dims 0-63 | 64-127, [128 keys][128 B]
-constexpr int FA_V_OFF = 131072;   // 2 slots x 32 KB, same layout (read MN-major)
-constexpr int FA_STAGE_OFF = 196608;  // 2 x 16 KB output staging, one per softmax warpgroup
-constexpr int FA_BAR_OFF = 229376;
+constexpr int FA_Q_OFF = 0;             // 2 x 16 KB: head dims 0-63 | 64-127, [128 rows][128 B]
+constexpr int FA_K_OFF = 32768;         // 2 buffers x (2 x 8 KB), [64 keys][128 B]
+constexpr int FA_V_OFF = 65536;         // 2 buffers x (2 x 8 KB): head dims 0-63 | 64-127
+constexpr int FA_BAR_OFF = 98304;
 constexpr int FA_SMEM = FA_BAR_OFF + 256 + 1024;
-constexpr uint32_t FA_TMEM_COLS = 512;  // S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512)
+constexpr uint32_t FA_TMEM_COLS = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
 
 // The O accumulator and row sum keep a stale reference max until the running max
-// exceeds it by this much (base-2 log): P values stay <= 2^8, and most blocks skip
+// exceeds it by this much (base-2 log): P values stay <= 2^8, and most tiles skip
 // the TMEM read-scale-write of O.
 constexpr float FA_RESCALE_THRESHOLD = 8.0f;
 
-// Blocks of 256 query rows per sequence.
-__host__ __device__ constexpr int fa_blocks(int seq) { return (seq / FA_BQ + 1) / 2; }
-
-// One work item: block mb of (batch b, head h); heaviest (largest mb) first.
-struct FaItem {
-  int mb, b, h, n_t, n_steps;
-  __device__ FaItem(int w, int seq, int heads, int batch) {
-    const int n_blk = fa_blocks(seq);
-    const int hb_count = heads * batch;
-    mb = n_blk - 1 - w / hb_count;
-    const int hb = w % hb_count;
-    b = hb / heads;
-    h = hb - b * heads;
-    n_t = (2 * mb + 1 < seq / FA_BQ) ? 2 : 1;  // query tiles in this block
-    n_steps = 2 * mb + n_t;                    // key blocks (tile n_t - 1 needs them all)
+// The sequence of 64-key steps one CTA works through: its tiles (see above) one after
+// the other. Every role keeps its own cursor and advances it in the same order.
+// The 64-key steps one CTA works through: the tiles of its list in the schedule table
+// (sched: [gridDim.x + 1] offsets into the items that follow them; an item is
+// (batch * heads + head) * n_qt + query tile), one after the other. Every role keeps its
+// own cursor and advances it in the same order.
+struct FaCursor {
+  const int* p;    // current item
+  const int* end;  // end of this CTA's list
+  int n_qt, heads;
+  int ord;  // tiles of this CTA before the current one
+  int qt, b, h, kt, n_kt;
+  __device__ FaCursor(const int* __restrict__ sched, int seq, int heads_)
+      : n_qt(seq / 128), heads(heads_), ord(0) {
+    const int* items = sched + gridDim.x + 1;
+    p = items + __ldg(sched + blockIdx.x);
+    end = items + __ldg(sched + blockIdx.x + 1);
+    pick();
   }
-  __device__ int qt(int t) const { return 2 * mb + t; }
-  __device__ bool active(int t, int j) const { return t < n_t && j <= qt(t); }
+  __device__ void pick() {
+    if (p < end) {
+      const int w = __ldg(p);
+      const int hb = w / n_qt;
+      qt = w - hb * n_qt;
+      b = hb / heads;
+      h = hb - b * heads;
+      kt = 0;
+      n_kt = (qt + 1) * (128 / 64);
+    }
+  }
+  __device__ bool valid() const { return p < end; }
+  __device__ bool last_step() const { return kt == n_kt - 1; }
+  __device__ void next_tile() {
+    ++p;
+    ++ord;
+    pick();
+  }
+  __device__ void next() {
+    if (++kt == n_kt) next_tile();
+  }
 };
 
-__global__ void __launch_bounds__(FA_THREADS, 1)
+__global__ void __launch_bounds__(FA_THREADS, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmO, int seq, int heads,
-                       int kv_heads, int batch, float scale_log2, float* __restrict__ lse,
-                       int* err) {
+                       int kv_heads, const int* __restrict__ sched, float scale_log2,
+                       float* __restrict__ lse, int* err) {
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FA_BAR_OFF);
-  uint64_t* q_full = bars + 0;    // [2] per tile: Q_t loaded
-  uint64_t* q_free = bars + 2;    // [2] per tile: the item's S_t MMAs done (Q_t reusable)
-  uint64_t* k_full = bars + 4;    // [2] per slot
-  uint64_t* k_empty = bars + 6;   // [2]
-  uint64_t* v_full = bars + 8;    // [2]
-  uint64_t* v_empty = bars + 10;  // [2]
-  uint64_t* s_full = bars + 12;   // [2] per tile
-  uint64_t* p_full = bars + 14;   // [2] per tile (one arrival per softmax warp)
-  uint64_t* o_final = bars + 16;  // [2] per tile: the item's last PV_t is done
-  uint64_t* drain = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 12;
+  uint64_t* drain = bars + 13;
+  uint64_t* q_empty = bars + 14;  // a tile's last S is done: the Q buffer takes the next Q
+  uint64_t* o_done = bars + 15;   // a tile's output has left the V buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_items = fa_blocks(seq) * heads * batch;
   const int group = heads / kv_heads;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_free[i], 1);
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_final[i], 1);
-    }
+    mbar_init(q_full, 1);
+    mbar_init(&k_full[0], 1);
+    mbar_init(&k_full[1], 1);
+    mbar_init(&k_empty[0], 1);
+    mbar_init(&k_empty[1], 1);
+    mbar_init(&v_full[0], 1);
+    mbar_init(&v_full[1], 1);
+    mbar_init(&v_empty[0], 1);
+    mbar_init(&v_empty[1], 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmO);
   }
-  if (warp == 9) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, FA_TMEM_COLS);
     tmem_relinquish();
   }
@@ -151,274 +163,257 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s0 = tmem, t_o = tmem + 128;
   pdl_enter();  // lets the next GEMM (launched with PDL) schedule its CTAs early
 
-  if (warp >= 8) {
-    regs_dec<FA_CONTROL_REGS>();  // the whole warpgroup 8..11
-    if (warp == 8 && lane == 0) {
-      // ---------------- producer: per item Q0, Q1 (each once the previous item's S MMAs of
-      // that tile are done), then K_j and V_j one block ahead through the rings
-      uint32_t g = 0;        // key blocks loaded so far (ring position)
-      uint32_t q_loads = 0;  // Q tiles loaded so far: tile 0 in bits 0..15, tile 1 in 16..31
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-        const FaItem it(w, seq, heads, batch);
-        const int q_row0 = (it.b * heads + it.h) * seq;
-        const int kv_row0 = (it.b * kv_heads + it.h / group) * seq;
-        for (int t = 0; t < it.n_t && ok; ++t) {
-          const uint32_t nq = (q_loads >> (16 * t)) & 0xffffu;
-          if (nq > 0 && !mbar_wait(&q_free[t], (nq - 1) & 1, err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* dst = smem + FA_Q_OFF + t * 32768;
-          mbar_arrive_expect_tx(&q_full[t], 32768);
-          tma_load_2d(dst, &tmQ, &q_full[t], 0, q_row0 + it.qt(t) * FA_BQ);
-          tma_load_2d(dst + 16384, &tmQ, &q_full[t], 64, q_row0 + it.qt(t) * FA_BQ);
-          q_loads += 1u << (16 * t);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer: per tile its Q (once the previous tile's last S is
+      // done), K one step ahead of V; a tile's first V once the previous tile's output has
+      // left the V buffers
+      FaCursor kc(sched, seq, heads), vc(sched, seq, heads);
+      uint32_t gk = 0, gv = 0;  // steps loaded (ring positions)
+      auto load_k = [&]() -> bool {
+        if (kc.kt == 0) {  // the tile's Q first
+          if (kc.ord > 0 && !mbar_wait(q_empty, (kc.ord - 1) & 1, err)) return false;
+          const int q_row = (kc.b * heads + kc.h) * seq + kc.qt * FA_BQ;
+          mbar_arrive_expect_tx(q_full, 32768);
+          tma_load_2d(smem + FA_Q_OFF, &tmQ, q_full, 0, q_row);
+          tma_load_2d(smem + FA_Q_OFF + 16384, &tmQ, q_full, 64, q_row);
         }
-        for (int j = 0; j < it.n_steps && ok; ++j, ++g) {
-          const int sl = g & 1;
-          const uint32_t ph = ((g >> 1) & 1) ^ 1u;
-          const int row = kv_row0 + j * FA_BKV;
-          if (!mbar_wait(&k_empty[sl], ph, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[sl], 32768);
-          uint8_t* kd = smem + FA_K_OFF + sl * 32768;
-          tma_load_2d(kd, &tmK, &k_full[sl], 0, row);
-          tma_load_2d(kd + 16384, &tmK, &k_full[sl], 64, row);
-          if (!mbar_wait(&v_empty[sl], ph, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[sl], 32768);
-          uint8_t* vd = smem + FA_V_OFF + sl * 32768;
-          tma_load_2d(vd, &tmV, &v_full[sl], 0, row);
-          tma_load_2d(vd + 16384, &tmV, &v_full[sl], 64, row);
-        }
+        const int kb = gk & 1;
+        if (!mbar_wait(&k_empty[kb], ((gk >> 1) & 1) ^ 1u, err)) return false;
+        const int row = (kc.b * kv_heads + kc.h / group) * seq + kc.kt * FA_BKV;
+        mbar_arrive_expect_tx(&k_full[kb], 16384);
+        uint8_t* dst = smem + FA_K_OFF + kb * 16384;
+        tma_load_2d(dst, &tmK, &k_full[kb], 0, row);
+        tma_load_2d(dst + 8192, &tmK, &k_full[kb], 64, row);
+        kc.next();
+        ++gk;
+        return true;
+      };
+      bool ok = !kc.valid() || load_k();
+      while (ok && vc.valid()) {
+        if (kc.valid() && !load_k()) break;
+        const int vb = gv & 1;
+        if (!mbar_wait(&v_empty[vb], ((gv >> 1) & 1) ^ 1u, err)) break;
+        if (vc.kt == 0 && vc.ord > 0 && !mbar_wait(o_done, (vc.ord - 1) & 1, err)) break;
+        const int row = (vc.b * kv_heads + vc.h / group) * seq + vc.kt * FA_BKV;
+        mbar_arrive_expect_tx(&v_full[vb], 16384);
+        uint8_t* vdst = smem + FA_V_OFF + vb * 16384;
+        tma_load_2d(vdst, &tmV, &v_full[vb], 0, row);
+        tma_load_2d(vdst + 8192, &tmV, &v_full[vb], 64, row);
+        vc.next();
+        ++gv;
       }
-    } else if (warp == 9 && lane == 0) {
-      // ---------------- MMA issuer
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer: S one step ahead of PV within a tile; at a tile
+      // boundary the tile's last PV first (the next tile's first S waits for its Q)
       constexpr uint32_t idesc_s = umma_idesc_f16(FA_BQ, FA_BKV);
       constexpr uint32_t idesc_pv = umma_idesc_f16_bmn(FA_BQ, 128);
-      uint32_t g = 0;       // key blocks of earlier items (ring position)
-      uint32_t q_uses = 0;  // Q tiles consumed so far, one bit of parity per tile (bit t)
-      uint32_t steps = 0;   // key blocks of each tile so far, parity per tile (p_full phase)
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-        const FaItem it(w, seq, heads, batch);
-        const int last_t = it.n_t - 1;  // the tile that uses every key block last
-        auto issue_s = [&](int t, int j) -> bool {
-          const uint32_t gj = g + (uint32_t)j;
-          if (j == 0) {
-            if (!mbar_wait(&q_full[t], (q_uses >> t) & 1u, err)) return false;
-            q_uses ^= 1u << t;
-          }
-          if (!mbar_wait(&k_full[gj & 1], (gj >> 1) & 1, err)) return false;
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(smem + FA_Q_OFF + t * 32768);
-          const uint32_t k_addr = smem_u32(smem + FA_K_OFF + (gj & 1) * 32768);
+      const uint32_t q_addr = smem_u32(smem + FA_Q_OFF);
+      const uint32_t k_addr = smem_u32(smem + FA_K_OFF);
+      const uint32_t v_addr = smem_u32(smem + FA_V_OFF);
+      FaCursor sc(sched, seq, heads), pc(sched, seq, heads);
+      uint32_t gs = 0, gp = 0;  // steps issued
+      auto issue_s = [&]() -> bool {
+        const int kb = gs & 1;
+        if (sc.kt == 0 && !mbar_wait(q_full, sc.ord & 1, err)) return false;
+        if (!mbar_wait(&k_full[kb], (gs >> 1) & 1, err)) return false;
+        tc_fence_after();
+        const uint32_t d = t_s0 + (uint32_t)(kb * FA_BKV);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {  // head dim in steps of 16
-            const uint32_t off = (uint32_t)((k >> 2) * 16384 + (k & 3) * 32);
-            umma_f16_ss(tmem + (uint32_t)(t * 128), sw128_kmajor_desc(q_addr + off),
-                        sw128_kmajor_desc(k_addr + off), idesc_s, k != 0);
-          }
-          umma_commit(&s_full[t]);
-          if (t == last_t) umma_commit(&k_empty[gj & 1]);  // both tiles' S of block j issued
-          if (j == it.qt(t)) umma_commit(&q_free[t]);      // the item's last S of tile t
-          return true;
-        };
-        auto issue_pv = [&](int t, int j) -> bool {
-          const uint32_t gj = g + (uint32_t)j;
-          if (!mbar_wait(&p_full[t], (steps >> t) & 1u, err)) return false;
-          steps ^= 1u << t;
-          if (!mbar_wait(&v_full[gj & 1], (gj >> 1) & 1, err)) return false;
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(smem + FA_V_OFF + (gj & 1) * 32768);
-          const uint32_t p_tmem = tmem + (uint32_t)(t * 128);  // P over S_t's columns
-#pragma unroll
-          for (int k = 0; k < FA_BKV / 16; ++k)  // keys in steps of 16 (8 packed columns)
-            umma_f16_ts(tmem + 256u + (uint32_t)(t * 128), p_tmem + k * 8,
-                        sw128_mnmajor_desc(v_addr + k * 2048, 16384), idesc_pv, (j | k) != 0);
-          if (t == last_t) umma_commit(&v_empty[gj & 1]);
-          if (j == it.qt(t)) umma_commit(&o_final[t]);
-          return true;
-        };
-        for (int t = 0; t < it.n_t && ok; ++t) ok = issue_s(t, 0);
-        for (int j = 0; j < it.n_steps && ok; ++j) {
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (!it.active(t, j)) continue;
-            ok = issue_pv(t, j);
-            if (ok && it.active(t, j + 1)) ok = issue_s(t, j + 1);
-          }
+        for (int k = 0; k < 8; ++k) {  // head dim in steps of 16
+          const uint32_t off = (uint32_t)((k >> 2) * 16384 + (k & 3) * 32);
+          const uint32_t koff = (uint32_t)(kb * 16384 + (k >> 2) * 8192 + (k & 3) * 32);
+          umma_f16_ss(d, sw128_kmajor_desc(q_addr + off), sw128_kmajor_desc(k_addr + koff),
+                      idesc_s, k != 0);
         }
-        g += (uint32_t)it.n_steps;
+        umma_commit(&k_empty[kb]);
+        umma_commit(&s_full[kb]);
+        if (sc.last_step()) umma_commit(q_empty);
+        sc.next();
+        ++gs;
+        return true;
+      };
+      auto issue_pv = [&]() -> bool {
+        const int vb = gp & 1;
+        if (!mbar_wait(p_full, gp & 1, err)) return false;
+        if (!mbar_wait(&v_full[vb], (gp >> 1) & 1, err)) return false;
+        tc_fence_after();
+        const uint32_t p_tmem = t_s0 + (uint32_t)(vb * FA_BKV);  // P over S's columns
+#pragma unroll
+        for (int k = 0; k < FA_BKV / 16; ++k) {  // keys in steps of 16 (8 packed columns)
+          umma_f16_ts(t_o, p_tmem + k * 8,
+                      sw128_mnmajor_desc(v_addr + vb * 16384 + k * 2048, 8192), idesc_pv,
+                      (pc.kt | k) != 0);
+        }
+        umma_commit(&v_empty[vb]);
+        umma_commit(pv_done);
+        pc.next();
+        ++gp;
+        return true;
+      };
+      bool ok = !sc.valid() || issue_s();
+      while (ok && pc.valid()) {
+        // S of the step after the one whose PV is next, unless that step opens a new tile
+        const bool s_first = sc.valid() && sc.kt != 0;
+        if (s_first && !issue_s()) break;
+        if (!issue_pv()) break;
+        if (!s_first && sc.valid() && !issue_s()) break;
       }
-      // Drain: every MMA issued here completes before TMEM is released.
       umma_commit(drain);
       mbar_wait(drain, 0, err);
     }
   } else {
-    regs_inc<FA_SOFTMAX_REGS>();
-    // ---------------- softmax warpgroups: thread = query row r (TMEM lane r) of tile t
-    const int t = warp >> 2;
+    // ---------------- softmax warps: thread = query row r (TMEM lane r)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + (uint32_t)(t * 128);
-    const uint32_t t_o = tmem + lane_off + 256u + (uint32_t)(t * 128);
-    uint8_t* stage = smem + FA_STAGE_OFF + t * 16384;  // [128 rows][128 B], 128-byte swizzle
-    uint32_t steps = 0, tiles = 0;  // s_full and o_final phases
     bool ok = true;
-    // Every warp of the group walks every item and reaches every named barrier whether or
-    // not an earlier wait failed (a failed wait only skips the work), so no warp is ever
-    // left waiting at a barrier for a warp that stopped.
-    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-      const FaItem it(w, seq, heads, batch);
-      if (t >= it.n_t) continue;
-      const int qt = it.qt(t);
+    // Every warp walks every tile and reaches the named barrier of every tile whether or
+    // not an earlier wait failed (a failed wait only skips the remaining work).
+    FaCursor cur(sched, seq, heads);
+    uint32_t g0 = 0;  // steps of the tiles before
+    for (; cur.valid(); g0 += (uint32_t)cur.n_kt, cur.next_tile()) {
+      const int qt = cur.qt;
+      const int q_idx = qt * FA_BQ + r;
+      const int n_kv = cur.n_kt;
       float m_run = -CUDART_INF_F, l_run = 0.f;
-      int j = 0;
-      float corr = 1.0f;
-      bool need = false;
-      // One key block: all 128 scores of the row from TMEM (four loads in flight, one
-      // wait), the row max of the raw scores (the scale > 0 commutes with max), the lazy
-      // rescale decision, then P = 2^(s c - m) on the MUFU, the row sum and P as fp16
-      // pairs over the scores (chunk c -> columns 16c..16c+15). Scores and exponent
-      // arguments go two lanes per instruction (f32x2) where the math allows.
-      auto softmax_block = [&](auto masked) {
-        constexpr bool MASK = decltype(masked)::value;
-        uint32_t sv[4][32];
+      for (int jt = 0; jt < n_kv && ok; ++jt) {
+        const uint32_t g = g0 + (uint32_t)jt;
+        const int kb = g & 1;
+        if (!mbar_wait(&s_full[kb], (g >> 1) & 1, err)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sa[32], sb[32];
+        tmem_ld_32x32b_x32(t_s0 + lane_off + (uint32_t)(kb * FA_BKV), sa);
+        tmem_ld_32x32b_x32(t_s0 + lane_off + (uint32_t)(kb * FA_BKV + 32), sb);
+        tmem_ld_wait_regs(sa);
+        tmem_ld_wait_regs(sb);
+        // Raw scores; the scale (> 0) commutes with max, so it is folded into the
+        // exponent argument. Reductions use 8 independent accumulators (short chains).
+        float s[64];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s + c * 32, sv[c]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_wait_regs(sv[c]);
-        if constexpr (MASK) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i > r) sv[c][i] = __float_as_uint(-CUDART_INF_F);
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(sa[i]);
+          s[32 + i] = __uint_as_float(sb[i]);
         }
-        float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+        const int key0 = jt * FA_BKV;
+        if (key0 + FA_BKV - 1 > q_idx) {  // diagonal tile: mask keys after the query
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int i = 0; i < 64; ++i)
+            if (key0 + i > q_idx) s[i] = -CUDART_INF_F;
+        }
+        float m8[8];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], __uint_as_float(sv[c][i]),
-                                     __uint_as_float(sv[c][i + 1]));
-        const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * scale_log2;
+        for (int a = 0; a < 8; ++a) m8[a] = s[a];
+#pragma unroll
+        for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
         // Lazy rescaling: move the reference max only when it is exceeded by the threshold.
-        corr = 1.0f;
-        need = false;
-        if (j == 0) {
-          m_run = mx;  // key block 0 holds key 0 <= every query, so mx is finite
+        float corr = 1.0f;
+        bool need = false;
+        if (jt == 0) {
+          m_run = mx;  // key tile 0 always holds key 0 <= every query, so mx is finite
         } else if (mx > m_run + FA_RESCALE_THRESHOLD) {
           need = true;
           corr = exp2_mufu(m_run - mx);
           m_run = mx;
           l_run *= corr;
         }
-        const float2 sc2 = make_float2(scale_log2, scale_log2);
-        const float2 nm2 = make_float2(-m_run, -m_run);
-        float2 l4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                        make_float2(0.f, 0.f)};
+        const float neg_m = -m_run;
+        float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // All exponentials on the MUFU (ex2.approx): measured faster than sending half of
+        // them to an FMA-pipe polynomial (3.45-3.50 against 3.73 ms of attention per
+        // 600m-A forward), the MUFU not being the limit here.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float2 x = ffma2(
-                make_float2(__uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1])), sc2, nm2);
-            const float2 pp = make_float2(exp2_mufu(x.x), exp2_mufu(x.y));
-            l4[(i >> 1) & 3] = fadd2(l4[(i >> 1) & 3], pp);
-            pk[i >> 1] = pack_half2(pp.x, pp.y);
-          }
-          tmem_st_32x32b_x16(t_s + c * 16, pk);
+        for (int i = 0; i < 64; i += 2) {
+          s[i] = exp2_mufu(fmaf(s[i], scale_log2, neg_m));
+          s[i + 1] = exp2_mufu(fmaf(s[i + 1], scale_log2, neg_m));
+          l8[(i >> 1) & 7] += s[i] + s[i + 1];
         }
-        const float2 la = fadd2(l4[0], l4[1]), lb = fadd2(l4[2], l4[3]);
-        l_run += (la.x + la.y) + (lb.x + lb.y);
-      };
-      for (; ok && j <= qt; ++j) {
-        if (!mbar_wait(&s_full[t], steps++ & 1, err)) { ok = false; break; }
-        tc_fence_after();
-        // The diagonal block (j == qt) masks keys 128 j + i with i > r; every other block
-        // takes the variant without the mask (a uniform branch: no per-element selects).
-        if (j == qt) softmax_block(std::true_type{});
-        else softmax_block(std::false_type{});
-        // O holds this tile's P V of the blocks before (PV_t(j-1) was issued before
-        // S_t(j) and is complete): rescale it if any row of the warp needs it.
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(t_o + c * 32, o);
-            tmem_ld_wait_regs(o);
+        const float sum = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+        l_run += sum;
+        // P (fp16 pairs) over the first 32 columns of this row of S. The PV of two steps
+        // back read this buffer and completed before this S was computed.
+        {
+          uint32_t pk[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-            tmem_st_32x32b_x32(t_o + c * 32, o);
+          for (int i = 0; i < 32; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+          tmem_st_32x32b_x32(t_s0 + lane_off + (uint32_t)(kb * FA_BKV), pk);
+        }
+        if (jt > 0) {
+          // O holds this tile's P V of the steps before once the previous PV is done:
+          // rescale it if needed.
+          if (!mbar_wait(pv_done, (g - 1) & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(t_o + lane_off + c * 32, o);
+              tmem_ld_wait_regs(o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+              tmem_st_32x32b_x32(t_o + lane_off + c * 32, o);
+            }
           }
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
+        if (lane == 0) mbar_arrive(p_full);
       }
-      // ---------------- the tile's output: O / l in fp16, 64 columns at a time through
-      // the 16 KB staging buffer (128-byte swizzled like the output tensor map), each
-      // half written by one TMA store. O is read completely before the next item's first
-      // P of this tile is handed over, which is when its first PV may overwrite O.
-      const bool fin = ok && mbar_wait(&o_final[t], tiles++ & 1, err);
-      ok = ok && fin;
-      const int o_row = it.b * seq + qt * FA_BQ;
+      // ---------------- this tile's output: O / l in fp16 into the V buffers (free once
+      // the tile's last PV is done), 128-byte swizzled like the output tensor map (two
+      // 64-column halves of [128 rows][128 B]), then one TMA store of the 128 x 128 tile.
+      const bool fin = ok && mbar_wait(pv_done, (g0 + n_kv - 1) & 1, err);
       if (fin) {
         tc_fence_after();
-        if (lse) lse[(it.b * heads + it.h) * seq + qt * FA_BQ + r] = m_run + log2f(l_run);
-      }
-      const float inv = 1.0f / l_run;
+        const float inv = __fdividef(1.0f, l_run);  // l_run >= 1: the max term is 2^0
+        // Log-sum-exp of the scaled scores in base 2 (lse2 = log2 sum_k 2^(s_k c)), kept
+        // for the backward pass: P = 2^(s c - lse2).
+        if (lse) lse[(cur.b * heads + cur.h) * seq + qt * FA_BQ + r] = m_run + __log2f(l_run);
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t o[2][32];
-        if (fin) {
-          tmem_ld_32x32b_x32(t_o + half * 64, o[0]);
-          tmem_ld_32x32b_x32(t_o + half * 64 + 32, o[1]);
-          tmem_ld_wait_regs(o[0]);
-          tmem_ld_wait_regs(o[1]);
-          // the staging buffer's previous store (if any) has finished reading it
-          if (quad == 0 && lane == 0) bulk_wait_read<0>();
-        }
-        // the four warps of this tile (every warp of the group reaches both barriers,
-        // done or not)
-        if (t == 0) named_barrier_sync_c<1>(128);
-        else named_barrier_sync_c<2>(128);
-        if (fin) {
-          uint8_t* row_p = stage + r * 128;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o + lane_off + c * 32, o);
+          tmem_ld_wait_regs(o);
+          uint8_t* half_tile = smem + FA_V_OFF + (c >> 1) * 16384 + r * 128;
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t* q = o[c] + 8 * k;
-              uint4 v4;
-              v4.x = pack_half2(__uint_as_float(q[0]) * inv, __uint_as_float(q[1]) * inv);
-              v4.y = pack_half2(__uint_as_float(q[2]) * inv, __uint_as_float(q[3]) * inv);
-              v4.z = pack_half2(__uint_as_float(q[4]) * inv, __uint_as_float(q[5]) * inv);
-              v4.w = pack_half2(__uint_as_float(q[6]) * inv, __uint_as_float(q[7]) * inv);
-              const int chunk = c * 4 + k;  // 16-byte chunk within the 128-byte row
-              *reinterpret_cast<uint4*>(row_p + ((chunk ^ (r & 7)) << 4)) = v4;
-            }
+          for (int k = 0; k < 4; ++k) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
+            const int chunk = (c & 1) * 4 + k;  // 16-byte chunk within the 128-byte row
+            *reinterpret_cast<uint4*>(half_tile + ((chunk ^ (r & 7)) << 4)) = w;
+          }
         }
-        fence_proxy_async_smem();
-        if (t == 0) named_barrier_sync_c<1>(128);
-        else named_barrier_sync_c<2>(128);
-        if (fin && quad == 0 && lane == 0) {
-          tma_store_2d(&tmO, stage, it.h * 128 + half * 64, o_row);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_barrier_sync(1, 128);  // the four softmax warps
+      if (threadIdx.x == 64) {
+        if (fin) {
+          const int o_row = cur.b * seq + qt * FA_BQ;
+          tma_store_2d(&tmO, smem + FA_V_OFF, cur.h * 128, o_row);
+          tma_store_2d(&tmO, smem + FA_V_OFF + 16384, cur.h * 128 + 64, o_row);
           bulk_commit_group();
+          bulk_wait_read<0>();  // the V buffers stay untouched until the store has read them
         }
+        mbar_arrive(o_done);  // the producer may load V again
       }
     }
-    if (quad == 0 && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, FA_TMEM_COLS);
   }

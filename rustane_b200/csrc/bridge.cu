@@ -28,6 +28,7 @@
 #include <cmath>
 #include <cstdio>
 #include <algorithm>
+#include <queue>
 #include <chrono>
 #include <cstring>
 #include <map>
@@ -640,6 +641,157 @@ GemmPlan plan_gemm(const char* cls, int M, int N, int K, const DeviceInfo& di, b
 
 // Causal attention: tcgen05 kernel when seq is a multiple of 128 (tensor maps given),
 // otherwise the mma.sync kernel.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// A driver entry point resolved once through the runtime (no -lcuda link).
+template <class Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<Fn>(p);
+  return nullptr;
+}
+
+// The current device and the id of its context as this thread's kernels will see it:
+// cudaSetDevice makes the device's primary context current on this thread (creating it if
+// needed). Context ids are unique for the life of the process, unlike context handles, so
+// a device address cached under an id is never used in a later context (after a
+// cudaDeviceReset, say).
+cudaError_t current_context_id(int* dev, unsigned long long* id) {
+  static const CtxGetCurrentFn get_ctx = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return e;
+  e = cudaSetDevice(*dev);
+  if (e != cudaSuccess) return e;
+  CUcontext ctx = nullptr;
+  if (!get_ctx || !get_id || get_ctx(&ctx) != CUDA_SUCCESS || !ctx ||
+      get_id(ctx, id) != CUDA_SUCCESS)
+    return cudaErrorContextIsDestroyed;
+  return cudaSuccess;
+}
+
+// ---------------------------------------------- attention work schedule
+// attn_fwd_tc_kernel is persistent (two CTAs per SM) and takes its tiles from a table
+// made here once per shape. Tiles that run at the same time should share their K and V
+// through L2 (heaviest-first over all heads at once re-read them from HBM for every tile,
+// measured 15-20 % slower), and every CTA should end at about the same time. Two
+// candidate splits, the one whose last CTA ends first (by the cost model: a tile costs
+// its 64-key steps + 1 for its set-up and output) is used, the first on a tie:
+//   head-major: the tiles of one head after another, latest query tile first, dealt to
+//     the CTAs in rounds that alternate direction (snake);
+//   chunked greedy: heads in chunks whose K and V take at most ATTN_CHUNK_MB, within a
+//     chunk the latest query tiles of all its heads first, each tile to the CTA with the
+//     least work so far (greedy longest-processing-time list scheduling).
+// Head-major balances well when every CTA gets many tiles (seq 2048); the chunked greedy
+// split when CTAs get few (8-16 sequences of 512: 20-35 % shorter makespan). Both keep
+// the tiles that run together within a few MB of K and V. Table: [grid + 1] offsets,
+// then the items ((batch * heads + head) * n_qt + query tile) of CTA 0, CTA 1, ...
+constexpr double ATTN_CHUNK_MB = 8.0;
+
+std::vector<int> attn_schedule_table(int batch, int heads, int kv_heads, int seq, int grid_max,
+                                     int* grid_out) {
+  const int n_qt = seq / FA_BQ, hb_count = batch * heads;
+  const long n_items = (long)n_qt * hb_count;
+  const int grid = (int)std::max<long>(1, std::min<long>(n_items, grid_max));
+  auto cost = [&](int w) { return 2L * (w % n_qt + 1) + 1; };
+  // head-major, snake
+  std::vector<std::vector<int>> hm(grid);
+  std::vector<long> hm_load(grid, 0);
+  for (long k = 0; k < n_items; ++k) {
+    const long rd = k / grid;
+    const int c = (int)(rd & 1 ? grid - 1 - k % grid : k % grid);
+    const int hb = (int)(k / n_qt), qt = n_qt - 1 - (int)(k % n_qt);
+    hm[c].push_back(hb * n_qt + qt);
+    hm_load[c] += cost(hb * n_qt + qt);
+  }
+  // chunked greedy
+  const double kv_bytes_per_head = (double)seq * 128 * 2 * 2 / std::max(1, heads / kv_heads);
+  const char* env = getenv("CB_ATTN_CHUNK_MB");  // tuning override of the chunk budget
+  const double budget_mb = env && atof(env) > 0 ? atof(env) : ATTN_CHUNK_MB;
+  const int chunk =
+      std::max(1, std::min(hb_count, (int)(budget_mb * (1 << 20) / kv_bytes_per_head)));
+  std::vector<std::vector<int>> gr(grid);
+  using Slot = std::pair<long, int>;  // (work so far, CTA): the least work, then the lowest CTA
+  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> heap;
+  for (int c = 0; c < grid; ++c) heap.push({0, c});
+  long gr_max = 0;
+  for (int c0 = 0; c0 < hb_count; c0 += chunk) {
+    const int ce = std::min(chunk, hb_count - c0);
+    for (int qt = n_qt - 1; qt >= 0; --qt)
+      for (int i = 0; i < ce; ++i) {
+        const Slot top = heap.top();
+        heap.pop();
+        const int w = (c0 + i) * n_qt + qt;
+        gr[top.second].push_back(w);
+        heap.push({top.first + cost(w), top.second});
+        gr_max = std::max(gr_max, top.first + cost(w));
+      }
+  }
+  const long hm_max = *std::max_element(hm_load.begin(), hm_load.end());
+  const std::vector<std::vector<int>>& lists = gr_max < hm_max ? gr : hm;
+  std::vector<int> table;
+  table.reserve(grid + 1 + n_items);
+  int off = 0;
+  for (int c = 0; c < grid; ++c) {
+    table.push_back(off);
+    off += (int)lists[c].size();
+  }
+  table.push_back(off);
+  for (int c = 0; c < grid; ++c) table.insert(table.end(), lists[c].begin(), lists[c].end());
+  *grid_out = grid;
+  return table;
+}
+
+struct AttnSched {
+  int grid = 0;
+  int* table = nullptr;  // device copy of attn_schedule_table
+};
+
+std::mutex g_attn_sched_mu;
+// keyed by (context id, batch, heads, kv heads, seq)
+std::map<std::tuple<unsigned long long, int, int, int, int>, AttnSched> g_attn_sched;
+
+// The schedule of one shape on the current device, made and uploaded on first use. The
+// upload cannot happen while `st` is being captured into a graph: forwards prepare their
+// shapes before capture (prepare_attention), and a capture that meets an unprepared
+// shape fails with cudaErrorStreamCaptureUnsupported.
+cudaError_t attn_schedule(int batch, int heads, int kv_heads, int seq, cudaStream_t st,
+                          const AttnSched** out) {
+  int dev = 0;
+  unsigned long long ctx_id = 0;
+  cudaError_t e = current_context_id(&dev, &ctx_id);
+  if (e != cudaSuccess) return e;
+  const std::tuple<unsigned long long, int, int, int, int> key{ctx_id, batch, heads, kv_heads,
+                                                                seq};
+  std::lock_guard<std::mutex> lock(g_attn_sched_mu);
+  auto it = g_attn_sched.find(key);
+  if (it != g_attn_sched.end()) {
+    *out = &it->second;
+    return cudaSuccess;
+  }
+  if (st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+      return cudaErrorStreamCaptureUnsupported;
+  }
+  AttnSched s;
+  const std::vector<int> table =
+      attn_schedule_table(batch, heads, kv_heads, seq, 2 * num_sms_of(dev), &s.grid);
+  e = cudaMalloc(&s.table, table.size() * sizeof(int));
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy(s.table, table.data(), table.size() * sizeof(int), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(s.table);
+    return e;
+  }
+  *out = &(g_attn_sched[key] = s);
+  return cudaSuccess;
+}
+
 cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
                              const __half* q, const __half* k, const __half* v, __half* out,
                              int batch, int heads, int kv_heads, int seq, int* err,
@@ -648,13 +800,11 @@ cudaError_t launch_attention(const CUtensorMap* tq, const CUtensorMap* tk, const
   CUtensorMap to;  // the output [batch*seq, heads*128] in 128-query x 64-column boxes
   if (tq && seq % FA_BQ == 0 &&
       make_tmap_rows(&to, out, (uint64_t)heads * 128, (uint64_t)batch * seq, FA_BQ)) {
-    // persistent: one CTA per SM over the blocks of 256 query rows, heaviest first
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int items = fa_blocks(seq) * heads * batch;
-    const int grid = std::min(items, num_sms_of(dev));
-    attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, st>>>(*tq, *tk, *tv, to, seq, heads,
-                                                          kv_heads, batch, scale_log2, lse, err);
+    const AttnSched* sch = nullptr;
+    const cudaError_t e = attn_schedule(batch, heads, kv_heads, seq, st, &sch);
+    if (e != cudaSuccess) return e;
+    attn_fwd_tc_kernel<<<sch->grid, FA_THREADS, FA_SMEM, st>>>(
+        *tq, *tk, *tv, to, seq, heads, kv_heads, sch->table, scale_log2, lse, err);
   } else {
     dim3 grid(seq / ATT_BQ, heads, batch);
     attn_fwd_causal_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(q, k, v, out, seq, heads,
@@ -1794,6 +1944,21 @@ cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t 
   return tp_partition(cfg, tp_world, tp_rank, info, &why);
 }
 
+cb_status cb_attention_schedule(int32_t batch, int32_t heads, int32_t kv_heads, int32_t seq,
+                                int32_t sms, int32_t* table, size_t cap, int32_t* grid,
+                                size_t* len) {
+  if (!grid || !len || batch < 1 || heads < 1 || kv_heads < 1 || heads % kv_heads != 0 ||
+      seq < FA_BQ || seq % FA_BQ != 0 || sms < 1 || (long)batch * heads * (seq / FA_BQ) > (1L << 30))
+    return CB_ERR_INVALID_ARG;
+  int g = 0;
+  const std::vector<int> t = attn_schedule_table(batch, heads, kv_heads, seq, 2 * sms, &g);
+  *grid = g;
+  *len = t.size();
+  if (!table || t.size() > cap) return CB_ERR_INVALID_ARG;
+  std::memcpy(table, t.data(), t.size() * sizeof(int));
+  return CB_OK;
+}
+
 cb_status cb_destroy(cb_ctx* ctx) {
   if (!ctx) return CB_OK;
   cudaSetDevice(ctx->device);
@@ -2245,6 +2410,20 @@ cb_status cb_eval_windows(cb_ctx* ctx, const cb_tokens* data, const int32_t* tok
   return CB_OK;
 }
 
+// Makes the attention schedules a forward of `batch` sequences may launch (also the
+// sequence chunks of the tensor-parallel forward) before anything is captured.
+cudaError_t prepare_attention(cb_ctx* c, int batch) {
+  if (c->cfg.seq % FA_BQ != 0) return cudaSuccess;
+  for (int k = 1; k <= 8 && k <= batch; ++k) {
+    if (batch % k != 0) continue;
+    const AttnSched* s = nullptr;
+    const cudaError_t e =
+        attn_schedule(batch / k, c->heads_l, c->kv_heads_l, c->cfg.seq, nullptr, &s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStream_t st) {
   if (ctx->nccl_failed)
     return fail(ctx, CB_ERR_NCCL, "the tensor-parallel communicator was aborted: " + ctx->nccl_why);
@@ -2262,6 +2441,7 @@ static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStre
     if (it == ctx->graphs.end()) {
       cudaGraph_t graph = nullptr;
       cudaGraphExec_t exec = nullptr;
+      CB_CUDA(prepare_attention(ctx, batch));
       CB_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
       cudaError_t e = enqueue_forward(ctx, batch, softcap, ctx->stream, false);
       cudaError_t e2 = cudaStreamEndCapture(ctx->stream, &graph);
@@ -2739,39 +2919,15 @@ std::mutex g_noalloc_mu;
 void* g_noalloc_addr[64] = {};
 unsigned long long g_noalloc_ctx_id[64] = {};
 
-typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
-typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
-
-// A driver entry point resolved once through the runtime (no -lcuda link).
-template <class Fn>
-Fn driver_fn(const char* name) {
-  void* p = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess &&
-      q == cudaDriverEntryPointSuccess)
-    return reinterpret_cast<Fn>(p);
-  return nullptr;
-}
-
 // Device address of g_lm_ce_scratch on the current device: looked up once per device
 // and again whenever the device's current context is not the one it was looked up in
 // (context ids are unique for the life of the process, unlike context handles).
 cudaError_t noalloc_scratch(void** out) {
-  static const CtxGetCurrentFn get_ctx = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
-  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  unsigned long long id = 0;
+  cudaError_t e = current_context_id(&dev, &id);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  // cudaSetDevice makes the device's primary context current on this thread (creating
-  // it if needed), so the context read below is the one this call's kernels run in.
-  e = cudaSetDevice(dev);
-  if (e != cudaSuccess) return e;
-  CUcontext ctx = nullptr;
-  unsigned long long id = 0;
-  if (!get_ctx || !get_id || get_ctx(&ctx) != CUDA_SUCCESS || !ctx ||
-      get_id(ctx, &id) != CUDA_SUCCESS)
-    return cudaErrorContextIsDestroyed;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_addr[dev] || g_noalloc_ctx_id[dev] != id) {
     void* p = nullptr;

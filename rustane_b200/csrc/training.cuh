@@ -742,6 +742,7 @@ cb_status cb_forward_backward(cb_ctx* ctx, const uint32_t* tokens, const uint32_
   if (it == t->graphs.end()) {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    CB_CUDA(prepare_attention(ctx, batch));
     CB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = enqueue_train_step(ctx, batch, softcap, loss_scale, st);
     cudaError_t e2 = cudaStreamEndCapture(st, &graph);
