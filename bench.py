@@ -399,8 +399,8 @@ def run_decode_workload(args):
     cfg = CONFIGS[args.config]
     B = args.decode_batch
     plen = cfg.seq // 2
-    if args.warmup + args.steps > cfg.seq - plen:
-        raise SystemExit("warmup + steps must fit in the second half of the sequence window")
+    if args.warmup + 2 * args.steps > cfg.seq - plen:
+        raise SystemExit("warmup + 2 x steps must fit in the second half of the sequence window")
     rng = np.random.default_rng(args.seed)
     k = CompiledKernels(cfg, 0, B)
     k.init_weights(args.seed, CB_INIT_NORMAL, 0.02)
@@ -421,6 +421,14 @@ def run_decode_workload(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
+    # the same steps returning only the greedy tokens (the logits stay on the device)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, cur = k.decode_step(cur, logits=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_tokens = e0.elapsed_time(e1) / args.steps
     weight_bytes = 2.0 * (cfg.linear_params() + cfg.vocab * cfg.dim)
     mean_keys = pos0 + (args.steps + 1) / 2.0
     kv_bytes = 2.0 * 2 * cfg.nlayers * B * cfg.kv_heads * 128 * mean_keys
@@ -441,6 +449,10 @@ def run_decode_workload(args):
                      "bytes_per_step": weight_bytes + kv_bytes, "traffic": None},
         "e2e": {"value": B / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B * (cfg.vocab + 1)},
+        "tokens_only": {"ms_per_step": ms_tokens, "value": B / (ms_tokens / 1e3),
+                        "d2h_bytes_per_step": 4 * B,
+                        "note": "the same steps returning only the greedy next tokens "
+                                "(positions after the timed ones)"},
         "clocks": clk,
     }
     k.close()
@@ -621,6 +633,16 @@ def run_train_workload(args):
     kern.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def tp_exchange_label() -> str:
+    """How the tensor-parallel ranks combine the O and down projections (CB_TP_REDUCE)."""
+    mode = os.environ.get("CB_TP_REDUCE", "sp16")
+    if mode == "allreduce":
+        return "fp32 NCCL all-reduce after the O and down projections"
+    width = "fp32" if mode == "sp32" else "fp16"
+    return (f"sequence parallel: {width} NCCL reduce-scatter of the O and down partial sums, "
+            "residual + RMSNorm on each rank's token rows, fp16 all-gather of the normalised rows")
 
 
 def main():
@@ -835,8 +857,8 @@ def main():
                              f"{cfg.nlayers}L/{cfg.heads}x128, vocab {cfg.vocab}, tied head), "
                              f"seq {cfg.seq}, global batch {args.global_batch}"),
                 "global_batch": args.global_batch, "seq_len": cfg.seq,
-                "parallelism": (f"tp{world} (Megatron column/row split, NCCL all-reduce after "
-                                "O and down projections)" if args.tp and world > 1 else
+                "parallelism": (f"tp{world} (Megatron column/row split; {tp_exchange_label()})"
+                                if args.tp and world > 1 else
                                 f"dp{world} (sequence sharding, no communication)"),
                 "per_gpu_batch": per,
                 "l2": "no flush: every step reads >1.1 GB of weights and >1 GB of "
@@ -850,7 +872,8 @@ def main():
             "cpu_baseline": cpu,
             "speedup_over_cpu": speedup,
             "e2e": e2e,
-            "gpu_launches": int(sum(v["launches"] for v in times.values())),
+            "gpu_launches": int(sum(v["launches"] for k, v in times.items()
+                                    if not k.startswith("nccl"))),
             "clocks": clk,
             "ms_per_step_profiled": all_ms / args.steps,
         }

@@ -97,6 +97,7 @@ pub mod ffi {
         pub fn cb_create_tp(cfg: *const cb_model_config, device: i32, max_batch: i32, tp_rank: i32, tp_world: i32, nccl_unique_id: *const c_void, out: *mut *mut cb_ctx) -> cb_status;
         pub fn cb_nccl_unique_id(out128: *mut c_void) -> cb_status;
         pub fn cb_tp_info(ctx: *const cb_ctx, info: *mut i32) -> cb_status;
+        pub fn cb_tp_peer_lost(ctx: *mut cb_ctx, why: *const c_char) -> cb_status;
         pub fn cb_tp_partition(cfg: *const cb_model_config, tp_world: i32, tp_rank: i32, info: *mut i32) -> cb_status;
         pub fn cb_destroy(ctx: *mut cb_ctx) -> cb_status;
         pub fn cb_init_weights(ctx: *mut cb_ctx, seed: u64, scheme: i32, sigma: f32) -> cb_status;

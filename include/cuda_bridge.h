@@ -111,18 +111,23 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
  * 4943-5139): rank r holds a near-even share of the kv heads (with their query
  * heads) for Wq/Wk/Wv (column-parallel) and Wo (row-parallel), and of the hidden
  * width in 64-column blocks for W1/W3 (column) and W2 (row). The row-parallel
- * partial outputs are summed with an NCCL all-reduce where the reference summed
- * shard outputs on the CPU (layer.rs:5121, 2018). Embedding, norms, residual and
- * the LM head + loss are replicated. Every rank passes the same 128-byte NCCL
- * unique id (from cb_nccl_unique_id on one rank) and must run the same sequence
+ * partial outputs are combined by NCCL where the reference summed shard outputs on
+ * the CPU (layer.rs:5121, 2018): by default sequence parallel (an fp16 reduce-scatter
+ * over the token rows, residual + RMSNorm of each rank's own rows, an all-gather of
+ * the normalised rows; $CB_TP_REDUCE=sp32 sends fp32 partial sums, =allreduce uses an
+ * fp32 all-reduce with every row replicated). Embedding, the LM head + loss are
+ * replicated, so every rank returns the same loss. Every rank passes the same 128-byte
+ * NCCL unique id (from cb_nccl_unique_id on one rank) and must run the same sequence
  * of calls. NCCL is loaded at run time ($CB_NCCL_LIB or libnccl.so.2).
  *
- * Failure handling: the communicator is non-blocking. Its set-up and every wait of a
- * forward poll the stream and ncclCommGetAsyncError against a host deadline
- * ($CB_NCCL_TIMEOUT_MS, default 120000). When a peer has left (its collective never
- * completes) or NCCL reports an error, the communicator is aborted (ncclCommAbort makes
- * its kernels return) and the call returns CB_ERR_NCCL; every later call on the context
- * returns CB_ERR_NCCL at once, and the context should be destroyed. */
+ * Failure handling: the communicator is non-blocking. A caller that learns on the host
+ * that a peer has left (its own heartbeat or store) calls cb_tp_peer_lost before the
+ * next step, so no collective is ever launched toward the missing peer. As a last
+ * resort, the communicator's set-up and every wait of a forward also poll the stream
+ * and ncclCommGetAsyncError against a host deadline ($CB_NCCL_TIMEOUT_MS, default
+ * 120000); on expiry or an NCCL error the communicator is aborted (ncclCommAbort) and
+ * the call returns CB_ERR_NCCL. After either, every call on the context returns
+ * CB_ERR_NCCL at once, and the context should be destroyed. */
 cb_status cb_create_tp(const cb_model_config* cfg, int32_t device, int32_t max_batch,
                        int32_t tp_rank, int32_t tp_world, const void* nccl_unique_id,
                        cb_ctx** out);
@@ -134,6 +139,15 @@ cb_status cb_nccl_unique_id(void* out);
  *            first head, first kv head, first hidden column} of a context. */
 cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info);
 
+/* Between steps (none of the context's work in flight): a peer rank has left, as the
+ * caller learned on the host. The communicator is aborted with no collective
+ * outstanding, and every later call on the context returns CB_ERR_NCCL with `why`
+ * (nullable) in cb_last_error. The counterpart of the reference supervisor ending a
+ * worker whose peer failed (crates/engine/src/bin/theory_runner.rs:9-15,
+ * crates/engine/tests/theory_runner_supervisor.rs:14-74). CB_ERR_INVALID_ARG for a
+ * context that is not tensor-parallel. */
+cb_status cb_tp_peer_lost(cb_ctx* ctx, const char* why);
+
 /* The same info[8] for rank tp_rank of a tp_world split of `cfg`, without a context
  * or a GPU (the split cb_create_tp uses; host-side sharding code and tests share it).
  * CB_ERR_INVALID_ARG for an invalid config, rank or world (world above the kv heads
@@ -141,7 +155,11 @@ cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info);
 cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
                           int32_t* info);
 
-/* Frees every device resource of the context. NULL is accepted. */
+/* Frees every device resource of the context. NULL is accepted. One exception: a
+ * tensor-parallel context whose communicator was aborted while one of its collectives
+ * still runs (a peer left in the middle of a step) keeps its device memory until the
+ * process ends, since freeing it would wait for that collective; CB_ERR_NCCL is then
+ * returned (the reason in cb_create_error). The context is invalid afterwards either way. */
 cb_status cb_destroy(cb_ctx* ctx);
 
 /* Generates weights on the device (no host copy of the model is needed).

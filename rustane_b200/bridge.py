@@ -37,7 +37,7 @@ STATUS_NAMES = {
 # Every symbol include/cuda_bridge.h declares (checked by the CPU test suite).
 EXPORTED = [
     "cb_version", "cb_device_count", "cb_create", "cb_create_tp", "cb_nccl_unique_id",
-    "cb_tp_info", "cb_tp_partition", "cb_destroy", "cb_init_weights",
+    "cb_tp_info", "cb_tp_peer_lost", "cb_tp_partition", "cb_destroy", "cb_init_weights",
     "cb_load_weights_f32", "cb_forward_loss", "cb_forward_loss_async",
     "cb_check_device_error", "cb_selftest_wait_timeout", "cb_sampled_logits",
     "cb_set_profiling", "cb_kernel_times",
@@ -106,6 +106,7 @@ def load_library(path: Path | None = None) -> C.CDLL:
                                C.POINTER(vp)]),
         "cb_nccl_unique_id": (i32, [vp]),
         "cb_tp_info": (i32, [vp, pi32]),
+        "cb_tp_peer_lost": (i32, [vp, C.c_char_p]),
         "cb_tp_partition": (i32, [C.POINTER(cb_model_config), i32, i32, pi32]),
         "cb_destroy": (i32, [vp]),
         "cb_init_weights": (i32, [vp, u64, i32, f32]),

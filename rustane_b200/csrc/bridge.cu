@@ -178,6 +178,8 @@ struct NcclApi {
   decltype(&ncclCommInitRank) init_rank = nullptr;
   decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclCommDestroy) destroy = nullptr;
   decltype(&ncclCommAbort) abort = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
@@ -209,11 +211,15 @@ const NcclApi& nccl_api() {
     a.init_rank_config =
         reinterpret_cast<decltype(a.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.reduce_scatter =
+        reinterpret_cast<decltype(a.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
     a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
     a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
-    if (!a.get_unique_id || !a.init_rank || !a.all_reduce || !a.destroy || !a.abort ||
+    if (!a.get_unique_id || !a.init_rank || !a.all_reduce || !a.reduce_scatter ||
+        !a.all_gather || !a.destroy || !a.abort ||
         !a.error_string || !a.async_error) {
       api.why = "libnccl.so.2 lacks a required symbol";
       return;
@@ -270,6 +276,14 @@ void set_gemm_attrs_for() {
   }
 }
 
+// 128-wide single-CTA tiles only (the decode GEMMs, M <= 128 rows), with the split-K
+// (SplitFix) variant.
+template <class Epi>
+void set_gemm_attrs_128() {
+  set_gemm_attr<128, Epi, 0>();
+  set_gemm_attr_fix<128, Epi, 0, true>();
+}
+
 void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiStoreF16>();
   set_gemm_attrs_for<EpiStoreF32>();
@@ -297,6 +311,9 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<RowScaled<EpiCrossEntropy>>();
   set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32>();  // decode (decode.cuh)
+  set_gemm_attrs_128<EpiDecodeQkv>();
+  set_gemm_attrs_128<RowScaled<EpiDecodeQkv>>();
+  set_gemm_attrs_128<RowScaled<EpiDecodeLogits>>();
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwiglu>();
@@ -887,12 +904,15 @@ enum KClass {
   K_CE_FINAL,
   K_LOSS_MEAN,
   K_ALLREDUCE,
+  K_RSCATTER,
+  K_AGATHER,
   K_NUM
 };
 const char* kclass_name[K_NUM] = {"embed_rmsnorm", "add_rmsnorm",   "gemm_qkv_rope",
                                   "attention",     "gemm_o",        "gemm_w13_swiglu",
                                   "gemm_w2",       "gemm_lmhead_ce", "ce_finalize",
-                                  "loss_mean",     "nccl_allreduce"};
+                                  "loss_mean",     "nccl_allreduce", "nccl_reduce_scatter",
+                                  "nccl_all_gather"};
 
 struct KStat {
   int64_t launches = 0;
@@ -1318,6 +1338,213 @@ int tp_chunks(const cb_ctx* c, int batch) {
   return c->tp_world > 1 ? n : 1;
 }
 
+// How the tensor-parallel ranks combine the row-parallel projections (O, down), from
+// CB_TP_REDUCE (read once per process):
+//   "sp16" (default) sequence parallel: each projection's partial sums are written in fp16
+//     and reduce-scattered over the token rows, each rank adds the sums of its own rows to
+//     the residual and normalises them, and the normalised fp16 rows are all-gathered for
+//     the next column-parallel GEMM (2 + 2 bytes per element cross NVLink, against 8 for
+//     an fp32 all-reduce, and the residual + RMSNorm runs on 1/world of the rows);
+//   "sp32" the same with fp32 partial sums (4 + 2 bytes);
+//   "allreduce" the fp32 partial sums are all-reduced and every rank keeps every row.
+enum TpReduce { TP_ALLREDUCE = 0, TP_SP16 = 1, TP_SP32 = 2 };
+int tp_reduce_mode() {
+  static const int mode = [] {
+    const char* e = getenv("CB_TP_REDUCE");
+    if (e && !strcmp(e, "allreduce")) return (int)TP_ALLREDUCE;
+    if (e && !strcmp(e, "sp32")) return (int)TP_SP32;
+    return (int)TP_SP16;
+  }();
+  return mode;
+}
+
+// Sequence-parallel tensor-parallel forward: the reference's head / hidden split of the
+// layer (layer.rs:1906-2053,4943-5139, shard outputs summed on the CPU at layer.rs:2018,
+// 5121) with the sum done as a reduce-scatter over the token rows.
+// Rows: the batch's T tokens in `chunks` chunks of Tc rows; within chunk j rank r owns rows
+// [j Tc + r Tl, j Tc + (r + 1) Tl), Tl = Tc / world. Per layer and chunk:
+//   compute stream: QKV (every row of the chunk, this rank's heads), attention, O
+//     projection -> partial alpha * (A Wo) in delta (fp16) or delta32 (fp32);
+//   comm stream:    reduce-scatter of the partials (a rank receives the sums of its own
+//     rows), residual add + RMSNorm of those rows (x, xn), all-gather of the normalised
+//     fp16 rows into every rank's xn; then the same after W1/W3 -> down.
+// The compute stream works on the other chunk while one chunk's rows are exchanged (NCCL
+// capped at TP_COMM_SMS CTAs, the GEMMs on the other SMs). A rank keeps the residual x
+// only for its own rows; after the last layer the final rows of x are all-gathered too
+// (sampled logits read them). The LM head and the loss run over all rows on every rank,
+// so every rank returns the same loss and per-token losses.
+// With `prof` (eager profiling, chunks == 1) everything runs on `st`, events between
+// the launches.
+cudaError_t enqueue_forward_tp_sp(cb_ctx* c, int batch, int chunks, float softcap,
+                                  cudaStream_t st, bool prof, bool f16) {
+  const cb_model_config& cfg = c->cfg;
+  const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
+  const int T = batch * S, bc = batch / chunks, Tc = bc * S, G = c->tp_world, Tl = Tc / G;
+  const int rk = c->tp_rank;
+  const int H = c->heads_l, Hk = c->kv_heads_l, qd = c->q_dim, kvd = c->kv_dim, nq = c->n_qkv;
+  const float alpha = 1.0f / sqrtf(2.0f * (float)L);  // layer.rs:4420
+  const bool two = !prof && c->comm_stream != nullptr;
+  cudaStream_t cs = two ? c->comm_stream : st;
+  DeviceInfo dt = device_info(c->device);
+  if (two) {  // the GEMMs leave TP_COMM_SMS SMs to NCCL
+    dt.sms = std::max(1, dt.sms - TP_COMM_SMS);
+    dt.pair_clusters = std::max(1, std::min(dt.pair_clusters, dt.sms / 2));
+  }
+  const ncclDataType_t part_type = f16 ? ncclHalf : ncclFloat32;
+  const size_t esz = f16 ? 2 : 4;
+  char* part = f16 ? reinterpret_cast<char*>(c->delta) : reinterpret_cast<char*>(c->delta32);
+  cudaError_t e;
+  int ev = 0;
+  auto mark = [&](int cls, double flops, double bytes) {
+    if (!prof) return;
+    c->ev_class.push_back(cls);
+    c->ev_flops.push_back(flops);
+    c->ev_bytes.push_back(bytes);
+    cudaEventRecord(c->events[++ev], st);
+  };
+  if (prof) {
+    c->ev_class.clear();
+    c->ev_flops.clear();
+    c->ev_bytes.clear();
+    cudaEventRecord(c->events[0], st);
+  }
+#define TRYS(...)                                     \
+  do {                                                \
+    if ((e = (__VA_ARGS__)) != cudaSuccess) return e; \
+  } while (0)
+  cudaEvent_t* ev_proj = c->tp_ev;                 // chunk j's partial projection written
+  cudaEvent_t* ev_rows = c->tp_ev + TP_MAX_CHUNKS;  // chunk j's normalised rows gathered
+  const int m_qkv = pick_mode(Tc, nq, dt), m_o = pick_mode(Tc, d, dt);
+  const int m_13 = pick_mode(Tc, 2 * hid, dt);
+  const double Tcd = (double)Tc;
+
+  embed_rmsnorm_kernel<<<(T + ROW_WARPS - 1) / ROW_WARPS, ROW_WARPS * 32, 0, st>>>(
+      c->tokens, c->embed, c->gamma, c->x, c->xn, T, d, V, c->dev_err);
+  TRYS(cudaGetLastError());
+  mark(K_EMBED_NORM, 0, (double)T * (4 + d * (2 + 4 + 2)));
+  if (two) {  // the communication stream joins the capture here
+    TRYS(cudaEventRecord(c->tp_ev[3 * TP_MAX_CHUNKS], st));
+    TRYS(cudaStreamWaitEvent(cs, c->tp_ev[3 * TP_MAX_CHUNKS], 0));
+  }
+  // Chunk j's partials -> sums of this rank's rows -> residual + RMSNorm(gamma) -> every
+  // rank's normalised rows (and, after the last layer, the residual rows themselves).
+  auto exchange = [&](int j, const float* gamma, bool last) -> cudaError_t {
+    const size_t r0 = (size_t)j * Tc, own = r0 + (size_t)rk * Tl;
+    if (two) {
+      TRYS(cudaEventRecord(ev_proj[j], st));
+      TRYS(cudaStreamWaitEvent(cs, ev_proj[j], 0));
+    }
+    ncclResult_t nr = nccl_api().reduce_scatter(part + r0 * d * esz, part + own * d * esz,
+                                                (size_t)Tl * d, part_type, ncclSum, c->comm, cs);
+    if (nccl_settle(c, nr, "ncclReduceScatter") != ncclSuccess) return cudaErrorUnknown;
+    mark(K_RSCATTER, 0, Tcd * d * esz);
+    TRYS(f16 ? launch_add_rmsnorm(c->x + own * d, c->x + own * d, c->delta + own * d, gamma,
+                                  c->xn + own * d, Tl, d, cs)
+             : launch_add_rmsnorm(c->x + own * d, c->x + own * d, c->delta32 + own * d, gamma,
+                                  c->xn + own * d, Tl, d, cs));
+    mark(K_RMSNORM, 0, (double)Tl * d * (4 + esz + 4 + 2));
+    nr = nccl_api().all_gather(c->xn + own * d, c->xn + r0 * d, (size_t)Tl * d, ncclHalf,
+                               c->comm, cs);
+    if (nccl_settle(c, nr, "ncclAllGather") != ncclSuccess) return cudaErrorUnknown;
+    mark(K_AGATHER, 0, Tcd * d * 2);
+    if (last) {
+      nr = nccl_api().all_gather(c->x + own * d, c->x + r0 * d, (size_t)Tl * d, ncclFloat32,
+                                 c->comm, cs);
+      if (nccl_settle(c, nr, "ncclAllGather") != ncclSuccess) return cudaErrorUnknown;
+      mark(K_AGATHER, 0, Tcd * d * 4);
+    }
+    if (two) TRYS(cudaEventRecord(ev_rows[j], cs));
+    return cudaSuccess;
+  };
+  const double attn_flops = 2.0 * 2.0 * (double)bc * H * 128.0 * S * (S + 1) / 2.0;
+  for (int l = 0; l < L; ++l) {
+    for (int j = 0; j < chunks; ++j) {  // attention half
+      const size_t r0 = (size_t)j * Tc;
+      if (two && l > 0) TRYS(cudaStreamWaitEvent(st, ev_rows[j], 0));
+      __half* qj = c->q + r0 * qd;
+      __half* kj = c->k + r0 * kvd;
+      __half* vj = c->v + r0 * kvd;
+      CUtensorMap ta, tq, tk, tv, to;
+      if (!make_tmap(&ta, c->xn + r0 * d, d, Tc, 1, 128) ||
+          !make_tmap(&to, c->attn + r0 * qd, qd, Tc, 1, 128) ||
+          !make_tmap_qkv(&tq, qj, (uint64_t)Tc * H, FA_BQ) ||
+          !make_tmap_qkv(&tk, kj, (uint64_t)Tc * Hk, FA_BKV) ||
+          !make_tmap_qkv(&tv, vj, (uint64_t)Tc * Hk, FA_BKV))
+        return cudaErrorInvalidValue;
+      {
+        EpiQkvRope ep{qj, kj, vj, c->rope, S, H, Hk};
+        TRYS(launch_gemm(m_qkv, ta, c->tm_wqkv[0], c->tm_wqkv[1], Tc, nq, d, l, ep, c->dev_err,
+                         dt, st));
+      }
+      mark(K_GEMM_QKV, 2.0 * Tcd * nq * d, Tcd * d * 2 + (double)nq * d * 2 + Tcd * nq * 2);
+      TRYS(launch_attention(S % FA_BQ == 0 ? &tq : nullptr, &tk, &tv, qj, kj, vj,
+                            c->attn + r0 * qd, bc, H, Hk, S, c->dev_err, st));
+      mark(K_ATTN, attn_flops, Tcd * (qd + 2 * kvd) * 2 + Tcd * qd * 2);
+      if (f16) {
+        EpiScaledF16 ep{c->delta + r0 * d, d, alpha};
+        TRYS(launch_gemm(m_o, to, c->tm_wo[0], c->tm_wo[1], Tc, d, qd, l, ep, c->dev_err, dt, st));
+      } else {
+        EpiScaledF32 ep{c->delta32 + r0 * d, d, alpha};
+        TRYS(launch_gemm(m_o, to, c->tm_wo[0], c->tm_wo[1], Tc, d, qd, l, ep, c->dev_err, dt, st));
+      }
+      mark(K_GEMM_O, 2.0 * Tcd * d * qd, Tcd * qd * 2 + (double)d * qd * 2 + Tcd * d * esz);
+      TRYS(exchange(j, c->gamma + (size_t)l * 2 * d + d, false));
+    }
+    const bool last = l + 1 == L;
+    const float* g_next = last ? c->gamma_final : c->gamma + (size_t)(l + 1) * 2 * d;
+    for (int j = 0; j < chunks; ++j) {  // FFN half
+      const size_t r0 = (size_t)j * Tc;
+      if (two) TRYS(cudaStreamWaitEvent(st, ev_rows[j], 0));
+      CUtensorMap ta, tg;
+      if (!make_tmap(&ta, c->xn + r0 * d, d, Tc, 1, 128) ||
+          !make_tmap(&tg, c->g + r0 * hid, hid, Tc, 1, 128))
+        return cudaErrorInvalidValue;
+      {
+        EpiSwiglu ep{c->g + r0 * hid, hid};
+        TRYS(launch_gemm(m_13, ta, c->tm_w13[0], c->tm_w13[1], Tc, 2 * hid, d, l, ep, c->dev_err,
+                         dt, st));
+      }
+      mark(K_GEMM_W13, 2.0 * Tcd * 2 * hid * d, Tcd * d * 2 + 2.0 * hid * d * 2 + Tcd * hid * 2);
+      if (f16) {
+        EpiScaledF16 ep{c->delta + r0 * d, d, alpha};
+        TRYS(launch_gemm(m_o, tg, c->tm_w2[0], c->tm_w2[1], Tc, d, hid, l, ep, c->dev_err, dt, st));
+      } else {
+        EpiScaledF32 ep{c->delta32 + r0 * d, d, alpha};
+        TRYS(launch_gemm(m_o, tg, c->tm_w2[0], c->tm_w2[1], Tc, d, hid, l, ep, c->dev_err, dt, st));
+      }
+      mark(K_GEMM_W2, 2.0 * Tcd * d * hid, Tcd * hid * 2 + (double)d * hid * 2 + Tcd * d * esz);
+      TRYS(exchange(j, g_next, last));
+    }
+  }
+  if (two)  // join the communication stream back
+    for (int j = 0; j < chunks; ++j) TRYS(cudaStreamWaitEvent(st, ev_rows[j], 0));
+  const DeviceInfo& di = device_info(c->device);
+  const int m_head = pick_mode(T, V, di);
+  const int nparts = (V + mode_block_n(m_head) - 1) / mode_block_n(m_head);
+  {
+    EpiCrossEntropy ep{};
+    ep.part = c->ce_part;
+    ep.nparts = nparts;
+    ep.targets = c->targets;
+    ep.tgt_logit = c->tgt_logit;
+    ep.softcap = softcap;
+    TRYS(launch_gemm(m_head, c->tm_xn, c->tm_embed[0], c->tm_embed[1], T, V, d, 0, ep,
+                     c->dev_err, di, st));
+  }
+  mark(K_GEMM_HEAD, 2.0 * T * (double)V * d,
+       (double)T * d * 2 + (double)V * d * 2 + (double)T * nparts * 8 + T * 8.0);
+  const int row_blocks = (T + ROW_WARPS - 1) / ROW_WARPS;
+  ce_finalize_kernel<<<row_blocks, ROW_WARPS * 32, 0, st>>>(c->ce_part, nparts, c->tgt_logit,
+                                                            c->tok_loss, c->block_sums, T);
+  TRYS(cudaGetLastError());
+  mark(K_CE_FINAL, 0, (double)T * nparts * 8 + T * 8.0);
+  loss_mean_kernel<<<1, 256, 0, st>>>(c->block_sums, row_blocks, T, c->loss);
+  TRYS(cudaGetLastError());
+  mark(K_LOSS_MEAN, 0, row_blocks * 4.0);
+#undef TRYS
+  return cudaSuccess;
+}
+
 // Per-layer destination of K and V (the decode KV cache): layer l's [batch, kv_heads,
 // seq, 128] blocks at k + l * layer_stride and v + l * layer_stride.
 struct KvDest {
@@ -1331,6 +1558,15 @@ struct KvDest {
 // and V are kept (prefill of the decode cache) instead of reusing one buffer.
 cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st, bool prof,
                             const KvDest* kv = nullptr) {
+  if (!kv && c->tp_world > 1 && tp_reduce_mode() != TP_ALLREDUCE) {
+    // sequence parallel, when every chunk's rows split evenly over the ranks
+    const int T = batch * c->cfg.seq;
+    int chunks = prof ? 1 : tp_chunks(c, batch);
+    if ((T / chunks) % c->tp_world != 0) chunks = 1;
+    if (T % c->tp_world == 0)
+      return enqueue_forward_tp_sp(c, batch, chunks, softcap, st, prof,
+                                   tp_reduce_mode() == TP_SP16);
+  }
   if (!prof && !kv && c->tp_world > 1 && c->comm_stream) {
     const int chunks = tp_chunks(c, batch);
     if (chunks > 1) return enqueue_forward_tp_chunked(c, batch, chunks, softcap, st);
@@ -1518,10 +1754,11 @@ cudaError_t enqueue_forward(cb_ctx* c, int batch, float softcap, cudaStream_t st
 }
 
 // Upper bound on the profiled launches of one forward: 7 per layer with the separate
-// residual + norm pass (5 when it is fused into the projections), + 2 all-reduces per
-// layer under tensor parallelism.
+// residual + norm pass (5 when it is fused into the projections); under tensor
+// parallelism 9 with all-reduces, 11 sequence parallel (2 x (reduce-scatter, norm,
+// all-gather)) plus the final all-gather of the residual rows.
 int launches_per_forward(const cb_ctx* c) {
-  return (c->tp_world > 1 ? 9 : 7) * c->cfg.nlayers + 4;
+  return (c->tp_world > 1 ? 11 : 7) * c->cfg.nlayers + 5;
 }
 
 // ---------------------------------------------------------- standalone LM head + CE
@@ -1883,6 +2120,21 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
     nr = nccl_api().all_reduce(ctx->delta32, ctx->delta32, 1, ncclFloat32, ncclSum, ctx->comm,
                                ctx->stream);
     if (nccl_settle(ctx, nr, "ncclAllReduce") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
+    // Likewise the reduce-scatters and all-gathers of the sequence-parallel forward, at
+    // their largest size (the contents are not used).
+    const size_t n = T * d / tp_world;
+    nr = nccl_api().reduce_scatter(ctx->delta, ctx->delta + (size_t)tp_rank * n, n, ncclHalf,
+                                   ncclSum, ctx->comm, ctx->stream);
+    if (nccl_settle(ctx, nr, "ncclReduceScatter") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
+    nr = nccl_api().reduce_scatter(ctx->delta32, ctx->delta32 + (size_t)tp_rank * n, n,
+                                   ncclFloat32, ncclSum, ctx->comm, ctx->stream);
+    if (nccl_settle(ctx, nr, "ncclReduceScatter") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
+    nr = nccl_api().all_gather(ctx->delta + (size_t)tp_rank * n, ctx->delta, n, ncclHalf,
+                               ctx->comm, ctx->stream);
+    if (nccl_settle(ctx, nr, "ncclAllGather") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
+    nr = nccl_api().all_gather(ctx->delta32 + (size_t)tp_rank * n, ctx->delta32, n, ncclFloat32,
+                               ctx->comm, ctx->stream);
+    if (nccl_settle(ctx, nr, "ncclAllGather") != ncclSuccess) return bail(CB_ERR_NCCL, ctx->err);
     if (sync_ctx_stream(ctx, ctx->stream) != CB_OK) return bail(CB_ERR_NCCL, ctx->err);
   }
 
@@ -1937,6 +2189,16 @@ cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info) {
   return CB_OK;
 }
 
+cb_status cb_tp_peer_lost(cb_ctx* ctx, const char* why) {
+  if (!ctx) return CB_ERR_INVALID_ARG;
+  if (ctx->tp_world <= 1) return fail(ctx, CB_ERR_INVALID_ARG, "not a tensor-parallel context");
+  if (!ctx->nccl_failed) {
+    cudaSetDevice(ctx->device);
+    nccl_abort(ctx, std::string("a peer rank left: ") + (why ? why : "reported by the caller"));
+  }
+  return CB_OK;
+}
+
 cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
                           int32_t* info) {
   if (!info) return CB_ERR_INVALID_ARG;
@@ -1963,6 +2225,15 @@ cb_status cb_destroy(cb_ctx* ctx) {
   if (!ctx) return CB_OK;
   cudaSetDevice(ctx->device);
   if (ctx->stream) sync_ctx_stream(ctx, ctx->stream);  // bounded for tensor-parallel contexts
+  if (ctx->nccl_failed && ((ctx->stream && cudaStreamQuery(ctx->stream) == cudaErrorNotReady) ||
+                           (ctx->comm_stream &&
+                            cudaStreamQuery(ctx->comm_stream) == cudaErrorNotReady))) {
+    // A collective toward a departed peer is still running although the communicator was
+    // aborted: freeing device memory would wait for it. The context's device memory is
+    // left to the end of the process.
+    g_create_error = "context leaked: a collective of the aborted communicator did not end";
+    return CB_ERR_NCCL;
+  }
   free_ctx(ctx);
   return CB_OK;
 }

@@ -300,16 +300,17 @@ class CompiledKernels:
                                         batch, length, softcap, _fptr(out)))
         return out
 
-    def decode_step(self, tokens):
+    def decode_step(self, tokens, logits: bool = True):
         """Feed one token per sequence at the current position; returns (logits
-        [batch, vocab], greedy next tokens [batch])."""
+        [batch, vocab], greedy next tokens [batch]), or (None, next tokens) with
+        logits=False (the logits then stay on the device)."""
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
-        logits = np.empty((t.size, self.cfg.vocab), np.float32)
+        z = np.empty((t.size, self.cfg.vocab), np.float32) if logits else None
         nxt = np.empty(t.size, np.uint32)
         self._check(self.lib.cb_decode_step(
-            self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, _fptr(logits),
-            nxt.ctypes.data_as(C.POINTER(C.c_uint32))))
-        return logits, nxt
+            self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size,
+            _fptr(z) if logits else None, nxt.ctypes.data_as(C.POINTER(C.c_uint32))))
+        return z, nxt
 
     def decode_position(self) -> int:
         p = C.c_int32()
@@ -415,6 +416,11 @@ class CompiledKernels:
         return {arr[i].name.decode(): dict(launches=arr[i].launches, total_ms=arr[i].total_ms,
                                            flops=arr[i].flops, bytes=arr[i].bytes)
                 for i in range(n.value)}
+
+    def tp_peer_lost(self, why: str = "a peer rank left") -> None:
+        """Between steps: a peer rank has left (learned on the host). The communicator is
+        aborted with nothing in flight; later calls raise CudaBridgeError (CB_ERR_NCCL)."""
+        self._check(self.lib.cb_tp_peer_lost(self.handle, why.encode()))
 
     def tp_info(self) -> dict:
         a = (C.c_int32 * 8)()

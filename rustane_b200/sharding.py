@@ -13,6 +13,9 @@ Two pieces, both host logic:
   results (time, loss) are combined, on the host side of the job.
 * The tensor-parallel split (`tp_partition`), answered by the bridge library
   itself (cb_tp_partition), so host code sees exactly the split cb_create_tp uses.
+* The token rows a tensor-parallel rank owns in the sequence-parallel forward
+  (`sequence_parallel_rows`): the rows whose residual it keeps, adds its reduce-scattered
+  projection sums to and normalises before the all-gather.
 """
 from __future__ import annotations
 
@@ -152,6 +155,32 @@ def tp_partition(cfg, world: int, rank: int) -> TpPartition:
     if rc != B.CB_OK:
         raise ValueError(f"no {world}-way tensor-parallel split of this config (rank {rank})")
     return TpPartition(*list(info))
+
+
+def sequence_parallel_chunks(batch: int, seq: int, world: int, chunks: int = 2) -> int:
+    """Chunks the sequence-parallel forward splits a batch into: the requested count
+    (CB_TP_CHUNKS, default 2) lowered until it divides the batch, and 1 when a chunk's
+    rows would not split evenly over the ranks (the rule of enqueue_forward in bridge.cu)."""
+    n = max(1, min(chunks, 8))
+    while n > 1 and batch % n:
+        n -= 1
+    if (batch * seq // n) % world:
+        n = 1
+    return n
+
+
+def sequence_parallel_rows(batch: int, seq: int, world: int, rank: int,
+                           chunks: int = 2) -> List[Tuple[int, int]]:
+    """[start, stop) token-row ranges rank `rank` owns in the sequence-parallel forward:
+    the batch's rows in chunks of Tc rows, and within chunk j the rank's contiguous slice
+    of Tc / world rows (NCCL's reduce-scatter / all-gather layout)."""
+    T = batch * seq
+    if T % world:
+        raise ValueError(f"{T} token rows do not split over {world} ranks")
+    n = sequence_parallel_chunks(batch, seq, world, chunks)
+    tc = T // n
+    tl = tc // world
+    return [(j * tc + rank * tl, j * tc + (rank + 1) * tl) for j in range(n)]
 
 
 def reduce_max(value: float, device=None) -> float:

@@ -106,11 +106,17 @@ TP_CASES = {
 }
 
 
-def _tp_forward64(m, part, tokens, targets, all_reduce):
+def _tp_forward64(m, part, tokens, targets, all_reduce, seq_parallel=None):
     """One rank's Megatron forward in float64: Wq/Wk/Wv and W1/W3 column slices of its
     heads and hidden columns, Wo and W2 row slices, the partial O and down outputs summed
     over the ranks (where the GPU contexts call an NCCL all-reduce), everything else
-    replicated (layer.rs:1906-2053, 4943-5139)."""
+    replicated (layer.rs:1906-2053, 4943-5139).
+
+    With seq_parallel = (rows, reduce_scatter, all_gather) the partial outputs are
+    reduce-scattered instead: the rank adds the sums of its own token rows (`rows`, from
+    sequence_parallel_rows) to its residual rows, normalises them, and all-gathers the
+    normalised rows (and, at the end, the residual rows), as the sequence-parallel GPU
+    forward does."""
     import torch
     cfg = m.cfg
     S, hd = cfg.seq, cfg.hd
@@ -135,8 +141,30 @@ def _tp_forward64(m, part, tokens, targets, all_reduce):
         return torch.stack([a * cos - b * sin, b * cos + a * sin], -1).view(v.shape)
 
     mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
-    for lw in m.layers:
-        xn = norm(x, lw["gamma1"])
+    B0, d = x.shape[0], x.shape[-1]
+
+    def combine(x, partial, gamma):
+        """x + alpha * (sum over ranks of partial) and its normalised rows"""
+        if seq_parallel is None:
+            x = x + alpha * all_reduce(partial)
+            return x, norm(x, gamma)
+        rows, reduce_scatter, all_gather = seq_parallel
+        flat, xf = partial.reshape(B0 * S, d), x.reshape(B0 * S, d).clone()
+        xn_own = []
+        for (r0, r1), chunk in zip(rows, _chunks_of(flat, rows)):
+            mine = reduce_scatter(chunk)
+            xf[r0:r1] = xf[r0:r1] + alpha * mine
+            xn_own.append(norm(xf[r0:r1], gamma))
+        xn = torch.cat([all_gather(o) for o in xn_own]).reshape(B0, S, d)
+        # rows of other ranks are not kept: poison them so a missed row shows
+        keep = torch.zeros(B0 * S, dtype=torch.bool)
+        for r0, r1 in rows:
+            keep[r0:r1] = True
+        xf[~keep] = float("nan")
+        return xf.reshape(B0, S, d), xn
+
+    xn = norm(x, m.layers[0]["gamma1"]) if m.layers else None
+    for li, lw in enumerate(m.layers):
         q = rope(xn @ f(lw["wq"])[:, q0:q1])
         k = rope(xn @ f(lw["wk"])[:, k0:k1])
         v = xn @ f(lw["wv"])[:, k0:k1]
@@ -148,17 +176,28 @@ def _tp_forward64(m, part, tokens, targets, all_reduce):
         k, v = k.repeat_interleave(grp, dim=1), v.repeat_interleave(grp, dim=1)
         sc = (q @ k.transpose(-1, -2) / np.sqrt(float(hd))).masked_fill(mask, float("-inf"))
         a = (torch.softmax(sc, -1) @ v).transpose(1, 2).reshape(B_, S, -1)
-        x = x + alpha * all_reduce(a @ f(lw["wo"])[q0:q1, :])
-        xn = norm(x, lw["gamma2"])
+        x, xn = combine(x, a @ f(lw["wo"])[q0:q1, :], lw["gamma2"])
         h1, h3 = xn @ f(lw["w1"])[:, c0:c1], xn @ f(lw["w3"])[:, c0:c1]
-        x = x + alpha * all_reduce((h1 * torch.sigmoid(h1) * h3) @ f(lw["w2"])[:, c0:c1].T)
+        g_next = m.layers[li + 1]["gamma1"] if li + 1 < len(m.layers) else m.gamma_final
+        x, xn = combine(x, (h1 * torch.sigmoid(h1) * h3) @ f(lw["w2"])[:, c0:c1].T, g_next)
+    if seq_parallel is not None:  # the final residual rows are gathered too
+        rows, _, all_gather = seq_parallel
+        xf = x.reshape(B0 * S, d)
+        x = torch.cat([all_gather(xf[r0:r1]) for r0, r1 in rows]).reshape(B0, S, d)
     z = norm(x, m.gamma_final) @ E.T
     tgt = torch.from_numpy(np.asarray(targets, np.int64)).view(-1, S)
     ptl = torch.logsumexp(z, -1) - torch.gather(z, -1, tgt[..., None])[..., 0]
     return ptl.reshape(-1).numpy()
 
 
-def _tp_rank_main(rank, world, port, case, out):
+def _chunks_of(flat, rows):
+    """The chunks of rows that the ranks' slices `rows` belong to (all ranks' rows)."""
+    n = len(rows)
+    tc = flat.shape[0] // n
+    return [flat[j * tc:(j + 1) * tc] for j in range(n)]
+
+
+def _tp_rank_main(rank, world, port, case, out, seq_parallel=False):
     import torch.distributed as dist
     from oracle.oracle import OracleModel
     from rustane_b200.sharding import tp_partition
@@ -175,24 +214,44 @@ def _tp_rank_main(rank, world, port, case, out):
             dist.all_reduce(t)
             return t
 
+        sp = None
+        if seq_parallel:
+            import torch
+            from rustane_b200.sharding import sequence_parallel_rows
+
+            def reduce_scatter(t):
+                o = torch.empty((t.shape[0] // world,) + tuple(t.shape[1:]), dtype=t.dtype)
+                dist.reduce_scatter_tensor(o, t.contiguous())
+                return o
+
+            def all_gather(t):
+                o = torch.empty((t.shape[0] * world,) + tuple(t.shape[1:]), dtype=t.dtype)
+                dist.all_gather_into_tensor(o, t.contiguous())
+                return o
+
+            sp = (sequence_parallel_rows(2, cfg.seq, world, rank), reduce_scatter, all_gather)
         part = tp_partition(cfg, world, rank)
-        out[rank] = (part, _tp_forward64(m, part, tok, tgt, all_reduce))
+        out[rank] = (part, _tp_forward64(m, part, tok, tgt, all_reduce, sp))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("seq_parallel", [False, True], ids=["allreduce", "seqpar"])
 @pytest.mark.parametrize("case", sorted(TP_CASES))
-def test_tensor_parallel_split_equals_single_process(oracle_lib, bridge_lib, case):
+def test_tensor_parallel_split_equals_single_process(oracle_lib, bridge_lib, case,
+                                                     seq_parallel):
     """Two gloo ranks, each holding only its cb_tp_partition share of the heads and
     hidden columns, reproduce the single-process forward (float64, so the only
-    difference is summation order)."""
+    difference is summation order): with all-reduced projections, and sequence parallel
+    (reduce-scatter to the rows sequence_parallel_rows gives the rank, residual and norm
+    on those rows only, all-gather of the normalised rows)."""
     from oracle import torch_ref
     from oracle.oracle import OracleModel
     world = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_tp_rank_main, args=(world, _free_port(), case, out), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_tp_rank_main, args=(world, _free_port(), case, out, seq_parallel),
+                       nprocs=world, join=True, start_method="spawn")
     cfg = TP_CASES[case]
     parts = [out[r][0] for r in range(world)]
     # the shares tile the heads, kv heads and hidden columns exactly once
@@ -246,3 +305,24 @@ def test_tp_partition_properties(bridge_lib):
         assert max(p.hidden for p in parts) - min(p.hidden for p in parts) <= 64
 
     check()
+
+
+def test_sequence_parallel_rows_tile_the_batch():
+    """The ranks' sequence-parallel rows cover every token row exactly once, in equal
+    slices, for the chunk counts the forward picks."""
+    from rustane_b200.sharding import sequence_parallel_chunks, sequence_parallel_rows
+    for batch, seq, world in [(2, 64, 2), (16, 2048, 8), (4, 512, 2), (3, 512, 2), (1, 128, 4)]:
+        T = batch * seq
+        seen = np.zeros(T, np.int32)
+        n = sequence_parallel_chunks(batch, seq, world)
+        for r in range(world):
+            rows = sequence_parallel_rows(batch, seq, world, r)
+            assert len(rows) == n
+            for r0, r1 in rows:
+                assert r1 - r0 == T // n // world
+                seen[r0:r1] += 1
+        assert (seen == 1).all()
+    assert sequence_parallel_chunks(3, 512, 2) == 1   # 3 sequences do not split in 2
+    assert sequence_parallel_chunks(16, 2048, 8) == 2
+    with pytest.raises(ValueError):
+        sequence_parallel_rows(1, 63, 2, 0)
