@@ -276,14 +276,6 @@ void set_gemm_attrs_for() {
   }
 }
 
-// 128-wide single-CTA tiles only (the decode GEMMs, M <= 128 rows), with the split-K
-// (SplitFix) variant.
-template <class Epi>
-void set_gemm_attrs_128() {
-  set_gemm_attr<128, Epi, 0>();
-  set_gemm_attr_fix<128, Epi, 0, true>();
-}
-
 void set_all_kernel_attrs() {
   set_gemm_attrs_for<EpiStoreF16>();
   set_gemm_attrs_for<EpiStoreF32>();
@@ -311,9 +303,6 @@ void set_all_kernel_attrs() {
   set_gemm_attrs_for<RowScaled<EpiCrossEntropy>>();
   set_gemm_attrs_for<EpiPartialF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiPartialF32>();  // decode (decode.cuh)
-  set_gemm_attrs_128<EpiDecodeQkv>();
-  set_gemm_attrs_128<RowScaled<EpiDecodeQkv>>();
-  set_gemm_attrs_128<RowScaled<EpiDecodeLogits>>();
   set_gemm_attrs_for<EpiStoreF32, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiScaledF32Add, GEMM_A_MN | GEMM_B_MN>();
   set_gemm_attrs_for<EpiSwiglu>();

@@ -334,25 +334,6 @@ __global__ void decode_set_pos_kernel(int* pos_ptr, int advance, const float2* _
   if (threadIdx.x < 64) cs_pos[threadIdx.x] = rope[(size_t)threadIdx.x * seq + p];
 }
 
-// Last kernel of a fused decode step: each row's greedy next token from the LM head's
-// argmax key (argmax_key in gemm_tc.cuh; the key is cleared for the next step), then the
-// position moves to pos + 1 with its (cos, sin) row, as in decode_set_pos_kernel.
-__global__ void decode_finish_kernel(int* pos_ptr, const float2* __restrict__ rope, int seq,
-                                     float2* __restrict__ cs_pos, unsigned long long* best,
-                                     uint32_t* __restrict__ next, int B) {
-  pdl_enter();
-  for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const unsigned long long k = best[b];
-    next[b] = k ? 0xffffffffu - (uint32_t)(k & 0xffffffffull) : 0u;  // 0: no finite logit
-    best[b] = 0ull;
-  }
-  const int pos = *pos_ptr + 1;
-  __syncthreads();  // every thread has read the old position
-  if (threadIdx.x == 0) *pos_ptr = pos;
-  const int p = pos < seq ? pos : seq - 1;  // a full sequence takes no further step
-  if (threadIdx.x < 64) cs_pos[threadIdx.x] = rope[(size_t)threadIdx.x * seq + p];
-}
-
 }  // namespace cb
 
 // ------------------------------------------------------------------ host side
@@ -376,11 +357,6 @@ struct DecodeState {
   uint32_t* tok = nullptr;    // [max_batch]
   int* d_pos = nullptr;
   float2* d_cs = nullptr;     // [64] (cos, sin) of each RoPE pair at d_pos
-  // fused step (enqueue_decode_step_fused): per-row sums of x^2 per 128 columns, the LM
-  // head's argmax keys, x and xn as the residual epilogue's 32 x 32 boxes
-  float* ss_part = nullptr;          // [max_batch][d / 128]
-  unsigned long long* best = nullptr;  // [max_batch]
-  CUtensorMap tm_x, tm_xh;
   int pos = 0;                // host copy: position of the next token
   int batch = 0;              // sequences of the last prefill
   float softcap = 0.f;
@@ -438,16 +414,10 @@ static cb_status alloc_decode(cb_ctx* c) {
   get(&s->tok, B);
   get(&s->d_pos, 1);
   get(&s->d_cs, 64);
-  get(&s->ss_part, B * ((d + 127) / 128));
-  get(&s->best, B);
   if (ok) {
     ok = make_tmap(&s->tm_xn, s->xn, d, B, 1, 128) && make_tmap(&s->tm_o, s->o, qd, B, 1, 128) &&
          make_tmap(&s->tm_g, s->g, h, B, 1, 128);
   }
-  if (ok && d % 128 == 0)
-    ok = make_tmap_f32_rows(&s->tm_x, s->x, d, B, 32, 32, /*swizzle128=*/true) &&
-         make_tmap_h32(&s->tm_xh, s->xn, d, B);
-  if (ok) ok = cudaMemset(s->best, 0, B * sizeof(unsigned long long)) == cudaSuccess;
   if (ok)
     ok = cudaMallocHost(reinterpret_cast<void**>(&s->h_logits), B * V * sizeof(float)) ==
              cudaSuccess &&
@@ -470,112 +440,7 @@ static int decode_splits(int N, int K, const DeviceInfo& di) {
   return (kb + per - 1) / per;
 }
 
-// Split count of a fused decode GEMM: as decode_splits, at most CB_DECODE_MAX_SPLITS
-// (default 8): the tile's last split adds every other split's partial, so more splits
-// lengthen that serial tail.
-static int decode_fix_splits(int N, int K, const DeviceInfo& di) {
-  static const int cap = [] {
-    const char* e = getenv("CB_DECODE_MAX_SPLITS");
-    return e ? std::max(1, std::min(DEC_MAX_SPLITS, atoi(e))) : 8;
-  }();
-  const int tiles = (N + 127) / 128, kb = (K + GEMM_BK - 1) / GEMM_BK;
-  int s = std::max(1, std::min(cap, (di.sms + tiles / 2) / tiles));
-  s = std::min(s, kb);
-  const int per = (kb + s - 1) / s;
-  return (kb + per - 1) / per;
-}
-
-// The fused decode step: the forward's fused epilogues on M = batch rows, each GEMM split
-// along K with the last-arriving split of a tile adding the partials in split order and
-// running the epilogue (SplitFix), so no element-wise pass follows a GEMM:
-//   QKV (EpiDecodeQkv: RoPE at pos, Q out, K/V into the cache) -> attention (+ combine) ->
-//   O projection (EpiResidualNorm: x += alpha * acc, fp16(x * gamma2), sums of x^2) ->
-//   W1/W3 (RowScaled<EpiSwiglu>: 1/rms applied to the accumulator) -> down
-//   (EpiResidualNorm with the next layer's gamma1) -> ... -> LM head
-//   (RowScaled<EpiDecodeLogits>: logits + softcap + argmax keys) -> decode_finish_kernel.
-// 4 L + 3 launches (plus one key-split combine per layer at small batch), against 9 L + 4.
-static cudaError_t enqueue_decode_step_fused(cb_ctx* c, int B, float softcap, cudaStream_t st) {
-  DecodeState* s = c->decode;
-  const cb_model_config& cfg = c->cfg;
-  const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
-  const int H = c->heads_l, Hk = c->kv_heads_l, qd = c->q_dim, nq = c->n_qkv;
-  const float alpha = 1.0f / sqrtf(2.0f * (float)L);
-  const DeviceInfo& di = device_info(c->device);
-  const int rb = (B + ROW_WARPS - 1) / ROW_WARPS;
-  const SplitFix fix{c->fix_ws, c->fix_cnt};
-  cudaError_t e;
-  auto gemm = [&](const CUtensorMap& ta, const CUtensorMap& tb, int N, int K, int layer,
-                  const auto& ep, const CUtensorMap* tc = nullptr,
-                  const CUtensorMap* td = nullptr) -> cudaError_t {
-    const int sp = decode_fix_splits(N, K, di);
-    const int tiles = (N + 127) / 128;
-    if (tiles > FIX_COUNTERS || (size_t)tiles * sp * GEMM_BM * 128 * sizeof(float) > FIX_WS_BYTES)
-      return cudaErrorInvalidValue;
-    return launch_gemm_bn<128>(ta, tb, B, N, K, layer, ep, c->dev_err, di.sms, sp, st, tc, td,
-                               /*pdl=*/true, sp > 1 ? fix : SplitFix{});
-  };
-  auto scaled = [&](const auto& inner) {
-    using E = std::decay_t<decltype(inner)>;
-    return RowScaled<E>{inner, s->ss_part, d / 128, (float)d, RMS_EPS, 1.f};
-  };
-  const float* const no_rinv = nullptr;
-  if ((e = launch_k(embed_rmsnorm_kernel, dim3(rb), dim3(ROW_WARPS * 32), 0, st, false,
-                    (const uint32_t*)s->tok, (const __half*)c->embed, (const float*)c->gamma,
-                    s->x, s->xn, B, d, V, c->dev_err, (float*)no_rinv)) != cudaSuccess)
-    return e;
-  const float scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
-  const int kv_splits = std::max(1, std::min({DEC_MAX_KV_SPLITS, S / 64,
-                                              (2 * di.sms + B * H - 1) / (B * H)}));
-  for (int l = 0; l < L; ++l) {
-    __half* kc = s->kc + (size_t)l * s->layer_stride;
-    __half* vc = s->vc + (size_t)l * s->layer_stride;
-    const EpiDecodeQkv eq{s->q, kc, vc, s->d_cs, s->d_pos, S, H, Hk, 0};
-    e = l == 0 ? gemm(s->tm_xn, c->tm_wqkv[0], nq, d, l, eq)  // xn normalised by the embed kernel
-               : gemm(s->tm_xn, c->tm_wqkv[0], nq, d, l, scaled(eq));
-    if (e != cudaSuccess) return e;
-    if ((e = launch_k(decode_attn_kernel, dim3(H, B, kv_splits), dim3(128), 0, st, false,
-                      (const __half*)s->q, (const __half*)kc, (const __half*)vc,
-                      (const int*)s->d_pos, S, H, Hk, scale_log2, s->o, s->attn_acc)) != cudaSuccess)
-      return e;
-    if (kv_splits > 1 &&
-        (e = launch_k(decode_attn_combine_kernel, dim3((B * H + 7) / 8), dim3(256), 0, st, false,
-                      (const DecAttnPart*)s->attn_acc, kv_splits, H, B * H, s->o)) != cudaSuccess)
-      return e;
-    {
-      const EpiResidualNorm ep{c->gamma + (size_t)l * 2 * d + d, s->ss_part, d / 128, alpha, 0.f};
-      if ((e = gemm(s->tm_o, c->tm_wo[0], d, qd, l, ep, &s->tm_x, &s->tm_xh)) != cudaSuccess)
-        return e;
-    }
-    if ((e = gemm(s->tm_xn, c->tm_w13[0], 2 * hid, d, l, scaled(EpiSwiglu{s->g, hid}))) !=
-        cudaSuccess)
-      return e;
-    {
-      const float* gnext = l + 1 < L ? c->gamma + (size_t)(l + 1) * 2 * d : c->gamma_final;
-      const EpiResidualNorm ep{gnext, s->ss_part, d / 128, alpha, 0.f};
-      if ((e = gemm(s->tm_g, c->tm_w2[0], d, hid, l, ep, &s->tm_x, &s->tm_xh)) != cudaSuccess)
-        return e;
-    }
-  }
-  {
-    const EpiDecodeLogits el{s->logits, V, softcap, s->best, 0.f, 0};
-    if ((e = gemm(s->tm_xn, c->tm_embed[0], V, d, 0, scaled(el))) != cudaSuccess) return e;
-  }
-  return launch_k(decode_finish_kernel, dim3(1), dim3(128), 0, st, false, s->d_pos,
-                  (const float2*)c->rope, S, s->d_cs, s->best, s->next, B);
-}
-
-// The fused step needs whole 128-column groups for the residual epilogue and the split-K
-// workspace of a single-GPU context; CB_DECODE_FUSED=0 selects the unfused step.
-static bool decode_fused(const cb_ctx* c) {
-  static const bool off = [] {
-    const char* e = getenv("CB_DECODE_FUSED");
-    return e && !strcmp(e, "0");
-  }();
-  return !off && c->cfg.dim % 128 == 0 && c->fix_ws != nullptr;
-}
-
 static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStream_t st) {
-  if (decode_fused(c)) return enqueue_decode_step_fused(c, B, softcap, st);
   DecodeState* s = c->decode;
   const cb_model_config& cfg = c->cfg;
   const int S = cfg.seq, d = cfg.dim, hid = c->hidden_l, V = cfg.vocab, L = cfg.nlayers;
@@ -686,7 +551,6 @@ cb_status cb_prefill(cb_ctx* ctx, const uint32_t* tokens, int32_t batch, int32_t
   s->batch = batch;
   s->softcap = softcap;
   CB_CUDA(cudaMemcpyAsync(s->d_pos, &s->pos, sizeof(int), cudaMemcpyHostToDevice, st));
-  CB_CUDA(cudaMemsetAsync(s->best, 0, (size_t)ctx->max_batch * sizeof(unsigned long long), st));
   decode_set_pos_kernel<<<1, 64, 0, st>>>(s->d_pos, 0, ctx->rope, S, s->d_cs);
   CB_CUDA(cudaGetLastError());
   rc = read_device_error(ctx);

@@ -785,109 +785,6 @@ struct RowScaled {
   __device__ __forceinline__ void end_row(int row, int n_blk) { in.end_row(row, n_blk); }
 };
 
-// Decode (one new token per sequence, row = sequence b): the token's Q, K and V. RoPE at
-// the step's position on Q and K (sdpa_fwd.rs:53-60) with that position's (cos, sin)
-// row (cs_pos [64], written by the previous step's last kernel), Q to q [B][q_dim], K and
-// V into slot pos of this layer's cache [B][kv_heads][seq][128].
-struct EpiDecodeQkv {
-  struct Pre {
-    float2 cs[16];  // (cos, sin) of the chunk's 16 frequency pairs
-  };
-  static constexpr int OUT_BYTES = 64;
-  __half* q;
-  __half* kc;
-  __half* vc;
-  const float2* cs_pos;
-  const int* pos_ptr;
-  int seq;
-  int heads;
-  int kv_heads;
-  int pos;
-  __device__ __forceinline__ void begin_row(int, bool valid) { pos = valid ? *pos_ptr : 0; }
-  __device__ __forceinline__ void prefetch(int, int col0, Pre& p) {
-    if (col0 >= (heads + kv_heads) * 128) return;  // V columns are not rotated
-    const float2* cs = cs_pos + ((col0 & 127) >> 1);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) p.cs[i] = cs[i];
-  }
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&acc)[32], const Pre& p,
-                                        uint4 (&o)[8], uint8_t*& dst) {
-    const int q_dim = heads * 128, kv_dim = kv_heads * 128;
-    float r[32];
-    if (col0 < q_dim + kv_dim) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float a = acc[2 * i], bb = acc[2 * i + 1];
-        r[2 * i] = a * p.cs[i].x - bb * p.cs[i].y;
-        r[2 * i + 1] = bb * p.cs[i].x + a * p.cs[i].y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) r[i] = acc[i];
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = pack8_f16(r + 8 * j);
-    __half* d;
-    if (col0 < q_dim) {
-      d = q + (size_t)row * q_dim + col0;
-    } else {
-      const bool is_k = col0 < q_dim + kv_dim;
-      const int c = col0 - q_dim - (is_k ? 0 : kv_dim);
-      d = (is_k ? kc : vc) + (((size_t)row * kv_heads + (c >> 7)) * seq + pos) * 128 + (c & 127);
-    }
-    dst = reinterpret_cast<uint8_t*>(d);
-  }
-  __device__ __forceinline__ void end_row(int, int) {}
-};
-
-// Decode LM head: the row's logits (softcapped when softcap > 0, full_model.rs:456-461)
-// in fp32, and the greedy next token: each (row, N-tile) folds its largest logit (lowest
-// id on ties) into best[row] with a 64-bit atomicMax of (order-preserving bits of the
-// logit, 0xffffffff - id), which gives the same token whatever order the tiles finish in.
-// best[] starts at 0 (below every key) and is read and cleared by the step's last kernel.
-__device__ __forceinline__ unsigned long long argmax_key(float z, int id) {
-  const uint32_t u = __float_as_uint(z);
-  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)ord << 32) | (0xffffffffu - (uint32_t)id);
-}
-
-struct EpiDecodeLogits {
-  using Pre = NoPre;
-  static constexpr int OUT_BYTES = 128;
-  float* logits;
-  int ldo;
-  float softcap;
-  unsigned long long* best;  // [B]
-  float m;
-  int mi;
-  __device__ __forceinline__ void begin_row(int, bool) {
-    m = -CUDART_INF_F;
-    mi = 0x7fffffff;
-  }
-  __device__ __forceinline__ void prefetch(int, int, Pre&) {}
-  __device__ __forceinline__ void chunk(int row, int col0, const float (&v)[32], const Pre&,
-                                        uint4 (&o)[8], uint8_t*& dst) {
-    float z[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) z[i] = v[i];
-    if (softcap > 0.f) softcap_chunk(z, softcap, nullptr);
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (z[i] > m) {  // columns arrive in increasing order: ties keep the lower id
-        m = z[i];
-        mi = col0 + i;
-      }
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      o[j] = make_uint4(__float_as_uint(z[4 * j]), __float_as_uint(z[4 * j + 1]),
-                        __float_as_uint(z[4 * j + 2]), __float_as_uint(z[4 * j + 3]));
-    dst = reinterpret_cast<uint8_t*>(logits + (size_t)row * ldo + col0);
-  }
-  __device__ __forceinline__ void end_row(int row, int) {
-    if (mi != 0x7fffffff) atomicMax(best + row, argmax_key(m, mi));
-  }
-};
-
 // Split-K with a last-arrival reduction, for the fused epilogues that need whole sums
 // (residual + norm, RoPE, SwiGLU, cross-entropy) when a GEMM has too few tiles to fill
 // the GPU. Work unit = (tile, K split). Every unit writes its fp32 partial accumulator to
