@@ -388,6 +388,14 @@ impl Context {
     }
 
     /// Advances every sequence by one token; returns the greedy next tokens.
+    /// Between steps: a peer rank of this tensor-parallel context has left (learned by
+    /// the caller's own heartbeat or store). The communicator is aborted with nothing in
+    /// flight; every later call returns an error.
+    pub fn tp_peer_lost(&mut self, why: &str) -> Result<()> {
+        let c = CString::new(why).unwrap_or_default();
+        self.ok(unsafe { ffi::cb_tp_peer_lost(self.raw, c.as_ptr()) })
+    }
+
     pub fn decode_step(&mut self, tokens: &[u32], logits: Option<&mut Vec<f32>>)
                        -> Result<Vec<u32>> {
         let mut next = vec![0u32; tokens.len()];

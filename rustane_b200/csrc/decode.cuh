@@ -80,8 +80,11 @@ __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, in
 // Attention of one new query per (sequence, head) over cached keys 0..pos, split along
 // the keys into `nsplit` CTAs (blockIdx.z) of 4 warps; lanes split the 128 dims (4 each),
 // each warp takes 4 keys per step (independent dot-product reductions) with an online
-// softmax in base 2. A split writes its (max, sum, unnormalised output) to `acc` for
-// decode_attn_combine_kernel; with one split the kernel writes the output directly.
+// softmax in base 2, and loads the K and V rows of its next step before working on the
+// current one (two steps of loads in flight per warp: the kernel is bound by how many
+// bytes of the cache are on their way). A split writes its (max, sum, unnormalised
+// output) to `acc` for decode_attn_combine_kernel; with one split the kernel writes the
+// output directly.
 struct DecAttnPart {
   float m, l;
   float o[128];
@@ -113,17 +116,29 @@ __global__ void __launch_bounds__(128)
   }
   const __half* kb = kc + ((size_t)b * kv_heads + hk) * seq * 128 + lane * 4;
   const __half* vb = vc + ((size_t)b * kv_heads + hk) * seq * 128 + lane * 4;
-  float m = -CUDART_INF_F, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int key = k0 + warp * 4; key < k1; key += 16) {
-    float s[4];
-    uint2 vu[4];
+  // the 4 keys of a step from `base` (keys past the split's end re-read its last key and
+  // are masked below)
+  auto load = [&](int base, uint2 (&ku)[4], uint2 (&vu)[4]) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int kk = min(key + j, k1 - 1);
-      const uint2 ku = *reinterpret_cast<const uint2*>(kb + (size_t)kk * 128);
-      vu[j] = *reinterpret_cast<const uint2*>(vb + (size_t)kk * 128);
-      const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ku.x));
-      const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ku.y));
+      const int kk = min(base + j, k1 - 1);
+      ku[j] = __ldg(reinterpret_cast<const uint2*>(kb + (size_t)kk * 128));
+      vu[j] = __ldg(reinterpret_cast<const uint2*>(vb + (size_t)kk * 128));
+    }
+  };
+  float m = -CUDART_INF_F, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  uint2 ku[4], vu[4];
+  int key = k0 + warp * 4;
+  if (key < k1) load(key, ku, vu);
+  for (; key < k1; key += 16) {
+    uint2 kn[4], vn[4];
+    const bool more = key + 16 < k1;
+    if (more) load(key + 16, kn, vn);  // the next step's rows go out first
+    float s[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ku[j].x));
+      const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ku[j].y));
       s[j] = qv[0] * a0.x + qv[1] * a0.y + qv[2] * a1.x + qv[3] * a1.y;
     }
 #pragma unroll
@@ -134,14 +149,14 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < 4; ++j)
       if (key + j >= k1) s[j] = -CUDART_INF_F;
     const float mn = fmaxf(fmaxf(fmaxf(m, s[0]), fmaxf(s[1], s[2])), s[3]);
-    const float corr = exp2f(m - mn);
+    const float corr = exp2_mufu(m - mn);  // 2^-inf = 0 on the first step
     m = mn;
     l *= corr;
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[i] *= corr;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float p = exp2f(s[j] - mn);
+      const float p = exp2_mufu(s[j] - mn);
       l += p;
       const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vu[j].x));
       const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vu[j].y));
@@ -149,6 +164,13 @@ __global__ void __launch_bounds__(128)
       o[1] += p * v0.y;
       o[2] += p * v1.x;
       o[3] += p * v1.y;
+    }
+    if (more) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ku[j] = kn[j];
+        vu[j] = vn[j];
+      }
     }
   }
   if (lane == 0) {
@@ -213,33 +235,42 @@ __global__ void decode_attn_combine_kernel(const DecAttnPart* __restrict__ acc, 
   *reinterpret_cast<uint2*>(out + (size_t)i * 128 + lane * 4) = w;
 }
 
-// x[b] += alpha * (sum of the partials of row b); xn[b] = RMSNorm(x[b]) * gamma. One
-// block per row (the partial sums are many short independent loads: spread them).
-constexpr int DEC_NORM_THREADS = 512;
-constexpr int DEC_NORM_PER_THREAD = 16;  // rows up to 8192 wide
+// x[b] += alpha * (sum of the partials of row b); xn[b] = RMSNorm(x[b]) * gamma. A
+// cluster of DEC_NORM_CTAS CTAs per row (the partial sums are many short independent
+// loads: spread them over 4x the SMs of one block per row): CTA r adds the partials of
+// its quarter of the columns into x, the quarters' sums of x^2 meet through distributed
+// shared memory (added in rank order, so every CTA of the row computes the same 1/rms),
+// and each CTA normalises its quarter.
+constexpr int DEC_NORM_CTAS = 4;
+constexpr int DEC_NORM_THREADS = 256;
+constexpr int DEC_NORM_PER_THREAD = 8;  // rows up to 4 x 256 x 8 = 8192 wide
 
-__global__ void __launch_bounds__(DEC_NORM_THREADS)
+template <int MAXS>
+__global__ void __cluster_dims__(DEC_NORM_CTAS, 1, 1) __launch_bounds__(DEC_NORM_THREADS)
     decode_residual_norm_kernel(const float* __restrict__ part, int splits, int B, int dim,
                                 float alpha, float* __restrict__ x,
                                 const float* __restrict__ gamma, __half* __restrict__ xn) {
   pdl_enter();
   __shared__ float red[DEC_NORM_THREADS / 32];
-  const int b = blockIdx.x;
+  __shared__ float quarter;
+  const uint32_t rank = cluster_ctarank();
+  const int b = blockIdx.x / DEC_NORM_CTAS;
+  const int cols = (dim + DEC_NORM_CTAS - 1) / DEC_NORM_CTAS;
+  const int c0 = (int)rank * cols, c1 = min(dim, c0 + cols);
   const size_t slice = (size_t)B * dim;
   float* xr = x + (size_t)b * dim;
-  // The row stays in registers (dim <= DEC_NORM_THREADS * DEC_NORM_PER_THREAD), and gamma
-  // is loaded with the residual, so the kernel makes one round trip to memory before the
-  // reduction instead of three.
+  // The quarter row stays in registers, and gamma is loaded with the residual, so the
+  // kernel makes one round trip to memory before the reduction.
   float v[DEC_NORM_PER_THREAD], gm[DEC_NORM_PER_THREAD];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
-    const int c = threadIdx.x + i * DEC_NORM_THREADS;
+    const int c = c0 + threadIdx.x + i * DEC_NORM_THREADS;
     v[i] = 0.f;
     gm[i] = 0.f;
-    if (c < dim) {
+    if (c < c1) {
       gm[i] = __ldg(gamma + c);
-      v[i] = xr[c] + alpha * sum_parts(part, splits, slice, (size_t)b * dim + c);
+      v[i] = xr[c] + alpha * sum_parts<MAXS>(part, splits, slice, (size_t)b * dim + c);
       xr[c] = v[i];
       ss += v[i] * v[i];
     }
@@ -247,14 +278,23 @@ __global__ void __launch_bounds__(DEC_NORM_THREADS)
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < DEC_NORM_THREADS / 32; ++w) t += red[w];
+    quarter = t;
+  }
+  cluster_sync();  // every quarter's sum is in its CTA's shared memory
   float tot = 0.f;
 #pragma unroll
-  for (int w = 0; w < DEC_NORM_THREADS / 32; ++w) tot += red[w];
+  for (int r = 0; r < DEC_NORM_CTAS; ++r)
+    tot += ld_shared_cluster_f32(mapa_shared(smem_u32(&quarter), (uint32_t)r));
+  cluster_sync();  // no CTA leaves while a peer may still read its sum
   const float rinv = 1.0f / sqrtf(tot / (float)dim + RMS_EPS);
 #pragma unroll
   for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
-    const int c = threadIdx.x + i * DEC_NORM_THREADS;
-    if (c < dim) xn[(size_t)b * dim + c] = __float2half_rn(v[i] * rinv * gm[i]);
+    const int c = c0 + threadIdx.x + i * DEC_NORM_THREADS;
+    if (c < c1) xn[(size_t)b * dim + c] = __float2half_rn(v[i] * rinv * gm[i]);
   }
 }
 
@@ -381,9 +421,10 @@ void free_decode_state(DecodeState* s) {
 static cb_status alloc_decode(cb_ctx* c) {
   if (c->decode) return CB_OK;
   const cb_model_config& cfg = c->cfg;
-  if (cfg.dim > DEC_NORM_THREADS * DEC_NORM_PER_THREAD)
-    return fail(c, CB_ERR_UNSUPPORTED, "decode supports dim <= " +
-                                           std::to_string(DEC_NORM_THREADS * DEC_NORM_PER_THREAD));
+  if (cfg.dim > DEC_NORM_CTAS * DEC_NORM_THREADS * DEC_NORM_PER_THREAD)
+    return fail(c, CB_ERR_UNSUPPORTED,
+                "decode supports dim <= " +
+                    std::to_string(DEC_NORM_CTAS * DEC_NORM_THREADS * DEC_NORM_PER_THREAD));
   const size_t B = c->max_batch, S = cfg.seq, L = cfg.nlayers, d = cfg.dim, V = cfg.vocab;
   const size_t h = c->hidden_l, qd = c->q_dim, nq = c->n_qkv;
   DecodeState* s = new DecodeState;
@@ -433,8 +474,12 @@ static cb_status alloc_decode(cb_ctx* c) {
 // Split count for a decode GEMM (M <= 128 rows, 1-CTA 128-wide tiles): about one work
 // unit per SM, every split non-empty.
 static int decode_splits(int N, int K, const DeviceInfo& di) {
+  static const int cap = [] {  // CB_DECODE_MAX_SPLITS: a lower cap, for sweeps
+    const char* e = getenv("CB_DECODE_MAX_SPLITS");
+    return e ? std::max(1, std::min(DEC_MAX_SPLITS, atoi(e))) : DEC_MAX_SPLITS;
+  }();
   const int tiles = (N + 127) / 128, kb = (K + GEMM_BK - 1) / GEMM_BK;
-  int s = std::max(1, std::min(DEC_MAX_SPLITS, (di.sms + tiles / 2) / tiles));
+  int s = std::max(1, std::min(cap, (di.sms + tiles / 2) / tiles));
   s = std::min(s, kb);
   const int per = (kb + s - 1) / s;
   return (kb + per - 1) / per;
@@ -495,7 +540,9 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
                       (const DecAttnPart*)s->attn_acc, kv_splits, H, B * H, s->o)) != cudaSuccess)
       return e;
     if ((e = gemm(s->tm_o, c->tm_wo[0], d, qd, l, alpha, &sp)) != cudaSuccess) return e;
-    if ((e = launch_k(decode_residual_norm_kernel, dim3(B), dim3(DEC_NORM_THREADS), 0, st, false,
+    if ((e = launch_k(sp <= 4 ? decode_residual_norm_kernel<4>
+                              : decode_residual_norm_kernel<DEC_MAX_SPLITS>,
+                      dim3(B * DEC_NORM_CTAS), dim3(DEC_NORM_THREADS), 0, st, false,
                       part, sp, B, d, 1.0f, s->x, (const float*)(c->gamma + (size_t)l * 2 * d + d),
                       s->xn)) != cudaSuccess)
       return e;
@@ -506,7 +553,9 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
       return e;
     if ((e = gemm(s->tm_g, c->tm_w2[0], d, hid, l, alpha, &sp)) != cudaSuccess) return e;
     const float* gnext = l + 1 < L ? c->gamma + (size_t)(l + 1) * 2 * d : c->gamma_final;
-    if ((e = launch_k(decode_residual_norm_kernel, dim3(B), dim3(DEC_NORM_THREADS), 0, st, false,
+    if ((e = launch_k(sp <= 4 ? decode_residual_norm_kernel<4>
+                              : decode_residual_norm_kernel<DEC_MAX_SPLITS>,
+                      dim3(B * DEC_NORM_CTAS), dim3(DEC_NORM_THREADS), 0, st, false,
                       part, sp, B, d, 1.0f, s->x, gnext, s->xn)) != cudaSuccess)
       return e;
   }
