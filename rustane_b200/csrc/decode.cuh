@@ -235,42 +235,33 @@ __global__ void decode_attn_combine_kernel(const DecAttnPart* __restrict__ acc, 
   *reinterpret_cast<uint2*>(out + (size_t)i * 128 + lane * 4) = w;
 }
 
-// x[b] += alpha * (sum of the partials of row b); xn[b] = RMSNorm(x[b]) * gamma. A
-// cluster of DEC_NORM_CTAS CTAs per row (the partial sums are many short independent
-// loads: spread them over 4x the SMs of one block per row): CTA r adds the partials of
-// its quarter of the columns into x, the quarters' sums of x^2 meet through distributed
-// shared memory (added in rank order, so every CTA of the row computes the same 1/rms),
-// and each CTA normalises its quarter.
-constexpr int DEC_NORM_CTAS = 4;
-constexpr int DEC_NORM_THREADS = 256;
-constexpr int DEC_NORM_PER_THREAD = 8;  // rows up to 4 x 256 x 8 = 8192 wide
+// x[b] += alpha * (sum of the partials of row b); xn[b] = RMSNorm(x[b]) * gamma. One
+// block per row (the partial sums are many short independent loads: spread them).
+constexpr int DEC_NORM_THREADS = 512;
+constexpr int DEC_NORM_PER_THREAD = 16;  // rows up to 8192 wide
 
-template <int MAXS>
-__global__ void __cluster_dims__(DEC_NORM_CTAS, 1, 1) __launch_bounds__(DEC_NORM_THREADS)
+__global__ void __launch_bounds__(DEC_NORM_THREADS)
     decode_residual_norm_kernel(const float* __restrict__ part, int splits, int B, int dim,
                                 float alpha, float* __restrict__ x,
                                 const float* __restrict__ gamma, __half* __restrict__ xn) {
   pdl_enter();
   __shared__ float red[DEC_NORM_THREADS / 32];
-  __shared__ float quarter;
-  const uint32_t rank = cluster_ctarank();
-  const int b = blockIdx.x / DEC_NORM_CTAS;
-  const int cols = (dim + DEC_NORM_CTAS - 1) / DEC_NORM_CTAS;
-  const int c0 = (int)rank * cols, c1 = min(dim, c0 + cols);
+  const int b = blockIdx.x;
   const size_t slice = (size_t)B * dim;
   float* xr = x + (size_t)b * dim;
-  // The quarter row stays in registers, and gamma is loaded with the residual, so the
-  // kernel makes one round trip to memory before the reduction.
+  // The row stays in registers (dim <= DEC_NORM_THREADS * DEC_NORM_PER_THREAD), and gamma
+  // is loaded with the residual, so the kernel makes one round trip to memory before the
+  // reduction instead of three.
   float v[DEC_NORM_PER_THREAD], gm[DEC_NORM_PER_THREAD];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
-    const int c = c0 + threadIdx.x + i * DEC_NORM_THREADS;
+    const int c = threadIdx.x + i * DEC_NORM_THREADS;
     v[i] = 0.f;
     gm[i] = 0.f;
-    if (c < c1) {
+    if (c < dim) {
       gm[i] = __ldg(gamma + c);
-      v[i] = xr[c] + alpha * sum_parts<MAXS>(part, splits, slice, (size_t)b * dim + c);
+      v[i] = xr[c] + alpha * sum_parts(part, splits, slice, (size_t)b * dim + c);
       xr[c] = v[i];
       ss += v[i] * v[i];
     }
@@ -278,23 +269,14 @@ __global__ void __cluster_dims__(DEC_NORM_CTAS, 1, 1) __launch_bounds__(DEC_NORM
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < DEC_NORM_THREADS / 32; ++w) t += red[w];
-    quarter = t;
-  }
-  cluster_sync();  // every quarter's sum is in its CTA's shared memory
   float tot = 0.f;
 #pragma unroll
-  for (int r = 0; r < DEC_NORM_CTAS; ++r)
-    tot += ld_shared_cluster_f32(mapa_shared(smem_u32(&quarter), (uint32_t)r));
-  cluster_sync();  // no CTA leaves while a peer may still read its sum
+  for (int w = 0; w < DEC_NORM_THREADS / 32; ++w) tot += red[w];
   const float rinv = 1.0f / sqrtf(tot / (float)dim + RMS_EPS);
 #pragma unroll
   for (int i = 0; i < DEC_NORM_PER_THREAD; ++i) {
-    const int c = c0 + threadIdx.x + i * DEC_NORM_THREADS;
-    if (c < c1) xn[(size_t)b * dim + c] = __float2half_rn(v[i] * rinv * gm[i]);
+    const int c = threadIdx.x + i * DEC_NORM_THREADS;
+    if (c < dim) xn[(size_t)b * dim + c] = __float2half_rn(v[i] * rinv * gm[i]);
   }
 }
 
@@ -421,10 +403,9 @@ void free_decode_state(DecodeState* s) {
 static cb_status alloc_decode(cb_ctx* c) {
   if (c->decode) return CB_OK;
   const cb_model_config& cfg = c->cfg;
-  if (cfg.dim > DEC_NORM_CTAS * DEC_NORM_THREADS * DEC_NORM_PER_THREAD)
-    return fail(c, CB_ERR_UNSUPPORTED,
-                "decode supports dim <= " +
-                    std::to_string(DEC_NORM_CTAS * DEC_NORM_THREADS * DEC_NORM_PER_THREAD));
+  if (cfg.dim > DEC_NORM_THREADS * DEC_NORM_PER_THREAD)
+    return fail(c, CB_ERR_UNSUPPORTED, "decode supports dim <= " +
+                                           std::to_string(DEC_NORM_THREADS * DEC_NORM_PER_THREAD));
   const size_t B = c->max_batch, S = cfg.seq, L = cfg.nlayers, d = cfg.dim, V = cfg.vocab;
   const size_t h = c->hidden_l, qd = c->q_dim, nq = c->n_qkv;
   DecodeState* s = new DecodeState;
@@ -540,9 +521,7 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
                       (const DecAttnPart*)s->attn_acc, kv_splits, H, B * H, s->o)) != cudaSuccess)
       return e;
     if ((e = gemm(s->tm_o, c->tm_wo[0], d, qd, l, alpha, &sp)) != cudaSuccess) return e;
-    if ((e = launch_k(sp <= 4 ? decode_residual_norm_kernel<4>
-                              : decode_residual_norm_kernel<DEC_MAX_SPLITS>,
-                      dim3(B * DEC_NORM_CTAS), dim3(DEC_NORM_THREADS), 0, st, false,
+    if ((e = launch_k(decode_residual_norm_kernel, dim3(B), dim3(DEC_NORM_THREADS), 0, st, false,
                       part, sp, B, d, 1.0f, s->x, (const float*)(c->gamma + (size_t)l * 2 * d + d),
                       s->xn)) != cudaSuccess)
       return e;
@@ -553,9 +532,7 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
       return e;
     if ((e = gemm(s->tm_g, c->tm_w2[0], d, hid, l, alpha, &sp)) != cudaSuccess) return e;
     const float* gnext = l + 1 < L ? c->gamma + (size_t)(l + 1) * 2 * d : c->gamma_final;
-    if ((e = launch_k(sp <= 4 ? decode_residual_norm_kernel<4>
-                              : decode_residual_norm_kernel<DEC_MAX_SPLITS>,
-                      dim3(B * DEC_NORM_CTAS), dim3(DEC_NORM_THREADS), 0, st, false,
+    if ((e = launch_k(decode_residual_norm_kernel, dim3(B), dim3(DEC_NORM_THREADS), 0, st, false,
                       part, sp, B, d, 1.0f, s->x, gnext, s->xn)) != cudaSuccess)
       return e;
   }

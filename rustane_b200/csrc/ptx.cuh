@@ -397,13 +397,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
-// 32-bit load from a shared::cluster address (distributed shared memory of a peer CTA).
-__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
-}
-
 // Whole-cluster barrier (every thread of every CTA in the cluster).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
