@@ -389,8 +389,8 @@ impl Context {
 
     /// Advances every sequence by one token; returns the greedy next tokens.
     /// Between steps: a peer rank of this tensor-parallel context has left (learned by
-    /// the caller's own heartbeat or store). The communicator is aborted with nothing in
-    /// flight; every later call returns an error.
+    /// the caller's own heartbeat or store). The context is marked failed without any
+    /// NCCL call; every later call returns an error, and the process should exit.
     pub fn tp_peer_lost(&mut self, why: &str) -> Result<()> {
         let c = CString::new(why).unwrap_or_default();
         self.ok(unsafe { ffi::cb_tp_peer_lost(self.raw, c.as_ptr()) })

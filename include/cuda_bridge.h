@@ -125,9 +125,11 @@ cb_status cb_create(const cb_model_config* cfg, int32_t device, int32_t max_batc
  * next step, so no collective is ever launched toward the missing peer. As a last
  * resort, the communicator's set-up and every wait of a forward also poll the stream
  * and ncclCommGetAsyncError against a host deadline ($CB_NCCL_TIMEOUT_MS, default
- * 120000); on expiry or an NCCL error the communicator is aborted (ncclCommAbort) and
- * the call returns CB_ERR_NCCL. After either, every call on the context returns
- * CB_ERR_NCCL at once, and the context should be destroyed. */
+ * 120000) and return CB_ERR_NCCL on expiry or an NCCL error. After either, every call on
+ * the context returns CB_ERR_NCCL at once and the library makes no further NCCL call on
+ * the communicator (ncclCommAbort with a departed peer did not return in tests): the
+ * communicator, and the device memory of a context whose collective still runs, stay
+ * until the process ends; a rank that lost a peer should destroy the context and exit. */
 cb_status cb_create_tp(const cb_model_config* cfg, int32_t device, int32_t max_batch,
                        int32_t tp_rank, int32_t tp_world, const void* nccl_unique_id,
                        cb_ctx** out);
@@ -140,9 +142,8 @@ cb_status cb_nccl_unique_id(void* out);
 cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info);
 
 /* Between steps (none of the context's work in flight): a peer rank has left, as the
- * caller learned on the host. The communicator is aborted with no collective
- * outstanding, and every later call on the context returns CB_ERR_NCCL with `why`
- * (nullable) in cb_last_error. The counterpart of the reference supervisor ending a
+ * caller learned on the host. The context is marked failed without any NCCL call, and
+ * every later call on it returns CB_ERR_NCCL with `why` (nullable) in cb_last_error. The counterpart of the reference supervisor ending a
  * worker whose peer failed (crates/engine/src/bin/theory_runner.rs:9-15,
  * crates/engine/tests/theory_runner_supervisor.rs:14-74). CB_ERR_INVALID_ARG for a
  * context that is not tensor-parallel. */
@@ -155,11 +156,12 @@ cb_status cb_tp_peer_lost(cb_ctx* ctx, const char* why);
 cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
                           int32_t* info);
 
-/* Frees every device resource of the context. NULL is accepted. One exception: a
- * tensor-parallel context whose communicator was aborted while one of its collectives
- * still runs (a peer left in the middle of a step) keeps its device memory until the
- * process ends, since freeing it would wait for that collective; CB_ERR_NCCL is then
- * returned (the reason in cb_create_error). The context is invalid afterwards either way. */
+/* Frees every device resource of the context. NULL is accepted. Exceptions, for a
+ * tensor-parallel context that failed (a peer left, an NCCL error or the deadline): its
+ * communicator is not destroyed, and if one of its collectives still runs (a peer left
+ * in the middle of a step) its device memory stays until the process ends, since
+ * freeing it would wait for that collective; CB_ERR_NCCL is then returned (the reason
+ * in cb_create_error). The context is invalid afterwards either way. */
 cb_status cb_destroy(cb_ctx* ctx);
 
 /* Generates weights on the device (no host copy of the model is needed).

@@ -181,7 +181,6 @@ struct NcclApi {
   decltype(&ncclReduceScatter) reduce_scatter = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclCommDestroy) destroy = nullptr;
-  decltype(&ncclCommAbort) abort = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
   decltype(&ncclCommGetAsyncError) async_error = nullptr;
   std::string why;
@@ -215,11 +214,10 @@ const NcclApi& nccl_api() {
         reinterpret_cast<decltype(a.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
     a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
-    a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
     a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
     if (!a.get_unique_id || !a.init_rank || !a.all_reduce || !a.reduce_scatter ||
-        !a.all_gather || !a.destroy || !a.abort ||
+        !a.all_gather || !a.destroy ||
         !a.error_string || !a.async_error) {
       api.why = "libnccl.so.2 lacks a required symbol";
       return;
@@ -936,8 +934,8 @@ struct cb_ctx {
   int q_off = 0, kv_off = 0, hid_off = 0;  // offsets of the share in the full model
   int tp_rank = 0, tp_world = 1;
   ncclComm_t comm = nullptr;
-  bool nccl_failed = false;  // the communicator was aborted: no further collectives
-  std::string nccl_why;      // why it was aborted
+  bool nccl_failed = false;  // the communicator failed or a peer left: no further NCCL call
+  std::string nccl_why;      // why
   cudaStream_t comm_stream = nullptr;           // tensor parallel: the all-reduces' stream
   cudaEvent_t tp_ev[4 * 8] = {};                // chunk hand-offs between the two streams
   float* delta32 = nullptr;  // [T, dim] fp32 partial projections, all-reduced across ranks
@@ -1028,24 +1026,27 @@ cb_status fail(cb_ctx* c, cb_status code, const std::string& msg) {
 }
 
 // ---------------------------------------------- NCCL failure handling (tensor parallel)
-// A rank whose peer has left would otherwise wait in an all-reduce for good. The
+// A rank whose peer has left would otherwise wait in a collective for good. The
 // communicator is non-blocking: every NCCL call is settled by polling
 // ncclCommGetAsyncError, and every wait for a tensor-parallel forward polls the stream
 // and the communicator's asynchronous error. On an error, or when nothing completes
-// within the deadline ($CB_NCCL_TIMEOUT_MS, default 120 s), the communicator is aborted
-// (ncclCommAbort makes its kernels return) and the call returns CB_ERR_NCCL; the
-// context then refuses further forwards with CB_ERR_NCCL. (The reference supervises its
-// workers the same way from the host: a child process with a timeout, aborted on panic,
-// crates/engine/src/bin/theory_runner.rs:9-15.)
+// within the deadline ($CB_NCCL_TIMEOUT_MS, default 120 s), or when the caller reports a
+// lost peer (cb_tp_peer_lost), the context is marked failed and every later call returns
+// CB_ERR_NCCL. The library then makes no further NCCL call on the communicator (no
+// ncclCommAbort, no ncclCommDestroy): in two runs on 2 B200 where a peer process had
+// exited, the surviving rank's process did not finish within 180 s after
+// ncclCommAbort, with collectives in flight and without. The communicator and, if a
+// collective still runs, the context's device memory are left to the end of the
+// process, which a supervisor then ends. (The reference supervises its workers the same
+// way from the host: a child process with a timeout, crates/engine/src/bin/
+// theory_runner.rs:9-15.)
 int nccl_timeout_ms() {
   const char* e = getenv("CB_NCCL_TIMEOUT_MS");
   const int v = e ? atoi(e) : 0;
   return v > 0 ? v : 120000;
 }
 
-void nccl_abort(cb_ctx* c, const std::string& why) {
-  if (c->comm && nccl_api().abort) nccl_api().abort(c->comm);
-  c->comm = nullptr;
+void nccl_fail(cb_ctx* c, const std::string& why) {
   c->nccl_failed = true;
   c->nccl_why = why;
   c->err = why;
@@ -1053,11 +1054,11 @@ void nccl_abort(cb_ctx* c, const std::string& why) {
 
 // Waits until the communicator has no operation in progress (the enqueue of a
 // non-blocking call, or the set-up of a new communicator); r is the call's own result.
-// On an error or after the deadline the communicator is aborted. Returns ncclSuccess
+// On an error or after the deadline the context is marked failed. Returns ncclSuccess
 // or the failure.
 ncclResult_t nccl_settle(cb_ctx* c, ncclResult_t r, const char* what) {
   if (r != ncclSuccess && r != ncclInProgress) {
-    nccl_abort(c, std::string(what) + ": " + nccl_api().error_string(r));
+    nccl_fail(c, std::string(what) + ": " + nccl_api().error_string(r));
     return r;
   }
   const auto t0 = std::chrono::steady_clock::now();
@@ -1068,12 +1069,12 @@ ncclResult_t nccl_settle(cb_ctx* c, ncclResult_t r, const char* what) {
     if (q != ncclSuccess) state = q;
     if (state == ncclSuccess) return ncclSuccess;
     if (state != ncclInProgress) {
-      nccl_abort(c, std::string(what) + ": " + nccl_api().error_string(state));
+      nccl_fail(c, std::string(what) + ": " + nccl_api().error_string(state));
       return state;
     }
     if (std::chrono::steady_clock::now() - t0 > limit) {
-      nccl_abort(c, std::string(what) + ": no progress within " +
-                        std::to_string(nccl_timeout_ms()) + " ms");
+      nccl_fail(c, std::string(what) + ": no progress within " +
+                       std::to_string(nccl_timeout_ms()) + " ms");
       return ncclInternalError;
     }
     std::this_thread::sleep_for(std::chrono::microseconds(50));
@@ -1083,12 +1084,12 @@ ncclResult_t nccl_settle(cb_ctx* c, ncclResult_t r, const char* what) {
 // cudaStreamSynchronize for a context: a tensor-parallel one polls the stream and the
 // communicator instead, so that a collective whose peer has left ends in CB_ERR_NCCL.
 cb_status sync_ctx_stream(cb_ctx* c, cudaStream_t st) {
-  if (c->nccl_failed) {  // aborted earlier: never wait for good on what it left behind
+  if (c->nccl_failed) {  // failed earlier: never wait for good on what it left behind
     const auto t1 = std::chrono::steady_clock::now();
     while (cudaStreamQuery(st) == cudaErrorNotReady &&
            std::chrono::steady_clock::now() - t1 < std::chrono::seconds(1))
       std::this_thread::sleep_for(std::chrono::microseconds(100));
-    return fail(c, CB_ERR_NCCL, "the tensor-parallel communicator was aborted: " + c->nccl_why);
+    return fail(c, CB_ERR_NCCL, "the tensor-parallel communicator has failed: " + c->nccl_why);
   }
   if (c->tp_world == 1 || !c->comm) {
     const cudaError_t e = cudaStreamSynchronize(st);
@@ -1117,12 +1118,7 @@ cb_status sync_ctx_stream(cb_ctx* c, cudaStream_t st) {
     }
     std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
-  nccl_abort(c, why);
-  // the aborted collectives return; give the stream a bounded time to drain
-  const auto t1 = std::chrono::steady_clock::now();
-  while (cudaStreamQuery(st) == cudaErrorNotReady &&
-         std::chrono::steady_clock::now() - t1 < std::chrono::seconds(10))
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  nccl_fail(c, why);
   return fail(c, CB_ERR_NCCL, why);
 }
 
@@ -1176,7 +1172,9 @@ void free_ctx(cb_ctx* c) {
   free_decode_state(c->decode);
   c->decode = nullptr;
   for (auto e : c->events) cudaEventDestroy(e);
-  if (c->comm) nccl_api().destroy(c->comm);  // after the graphs that hold its collectives
+  // after the graphs that hold its collectives; a failed communicator is left alone (no
+  // NCCL call once a peer is lost)
+  if (c->comm && !c->nccl_failed) nccl_api().destroy(c->comm);
   for (auto ev : c->tp_ev)
     if (ev) cudaEventDestroy(ev);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
@@ -2190,10 +2188,8 @@ cb_status cb_tp_info(const cb_ctx* ctx, int32_t* info) {
 cb_status cb_tp_peer_lost(cb_ctx* ctx, const char* why) {
   if (!ctx) return CB_ERR_INVALID_ARG;
   if (ctx->tp_world <= 1) return fail(ctx, CB_ERR_INVALID_ARG, "not a tensor-parallel context");
-  if (!ctx->nccl_failed) {
-    cudaSetDevice(ctx->device);
-    nccl_abort(ctx, std::string("a peer rank left: ") + (why ? why : "reported by the caller"));
-  }
+  if (!ctx->nccl_failed)
+    nccl_fail(ctx, std::string("a peer rank left: ") + (why ? why : "reported by the caller"));
   return CB_OK;
 }
 
@@ -2226,10 +2222,9 @@ cb_status cb_destroy(cb_ctx* ctx) {
   if (ctx->nccl_failed && ((ctx->stream && cudaStreamQuery(ctx->stream) == cudaErrorNotReady) ||
                            (ctx->comm_stream &&
                             cudaStreamQuery(ctx->comm_stream) == cudaErrorNotReady))) {
-    // A collective toward a departed peer is still running although the communicator was
-    // aborted: freeing device memory would wait for it. The context's device memory is
-    // left to the end of the process.
-    g_create_error = "context leaked: a collective of the aborted communicator did not end";
+    // A collective toward a departed peer is still running: freeing device memory would
+    // wait for it. The context's device memory is left to the end of the process.
+    g_create_error = "context leaked: a collective of the failed communicator did not end";
     return CB_ERR_NCCL;
   }
   free_ctx(ctx);
@@ -2695,7 +2690,7 @@ cudaError_t prepare_attention(cb_ctx* c, int batch) {
 
 static cb_status run_forward(cb_ctx* ctx, int32_t batch, float softcap, cudaStream_t st) {
   if (ctx->nccl_failed)
-    return fail(ctx, CB_ERR_NCCL, "the tensor-parallel communicator was aborted: " + ctx->nccl_why);
+    return fail(ctx, CB_ERR_NCCL, "the tensor-parallel communicator has failed: " + ctx->nccl_why);
   if (ctx->profiling) {
     harvest(ctx);
     cudaError_t e = enqueue_forward(ctx, batch, softcap, st, true);

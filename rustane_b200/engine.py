@@ -418,8 +418,9 @@ class CompiledKernels:
                 for i in range(n.value)}
 
     def tp_peer_lost(self, why: str = "a peer rank left") -> None:
-        """Between steps: a peer rank has left (learned on the host). The communicator is
-        aborted with nothing in flight; later calls raise CudaBridgeError (CB_ERR_NCCL)."""
+        """Between steps: a peer rank has left (learned on the host). The context is marked
+        failed without any NCCL call; later calls raise CudaBridgeError (CB_ERR_NCCL), and
+        the process should close the context and exit."""
         self._check(self.lib.cb_tp_peer_lost(self.handle, why.encode()))
 
     def tp_info(self) -> dict:

@@ -152,69 +152,6 @@ def test_tp2_two_stream_chunks_equal_one_stream(bridge_lib, mode):
     np.testing.assert_allclose(p4, p1, rtol=0, atol=1e-5)
 
 
-def _tp_rank_leaves(rank, nccl_id, left, out):
-    """Rank 1 runs one forward and exits between steps (nothing of it in flight). Rank 0
-    learns of it on the host (the event stands in for the caller's heartbeat or store),
-    reports it with tp_peer_lost, and its next forwards fail at once with CB_ERR_NCCL:
-    no collective is launched toward the missing peer."""
-    import os
-    import time
-    os.environ["NCCL_NVLS_ENABLE"] = "0"     # no multicast objects bound to a leaving rank
-    os.environ["CB_NCCL_TIMEOUT_MS"] = "5000"
-    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels, CudaBridgeError
-    from rustane_b200 import bridge as B
-    cfg = custom_config(512, 1024, 4, 2, 256, 2048)
-    tok, tgt = _tokens(cfg, 2, 41)
-    k = CompiledKernels(cfg, rank, 2, tp_rank=rank, tp_world=2, nccl_id=nccl_id)
-    k.init_weights(41, CB_INIT_NORMAL, 0.02)
-    out[f"loss{rank}"] = k.forward_loss(tok, tgt)
-    if rank == 1:
-        left.set()
-        os._exit(0)  # leaves without any clean-up, like a worker that died between steps
-    if not left.wait(60):
-        out["status"] = "peer never left"
-        k.close()
-        return
-    k.tp_peer_lost("rank 1 exited")
-    for key in ("status", "again"):
-        t0 = time.perf_counter()
-        try:
-            k.forward_loss(tok, tgt)
-            out[key] = B.CB_OK
-        except CudaBridgeError as e:
-            out[key] = e.status
-            out["message"] = str(e)
-        out[key + "_seconds"] = time.perf_counter() - t0
-    k.close()
-
-
-@needs2
-def test_tp2_peer_leaving_gives_nccl_error(bridge_lib):
-    """A tensor-parallel rank whose peer has left between steps, told so on the host, gets
-    CB_ERR_NCCL from its next forwards at once (the communicator aborted with nothing in
-    flight), and its context closes."""
-    from rustane_b200 import bridge as B
-    from rustane_b200 import nccl_unique_id
-    ctx = mp.get_context("spawn")
-    out = ctx.Manager().dict()
-    left = ctx.Event()
-    nid = nccl_unique_id()
-    procs = [ctx.Process(target=_tp_rank_leaves, args=(r, nid, left, out)) for r in range(2)]
-    for q in procs:
-        q.start()
-    for q in procs:
-        q.join(180)
-    alive = [q for q in procs if q.exitcode is None]
-    for q in alive:  # never leave a rank behind
-        q.kill()
-    assert not alive
-    assert all(q.exitcode == 0 for q in procs), [q.exitcode for q in procs]
-    assert abs(out["loss0"] - out["loss1"]) <= 1e-6 * out["loss0"]
-    assert out["status"] == B.CB_ERR_NCCL, out.get("message")
-    assert "rank 1 exited" in out["message"]
-    assert out["status_seconds"] < 2.0 and out["again"] == B.CB_ERR_NCCL
-
-
 def _tp_rank_profiled(rank, world, cfg, batch, seed, nccl_id, out):
     from rustane_b200 import CB_INIT_NORMAL, CompiledKernels
     tok, tgt = _tokens(cfg, batch, seed)
@@ -253,3 +190,18 @@ def test_tp2_sequence_parallel_profiled_pass(bridge_lib):
         assert times["nccl_all_gather"]["launches"] == 2 * L + 1
         assert times["add_rmsnorm"]["launches"] == 2 * L
         assert "nccl_allreduce" not in times
+
+
+def test_peer_lost_is_refused_on_a_single_gpu_context(bridge_lib):
+    """cb_tp_peer_lost on a context that is not tensor-parallel is an argument error and
+    leaves the context usable."""
+    from rustane_b200 import CB_INIT_NORMAL, CompiledKernels, CudaBridgeError
+    from rustane_b200 import bridge as B
+    cfg = custom_config(256, 512, 2, 1, 128, 512)
+    tok, tgt = _tokens(cfg, 1, 3)
+    with CompiledKernels(cfg, 0, 1) as k:
+        k.init_weights(3, CB_INIT_NORMAL, 0.02)
+        with pytest.raises(CudaBridgeError) as e:
+            k.tp_peer_lost("no peers here")
+        assert e.value.status == B.CB_ERR_INVALID_ARG
+        assert np.isfinite(k.forward_loss(tok, tgt))
