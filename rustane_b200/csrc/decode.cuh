@@ -78,26 +78,27 @@ __global__ void decode_qkv_kernel(const float* __restrict__ part, int splits, in
 }
 
 // Attention of one new query per (sequence, head) over cached keys 0..pos, split along
-// the keys into `nsplit` CTAs (blockIdx.z) of 4 warps; lanes split the 128 dims (4 each),
-// each warp takes 4 keys per step (independent dot-product reductions) with an online
-// softmax in base 2, and loads the K and V rows of its next step before working on the
-// current one (two steps of loads in flight per warp: the kernel is bound by how many
-// bytes of the cache are on their way). A split writes its (max, sum, unnormalised
+// the keys into `nsplit` CTAs (blockIdx.z) of DEC_ATTN_WARPS warps; lanes split the 128
+// dims (4 each), each warp takes 4 keys per step (independent dot-product reductions)
+// with an online softmax in base 2. The kernel is bound by memory latency (the K and V
+// rows a warp waits on), so a CTA has 8 warps at 40 registers: at 64 sequences the 768
+// CTAs of one wave hold ~40 warps per SM. A split writes its (max, sum, unnormalised
 // output) to `acc` for decode_attn_combine_kernel; with one split the kernel writes the
 // output directly.
+constexpr int DEC_ATTN_WARPS = 8;
 struct DecAttnPart {
   float m, l;
   float o[128];
 };
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(DEC_ATTN_WARPS * 32)
     decode_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
                        const __half* __restrict__ vc, const int* __restrict__ pos_ptr,
                        int seq, int heads, int kv_heads, float scale_log2,
                        __half* __restrict__ out, DecAttnPart* __restrict__ acc) {
   pdl_enter();
-  __shared__ float sm_m[4], sm_l[4];
-  __shared__ float sm_o[4][128];
+  __shared__ float sm_m[DEC_ATTN_WARPS], sm_l[DEC_ATTN_WARPS];
+  __shared__ float sm_o[DEC_ATTN_WARPS][128];
   const int h = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
   const int hk = h / (heads / kv_heads);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -116,29 +117,17 @@ __global__ void __launch_bounds__(128)
   }
   const __half* kb = kc + ((size_t)b * kv_heads + hk) * seq * 128 + lane * 4;
   const __half* vb = vc + ((size_t)b * kv_heads + hk) * seq * 128 + lane * 4;
-  // the 4 keys of a step from `base` (keys past the split's end re-read its last key and
-  // are masked below)
-  auto load = [&](int base, uint2 (&ku)[4], uint2 (&vu)[4]) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int kk = min(base + j, k1 - 1);
-      ku[j] = __ldg(reinterpret_cast<const uint2*>(kb + (size_t)kk * 128));
-      vu[j] = __ldg(reinterpret_cast<const uint2*>(vb + (size_t)kk * 128));
-    }
-  };
   float m = -CUDART_INF_F, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  uint2 ku[4], vu[4];
-  int key = k0 + warp * 4;
-  if (key < k1) load(key, ku, vu);
-  for (; key < k1; key += 16) {
-    uint2 kn[4], vn[4];
-    const bool more = key + 16 < k1;
-    if (more) load(key + 16, kn, vn);  // the next step's rows go out first
+  for (int key = k0 + warp * 4; key < k1; key += 4 * DEC_ATTN_WARPS) {
     float s[4];
+    uint2 vu[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ku[j].x));
-      const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ku[j].y));
+      const int kk = min(key + j, k1 - 1);
+      const uint2 ku = __ldg(reinterpret_cast<const uint2*>(kb + (size_t)kk * 128));
+      vu[j] = __ldg(reinterpret_cast<const uint2*>(vb + (size_t)kk * 128));
+      const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ku.x));
+      const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ku.y));
       s[j] = qv[0] * a0.x + qv[1] * a0.y + qv[2] * a1.x + qv[3] * a1.y;
     }
 #pragma unroll
@@ -165,13 +154,6 @@ __global__ void __launch_bounds__(128)
       o[2] += p * v1.x;
       o[3] += p * v1.y;
     }
-    if (more) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ku[j] = kn[j];
-        vu[j] = vn[j];
-      }
-    }
   }
   if (lane == 0) {
     sm_m[warp] = m;
@@ -182,11 +164,11 @@ __global__ void __launch_bounds__(128)
   __syncthreads();
   if (warp == 0) {
     float mx = -CUDART_INF_F;
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm_m[w]);
+    for (int w = 0; w < DEC_ATTN_WARPS; ++w) mx = fmaxf(mx, sm_m[w]);
     float lt = 0.f, r[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < DEC_ATTN_WARPS; ++w) {
       if (sm_m[w] == -CUDART_INF_F) continue;  // a warp that saw no key
-      const float f = exp2f(sm_m[w] - mx);
+      const float f = exp2_mufu(sm_m[w] - mx);
       lt += sm_l[w] * f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) r[i] += sm_o[w][lane * 4 + i] * f;
@@ -512,7 +494,8 @@ static cudaError_t enqueue_decode_step(cb_ctx* c, int B, float softcap, cudaStre
                       part, sp, B, nq, H, Hk, dpos, (const float2*)s->d_cs, S, s->q, kc, vc)) !=
         cudaSuccess)
       return e;
-    if ((e = launch_k(decode_attn_kernel, dim3(H, B, kv_splits), dim3(128), 0, st, false,
+    if ((e = launch_k(decode_attn_kernel, dim3(H, B, kv_splits), dim3(DEC_ATTN_WARPS * 32), 0, st,
+                      false,
                       (const __half*)s->q, (const __half*)kc, (const __half*)vc, dpos, S, H, Hk,
                       scale_log2, s->o, s->attn_acc)) != cudaSuccess)
       return e;

@@ -823,8 +823,11 @@ __device__ __forceinline__ void splitfix_write(uint32_t t_row, int n_chunks, flo
 
 // splitfix_reduce: the accumulator's first n_chunks chunks replaced by the sum of all
 // splits' partials in split order (slab s at slab0 + s * slab_f4 float4s; this unit's own,
-// my_split, read from TMEM), in 16-column halves; the next split's loads are issued
-// before the current one's adds. Rows past M (row_ok false) load nothing.
+// my_split, read from TMEM), in 16-column halves. The other splits' pieces of a half are
+// loaded in batches of FIX_BATCH splits, all loads of a batch in flight before its adds
+// (one L2 round trip per batch and half, not one per split: with one split's loads in
+// flight the reduction ran at a few GB/s per CTA). Rows past M (row_ok false) load nothing.
+constexpr int FIX_BATCH = 4;
 __device__ __forceinline__ void splitfix_reduce(uint32_t t_row, int n_chunks, const float4* slab0,
                                              int slab_f4, int splits, int my_split, int rr,
                                              bool row_ok) {
@@ -833,45 +836,44 @@ __device__ __forceinline__ void splitfix_reduce(uint32_t t_row, int n_chunks, co
     const int c = h >> 1;
     uint32_t r[16];
     tmem_ld_32x32b_x16(t_row + h * 16, r);
-    float4 nxt[4];
-    auto load = [&](int sp) {
-      const float4* src = slab0 + (size_t)sp * slab_f4 + ((size_t)c * 8 + (h & 1) * 4) * 128 + rr;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) nxt[j] = row_ok ? __ldcg(src + j * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
-    };
-    int loaded = -1;  // the split whose half is in (or on its way to) nxt
-    if (my_split != 0) {
-      load(0);
-      loaded = 0;
-    }
-    tmem_ld_wait_regs16(r);
+    const float4* base = slab0 + ((size_t)c * 8 + (h & 1) * 4) * 128 + rr;
     float acc[16];
 #pragma unroll 1
-    for (int sp = 0; sp < splits; ++sp) {
-      float t[16];
-      if (sp == my_split) {
+    for (int sp0 = 0; sp0 < splits; sp0 += FIX_BATCH) {
+      float4 buf[FIX_BATCH][4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) t[i] = __uint_as_float(r[i]);
-      } else {
+      for (int i = 0; i < FIX_BATCH; ++i) {
+        const int sp = sp0 + i;
+        const bool ld = row_ok && sp < splits && sp != my_split;
+        const float4* src = base + (size_t)sp * slab_f4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          t[4 * j] = nxt[j].x;
-          t[4 * j + 1] = nxt[j].y;
-          t[4 * j + 2] = nxt[j].z;
-          t[4 * j + 3] = nxt[j].w;
+        for (int j = 0; j < 4; ++j)
+          buf[i][j] = ld ? __ldcg(src + j * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (sp0 == 0) tmem_ld_wait_regs16(r);
+#pragma unroll
+      for (int i = 0; i < FIX_BATCH; ++i) {
+        const int sp = sp0 + i;
+        if (sp >= splits) break;
+        float t[16];
+        if (sp == my_split) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) t[q] = __uint_as_float(r[q]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            t[4 * j] = buf[i][j].x;
+            t[4 * j + 1] = buf[i][j].y;
+            t[4 * j + 2] = buf[i][j].z;
+            t[4 * j + 3] = buf[i][j].w;
+          }
         }
-      }
-      int o = sp + 1;  // the next split read from memory
-      if (o == my_split) ++o;
-      if (o < splits && o != loaded) {
-        load(o);
-        loaded = o;
-      }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = (sp == 0) ? t[i] : acc[i] + t[i];
+        for (int q = 0; q < 16; ++q) acc[q] = (sp == 0) ? t[q] : acc[q] + t[q];
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(acc[i]);
+    for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(acc[q]);
     tmem_st_32x32b_x16(t_row + h * 16, r);
   }
 }
