@@ -57,8 +57,9 @@ def parse_args():
     p.add_argument("--global-batch", type=int, default=None,
                    help="sequences per step for the whole job (default 64; 16 for 32B)")
     p.add_argument("--tp", action="store_true",
-                   help="tensor parallelism over all ranks (Megatron split, NCCL all-reduce) "
-                        "instead of sequence sharding")
+                   help="tensor parallelism over all ranks (Megatron split; the exchange is "
+                        "set by CB_TP_REDUCE, sequence-parallel fp16 by default) instead of "
+                        "sequence sharding")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-budget-s", type=float, default=12.0,
                    help="CPU-baseline sample budget (seconds of oracle work)")
