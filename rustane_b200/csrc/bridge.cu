@@ -239,18 +239,19 @@ void split_even(int n, int world, int rank, int* begin, int* count) {
 enum GemmMode { GM_SINGLE128 = 0, GM_SINGLE256 = 1, GM_PAIR = 2 };
 
 // Tensor parallelism: the forward runs in TP chunks of sequences so that one chunk's
-// exchange (on its own stream, NCCL capped at tp_comm_sms() CTAs) overlaps the next
+// exchange (on its own stream, NCCL capped at tp_comm_sms(world) CTAs) overlaps the next
 // chunk's GEMMs (which then use the other SMs).
 constexpr int TP_MAX_CHUNKS = 8;
-constexpr int TP_COMM_SMS_DEFAULT = 16;
-// NCCL's CTA cap (and the SMs the overlapped GEMMs leave it): CB_TP_COMM_SMS, 4-64,
-// read once per process.
-int tp_comm_sms() {
-  static const int n = [] {
+// NCCL's CTA cap (and the SMs the overlapped GEMMs leave it): CB_TP_COMM_SMS (4-64, read
+// once per process), else 16 at two ranks and 32 from four ranks up. Measured on the ~32B
+// forward: at TP = 2, 16 CTAs 1200 ms against 32 CTAs 1226 ms per step; at TP = 8, where
+// the exchange is about half of the step, 16 CTAs 480 ms against 32 CTAs 393 ms.
+int tp_comm_sms(int world) {
+  static const int forced = [] {
     const char* e = getenv("CB_TP_COMM_SMS");
-    return e ? std::max(4, std::min(64, atoi(e))) : TP_COMM_SMS_DEFAULT;
+    return e ? std::max(4, std::min(64, atoi(e))) : 0;
   }();
-  return n;
+  return forced ? forced : (world >= 4 ? 32 : 16);
 }
 
 template <int BN, class Epi, int LAYOUT>
@@ -1207,7 +1208,7 @@ cudaError_t enqueue_forward_tp_chunked(cb_ctx* c, int batch, int chunks, float s
   const float alpha = 1.0f / sqrtf(2.0f * (float)L);
   cudaStream_t cs = c->comm_stream;
   DeviceInfo dt = device_info(c->device);
-  dt.sms = std::max(1, dt.sms - tp_comm_sms());
+  dt.sms = std::max(1, dt.sms - tp_comm_sms(c->tp_world));
   dt.pair_clusters = std::max(1, std::min(dt.pair_clusters, dt.sms / 2));
   cudaError_t e;
 #define TRYC(...)                                     \
@@ -1365,7 +1366,7 @@ int tp_reduce_mode() {
 //     rows), residual add + RMSNorm of those rows (x, xn), all-gather of the normalised
 //     fp16 rows into every rank's xn; then the same after W1/W3 -> down.
 // The compute stream works on the other chunk while one chunk's rows are exchanged (NCCL
-// capped at tp_comm_sms() CTAs, the GEMMs on the other SMs). A rank keeps the residual x
+// capped at tp_comm_sms(world) CTAs, the GEMMs on the other SMs). A rank keeps the residual x
 // only for its own rows; after the last layer the final rows of x are all-gathered too
 // (sampled logits read them). The LM head and the loss run over all rows on every rank,
 // so every rank returns the same loss and per-token losses.
@@ -1382,8 +1383,8 @@ cudaError_t enqueue_forward_tp_sp(cb_ctx* c, int batch, int chunks, float softca
   const bool two = !prof && c->comm_stream != nullptr;
   cudaStream_t cs = two ? c->comm_stream : st;
   DeviceInfo dt = device_info(c->device);
-  if (two) {  // the GEMMs leave tp_comm_sms() SMs to NCCL
-    dt.sms = std::max(1, dt.sms - tp_comm_sms());
+  if (two) {  // the GEMMs leave tp_comm_sms(world) SMs to NCCL
+    dt.sms = std::max(1, dt.sms - tp_comm_sms(c->tp_world));
     dt.pair_clusters = std::max(1, std::min(dt.pair_clusters, dt.sms / 2));
   }
   const ncclDataType_t part_type = f16 ? ncclHalf : ncclFloat32;
@@ -2090,12 +2091,12 @@ static cb_status create_ctx(const cb_model_config* cfg, int32_t device, int32_t 
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof(id));
     // NCCL's all-reduces run beside the GEMMs (tp_chunked_forward): cap them at
-    // tp_comm_sms() CTAs, the SMs the GEMMs leave free while they overlap.
+    // tp_comm_sms(world) CTAs, the SMs the GEMMs leave free while they overlap.
     // Non-blocking: the set-up (which waits for every rank) is polled with a deadline.
     ncclResult_t nr;
     if (nccl_api().init_rank_config) {
       ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
-      conf.maxCTAs = tp_comm_sms();
+      conf.maxCTAs = tp_comm_sms(tp_world);
       conf.blocking = 0;
       nr = nccl_api().init_rank_config(&ctx->comm, tp_world, id, tp_rank, &conf);
       if (ctx->comm) nr = nccl_settle(ctx, nr, "ncclCommInitRankConfig");
