@@ -152,7 +152,7 @@ cb_status cb_tp_peer_lost(cb_ctx* ctx, const char* why);
 /* The same info[8] for rank tp_rank of a tp_world split of `cfg`, without a context
  * or a GPU (the split cb_create_tp uses; host-side sharding code and tests share it).
  * CB_ERR_INVALID_ARG for an invalid config, rank or world (world above the kv heads
- * or the 64-column hidden blocks). */
+ * or the 64-column hidden blocks), with the reason in cb_create_error. */
 cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t tp_rank,
                           int32_t* info);
 

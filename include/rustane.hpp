@@ -27,6 +27,7 @@
 #define RUSTANE_HPP
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <chrono>
 #include <cstdint>
@@ -235,6 +236,52 @@ class CompiledKernels {
   static CompiledKernels compile(const ModelConfig& cfg, int32_t device = 0,
                                  int32_t max_batch = 1) {
     return CompiledKernels(cfg, device, max_batch);
+  }
+
+  // Tensor parallelism (cb_create_tp; the reference's head- and hidden-sharded layer,
+  // layer.rs:1906-2053,4943-5139): rank tp_rank of tp_world, one process or thread per
+  // GPU, every rank with the same NCCL unique id (nccl_unique_id() on one rank, handed to
+  // the others by the caller). Every rank returns the same losses.
+  using NcclId = std::array<uint8_t, 128>;
+  CompiledKernels(const ModelConfig& cfg, int32_t device, int32_t max_batch, int32_t tp_rank,
+                  int32_t tp_world, const NcclId& nccl_id)
+      : cfg_(cfg), device_(device), max_batch_(max_batch) {
+    const cb_model_config c = cfg.c();
+    cb_ctx* h = nullptr;
+    check(cb_create_tp(&c, device, max_batch, tp_rank, tp_world, nccl_id.data(), &h), nullptr,
+          "cb_create_tp");
+    ctx_.reset(h);
+  }
+  static NcclId nccl_unique_id() {
+    NcclId id{};
+    check(cb_nccl_unique_id(id.data()), nullptr, "cb_nccl_unique_id");
+    return id;
+  }
+
+  // This rank's share: heads, kv heads and hidden columns, and where they start.
+  struct TpShare {
+    int32_t rank, world, heads, kv_heads, hidden, head0, kv_head0, hidden0;
+  };
+  static TpShare share_of(const int32_t (&a)[8]) {
+    return TpShare{a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7]};
+  }
+  TpShare tp_info() const {
+    int32_t a[8];
+    check(cb_tp_info(ctx_.get(), a), ctx_.get(), "cb_tp_info");
+    return share_of(a);
+  }
+  // The split cb_create_tp would give rank tp_rank, without a context or a GPU.
+  static TpShare tp_partition(const ModelConfig& cfg, int32_t tp_world, int32_t tp_rank) {
+    const cb_model_config c = cfg.c();
+    int32_t a[8];
+    check(cb_tp_partition(&c, tp_world, tp_rank, a), nullptr, "cb_tp_partition");
+    return share_of(a);
+  }
+  // Between steps: a peer rank has left (learned by the caller's heartbeat or store); no
+  // collective is launched toward it, later calls throw (CB_ERR_NCCL), and the process
+  // should destroy the context and exit.
+  void tp_peer_lost(const std::string& why) {
+    check(cb_tp_peer_lost(ctx_.get(), why.c_str()), ctx_.get(), "cb_tp_peer_lost");
   }
 
   const ModelConfig& cfg() const { return cfg_; }

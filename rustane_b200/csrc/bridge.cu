@@ -2198,7 +2198,9 @@ cb_status cb_tp_partition(const cb_model_config* cfg, int32_t tp_world, int32_t 
                           int32_t* info) {
   if (!info) return CB_ERR_INVALID_ARG;
   std::string why;
-  return tp_partition(cfg, tp_world, tp_rank, info, &why);
+  const cb_status rc = tp_partition(cfg, tp_world, tp_rank, info, &why);
+  if (rc != CB_OK) g_create_error = why;  // cb_create_error() tells the caller why
+  return rc;
 }
 
 cb_status cb_attention_schedule(int32_t batch, int32_t heads, int32_t kv_heads, int32_t seq,

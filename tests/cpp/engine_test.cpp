@@ -137,9 +137,28 @@ static void host_type_tests() {
   EXPECT(threw);
 }
 
+// The tensor-parallel split as the C++ API reports it (no context, no GPU): 52 heads and
+// 17920 hidden columns (280 blocks of 64) over 8 ranks, every head and column once.
+static void tp_split_tests() {
+  const ModelConfig c = custom_config(6656, 17920, 52, 60, 2048);
+  int32_t heads = 0, hidden = 0, next_head = 0, next_col = 0;
+  for (int32_t r = 0; r < 8; ++r) {
+    const CompiledKernels::TpShare s = CompiledKernels::tp_partition(c, 8, r);
+    EXPECT(s.rank == r && s.world == 8);
+    EXPECT(s.heads == (r < 4 ? 7 : 6) && s.kv_heads == s.heads);
+    EXPECT(s.head0 == next_head && s.hidden0 == next_col && s.hidden % 64 == 0);
+    heads += s.heads, hidden += s.hidden;
+    next_head += s.heads, next_col += s.hidden;
+  }
+  EXPECT(heads == 52 && hidden == 17920);
+  EXPECT(throws_status([&] { CompiledKernels::tp_partition(c, 53, 0); }, CB_ERR_INVALID_ARG,
+                       "larger than the kv heads"));
+}
+
 static void cpu_tests() {
   bench_runner_tests();
   host_type_tests();
+  tp_split_tests();
   // model.rs doc comment: 600M preset ~579M parameters
   EXPECT(std::fabs(ModelConfig::target_600m().param_count() / 1e6 - 579.0) < 1.0);
   const ModelConfig c = custom_config(1536, 4096, 12, 20, 512);
